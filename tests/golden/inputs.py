@@ -1,0 +1,74 @@
+"""Seeded float64 inputs shared by the fixture generator and the tests.
+
+Every case is generated on the CPU in float64 with its own
+``torch.Generator().manual_seed(seed)``, so the generator script and the
+tests build bit-identical tensors without storing them.
+"""
+
+import torch
+
+f64 = dict(dtype=torch.float64)
+
+
+def _g(seed):
+    return torch.Generator().manual_seed(seed)
+
+
+def _znorm_walk(g, B, N):
+    s = torch.cumsum(0.1 * torch.randn(B, N, 1, generator=g, **f64), dim=1)
+    return (s - s.mean(1, keepdim=True)) / s.std(1, keepdim=True)
+
+
+def _udtw(seed, B, N, M, D, **kw):
+    g = _g(seed)
+    X, Y = torch.randn(B, N, D, generator=g, **f64), torch.randn(B, M, D, generator=g, **f64)
+    sx = torch.rand(B, N, 1, generator=g, **f64) + 0.5
+    sy = torch.rand(B, M, 1, generator=g, **f64) + 0.5
+    return [(X, True), (Y, True), (sx, True), (sy, True)], kw
+
+
+def _sdtw(seed, B, N, M, D, walk=False, **kw):
+    g = _g(seed)
+    if walk:
+        X, Y = _znorm_walk(g, B, N), _znorm_walk(g, B, M)
+    else:
+        X, Y = torch.randn(B, N, D, generator=g, **f64), torch.randn(B, M, D, generator=g, **f64)
+    return [(X, True), (Y, True)], kw
+
+
+def _cost(seed, shape, absnormal=False, **kw):
+    g = _g(seed)
+    c = torch.randn(*shape, generator=g, **f64).abs() if absnormal else \
+        torch.rand(*shape, generator=g, **f64)
+    return [(c, True)], kw
+
+
+def _qs(seed, qshape, sshape, **kw):
+    g = _g(seed)
+    return [(torch.randn(*qshape, generator=g, **f64), True),
+            (torch.randn(*sshape, generator=g, **f64), True)], kw
+
+
+SCALED_CASES = {
+    "udtw_cfg1": lambda: _udtw(101, 4, 30, 40, 8, gamma=1.0, beta=1.0),
+    "udtw_band": lambda: _udtw(102, 2, 48, 52, 6, gamma=0.1, beta=0.7, bandwidth=6),
+    "udtw_norm": lambda: _udtw(103, 2, 33, 37, 5, gamma=0.3, beta=0.5, normalize=True),
+    "udtw_nm": lambda: _udtw(104, 2, 70, 45, 3, gamma=0.5, beta=1.0),
+    "sdtw_cfg2": lambda: _sdtw(105, 3, 140, 140, 1, walk=True, gamma=0.1),
+    "sdtw_cfg5": lambda: _sdtw(106, 1, 256, 256, 64, gamma=0.01),
+    "sdtw_norm": lambda: _sdtw(107, 2, 64, 80, 4, gamma=0.2, normalize=True),
+    "sdtw_cost_band": lambda: _cost(108, (2, 70, 60), gamma=0.1, bandwidth=15),
+    "sdtw_cost_long": lambda: _cost(109, (2, 200, 170), gamma=0.05),
+    "jeanie_cfg3": lambda: _qs(110, (2, 15, 10, 32), (2, 10, 32), gamma=0.1, max_shift=1,
+                               metric="euclidean"),
+    "jeanie_2d": lambda: _qs(111, (2, 3, 4, 12, 16), (2, 14, 16), gamma=0.1, max_shift=(1, 2),
+                             metric="sqeuclidean"),
+    "jeanie_cost_big": lambda: _cost(112, (2, 9, 40, 50), gamma=0.1, max_shift=2),
+    "fvm_cfg4": lambda: _qs(113, (2, 7, 7, 10, 32), (2, 10, 32), gamma=0.1),
+    "fvm_cost_cfg4": lambda: _cost(114, (2, 7, 7, 10, 10), absnormal=True, gamma=0.1),
+}
+
+
+def make(name):
+    """(list of (tensor, requires_grad), kwargs) for a scaled case."""
+    return SCALED_CASES[name]()
