@@ -1,0 +1,119 @@
+/*
+ * torchwarp_b200 — C ABI of the B200 (sm_100a) differentiable-alignment kernels.
+ *
+ * Contract for every entry point:
+ *   - All tensor pointers are device pointers to contiguous row-major arrays
+ *     of the stated dtype (f32 = float, f64 = double).  The library never
+ *     allocates or frees memory: the caller passes outputs, the saved state
+ *     of a forward call (size from *_saved_bytes) and scratch workspace (size
+ *     from *_workspace_bytes).
+ *   - `stream` is a cudaStream_t (passed as void*); the work is enqueued on
+ *     it and the call returns without synchronising.  The device is the
+ *     caller's current device.
+ *   - Return value: TW_OK (0) or a TW_ERR_* code; tw_last_error() returns a
+ *     thread-local message for the last failure.  No exception crosses the ABI.
+ *   - A forward and its backward must see the same (B, N, M, dtype) and run on
+ *     the same device: the saved state is laid out by a plan derived from
+ *     those and the device's SM count.
+ *
+ * Reference interfaces replaced (hibana2077/torchwarp, path:line):
+ *   tw_sdtw_forward_*   <- udtw_forward()  src/torchwarp/csrc/udtw_cuda.cu:624-660
+ *                          and jeanie_forward() with K=1 (soft_dtw_from_cost)
+ *                          src/torchwarp/csrc/jeanie_cuda.cu:564-588
+ *   tw_sdtw_backward_*  <- udtw_backward() src/torchwarp/csrc/udtw_cuda.cu:662-697
+ *                          and jeanie_backward() with K=1 (jeanie_cuda.cu:590-619)
+ *   tw_udtw_cost_*      <- the cost/penalty construction inside
+ *                          udtw_fused_forward_kernel (udtw_cuda.cu:298-422) and
+ *                          torch.bmm in udtw/_ops.py:164-165
+ *   tw_udtw_features_grad_* <- udtw_fused_backward's chain rule
+ *                          (udtw_cuda.cu:557-568) plus _features_grads
+ *                          (udtw/_ops.py:179-183)
+ */
+#ifndef TORCHWARP_B200_H_
+#define TORCHWARP_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TW_OK 0
+#define TW_ERR_INVALID 1
+#define TW_ERR_UNSUPPORTED 2
+#define TW_ERR_LAUNCH 3
+#define TW_ERR_TIMEOUT 4
+#define TW_ERR_WORKSPACE 5
+
+/* Library version (major*10000 + minor*100 + patch). */
+int tw_version(void);
+/* Message of the last error on this host thread ("" if none). */
+const char* tw_last_error(void);
+
+/* ---------------------------------------------------------------------
+ * Soft-min DP on a precomputed cost (soft-DTW / uDTW), natural layout.
+ *   cost, penalty: [B, N, M]; penalty may be NULL (soft-DTW: no P output).
+ *   gamma > 0; bandwidth > 0 enables the Sakoe-Chiba band |i - j| <= band.
+ *   out_r [B]: R[N-1, M-1] (+inf if the band makes it unreachable);
+ *   out_p [B]: P[N-1, M-1] (only when penalty != NULL).
+ *   saved: tw_sdtw_saved_bytes() bytes, written here, read by the backward.
+ *   workspace: tw_sdtw_workspace_bytes() bytes of scratch.
+ * ------------------------------------------------------------------- */
+size_t tw_sdtw_saved_bytes(int B, int N, int M, int dtype_bytes, int has_penalty);
+size_t tw_sdtw_workspace_bytes(int B, int N, int M, int dtype_bytes, int has_penalty);
+
+int tw_sdtw_forward_f32(const float* cost, const float* penalty, int B, int N, int M,
+                        double gamma, double bandwidth, float* out_r, float* out_p,
+                        void* saved, size_t saved_bytes, void* workspace, size_t ws_bytes,
+                        void* stream);
+int tw_sdtw_forward_f64(const double* cost, const double* penalty, int B, int N, int M,
+                        double gamma, double bandwidth, double* out_r, double* out_p,
+                        void* saved, size_t saved_bytes, void* workspace, size_t ws_bytes,
+                        void* stream);
+
+/* Backward of the call above for L = sum_b grad_r[b]*out_r[b] + grad_p[b]*out_p[b].
+ *   d_cost, d_penalty: [B, N, M] outputs (d_penalty only when has_penalty). */
+int tw_sdtw_backward_f32(const float* grad_r, const float* grad_p, int B, int N, int M,
+                         double gamma, int has_penalty, const void* saved, size_t saved_bytes,
+                         float* d_cost, float* d_penalty, void* workspace, size_t ws_bytes,
+                         void* stream);
+int tw_sdtw_backward_f64(const double* grad_r, const double* grad_p, int B, int N, int M,
+                         double gamma, int has_penalty, const void* saved, size_t saved_bytes,
+                         double* d_cost, double* d_penalty, void* workspace, size_t ws_bytes,
+                         void* stream);
+
+/* ---------------------------------------------------------------------
+ * uDTW / soft-DTW cost from features (uDTW Eqs. 8, 16):
+ *   sq_ij  = max(|x_i|^2 + |y_j|^2 - 2 x_i.y_j, 0)
+ *   var_ij = max(0.5 (vx_i + vy_j), eps)
+ *   cost_ij = sq_ij / var_ij,  penalty_ij = beta * log(var_ij)
+ * X [B,N,D], Y [B,M,D], vx [B,N], vy [B,M] (vx/vy NULL: variance 1, no penalty).
+ * cost, penalty: [B,N,M] outputs (penalty may be NULL). */
+int tw_udtw_cost_f32(const float* X, const float* Y, const float* vx, const float* vy, int B,
+                     int N, int M, int D, double beta, double eps, float* cost, float* penalty,
+                     void* stream);
+int tw_udtw_cost_f64(const double* X, const double* Y, const double* vx, const double* vy, int B,
+                     int N, int M, int D, double beta, double eps, double* cost, double* penalty,
+                     void* stream);
+
+/* Chain rule of the cost above: given d_cost, d_penalty [B,N,M] (d_penalty may
+ * be NULL), the cost [B,N,M] it was built with, and the inputs, writes
+ *   dX [B,N,D], dY [B,M,D], dvx [B,N], dvy [B,M]  (dvx/dvy may be NULL).
+ * Zero-gradient conventions of torch.clamp_min: none through sq <= 0 or
+ * var_raw <= eps. */
+int tw_udtw_features_grad_f32(const float* X, const float* Y, const float* vx, const float* vy,
+                              const float* cost, const float* d_cost, const float* d_penalty,
+                              int B, int N, int M, int D, double beta, double eps, float* dX,
+                              float* dY, float* dvx, float* dvy, void* stream);
+int tw_udtw_features_grad_f64(const double* X, const double* Y, const double* vx,
+                              const double* vy, const double* cost, const double* d_cost,
+                              const double* d_penalty, int B, int N, int M, int D, double beta,
+                              double eps, double* dX, double* dY, double* dvx, double* dvy,
+                              void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TORCHWARP_B200_H_ */

@@ -1,0 +1,217 @@
+"""uDTW / soft-DTW native kernels vs the reference's golden vectors and the oracle (B200).
+
+float64 cases are held to the reference tests' tolerances (atol 1e-10,
+rtol 1e-9: tests/test_udtw.py:39-41 of hibana2077/torchwarp).  float32 is
+held to the reference's own float32 accuracy bar (max-normalised error vs
+the float64 truth < 1e-3, tests/test_udtw.py:125-136).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import golden_data as G
+
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL = 1e-10, 1e-9
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def tw():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    import torchwarp_b200
+    return torchwarp_b200
+
+
+def _t(a, dtype=torch.float64):
+    return torch.as_tensor(np.asarray(a), dtype=dtype, device=DEV)
+
+
+def _close(got, want, atol=ATOL, rtol=RTOL):
+    np.testing.assert_allclose(got.detach().double().cpu().numpy(), np.asarray(want), atol=atol,
+                               rtol=rtol)
+
+
+def _run_udtw(tw, inputs, dtype=torch.float64, **kw):
+    xs = [_t(x, dtype).requires_grad_(True) for x in inputs]
+    d, p = tw.UDTW(**kw)(*xs)
+    (d.sum() + 2.0 * p.sum()).backward()
+    return [d, p] + [x.grad for x in xs]
+
+
+@pytest.mark.parametrize("N,M", G.UDTW_SHAPES)
+@pytest.mark.parametrize("gamma", G.GAMMAS)
+@pytest.mark.parametrize("normalize", [False, True])
+def test_udtw_golden(tw, N, M, gamma, normalize):
+    ref = G.official("udtw.matches", N=N, M=M, gamma=gamma, normalize=normalize)
+    got = _run_udtw(tw, ref["inputs"], gamma=gamma, beta=0.7, normalize=normalize)
+    for a, b in zip(got, ref["outputs"]):
+        _close(a, b)
+
+
+@pytest.mark.parametrize("N,M,bandwidth", G.UDTW_BANDS)
+def test_udtw_bandwidth_golden(tw, N, M, bandwidth):
+    ref = G.official("udtw.bandwidth", N=N, M=M, bandwidth=bandwidth)
+    got = _run_udtw(tw, ref["inputs"], gamma=0.1, beta=0.7, bandwidth=bandwidth)
+    for a, b in zip(got, ref["outputs"]):
+        _close(a, b)
+
+
+@pytest.mark.parametrize("beta", G.UDTW_BETAS)
+def test_udtw_beta_golden(tw, beta):
+    ref = G.official("udtw.beta", beta=beta)
+    for a, b in zip(_run_udtw(tw, ref["inputs"], gamma=0.1, beta=beta), ref["outputs"]):
+        _close(a, b)
+
+
+def test_udtw_large_golden(tw):
+    ref = G.official("udtw.large", B=2, N=40, M=50)
+    for a, b in zip(_run_udtw(tw, ref["inputs"], gamma=0.1, beta=0.7), ref["outputs"]):
+        _close(a, b)
+
+
+def test_udtw_float32_accuracy(tw):
+    ref = G.official("udtw.float32")
+    got = _run_udtw(tw, ref["inputs"], dtype=torch.float32, gamma=0.1, beta=0.7)
+    for a, b in zip(got, ref["outputs"]):
+        err = np.abs(a.detach().double().cpu().numpy() - b).max() / np.abs(b).max()
+        assert err < 1e-3, err
+
+
+def test_udtw_diff_method_matches_gemm(tw):
+    ref = G.official("udtw.large", B=2, N=40, M=50)
+    a = _run_udtw(tw, ref["inputs"], gamma=0.1, beta=0.7, method="gemm")
+    b = _run_udtw(tw, ref["inputs"], gamma=0.1, beta=0.7, method="diff")
+    for x, y in zip(a, b):
+        _close(x, y.detach().cpu().numpy())
+
+
+@pytest.mark.parametrize("T,U", G.SDTW_SHAPES)
+@pytest.mark.parametrize("gamma", G.GAMMAS)
+def test_soft_dtw_cost_golden(tw, T, U, gamma):
+    ref = G.official("jeanie.soft_dtw", T=T, U=U, gamma=gamma)
+    c = _t(ref["cost"][None]).requires_grad_(True)
+    d = tw.functional.soft_dtw_from_cost(c, gamma=gamma)
+    d.sum().backward()
+    _close(d[0], ref["value"])
+    _close(c.grad[0], ref["grad"])
+
+
+def test_soft_dtw_cost_large_golden(tw):
+    ref = G.official("jeanie.large", name="soft_dtw", shape=(60, 70))
+    c = _t(ref["cost"][None]).requires_grad_(True)
+    d = tw.functional.soft_dtw_from_cost(c, gamma=0.1)
+    d.sum().backward()
+    _close(d[0], ref["value"])
+    _close(c.grad[0], ref["grad"])
+
+
+SCALED = ["udtw_cfg1", "udtw_band", "udtw_norm", "udtw_nm", "sdtw_cfg2", "sdtw_cfg5",
+          "sdtw_norm", "sdtw_cost_band", "sdtw_cost_long"]
+
+
+@pytest.mark.parametrize("name", SCALED)
+def test_scaled_reference_backend(tw, name):
+    """Config-shaped cases against the reference's float64 PyTorch backend."""
+    ins, kw, vals, grads = G.scaled(name)
+    xs = [_t(x).requires_grad_(True) for x in ins]
+    if name.startswith("udtw"):
+        d, p = tw.functional.udtw(*xs, **kw)
+        (d.sum() + 2.0 * p.sum()).backward()
+        got_v = [d, p]
+    elif name.startswith("sdtw_cost"):
+        d = tw.functional.soft_dtw_from_cost(xs[0], **kw)
+        d.sum().backward()
+        got_v = [d]
+    else:
+        d = tw.functional.soft_dtw(xs[0], xs[1], **kw)
+        d.sum().backward()
+        got_v = [d]
+    for a, b in zip(got_v, vals):
+        _close(a, b)
+    for x, g in zip(xs, grads):
+        _close(x.grad, g, atol=1e-9, rtol=1e-8)
+
+
+@pytest.mark.parametrize("B,N,M,band", [
+    (1, 1, 1, 0), (3, 1, 9, 0), (3, 9, 1, 0), (5, 33, 7, 0), (4, 31, 32, 0), (2, 64, 65, 0),
+    (7, 65, 64, 0), (2, 129, 140, 0), (3, 200, 260, 0), (300, 17, 23, 0), (611, 40, 41, 0),
+    (2, 150, 160, 12), (3, 96, 100, 5.5),
+])
+def test_dp_vs_oracle(tw, orc, B, N, M, band):
+    """Shapes that cross the sub-band, band-pass and pairs-per-warp boundaries."""
+    g = torch.Generator().manual_seed(B * 1000 + N * 10 + M)
+    C = torch.rand(B, N, M, generator=g, dtype=torch.float64)
+    Q = torch.randn(B, N, M, generator=g, dtype=torch.float64)
+    gr = torch.rand(B, generator=g, dtype=torch.float64)
+    gp = torch.randn(B, generator=g, dtype=torch.float64)
+    c, q = C.to(DEV).requires_grad_(True), Q.to(DEV).requires_grad_(True)
+    d, p = tw.functional.udtw_from_cost(c, q, gamma=0.3, bandwidth=band or None)
+    (d * gr.to(DEV) + p * gp.to(DEV)).sum().backward()
+    od, op, dC, dQ = orc.udtw_from_cost(C.numpy(), Q.numpy(), gamma=0.3, bandwidth=band or None,
+                                        g_d=gr.numpy(), g_p=gp.numpy())
+    _close(d, od)
+    _close(p, op)
+    _close(c.grad, dC)
+    _close(q.grad, dQ)
+
+
+@pytest.mark.parametrize("B,N,M", [(4, 250, 300), (33, 128, 1024)])
+def test_soft_dtw_cost_vs_oracle(tw, orc, B, N, M):
+    g = torch.Generator().manual_seed(N + M)
+    C = torch.rand(B, N, M, generator=g, dtype=torch.float64)
+    c = C.to(DEV).requires_grad_(True)
+    d = tw.functional.soft_dtw_from_cost(c, gamma=0.05)
+    d.sum().backward()
+    od, dC = orc.soft_dtw_from_cost(C.numpy(), gamma=0.05)
+    _close(d, od)
+    _close(c.grad, dC)
+
+
+def test_soft_dtw_features_fp32_vs_fp64(tw, orc):
+    """cfg5-shaped soft-DTW (N=M=1024, D=64, gamma=0.01) in float32 against
+    the float64 oracle: the forward value within 1e-5 relative."""
+    g = torch.Generator().manual_seed(5)
+    X = torch.randn(2, 1024, 64, generator=g, dtype=torch.float64)
+    Y = torch.randn(2, 1024, 64, generator=g, dtype=torch.float64)
+    x = X.float().to(DEV).requires_grad_(True)
+    d = tw.functional.soft_dtw(x, Y.float().to(DEV), gamma=0.01)
+    d.sum().backward()
+    od, odx, _ = orc.soft_dtw(X.float().double().numpy(), Y.float().double().numpy(), gamma=0.01)
+    rel = np.abs(d.detach().double().cpu().numpy() - od) / np.abs(od)
+    assert rel.max() < 1e-5, rel
+    assert torch.isfinite(x.grad).all()
+
+
+def test_bitwise_deterministic(tw):
+    g = torch.Generator().manual_seed(11)
+    X = torch.randn(64, 300, 16, generator=g).to(DEV)
+    Y = torch.randn(64, 280, 16, generator=g).to(DEV)
+    S = (torch.rand(64, 300, 1, generator=g) + 0.5).to(DEV)
+    T = (torch.rand(64, 280, 1, generator=g) + 0.5).to(DEV)
+
+    def run():
+        xs = [t.clone().requires_grad_(True) for t in (X, Y, S, T)]
+        d, p = tw.UDTW(gamma=0.1, beta=0.7)(*xs)
+        (d.sum() + p.sum()).backward()
+        return [d.detach(), p.detach()] + [t.grad for t in xs]
+
+    first = run()
+    for _ in range(2):
+        assert all(torch.equal(a, b) for a, b in zip(run(), first))
+
+
+def test_unreachable_band_raises(tw):
+    g = torch.Generator().manual_seed(0)
+    xs = [torch.rand(1, 3, 5, generator=g), torch.rand(1, 9, 5, generator=g),
+          torch.rand(1, 3, 1, generator=g) + 0.5, torch.rand(1, 9, 1, generator=g) + 0.5]
+    with pytest.raises(ValueError):
+        tw.UDTW(gamma=0.1, bandwidth=2)(*[x.to(DEV) for x in xs])
+
+
+def test_cpu_tensors_rejected(tw):
+    with pytest.raises(RuntimeError, match="CUDA"):
+        tw.functional.soft_dtw_from_cost(torch.rand(1, 3, 4), gamma=0.1)

@@ -1,0 +1,14 @@
+"""torchwarp_b200: differentiable sequence alignment (soft-DTW, uDTW, JEANIE, FVM)
+on NVIDIA B200 (sm_100a) kernels, with the public API of hibana2077/torchwarp.
+
+    import torchwarp_b200 as torchwarp
+    import torchwarp_b200.functional as TF
+"""
+
+from . import functional
+from .sdtw import SoftDTW
+from .udtw import UDTW
+
+__version__ = "0.1.0"
+
+__all__ = ["UDTW", "SoftDTW", "functional"]

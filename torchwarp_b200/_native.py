@@ -1,0 +1,96 @@
+"""ctypes binding of libtorchwarp_b200.so (the C ABI in include/torchwarp_b200.h).
+
+The library is built ahead of time (``python -m torchwarp_b200.build``); it is
+loaded on first use and a missing or stale build is an error, never a silent
+fallback.  Helpers here turn torch tensors into raw pointers and the current
+CUDA stream into the ``void* stream`` argument.
+"""
+
+import ctypes
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libtorchwarp_b200.so"
+
+_c_p = ctypes.c_void_p
+_c_i = ctypes.c_int
+_c_d = ctypes.c_double
+_c_sz = ctypes.c_size_t
+
+# name -> (restype, argtypes); one entry per symbol of include/torchwarp_b200.h
+SIGNATURES = {
+    "tw_version": (_c_i, []),
+    "tw_last_error": (ctypes.c_char_p, []),
+    "tw_sdtw_saved_bytes": (_c_sz, [_c_i, _c_i, _c_i, _c_i, _c_i]),
+    "tw_sdtw_workspace_bytes": (_c_sz, [_c_i, _c_i, _c_i, _c_i, _c_i]),
+    "tw_sdtw_forward_f32": (_c_i, [_c_p, _c_p, _c_i, _c_i, _c_i, _c_d, _c_d, _c_p, _c_p, _c_p,
+                                   _c_sz, _c_p, _c_sz, _c_p]),
+    "tw_sdtw_forward_f64": (_c_i, [_c_p, _c_p, _c_i, _c_i, _c_i, _c_d, _c_d, _c_p, _c_p, _c_p,
+                                   _c_sz, _c_p, _c_sz, _c_p]),
+    "tw_sdtw_backward_f32": (_c_i, [_c_p, _c_p, _c_i, _c_i, _c_i, _c_d, _c_i, _c_p, _c_sz, _c_p,
+                                    _c_p, _c_p, _c_sz, _c_p]),
+    "tw_sdtw_backward_f64": (_c_i, [_c_p, _c_p, _c_i, _c_i, _c_i, _c_d, _c_i, _c_p, _c_sz, _c_p,
+                                    _c_p, _c_p, _c_sz, _c_p]),
+    "tw_udtw_cost_f32": (_c_i, [_c_p, _c_p, _c_p, _c_p, _c_i, _c_i, _c_i, _c_i, _c_d, _c_d, _c_p,
+                                _c_p, _c_p]),
+    "tw_udtw_cost_f64": (_c_i, [_c_p, _c_p, _c_p, _c_p, _c_i, _c_i, _c_i, _c_i, _c_d, _c_d, _c_p,
+                                _c_p, _c_p]),
+    "tw_udtw_features_grad_f32": (_c_i, [_c_p] * 7 + [_c_i] * 4 + [_c_d, _c_d] + [_c_p] * 5),
+    "tw_udtw_features_grad_f64": (_c_i, [_c_p] * 7 + [_c_i] * 4 + [_c_d, _c_d] + [_c_p] * 5),
+}
+
+_LIB = None
+
+
+class NativeError(RuntimeError):
+    """A C-ABI call returned a non-zero status."""
+
+
+def lib():
+    """Load (once) and return the CDLL with every signature declared."""
+    global _LIB
+    if _LIB is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(
+                "torchwarp_b200: native library {} is missing; build it with "
+                "`python -m torchwarp_b200.build` (CUDA 12.9+, sm_100a)".format(LIB_PATH))
+        L = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _LIB = L
+    return _LIB
+
+
+def check(status, what):
+    if status != 0:
+        msg = lib().tw_last_error().decode(errors="replace")
+        raise NativeError("{} failed (status {}): {}".format(what, status, msg))
+
+
+def ptr(t):
+    """Device pointer of a tensor (None -> NULL)."""
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def stream_of(t):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def suffix(dtype):
+    if dtype == torch.float32:
+        return "f32"
+    if dtype == torch.float64:
+        return "f64"
+    raise TypeError("torchwarp_b200 kernels take float32 or float64, got {}".format(dtype))
+
+
+def require_cuda(*tensors):
+    """The native path is the only path: CPU tensors are rejected loudly."""
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError(
+                "torchwarp_b200 runs only on CUDA tensors (B200, sm_100a); got a tensor on {}. "
+                "There is no CPU fallback.".format(t.device))

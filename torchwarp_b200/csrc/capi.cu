@@ -1,0 +1,233 @@
+// extern "C" entry points of libtorchwarp_b200.so; see include/torchwarp_b200.h.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/torchwarp_b200.h"
+#include "common.cuh"
+#include "sdtw_stream.cuh"
+
+namespace tw {
+
+static thread_local char g_err[512] = "";
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+// SM count of the current device, read once per device.
+static int device_sms() {
+  static std::mutex mu;
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+static size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+static bool dims_ok(int B, int N, int M) { return B >= 0 && N > 0 && M > 0; }
+
+static int check_dims(const char* who, int B, int N, int M) {
+  if (!dims_ok(B, N, M))
+    return set_error(kInvalid, "%s: invalid sizes B=%d N=%d M=%d (need B >= 0, N, M > 0)", who, B,
+                     N, M);
+  const long long steps = ((long long)B * ((N + 127) / 128)) * (long long)(M + 256);
+  if (steps > (1LL << 30))
+    return set_error(kUnsupported, "%s: problem too large for one launch (B=%d N=%d M=%d)", who,
+                     B, N, M);
+  return kOk;
+}
+
+template <typename T>
+static int sdtw_fwd(const T* cost, const T* pen, int B, int N, int M, double gamma, double band,
+                    T* out_r, T* out_p, void* saved, size_t saved_bytes, void* ws, size_t ws_bytes,
+                    cudaStream_t st) {
+  g_err[0] = 0;
+  if (int e = check_dims("tw_sdtw_forward", B, N, M)) return e;
+  if (!(gamma > 0)) return set_error(kInvalid, "tw_sdtw_forward: gamma must be > 0");
+  if (B == 0) return kOk;
+  if (!cost || !out_r || !saved || !ws || (pen && !out_p))
+    return set_error(kInvalid, "tw_sdtw_forward: null pointer argument");
+  const bool has_p = pen != nullptr;
+  StreamPlan p = make_stream_plan(B, N, M, sizeof(T), has_p, device_sms());
+  const size_t sb = align256(p.saved_elems() * sizeof(T)) * (has_p ? 2 : 1);
+  const size_t wb = align256(p.delay_elems() * sizeof(T)) * (has_p ? 2 : 1);
+  if (saved_bytes < sb) return set_error(kWorkspace, "tw_sdtw_forward: saved needs %zu bytes", sb);
+  if (ws_bytes < wb) return set_error(kWorkspace, "tw_sdtw_forward: workspace needs %zu bytes", wb);
+  SdtwArgs<T> a;
+  a.C = cost;
+  a.Q = pen;
+  a.out_r = out_r;
+  a.out_p = out_p;
+  a.sR = static_cast<T*>(saved);
+  a.sP = has_p ? reinterpret_cast<T*>(static_cast<char*>(saved) + sb / 2) : nullptr;
+  a.dlR = static_cast<T*>(ws);
+  a.dlP = has_p ? reinterpret_cast<T*>(static_cast<char*>(ws) + wb / 2) : nullptr;
+  const double kappa = 1.4426950408889634 / gamma;
+  a.kappa = (T)kappa;
+  a.inv_kappa = (T)(1.0 / kappa);
+  a.inv_gamma = (T)(1.0 / gamma);
+  a.pad_raw = (T)((double)Big<T>::value / kappa);
+  if (!std::isfinite((double)a.pad_raw)) a.pad_raw = (T)(Big<T>::value);
+  a.band = (T)band;
+  a.vec = ((M * sizeof(T)) % 16 == 0) && ((uintptr_t)cost % 16 == 0) &&
+          (!pen || (uintptr_t)pen % 16 == 0);
+  a.p = p;
+  return sdtw_stream_forward<T>(a, has_p, band > 0, st);
+}
+
+template <typename T>
+static int sdtw_bwd(const T* grad_r, const T* grad_p, int B, int N, int M, double gamma,
+                    int has_pen, const void* saved, size_t saved_bytes, T* d_cost, T* d_pen,
+                    void* ws, size_t ws_bytes, cudaStream_t st) {
+  g_err[0] = 0;
+  if (int e = check_dims("tw_sdtw_backward", B, N, M)) return e;
+  if (!(gamma > 0)) return set_error(kInvalid, "tw_sdtw_backward: gamma must be > 0");
+  if (B == 0) return kOk;
+  const bool has_p = has_pen != 0;
+  if (!grad_r || !saved || !d_cost || !ws || (has_p && (!grad_p || !d_pen)))
+    return set_error(kInvalid, "tw_sdtw_backward: null pointer argument");
+  StreamPlan p = make_stream_plan(B, N, M, sizeof(T), has_p, device_sms());
+  const size_t sb = align256(p.saved_elems() * sizeof(T)) * (has_p ? 2 : 1);
+  const size_t wb = align256(p.delay_elems() * sizeof(T)) * (has_p ? 2 : 1);
+  if (saved_bytes < sb) return set_error(kWorkspace, "tw_sdtw_backward: saved needs %zu bytes", sb);
+  if (ws_bytes < wb) return set_error(kWorkspace, "tw_sdtw_backward: workspace needs %zu bytes", wb);
+  SdtwArgs<T> a;
+  a.sR = const_cast<T*>(static_cast<const T*>(saved));
+  a.sP = has_p ? reinterpret_cast<T*>(const_cast<char*>(static_cast<const char*>(saved)) + sb / 2)
+               : nullptr;
+  a.dlR = static_cast<T*>(ws);
+  a.dlP = has_p ? reinterpret_cast<T*>(static_cast<char*>(ws) + wb / 2) : nullptr;
+  a.grad_r = grad_r;
+  a.grad_p = grad_p;
+  a.dC = d_cost;
+  a.dQ = d_pen;
+  const double kappa = 1.4426950408889634 / gamma;
+  a.kappa = (T)kappa;
+  a.inv_kappa = (T)(1.0 / kappa);
+  a.inv_gamma = (T)(1.0 / gamma);
+  a.vec = ((M * sizeof(T)) % 16 == 0) && ((uintptr_t)d_cost % 16 == 0) &&
+          (!d_pen || (uintptr_t)d_pen % 16 == 0);
+  a.p = p;
+  return sdtw_stream_backward<T>(a, has_p, false, st);
+}
+
+int udtw_cost_f32(const float*, const float*, const float*, const float*, int, int, int, int,
+                  double, double, float*, float*, cudaStream_t);
+int udtw_cost_f64(const double*, const double*, const double*, const double*, int, int, int, int,
+                  double, double, double*, double*, cudaStream_t);
+int udtw_grad_f32(const float*, const float*, const float*, const float*, const float*,
+                  const float*, const float*, int, int, int, int, double, double, float*, float*,
+                  float*, float*, cudaStream_t);
+int udtw_grad_f64(const double*, const double*, const double*, const double*, const double*,
+                  const double*, const double*, int, int, int, int, double, double, double*,
+                  double*, double*, double*, cudaStream_t);
+
+}  // namespace tw
+
+using namespace tw;
+
+extern "C" {
+
+int tw_version(void) { return 100; }
+
+const char* tw_last_error(void) { return g_err; }
+
+size_t tw_sdtw_saved_bytes(int B, int N, int M, int dtype_bytes, int has_penalty) {
+  if (!dims_ok(B, N, M) || B == 0 || (dtype_bytes != 4 && dtype_bytes != 8)) return 0;
+  StreamPlan p = make_stream_plan(B, N, M, dtype_bytes, has_penalty != 0, device_sms());
+  return align256(p.saved_elems() * dtype_bytes) * (has_penalty ? 2 : 1);
+}
+
+size_t tw_sdtw_workspace_bytes(int B, int N, int M, int dtype_bytes, int has_penalty) {
+  if (!dims_ok(B, N, M) || B == 0 || (dtype_bytes != 4 && dtype_bytes != 8)) return 0;
+  StreamPlan p = make_stream_plan(B, N, M, dtype_bytes, has_penalty != 0, device_sms());
+  return align256(p.delay_elems() * dtype_bytes) * (has_penalty ? 2 : 1);
+}
+
+int tw_sdtw_forward_f32(const float* cost, const float* penalty, int B, int N, int M,
+                        double gamma, double bandwidth, float* out_r, float* out_p, void* saved,
+                        size_t saved_bytes, void* workspace, size_t ws_bytes, void* stream) {
+  return sdtw_fwd<float>(cost, penalty, B, N, M, gamma, bandwidth, out_r, out_p, saved,
+                         saved_bytes, workspace, ws_bytes, (cudaStream_t)stream);
+}
+int tw_sdtw_forward_f64(const double* cost, const double* penalty, int B, int N, int M,
+                        double gamma, double bandwidth, double* out_r, double* out_p, void* saved,
+                        size_t saved_bytes, void* workspace, size_t ws_bytes, void* stream) {
+  return sdtw_fwd<double>(cost, penalty, B, N, M, gamma, bandwidth, out_r, out_p, saved,
+                          saved_bytes, workspace, ws_bytes, (cudaStream_t)stream);
+}
+
+int tw_sdtw_backward_f32(const float* grad_r, const float* grad_p, int B, int N, int M,
+                         double gamma, int has_penalty, const void* saved, size_t saved_bytes,
+                         float* d_cost, float* d_penalty, void* workspace, size_t ws_bytes,
+                         void* stream) {
+  return sdtw_bwd<float>(grad_r, grad_p, B, N, M, gamma, has_penalty, saved, saved_bytes, d_cost,
+                         d_penalty, workspace, ws_bytes, (cudaStream_t)stream);
+}
+int tw_sdtw_backward_f64(const double* grad_r, const double* grad_p, int B, int N, int M,
+                         double gamma, int has_penalty, const void* saved, size_t saved_bytes,
+                         double* d_cost, double* d_penalty, void* workspace, size_t ws_bytes,
+                         void* stream) {
+  return sdtw_bwd<double>(grad_r, grad_p, B, N, M, gamma, has_penalty, saved, saved_bytes,
+                          d_cost, d_penalty, workspace, ws_bytes, (cudaStream_t)stream);
+}
+
+int tw_udtw_cost_f32(const float* X, const float* Y, const float* vx, const float* vy, int B,
+                     int N, int M, int D, double beta, double eps, float* cost, float* penalty,
+                     void* stream) {
+  g_err[0] = 0;
+  if (B < 0 || N <= 0 || M <= 0 || D <= 0 || !X || !Y || !cost || ((vx == nullptr) != (vy == nullptr)))
+    return set_error(kInvalid, "tw_udtw_cost: invalid arguments");
+  return udtw_cost_f32(X, Y, vx, vy, B, N, M, D, beta, eps, cost, penalty, (cudaStream_t)stream);
+}
+int tw_udtw_cost_f64(const double* X, const double* Y, const double* vx, const double* vy, int B,
+                     int N, int M, int D, double beta, double eps, double* cost, double* penalty,
+                     void* stream) {
+  g_err[0] = 0;
+  if (B < 0 || N <= 0 || M <= 0 || D <= 0 || !X || !Y || !cost || ((vx == nullptr) != (vy == nullptr)))
+    return set_error(kInvalid, "tw_udtw_cost: invalid arguments");
+  return udtw_cost_f64(X, Y, vx, vy, B, N, M, D, beta, eps, cost, penalty, (cudaStream_t)stream);
+}
+
+int tw_udtw_features_grad_f32(const float* X, const float* Y, const float* vx, const float* vy,
+                              const float* cost, const float* d_cost, const float* d_penalty,
+                              int B, int N, int M, int D, double beta, double eps, float* dX,
+                              float* dY, float* dvx, float* dvy, void* stream) {
+  g_err[0] = 0;
+  if (B < 0 || N <= 0 || M <= 0 || D <= 0 || !X || !Y || !cost || !d_cost || !dX || !dY ||
+      ((vx == nullptr) != (vy == nullptr)))
+    return set_error(kInvalid, "tw_udtw_features_grad: invalid arguments");
+  return udtw_grad_f32(X, Y, vx, vy, cost, d_cost, d_penalty, B, N, M, D, beta, eps, dX, dY, dvx,
+                       dvy, (cudaStream_t)stream);
+}
+int tw_udtw_features_grad_f64(const double* X, const double* Y, const double* vx,
+                              const double* vy, const double* cost, const double* d_cost,
+                              const double* d_penalty, int B, int N, int M, int D, double beta,
+                              double eps, double* dX, double* dY, double* dvx, double* dvy,
+                              void* stream) {
+  g_err[0] = 0;
+  if (B < 0 || N <= 0 || M <= 0 || D <= 0 || !X || !Y || !cost || !d_cost || !dX || !dY ||
+      ((vx == nullptr) != (vy == nullptr)))
+    return set_error(kInvalid, "tw_udtw_features_grad: invalid arguments");
+  return udtw_grad_f64(X, Y, vx, vy, cost, d_cost, d_penalty, B, N, M, D, beta, eps, dX, dY, dvx,
+                       dvy, (cudaStream_t)stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,81 @@
+// Warp-stream soft-min dynamic program for soft-DTW / uDTW (sm_100a).
+//
+// Work decomposition (host plan, StreamPlan):
+//   * One warp owns the pairs [p0, p0 + npairs).  A pair's N rows are cut into
+//     NB bands of 32*KS rows; a band is one "pass" over L >= M + 1 stream
+//     columns (column j < M is data, j >= M is padding with cost +Big).
+//   * Inside a band, lane l owns rows 32k + l of the KS sub-bands k.  Sub-band
+//     k lags sub-band k-1 by 32 steps and lane l lags lane l-1 by one step, so
+//     at warp step t every lane works on stream column t - 32k - l: all KS
+//     cells of a lane lie on one anti-diagonal and are independent (ILP = KS).
+//   * Passes follow each other without a gap: after a lane finishes column
+//     L-1 of one band it starts column 0 of the next band (or the next pair),
+//     so the warp never drains between bands or pairs.
+//   * Row i-1 -> row i hand-off is one rotating __shfl per sub-band (lane 31 of
+//     sub-band k-1 feeds lane 0 of sub-band k); band b -> band b+1 goes through
+//     a per-warp delay line of L values in global scratch.
+//
+// Saved state: R (and P for uDTW) of every cell, in stream order
+// [warp][t][k][lane] (one coalesced 128-byte row per sub-band and step), in
+// the log2 domain R' = R * log2(e) / gamma.  The backward sweep replays the
+// stream in reverse and needs nothing else: the soft-min weights of a cell's
+// three predecessors are recomputed from their saved R', so neither the cost
+// nor the penalty is read again.
+#pragma once
+
+#include "common.cuh"
+
+namespace tw {
+
+struct StreamPlan {
+  int B = 0, N = 0, M = 0;
+  int KS = 1;        // sub-bands per warp
+  int NB = 1;        // bands per pair
+  int L = 0;         // stream columns per band pass (multiple of 8)
+  int warps = 0;     // warps launched
+  int wpc = 4;       // warps per CTA
+  int base = 0, rem = 0;   // warp w: base + (w < rem) pairs from w*base + min(w, rem)
+  long long tmax = 0;      // saved rows per warp (multiple of 8)
+  size_t smem_fwd = 0, smem_bwd = 0;   // dynamic shared memory per CTA
+
+  long long saved_elems() const { return (long long)warps * tmax * KS * 32; }
+  long long delay_elems() const { return (long long)warps * L; }
+};
+
+// elem_bytes: 4 or 8.  has_p: uDTW penalty accumulator.  sms: SM count.
+StreamPlan make_stream_plan(int B, int N, int M, int elem_bytes, bool has_p, int sms);
+
+template <typename T>
+struct SdtwArgs {
+  // forward inputs / outputs
+  const T* C = nullptr;      // cost [B,N,M]
+  const T* Q = nullptr;      // penalty [B,N,M] (uDTW) or null
+  T* out_r = nullptr;        // [B]
+  T* out_p = nullptr;        // [B] (uDTW) or null
+  // saved stream (written by forward, read by backward)
+  T* sR = nullptr;
+  T* sP = nullptr;
+  // per-warp delay lines (global scratch)
+  T* dlR = nullptr;
+  T* dlP = nullptr;
+  // backward
+  const T* grad_r = nullptr;  // [B]
+  const T* grad_p = nullptr;  // [B] or null
+  T* dC = nullptr;            // [B,N,M]
+  T* dQ = nullptr;            // [B,N,M] or null
+  // scalars
+  T kappa = 1;      // log2(e) / gamma
+  T inv_kappa = 1;  // gamma * ln 2
+  T inv_gamma = 1;
+  T pad_raw = 0;    // Big / kappa: raw cost of a padding column
+  T band = 0;       // Sakoe-Chiba band (> 0 active)
+  int vec = 0;      // 16-byte global accesses allowed for C/Q/dC/dQ
+  StreamPlan p;
+};
+
+template <typename T>
+int sdtw_stream_forward(const SdtwArgs<T>& a, bool has_p, bool has_band, cudaStream_t st);
+template <typename T>
+int sdtw_stream_backward(const SdtwArgs<T>& a, bool has_p, bool has_band, cudaStream_t st);
+
+}  // namespace tw

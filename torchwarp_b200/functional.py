@@ -1,0 +1,18 @@
+"""Functional interface: one function per module, plus ``*_from_cost`` variants.
+
+    import torchwarp_b200.functional as TF
+"""
+
+from .sdtw import soft_dtw, soft_dtw_from_cost, softmin, softmin_weights
+from .udtw.functional import UDTWOutput, pairwise_matrices, udtw, udtw_from_cost
+
+__all__ = [
+    "udtw",
+    "udtw_from_cost",
+    "pairwise_matrices",
+    "UDTWOutput",
+    "soft_dtw",
+    "soft_dtw_from_cost",
+    "softmin",
+    "softmin_weights",
+]

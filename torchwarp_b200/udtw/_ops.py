@@ -1,0 +1,278 @@
+"""uDTW / soft-DTW as torch custom operators over the native C ABI.
+
+Mirrors the reference op layer (hibana2077/torchwarp src/torchwarp/udtw/_ops.py:
+custom ops ``dp``/``dp_backward``/``fused``/``fused_backward`` at :100-211,
+autograd Functions at :262-415) with the native sm_100a kernels as the only
+implementation:
+
+* ``torchwarp_b200::sdtw_dp(cost, penalty?, gamma, bandwidth)`` ->
+  (out_r [B], out_p [B], saved): the soft-min DP on a precomputed cost
+  (and uDTW penalty).  ``saved`` is the kernel's opaque saved stream
+  (uint8), replacing the reference's diagonal-major R and P.
+* ``torchwarp_b200::sdtw_dp_backward(saved, grad_r, grad_p, N, M, gamma,
+  has_penalty)`` -> (d_cost, d_penalty).
+* ``torchwarp_b200::udtw_fused(X, Y, vx?, vy?, gamma, beta, eps, bandwidth)``
+  -> (out_r, out_p, saved, cost): cost built by the native cost kernel from
+  the features, then the DP.  ``vx``/``vy`` None means unit variance and no
+  penalty (soft-DTW).
+* ``torchwarp_b200::udtw_fused_backward(...)`` -> (dX, dY, dvx, dvy).
+
+Each op has a fake (meta) implementation for torch.compile, a vmap rule that
+folds the vmapped dimension into the batch, and runs in float32 under
+autocast.  First-order reverse mode calls the native backward; the backward
+itself is not differentiable (create_graph=True through it raises).
+"""
+
+from typing import Optional, Tuple
+
+import torch
+from torch import Tensor
+
+from .. import _native as nat
+
+# ------------------------------------------------------------------ helpers
+
+
+def _saved_bytes(B, N, M, dtype, has_p):
+    return int(nat.lib().tw_sdtw_saved_bytes(B, N, M, torch.empty((), dtype=dtype).element_size(),
+                                             int(has_p)))
+
+
+def _ws_bytes(B, N, M, dtype, has_p):
+    return int(nat.lib().tw_sdtw_workspace_bytes(B, N, M,
+                                                 torch.empty((), dtype=dtype).element_size(),
+                                                 int(has_p)))
+
+
+def _register_vmap(op, n_tensors):
+    """vmap rule: fold the vmapped dimension into the leading batch dim."""
+    def rule(info, in_dims, *args):
+        V = info.batch_size
+        folded = []
+        for k, (a, d) in enumerate(zip(args, in_dims)):
+            if k < n_tensors and isinstance(a, Tensor):
+                a = a.unsqueeze(0).expand(V, *a.shape) if d is None else a.movedim(d, 0)
+                a = a.reshape(V * a.shape[1], *a.shape[2:]).contiguous()
+            folded.append(a)
+        outs = op(*folded)
+        outs = tuple(o.reshape(V, o.shape[0] // V, *o.shape[1:]) for o in outs)
+        return outs, tuple(0 for _ in outs)
+    op.register_vmap(rule)
+
+
+def _register_autocast(op):
+    for device in ("cuda", "cpu"):
+        torch.library.register_autocast(op, device, torch.float32)
+
+
+def _dp_forward(cost, penalty, gamma, bandwidth):
+    nat.require_cuda(cost, penalty)
+    B, N, M = cost.shape
+    cost = cost.contiguous()
+    penalty = None if penalty is None else penalty.contiguous()
+    has_p = penalty is not None
+    out_r = cost.new_empty(B)
+    out_p = cost.new_zeros(B)
+    if B == 0:
+        return out_r, out_p, torch.empty(0, dtype=torch.uint8, device=cost.device)
+    with torch.cuda.device(cost.device):
+        sb = _saved_bytes(B, N, M, cost.dtype, has_p)
+        wb = _ws_bytes(B, N, M, cost.dtype, has_p)
+        saved = torch.empty(sb, dtype=torch.uint8, device=cost.device)
+        ws = torch.empty(wb, dtype=torch.uint8, device=cost.device)
+        fn = getattr(nat.lib(), "tw_sdtw_forward_" + nat.suffix(cost.dtype))
+        nat.check(fn(nat.ptr(cost), nat.ptr(penalty), B, N, M, float(gamma), float(bandwidth),
+                     nat.ptr(out_r), nat.ptr(out_p) if has_p else None, nat.ptr(saved), sb,
+                     nat.ptr(ws), wb, nat.stream_of(cost)), "tw_sdtw_forward")
+    return out_r, out_p, saved
+
+
+def _dp_backward(saved, grad_r, grad_p, N, M, gamma, has_p):
+    nat.require_cuda(grad_r)
+    B = grad_r.shape[0]
+    dtype = grad_r.dtype
+    d_cost = grad_r.new_empty(B, N, M)
+    d_pen = grad_r.new_empty(B, N, M) if has_p else grad_r.new_zeros(B, N, M)
+    if B == 0:
+        return d_cost, d_pen
+    grad_r = grad_r.contiguous()
+    grad_p = grad_p.to(dtype).contiguous()
+    with torch.cuda.device(grad_r.device):
+        wb = _ws_bytes(B, N, M, dtype, has_p)
+        ws = torch.empty(wb, dtype=torch.uint8, device=grad_r.device)
+        fn = getattr(nat.lib(), "tw_sdtw_backward_" + nat.suffix(dtype))
+        nat.check(fn(nat.ptr(grad_r), nat.ptr(grad_p) if has_p else None, B, N, M, float(gamma),
+                     int(has_p), nat.ptr(saved), saved.numel(), nat.ptr(d_cost),
+                     nat.ptr(d_pen) if has_p else None, nat.ptr(ws), wb,
+                     nat.stream_of(grad_r)), "tw_sdtw_backward")
+    return d_cost, d_pen
+
+
+# ------------------------------------------------- DP on precomputed matrices
+
+@torch.library.custom_op("torchwarp_b200::sdtw_dp", mutates_args=())
+def sdtw_dp(cost: Tensor, penalty: Optional[Tensor], gamma: float,
+            bandwidth: float) -> Tuple[Tensor, Tensor, Tensor]:
+    return _dp_forward(cost, penalty, gamma, bandwidth)
+
+
+@sdtw_dp.register_fake
+def _(cost, penalty, gamma, bandwidth):
+    B, N, M = cost.shape
+    nbytes = _saved_bytes(B, N, M, cost.dtype, penalty is not None) if B else 0
+    return (cost.new_empty(B), cost.new_empty(B),
+            cost.new_empty(nbytes, dtype=torch.uint8))
+
+
+@torch.library.custom_op("torchwarp_b200::sdtw_dp_backward", mutates_args=())
+def sdtw_dp_backward(saved: Tensor, grad_r: Tensor, grad_p: Tensor, N: int, M: int, gamma: float,
+                     has_penalty: bool) -> Tuple[Tensor, Tensor]:
+    return _dp_backward(saved, grad_r, grad_p, N, M, gamma, has_penalty)
+
+
+@sdtw_dp_backward.register_fake
+def _(saved, grad_r, grad_p, N, M, gamma, has_penalty):
+    B = grad_r.shape[0]
+    return grad_r.new_empty(B, N, M), grad_r.new_empty(B, N, M)
+
+
+_register_autocast(sdtw_dp)
+_register_autocast(sdtw_dp_backward)
+
+
+# ------------------------------------- cost built from the features, then DP
+
+@torch.library.custom_op("torchwarp_b200::udtw_fused", mutates_args=())
+def udtw_fused(X: Tensor, Y: Tensor, vx: Optional[Tensor], vy: Optional[Tensor], gamma: float,
+               beta: float, eps: float, bandwidth: float) -> Tuple[Tensor, Tensor, Tensor, Tensor]:
+    nat.require_cuda(X, Y, vx, vy)
+    B, N, D = X.shape
+    M = Y.shape[1]
+    X, Y = X.contiguous(), Y.contiguous()
+    vx = None if vx is None else vx.contiguous()
+    vy = None if vy is None else vy.contiguous()
+    cost = X.new_empty(B, N, M)
+    pen = X.new_empty(B, N, M) if vx is not None else None
+    if B:
+        with torch.cuda.device(X.device):
+            fn = getattr(nat.lib(), "tw_udtw_cost_" + nat.suffix(X.dtype))
+            nat.check(fn(nat.ptr(X), nat.ptr(Y), nat.ptr(vx), nat.ptr(vy), B, N, M, D,
+                         float(beta), float(eps), nat.ptr(cost), nat.ptr(pen),
+                         nat.stream_of(X)), "tw_udtw_cost")
+    out_r, out_p, saved = _dp_forward(cost, pen, gamma, bandwidth)
+    return out_r, out_p, saved, cost
+
+
+@udtw_fused.register_fake
+def _(X, Y, vx, vy, gamma, beta, eps, bandwidth):
+    B, N, M = X.shape[0], X.shape[1], Y.shape[1]
+    nbytes = _saved_bytes(B, N, M, X.dtype, vx is not None) if B else 0
+    return (X.new_empty(B), X.new_empty(B), X.new_empty(nbytes, dtype=torch.uint8),
+            X.new_empty(B, N, M))
+
+
+@torch.library.custom_op("torchwarp_b200::udtw_fused_backward", mutates_args=())
+def udtw_fused_backward(X: Tensor, Y: Tensor, vx: Optional[Tensor], vy: Optional[Tensor],
+                        cost: Tensor, saved: Tensor, grad_r: Tensor, grad_p: Tensor, gamma: float,
+                        beta: float, eps: float) -> Tuple[Tensor, Tensor, Tensor, Tensor]:
+    B, N, D = X.shape
+    M = Y.shape[1]
+    has_p = vx is not None
+    d_cost, d_pen = _dp_backward(saved, grad_r, grad_p, N, M, gamma, has_p)
+    X, Y = X.contiguous(), Y.contiguous()
+    dX, dY = torch.empty_like(X), torch.empty_like(Y)
+    dvx = torch.zeros_like(vx) if has_p else X.new_zeros(B, N)
+    dvy = torch.zeros_like(vy) if has_p else X.new_zeros(B, M)
+    if B:
+        with torch.cuda.device(X.device):
+            fn = getattr(nat.lib(), "tw_udtw_features_grad_" + nat.suffix(X.dtype))
+            nat.check(fn(nat.ptr(X), nat.ptr(Y), nat.ptr(vx.contiguous() if has_p else None),
+                         nat.ptr(vy.contiguous() if has_p else None), nat.ptr(cost),
+                         nat.ptr(d_cost), nat.ptr(d_pen) if has_p else None, B, N, M, D,
+                         float(beta), float(eps), nat.ptr(dX), nat.ptr(dY),
+                         nat.ptr(dvx) if has_p else None, nat.ptr(dvy) if has_p else None,
+                         nat.stream_of(X)), "tw_udtw_features_grad")
+    return dX, dY, dvx, dvy
+
+
+@udtw_fused_backward.register_fake
+def _(X, Y, vx, vy, cost, saved, grad_r, grad_p, gamma, beta, eps):
+    B, N, M = X.shape[0], X.shape[1], Y.shape[1]
+    return (torch.empty_like(X), torch.empty_like(Y), X.new_empty(B, N), X.new_empty(B, M))
+
+
+_register_autocast(udtw_fused)
+_register_autocast(udtw_fused_backward)
+
+
+# ------------------------------------------------------- autograd Functions
+
+def _zeros_if_none(g, like, B):
+    return like.new_zeros(B) if g is None else g
+
+
+class DP(torch.autograd.Function):
+    """(cost, penalty?) -> (distance, penalty_sum, saved)."""
+
+    @staticmethod
+    def forward(cost, penalty, gamma, bandwidth):
+        return sdtw_dp(cost, penalty, gamma, bandwidth)
+
+    @staticmethod
+    def setup_context(ctx, inputs, output):
+        cost, penalty, gamma, bandwidth = inputs
+        ctx.mark_non_differentiable(output[2])
+        ctx.set_materialize_grads(False)
+        ctx.save_for_backward(output[2])
+        ctx.shape = tuple(cost.shape)
+        ctx.dtype = cost.dtype
+        ctx.args = (gamma, penalty is not None)
+
+    @staticmethod
+    @torch.autograd.function.once_differentiable
+    def backward(ctx, g_r, g_p, _g_saved):
+        (saved,) = ctx.saved_tensors
+        gamma, has_p = ctx.args
+        B, N, M = ctx.shape
+        like = saved.new_empty(0, dtype=ctx.dtype)
+        g_r = _zeros_if_none(g_r, like, B).to(ctx.dtype)
+        g_p = _zeros_if_none(g_p, like, B).to(ctx.dtype)
+        d_cost, d_pen = sdtw_dp_backward(saved, g_r, g_p, N, M, gamma, has_p)
+        return d_cost, (d_pen if has_p else None), None, None
+
+
+class Fused(torch.autograd.Function):
+    """(X, Y, vx?, vy?) -> (distance, penalty_sum, saved, cost)."""
+
+    @staticmethod
+    def forward(X, Y, vx, vy, gamma, beta, eps, bandwidth):
+        return udtw_fused(X, Y, vx, vy, gamma, beta, eps, bandwidth)
+
+    @staticmethod
+    def setup_context(ctx, inputs, output):
+        X, Y, vx, vy, gamma, beta, eps, bandwidth = inputs
+        ctx.mark_non_differentiable(output[2], output[3])
+        ctx.set_materialize_grads(False)
+        ctx.save_for_backward(X, Y, vx, vy, output[2], output[3])
+        ctx.args = (gamma, beta, eps)
+
+    @staticmethod
+    @torch.autograd.function.once_differentiable
+    def backward(ctx, g_r, g_p, _g_saved, _g_cost):
+        X, Y, vx, vy, saved, cost = ctx.saved_tensors
+        gamma, beta, eps = ctx.args
+        B = X.shape[0]
+        g_r = _zeros_if_none(g_r, X, B)
+        g_p = _zeros_if_none(g_p, X, B)
+        dX, dY, dvx, dvy = udtw_fused_backward(X, Y, vx, vy, cost, saved, g_r, g_p, gamma, beta,
+                                               eps)
+        has_p = vx is not None
+        return dX, dY, (dvx if has_p else None), (dvy if has_p else None), None, None, None, None
+
+
+def dp_apply(cost, penalty, gamma, bandwidth):
+    return DP.apply(cost, penalty, gamma, bandwidth)
+
+
+def fused_apply(X, Y, vx, vy, gamma, beta, eps, bandwidth):
+    return Fused.apply(X, Y, vx, vy, gamma, beta, eps, bandwidth)
