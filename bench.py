@@ -1,0 +1,351 @@
+#!/usr/bin/env python
+"""Headline benchmark: fwd+bwd soft-DTW DP cells/s, B=4096 pairs, N=M=1024, D=64, fp32.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = soft-DTW forward + backward (gradients for X and Y) over the whole
+batch through the public API (torchwarp_b200.functional.soft_dtw, gamma=0.01,
+squared-Euclidean cost).  With N GPUs (torchrun, one process per GPU) the
+batch of 4096 pairs is sharded N ways (strong scaling); the only exchange is
+an NCCL all_gather of the per-pair distances.
+
+Printed (rank 0), one JSON line:
+  value     cells/s over all GPUs, inputs resident in HBM, timed with CUDA
+            events between barriers, max over ranks;
+  e2e       the same step with X, Y copied from pinned host memory and the
+            distances copied back inside the timed region;
+  roofline  the dominant native kernel: algorithmic bytes per launch (cost
+            read or cost-gradient write, 4 B/cell) / its average CUDA-event
+            duration in the timed region, against MEASURED_PEAKS.json;
+  cpu_baseline  the float64 CPU oracle (oracle/, one thread) on a bounded
+            sample of the same workload (rank 0, N=1 only).
+``--impl reference`` times the CPU implementation of the reference's path
+(the oracle port, all host threads) on the same workload and prints the
+same line with "impl": "reference".
+"""
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "fwd+bwd DP cells/s (soft-DTW B=4096 N=M=1024)"
+UNIT = "cells/s"
+ALGO_BYTES_PER_CELL = 8      # soft-DTW fwd+bwd: cost read + cost-gradient write
+KERNEL_BYTES_PER_CELL = 4    # one DP sweep: its cost read (fwd) or gradient write (bwd)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=4096)
+    ap.add_argument("--length", type=int, default=1024)
+    ap.add_argument("--dim", type=int, default=64)
+    ap.add_argument("--gamma", type=float, default=0.01)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    return ap.parse_args()
+
+
+def config(a, world):
+    return {"workload": "soft_dtw fwd+bwd, squared-Euclidean cost, gamma={}".format(a.gamma),
+            "global_batch": a.batch, "N": a.length, "M": a.length, "D": a.dim,
+            "per_gpu_batch": a.batch // world, "parallelism": "dp{}".format(world),
+            "l2": "inputs larger than L2 (X,Y {:.1f} GB, cost {:.1f} GB)".format(
+                2 * a.batch // world * a.length * a.dim * 4 / 1e9,
+                a.batch // world * a.length * a.length * 4 / 1e9)}
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# --------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """Samples SM clock, power and clock-event reasons with NVML every 200 ms."""
+
+    NAMES = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+             0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, device):
+        self.samples, self.stop, self.h, self.max_mhz = [], threading.Event(), None, None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            self.h = pynvml.nvmlDeviceGetHandleByUUID(("GPU-" + uuid).encode())
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.nv = pynvml
+        except Exception:  # sampling is best effort; the number is still reported
+            self.h = None
+
+    def _run(self):
+        nv = self.nv
+        while not self.stop.is_set():
+            try:
+                self.samples.append((nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM),
+                                     nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)))
+            except Exception:
+                pass
+            self.stop.wait(0.2)
+
+    def __enter__(self):
+        if self.h is not None:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.h is not None:
+            self.stop.set()
+            self.t.join()
+        return False
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"]}
+        mhz = [s[0] for s in self.samples]
+        mask = 0
+        for _, r in self.samples:
+            mask |= r
+        reasons = [n for bit, n in self.NAMES.items() if mask & bit]
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(mhz)}
+
+
+# --------------------------------------------------------------- ours
+
+def run_ours(a):
+    import torch.distributed as dist
+
+    import torchwarp_b200 as twb
+    from torchwarp_b200 import _native
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    if a.batch % world:
+        raise SystemExit("batch {} not divisible by {} GPUs".format(a.batch, world))
+    Bl, N, D = a.batch // world, a.length, a.dim
+    cells_total = a.batch * N * N
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    X = torch.randn(Bl, N, D, device=dev, generator=g)
+    Y = torch.randn(Bl, N, D, device=dev, generator=g)
+    gathered = [torch.empty(Bl, device=dev) for _ in range(world)]
+
+    def step(x, y):
+        x = x.detach().requires_grad_(True)
+        y = y.detach().requires_grad_(True)
+        d = twb.functional.soft_dtw(x, y, gamma=a.gamma)
+        d.sum().backward()
+        if world > 1:
+            dist.all_gather(gathered, d.detach())
+        return d, x.grad, y.grad
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def timed(fn, steps):
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        barrier()
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    for _ in range(a.warmup):
+        step(X, Y)
+    with ClockSampler(local) as clk, _native.LaunchTimer() as lt:
+        ms = timed(lambda: step(X, Y), a.steps)
+    torch.cuda.synchronize()
+    kern = lt.totals()
+    ms_step = ms / a.steps
+    value = cells_total / (ms_step / 1e3)
+
+    e2e = None
+    if not a.no_e2e:
+        Xh = X.cpu().pin_memory()
+        Yh = Y.cpu().pin_memory()
+        out_h = torch.empty(Bl, pin_memory=True)
+
+        def e2e_step():
+            x = Xh.to(dev, non_blocking=True)
+            y = Yh.to(dev, non_blocking=True)
+            d, _, _ = step(x, y)
+            out_h.copy_(d.detach(), non_blocking=True)
+
+        e2e_step()
+        ms_e = timed(e2e_step, a.steps)
+        e2e = {"value": cells_total / (ms_e / a.steps / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": int((Xh.numel() + Yh.numel()) * 4 * world),
+               "d2h_bytes_per_step": int(Bl * 4 * world), "ms_per_step": ms_e / a.steps}
+
+    # dominant native kernel of the timed region
+    name, (launches, tot) = max(kern.items(), key=lambda kv: kv[1][1])
+    per_launch_ms = tot / launches
+    peak, src = peaks()
+    cells_local = Bl * N * N
+    if name in ("sdtw_forward", "sdtw_backward"):
+        algo = cells_local * KERNEL_BYTES_PER_CELL
+    elif name == "udtw_cost":
+        algo = cells_local * 4 + 2 * Bl * N * D * 4
+    else:  # udtw_features_grad: cost and cost-gradient read, dX/dY written
+        algo = cells_local * 8 + 2 * Bl * N * D * 4
+    achieved = algo / (per_launch_ms / 1e3) / 1e9
+    roofline = {"bound": "hbm", "kernel": name, "achieved": achieved, "peak": peak,
+                "unit": "GB/s", "frac": achieved / peak, "peak_source": src,
+                "traffic": None, "algorithmic_bytes_per_launch": algo,
+                "avg_launch_ms": per_launch_ms,
+                "step_frac": (cells_local * ALGO_BYTES_PER_CELL / (ms_step / 1e3) / 1e9) / peak,
+                "kernels_ms_per_step": {k: v[1] / a.steps for k, v in kern.items()}}
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu:
+        cpu = cpu_baseline(a, X, Y)
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    launches_per_step = sum(v[0] for v in kern.values()) // a.steps
+    kernels_per_call = {"udtw_cost": 1, "sdtw_forward": 1, "sdtw_backward": 1,
+                        "udtw_features_grad": 2}
+    gpu_launches = sum(kernels_per_call.get(k, 1) * v[0] for k, v in kern.items())
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": config(a, world), "e2e": e2e, "roofline": roofline,
+            "cpu_baseline": cpu, "clocks": clk.summary(), "gpu_launches": gpu_launches,
+            "native_calls_per_step": launches_per_step}
+    print(json.dumps(line))
+
+
+# --------------------------------------------------------------- CPU arms
+
+def _oracle_sample(Xs, Ys, gamma):
+    import oracle
+    oracle.soft_dtw(Xs, Ys, gamma=gamma)
+
+
+def cpu_baseline(a, X, Y, sample_pairs=16):
+    """float64 oracle, one thread, on the first pairs of the same inputs."""
+    import oracle
+    try:
+        from threadpoolctl import threadpool_limits
+    except ImportError:  # pragma: no cover
+        threadpool_limits = None
+    oracle.lib()
+    Xs = X[:sample_pairs].double().cpu().numpy()
+    Ys = Y[:sample_pairs].double().cpu().numpy()
+    ctx = threadpool_limits(1) if threadpool_limits else None
+    t0 = time.perf_counter()
+    if ctx:
+        with ctx:
+            _oracle_sample(Xs, Ys, a.gamma)
+    else:
+        _oracle_sample(Xs, Ys, a.gamma)
+    dt = time.perf_counter() - t0
+    cells = sample_pairs * a.length * a.length
+    return {"value": cells / dt, "unit": UNIT, "cores": 1, "kind": "port",
+            "sample": "{} of the {} pairs (N=M={}, D={}), float64 fwd+bwd, {:.1f} s".format(
+                sample_pairs, a.batch, a.length, a.dim, dt)}
+
+
+def run_reference(a):
+    """The reference's CPU path, restated in oracle/ (the reference is Python +
+    JIT CUDA with no compiled CPU library), on every host thread."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    from concurrent.futures import ThreadPoolExecutor
+
+    import oracle
+    try:
+        from threadpoolctl import threadpool_limits
+    except ImportError:  # pragma: no cover
+        threadpool_limits = None
+    oracle.lib()
+    threads = os.cpu_count() or 1
+    per_thread = 1
+    pairs = threads * per_thread
+    rng = np.random.default_rng(1234)
+    Xs = rng.standard_normal((pairs, a.length, a.dim))
+    Ys = rng.standard_normal((pairs, a.length, a.dim))
+
+    def one(i):
+        sl = slice(i * per_thread, (i + 1) * per_thread)
+        oracle.soft_dtw(Xs[sl], Ys[sl], gamma=a.gamma)
+
+    def sample():
+        with ThreadPoolExecutor(threads) as ex:
+            list(ex.map(one, range(threads)))
+
+    ctx = threadpool_limits(1) if threadpool_limits else None
+    if ctx:
+        ctx.__enter__()
+    for _ in range(a.warmup):
+        sample()
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        sample()
+    dt = (time.perf_counter() - t0) / a.steps
+    if ctx:
+        ctx.__exit__(None, None, None)
+    cells = pairs * a.length * a.length
+    value = cells / dt
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": config(a, world), "impl": "reference",
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": "{} pairs per step (N=M={}, D={}) of the {}-pair "
+                                       "workload, float64 fwd+bwd".format(
+                                           pairs, a.length, a.dim, a.batch)},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+def main():
+    a = parse()
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_ours(a)
+
+
+if __name__ == "__main__":
+    main()

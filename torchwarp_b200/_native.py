@@ -94,3 +94,51 @@ def require_cuda(*tensors):
             raise RuntimeError(
                 "torchwarp_b200 runs only on CUDA tensors (B200, sm_100a); got a tensor on {}. "
                 "There is no CPU fallback.".format(t.device))
+
+
+# ------------------------------------------------------------ launch timing
+#
+# bench.py measures each native launch with CUDA events recorded on the
+# launching stream.  The recorder is off by default and adds nothing to a
+# call when it is off.
+
+_RECORDER = None
+
+
+class LaunchTimer:
+    """Context manager collecting (name, start_event, end_event) per C-ABI call."""
+
+    def __init__(self):
+        self.events = []
+
+    def __enter__(self):
+        global _RECORDER
+        _RECORDER = self
+        return self
+
+    def __exit__(self, *exc):
+        global _RECORDER
+        _RECORDER = None
+        return False
+
+    def totals(self):
+        """{name: (launches, total_ms)} after a torch.cuda.synchronize()."""
+        out = {}
+        for name, a, b in self.events:
+            n, ms = out.get(name, (0, 0.0))
+            out[name] = (n + 1, ms + a.elapsed_time(b))
+        return out
+
+
+def call(name, fn, *args):
+    """Invoke a C-ABI function, bracketing it with CUDA events when timing."""
+    rec = _RECORDER
+    if rec is None:
+        return fn(*args)
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    status = fn(*args)
+    b.record()
+    rec.events.append((name, a, b))
+    return status

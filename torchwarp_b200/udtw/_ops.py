@@ -81,9 +81,10 @@ def _dp_forward(cost, penalty, gamma, bandwidth):
         saved = torch.empty(sb, dtype=torch.uint8, device=cost.device)
         ws = torch.empty(wb, dtype=torch.uint8, device=cost.device)
         fn = getattr(nat.lib(), "tw_sdtw_forward_" + nat.suffix(cost.dtype))
-        nat.check(fn(nat.ptr(cost), nat.ptr(penalty), B, N, M, float(gamma), float(bandwidth),
-                     nat.ptr(out_r), nat.ptr(out_p) if has_p else None, nat.ptr(saved), sb,
-                     nat.ptr(ws), wb, nat.stream_of(cost)), "tw_sdtw_forward")
+        nat.check(nat.call("sdtw_forward", fn, nat.ptr(cost), nat.ptr(penalty), B, N, M,
+                           float(gamma), float(bandwidth), nat.ptr(out_r),
+                           nat.ptr(out_p) if has_p else None, nat.ptr(saved), sb, nat.ptr(ws), wb,
+                           nat.stream_of(cost)), "tw_sdtw_forward")
     return out_r, out_p, saved
 
 
@@ -101,10 +102,11 @@ def _dp_backward(saved, grad_r, grad_p, N, M, gamma, has_p):
         wb = _ws_bytes(B, N, M, dtype, has_p)
         ws = torch.empty(wb, dtype=torch.uint8, device=grad_r.device)
         fn = getattr(nat.lib(), "tw_sdtw_backward_" + nat.suffix(dtype))
-        nat.check(fn(nat.ptr(grad_r), nat.ptr(grad_p) if has_p else None, B, N, M, float(gamma),
-                     int(has_p), nat.ptr(saved), saved.numel(), nat.ptr(d_cost),
-                     nat.ptr(d_pen) if has_p else None, nat.ptr(ws), wb,
-                     nat.stream_of(grad_r)), "tw_sdtw_backward")
+        nat.check(nat.call("sdtw_backward", fn, nat.ptr(grad_r),
+                           nat.ptr(grad_p) if has_p else None, B, N, M, float(gamma), int(has_p),
+                           nat.ptr(saved), saved.numel(), nat.ptr(d_cost),
+                           nat.ptr(d_pen) if has_p else None, nat.ptr(ws), wb,
+                           nat.stream_of(grad_r)), "tw_sdtw_backward")
     return d_cost, d_pen
 
 
@@ -156,9 +158,9 @@ def udtw_fused(X: Tensor, Y: Tensor, vx: Optional[Tensor], vy: Optional[Tensor],
     if B:
         with torch.cuda.device(X.device):
             fn = getattr(nat.lib(), "tw_udtw_cost_" + nat.suffix(X.dtype))
-            nat.check(fn(nat.ptr(X), nat.ptr(Y), nat.ptr(vx), nat.ptr(vy), B, N, M, D,
-                         float(beta), float(eps), nat.ptr(cost), nat.ptr(pen),
-                         nat.stream_of(X)), "tw_udtw_cost")
+            nat.check(nat.call("udtw_cost", fn, nat.ptr(X), nat.ptr(Y), nat.ptr(vx), nat.ptr(vy),
+                               B, N, M, D, float(beta), float(eps), nat.ptr(cost), nat.ptr(pen),
+                               nat.stream_of(X)), "tw_udtw_cost")
     out_r, out_p, saved = _dp_forward(cost, pen, gamma, bandwidth)
     return out_r, out_p, saved, cost
 
@@ -186,7 +188,8 @@ def udtw_fused_backward(X: Tensor, Y: Tensor, vx: Optional[Tensor], vy: Optional
     if B:
         with torch.cuda.device(X.device):
             fn = getattr(nat.lib(), "tw_udtw_features_grad_" + nat.suffix(X.dtype))
-            nat.check(fn(nat.ptr(X), nat.ptr(Y), nat.ptr(vx.contiguous() if has_p else None),
+            nat.check(nat.call("udtw_features_grad", fn, nat.ptr(X), nat.ptr(Y),
+                               nat.ptr(vx.contiguous() if has_p else None),
                          nat.ptr(vy.contiguous() if has_p else None), nat.ptr(cost),
                          nat.ptr(d_cost), nat.ptr(d_pen) if has_p else None, B, N, M, D,
                          float(beta), float(eps), nat.ptr(dX), nat.ptr(dY),
