@@ -72,6 +72,21 @@ int tw_sdtw_forward_f64(const double* cost, const double* penalty, int B, int N,
                         void* saved, size_t saved_bytes, void* workspace, size_t ws_bytes,
                         void* stream);
 
+/* Allocation-free variant of tw_sdtw_forward_f32 (no counterpart in the
+ * reference; an addition of this library).  For callers that own every device
+ * allocation and can pass only inputs and outputs: the forward's scratch comes
+ * from a static 4 MiB device buffer inside the library instead of `workspace`.
+ * Same arguments and results as tw_sdtw_forward_f32 minus the workspace;
+ * `saved` is still the caller's (it is an output consumed by the backward).
+ * Limits: shapes whose scratch (tw_sdtw_workspace_bytes) exceeds 4 MiB are
+ * rejected with TW_ERR_WORKSPACE; every call shares the one buffer, so calls
+ * that overlap on the GPU race and must be serialised by the caller; the
+ * first call on a device looks up the buffer's device address and should
+ * come before any stream capture. */
+int tw_sdtw_forward_noalloc_f32(const float* cost, const float* penalty, int B, int N, int M,
+                                double gamma, double bandwidth, float* out_r, float* out_p,
+                                void* saved, size_t saved_bytes, void* stream);
+
 /* Backward of the call above for L = sum_b grad_r[b]*out_r[b] + grad_p[b]*out_p[b].
  *   d_cost, d_penalty: [B, N, M] outputs (d_penalty only when has_penalty). */
 int tw_sdtw_backward_f32(const float* grad_r, const float* grad_p, int B, int N, int M,

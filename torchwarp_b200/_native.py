@@ -28,6 +28,8 @@ SIGNATURES = {
                                    _c_sz, _c_p, _c_sz, _c_p]),
     "tw_sdtw_forward_f64": (_c_i, [_c_p, _c_p, _c_i, _c_i, _c_i, _c_d, _c_d, _c_p, _c_p, _c_p,
                                    _c_sz, _c_p, _c_sz, _c_p]),
+    "tw_sdtw_forward_noalloc_f32": (_c_i, [_c_p, _c_p, _c_i, _c_i, _c_i, _c_d, _c_d, _c_p, _c_p,
+                                           _c_p, _c_sz, _c_p]),
     "tw_sdtw_backward_f32": (_c_i, [_c_p, _c_p, _c_i, _c_i, _c_i, _c_d, _c_i, _c_p, _c_sz, _c_p,
                                     _c_p, _c_p, _c_sz, _c_p]),
     "tw_sdtw_backward_f64": (_c_i, [_c_p, _c_p, _c_i, _c_i, _c_i, _c_d, _c_i, _c_p, _c_sz, _c_p,

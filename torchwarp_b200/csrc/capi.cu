@@ -55,7 +55,7 @@ static int check_dims(const char* who, int B, int N, int M) {
 }
 
 template <typename T>
-static int sdtw_fwd(const T* cost, const T* pen, int B, int N, int M, double gamma, double band,
+int sdtw_fwd(const T* cost, const T* pen, int B, int N, int M, double gamma, double band,
                     T* out_r, T* out_p, void* saved, size_t saved_bytes, void* ws, size_t ws_bytes,
                     cudaStream_t st) {
   g_err[0] = 0;
@@ -127,6 +127,9 @@ static int sdtw_bwd(const T* grad_r, const T* grad_p, int B, int N, int M, doubl
   a.p = p;
   return sdtw_stream_backward<T>(a, has_p, false, st);
 }
+
+template int sdtw_fwd<float>(const float*, const float*, int, int, int, double, double, float*,
+                             float*, void*, size_t, void*, size_t, cudaStream_t);
 
 int udtw_cost_f32(const float*, const float*, const float*, const float*, int, int, int, int,
                   double, double, float*, float*, cudaStream_t);
