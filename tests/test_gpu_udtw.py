@@ -139,7 +139,7 @@ def test_scaled_reference_backend(tw, name):
 @pytest.mark.parametrize("B,N,M,band", [
     (1, 1, 1, 0), (3, 1, 9, 0), (3, 9, 1, 0), (5, 33, 7, 0), (4, 31, 32, 0), (2, 64, 65, 0),
     (7, 65, 64, 0), (2, 129, 140, 0), (3, 200, 260, 0), (300, 17, 23, 0), (611, 40, 41, 0),
-    (2, 150, 160, 12), (3, 96, 100, 5.5),
+    (2, 150, 160, 12), (3, 96, 100, 5.5), (700, 70, 60, 0), (650, 100, 95, 9),
 ])
 def test_dp_vs_oracle(tw, orc, B, N, M, band):
     """Shapes that cross the sub-band, band-pass and pairs-per-warp boundaries."""
@@ -159,7 +159,7 @@ def test_dp_vs_oracle(tw, orc, B, N, M, band):
     _close(q.grad, dQ)
 
 
-@pytest.mark.parametrize("B,N,M", [(4, 250, 300), (33, 128, 1024)])
+@pytest.mark.parametrize("B,N,M", [(4, 250, 300), (33, 128, 1024), (700, 70, 90)])
 def test_soft_dtw_cost_vs_oracle(tw, orc, B, N, M):
     g = torch.Generator().manual_seed(N + M)
     C = torch.rand(B, N, M, generator=g, dtype=torch.float64)

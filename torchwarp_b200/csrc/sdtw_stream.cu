@@ -10,6 +10,7 @@
 //             to each predecessor p (A_s = sum_p w_p P_p), and w_p * Pbar_s to
 //             its Pbar; w_p is recomputed from the saved R' of the predecessors.
 #include <climits>
+#include <cstdlib>
 
 #include "sdtw_stream.cuh"
 
@@ -26,7 +27,6 @@ template <> struct RingStride<double> { static constexpr int value = 66; };
 constexpr int RING = 64;   // stream columns a lane row can hold
 constexpr int TILE = 8;    // columns per copy tile / flush tile
 constexpr int LEAD = 3;    // forward: cost tiles issued ahead of use
-constexpr int SROWS = 32;  // backward: saved-stream rows staged in shared memory
 
 __device__ __forceinline__ int floor_div(int a, int b) {
   const int q = a / b;
@@ -41,39 +41,75 @@ struct WarpInfo {
   int w, wib, lane, npairs, p0, Q, Tw;
 };
 
+// Pair ranges are handed out in slot order s = (warp in CTA) * CTAs + CTA, so
+// the warps that get one extra pair are spread over all SMs.
 __device__ __forceinline__ bool warp_setup(const StreamPlan& p, int KS, WarpInfo& wi) {
   wi.lane = threadIdx.x & 31;
   wi.wib = threadIdx.x >> 5;
   wi.w = blockIdx.x * (blockDim.x >> 5) + wi.wib;
   if (wi.w >= p.warps) return false;
-  wi.npairs = p.base + (wi.w < p.rem ? 1 : 0);
+  const int slot = wi.wib * gridDim.x + blockIdx.x;
+  wi.npairs = p.base + (slot < p.rem ? 1 : 0);
   if (wi.npairs == 0) return false;
-  wi.p0 = wi.w * p.base + min(wi.w, p.rem);
+  wi.p0 = slot * p.base + min(slot, p.rem);
   wi.Q = wi.npairs * p.NB;
   wi.Tw = wi.Q * p.L + 32 * KS - 1;
   return true;
 }
 
+// Position of stream tile u (the 8 columns [8u, 8u+8)) in (pass, column)
+// space.  Kernels step cursors by one tile per 8-step block, so the hot loop
+// never divides by the runtime L or NB.
+struct Cursor {
+  int u;     // tile index
+  int q;     // pass (nothing to do when < 0 or >= Q)
+  int j0;    // first column of the tile within the pass (L is a multiple of 8)
+  int band;  // q mod NB
+  int pq;    // q div NB: pair index within the warp
+};
+
+__device__ __forceinline__ Cursor cursor_at(int u, const StreamPlan& p) {
+  Cursor c;
+  c.u = u;
+  c.q = floor_div(u * TILE, p.L);
+  c.j0 = u * TILE - c.q * p.L;
+  c.pq = floor_div(c.q, p.NB);
+  c.band = c.q - c.pq * p.NB;
+  return c;
+}
+__device__ __forceinline__ void cursor_next(Cursor& c, const StreamPlan& p) {
+  ++c.u;
+  c.j0 += TILE;
+  if (c.j0 >= p.L) {
+    c.j0 = 0;
+    ++c.q;
+    if (++c.band == p.NB) { c.band = 0; ++c.pq; }
+  }
+}
+__device__ __forceinline__ void cursor_prev(Cursor& c, const StreamPlan& p) {
+  --c.u;
+  c.j0 -= TILE;
+  if (c.j0 < 0) {
+    c.j0 = p.L - TILE;
+    --c.q;
+    if (--c.band < 0) { c.band = p.NB - 1; --c.pq; }
+  }
+}
+
 // ---------------------------------------------------------------- forward
 
-// Copy the 8 stream columns [8u, 8u+8) of this lane's row of sub-band k into
+// Copy the 8 stream columns of tile c of this lane's row of sub-band k into
 // its ring row (cp.async, zero-filled outside the data).
 template <typename T, int KS>
-__device__ __forceinline__ void load_row_tile(const T* __restrict__ src_base, T* ring_row, int u,
-                                              int k, const StreamPlan& p, const WarpInfo& wi,
-                                              int vec) {
-  if (u < 0) return;
-  const int sc0 = u * TILE;
-  const int q = sc0 / p.L;
-  if (q >= wi.Q) return;
-  const int j0 = sc0 - q * p.L;
-  if (j0 >= p.M) return;  // all padding: patched, never read from memory
-  const int pq = q / p.NB;
-  const int band = q - pq * p.NB;
-  const int row = band * 32 * KS + 32 * k + wi.lane;
+__device__ __forceinline__ void load_row_tile(const T* __restrict__ src_base, T* ring_row,
+                                              const Cursor& c, int k, const StreamPlan& p,
+                                              const WarpInfo& wi, int vec) {
+  if (c.q < 0 || c.q >= wi.Q || c.j0 >= p.M) return;  // nothing, or all padding
+  const int j0 = c.j0;
+  const int row = c.band * 32 * KS + 32 * k + wi.lane;
   const bool rv = row < p.N;
-  T* dst = ring_row + (sc0 & (RING - 1));
-  const T* src = src_base + ((long long)(wi.p0 + pq) * p.N + (rv ? row : 0)) * p.M;
+  T* dst = ring_row + ((c.u * TILE) & (RING - 1));
+  const T* src = src_base + ((long long)(wi.p0 + c.pq) * p.N + (rv ? row : 0)) * p.M;
   if (vec) {
     constexpr int PER = 16 / (int)sizeof(T);
 #pragma unroll
@@ -97,16 +133,11 @@ __device__ __forceinline__ void load_row_tile(const T* __restrict__ src_base, T*
 
 // Padding columns j >= M of a landed tile get the raw cost Big/kappa.
 template <typename T>
-__device__ __forceinline__ void patch_row_tile(T* ring_row, int u, const StreamPlan& p,
+__device__ __forceinline__ void patch_row_tile(T* ring_row, const Cursor& c, const StreamPlan& p,
                                                const WarpInfo& wi, T padv) {
-  if (u < 0) return;
-  const int sc0 = u * TILE;
-  const int q = sc0 / p.L;
-  if (q >= wi.Q) return;
-  const int j0 = sc0 - q * p.L;
-  if (j0 + TILE <= p.M) return;
-  T* dst = ring_row + (sc0 & (RING - 1));
-  for (int h = max(0, p.M - j0); h < TILE; ++h) dst[h] = padv;
+  if (c.q < 0 || c.q >= wi.Q || c.j0 + TILE <= p.M) return;
+  T* dst = ring_row + ((c.u * TILE) & (RING - 1));
+  for (int h = max(0, p.M - c.j0); h < TILE; ++h) dst[h] = padv;
 }
 
 // Value of "row -1" that lane 0 of sub-band 0 sees at stream column sc:
@@ -166,18 +197,26 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
   T* myC = ringC + lane * S;
   T* myQ = ringQ + lane * S;
 
+  Cursor ld[KS], pt[KS];  // next tile to load / to patch, per sub-band
+#pragma unroll
+  for (int k = 0; k < KS; ++k) {
+    ld[k] = cursor_at(-4 * k, p);
+    pt[k] = ld[k];
+  }
 #pragma unroll 1
   for (int pb = -LEAD; pb < 0; ++pb) {
 #pragma unroll
     for (int k = 0; k < KS; ++k) {
-      load_row_tile<T, KS>(a.C, myC + k * 32 * S, pb - 4 * k + LEAD, k, p, wi, a.vec);
-      if (HAS_P) load_row_tile<T, KS>(a.Q, myQ + k * 32 * S, pb - 4 * k + LEAD, k, p, wi, a.vec);
+      load_row_tile<T, KS>(a.C, myC + k * 32 * S, ld[k], k, p, wi, a.vec);
+      if (HAS_P) load_row_tile<T, KS>(a.Q, myQ + k * 32 * S, ld[k], k, p, wi, a.vec);
+      cursor_next(ld[k], p);
     }
     cp_async_commit();
   }
 
   T left[KS], up[KS], dg[KS], Pl[KS], Pu[KS], Pd[KS];
   int jk[KS], rowk[KS];
+  const int rows = 32 * KS;
 #pragma unroll
   for (int k = 0; k < KS; ++k) {
     left[k] = up[k] = dg[k] = big;
@@ -186,49 +225,50 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
       const int sc = -32 * k - lane;
       const int q = floor_div(sc, p.L);
       jk[k] = sc - q * p.L;
-      rowk[k] = pos_mod(q, p.NB) * 32 * KS + 32 * k + lane;
+      rowk[k] = pos_mod(q, p.NB) * rows + 32 * k + lane;
     }
   }
   if (lane == 0) dg[0] = T(0);
 
-  const T* dlR = a.dlR + (long long)wi.w * p.L;
-  const T* dlP = HAS_P ? a.dlP + (long long)wi.w * p.L : nullptr;
-  T* dlRw = a.dlR + (long long)wi.w * p.L;
-  T* dlPw = HAS_P ? a.dlP + (long long)wi.w * p.L : nullptr;
+  T* dlR = a.dlR + (long long)wi.w * p.L;
+  T* dlP = HAS_P ? a.dlP + (long long)wi.w * p.L : nullptr;
+  // row -1 values for lane 0 / sub-band 0, one 32-column window per register
   T rbR = row_above(dlR, lane, p, wi, big), rbRn = row_above(dlR, 32 + lane, p, wi, big);
   T rbP = T(0), rbPn = T(0);
   if (HAS_P) {
     rbP = row_above(dlP, lane, p, wi, T(0));
     rbPn = row_above(dlP, 32 + lane, p, wi, T(0));
   }
-  T wbR = T(0), wbP = T(0);
+  T wbR = T(0), wbP = T(0);  // bottom-row values collected for the delay line
 
-  const int rows = 32 * KS;
-  const int kstar = ((p.N - 1) % rows) / 32, lstar = (p.N - 1) % 32;
-  const long long NBL = (long long)p.NB * p.L;
-  long long cap_t = (long long)((p.N - 1) / rows) * p.L + (p.M - 1) + 32 * kstar + lstar;
-  int cap_i = 0;
-
-  T* sR = a.sR + (long long)wi.w * p.tmax * KS * 32 + lane;
-  T* sP = HAS_P ? a.sP + (long long)wi.w * p.tmax * KS * 32 + lane : nullptr;
+  const long long woff = (long long)wi.w * p.tmax * KS * 32;
   const T kap = a.kappa;
 
+  // The 8 steps of a block are straight-line code; every rare event (cost
+  // tiles, delay-line flush, window change) happens between blocks.
 #pragma unroll 1
   for (int t0 = 0; t0 < wi.Tw; t0 += TILE) {
     cp_async_wait<LEAD - 1>();
 #pragma unroll
-    for (int k = 0; k < KS; ++k) patch_row_tile(myC + k * 32 * S, t0 / TILE - 4 * k, p, wi, a.pad_raw);
+    for (int k = 0; k < KS; ++k) {
+      patch_row_tile(myC + k * 32 * S, pt[k], p, wi, a.pad_raw);
+      cursor_next(pt[k], p);
+    }
 #pragma unroll
     for (int k = 0; k < KS; ++k) {
-      load_row_tile<T, KS>(a.C, myC + k * 32 * S, t0 / TILE - 4 * k + LEAD, k, p, wi, a.vec);
-      if (HAS_P) load_row_tile<T, KS>(a.Q, myQ + k * 32 * S, t0 / TILE - 4 * k + LEAD, k, p, wi, a.vec);
+      load_row_tile<T, KS>(a.C, myC + k * 32 * S, ld[k], k, p, wi, a.vec);
+      if (HAS_P) load_row_tile<T, KS>(a.Q, myQ + k * 32 * S, ld[k], k, p, wi, a.vec);
+      cursor_next(ld[k], p);
     }
     cp_async_commit();
 
+    const bool wrapw = ((t0 + TILE) & 31) == 0;  // column t0+8 opens the next window
+    T* srow = a.sR + woff + lane + (long long)t0 * KS * 32;
+    T* prow = HAS_P ? a.sP + woff + lane + (long long)t0 * KS * 32 : nullptr;
+    const int c0 = (t0 - lane) & (RING - 1);
 #pragma unroll
     for (int s = 0; s < TILE; ++s) {
-      const int t = t0 + s;
-      const int ia = (t - lane) & (RING - 1);
+      const int ia = (c0 + s) & (RING - 1);
       T Rn[KS], Pn[KS];
 #pragma unroll
       for (int k = 0; k < KS; ++k) {
@@ -237,60 +277,29 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
         const T qv = HAS_P ? myQ[off] : T(0);
         cell_forward<T, HAS_P>(c, qv, left[k], up[k], dg[k], Pl[k], Pu[k], Pd[k], Rn[k], Pn[k]);
         if constexpr (HAS_BAND) {
-          if (fabs((T)(rowk[k] - jk[k])) > a.band) {
-            Rn[k] = big;
-            Pn[k] = T(0);
-          }
-          if (++jk[k] == p.L) {
-            jk[k] = 0;
-            rowk[k] += rows;
-            if (rowk[k] >= p.NB * rows) rowk[k] -= p.NB * rows;
-          }
+          const bool ok = fabs((T)(rowk[k] - jk[k])) <= a.band;
+          Rn[k] = ok ? Rn[k] : big;
+          Pn[k] = ok ? Pn[k] : T(0);
+          const int jn = jk[k] + 1;
+          const bool wrap = jn == p.L;
+          int rn = rowk[k] + rows;
+          rn = rn >= p.NB * rows ? rn - p.NB * rows : rn;
+          jk[k] = wrap ? 0 : jn;
+          rowk[k] = wrap ? rn : rowk[k];
         }
-        sR[((long long)t * KS + k) * 32] = Rn[k];
-        if (HAS_P) sP[((long long)t * KS + k) * 32] = Pn[k];
+        srow[(s * KS + k) * 32] = Rn[k];
+        if (HAS_P) prow[(s * KS + k) * 32] = Pn[k];
       }
-
-      if (t == cap_t) {
-        T v = Rn[0], vp = Pn[0];
-#pragma unroll
-        for (int k = 1; k < KS; ++k)
-          if (k == kstar) { v = Rn[k]; vp = Pn[k]; }
-        if (lane == lstar) {
-          a.out_r[wi.p0 + cap_i] = v >= big * T(0.5) ? T(INFINITY) : v * a.inv_kappa;
-          if (HAS_P) a.out_p[wi.p0 + cap_i] = vp;
-        }
-        ++cap_i;
-        cap_t = cap_i < wi.npairs ? cap_t + NBL : LLONG_MAX;
-      }
-
-      {  // bottom row of the band -> delay line (gathered 32 columns at a time)
-        const int scb = t - 32 * (KS - 1) - 31;
-        const T v = shfl(Rn[KS - 1], 31);
-        const T vp = HAS_P ? shfl(Pn[KS - 1], 31) : T(0);
-        if ((scb & 31) == lane) { wbR = v; wbP = vp; }
-        if ((scb & 31) == 31) {
-          const int scx = scb - 31 + lane;
-          if (scx >= 0) {
-            const int j = scx - (scx / p.L) * p.L;
-            dlRw[j] = wbR;
-            if (HAS_P) dlPw[j] = wbP;
-          }
-          __syncwarp();
-        }
-      }
-
-      if (((t + 1) & 31) == 0) {
-        rbR = rbRn;
-        rbRn = row_above(dlR, t + 33 + lane, p, wi, big);
-        if (HAS_P) {
-          rbP = rbPn;
-          rbPn = row_above(dlP, t + 33 + lane, p, wi, T(0));
-        }
-      }
-      const T bv = shfl(rbR, (t + 1) & 31);
-      const T bp = HAS_P ? shfl(rbP, (t + 1) & 31) : T(0);
-
+      // bottom row (column t - 32 KS + 1) is kept by lane t mod 32
+      const T v = shfl(Rn[KS - 1], 31);
+      const T vp = HAS_P ? shfl(Pn[KS - 1], 31) : T(0);
+      const bool mine = lane == ((t0 + s) & 31);
+      wbR = mine ? v : wbR;
+      if (HAS_P) wbP = mine ? vp : wbP;
+      // row -1 value for the next step (column t + 1)
+      const bool nextw = (s == TILE - 1) && wrapw;
+      const T bv = shfl(nextw ? rbRn : rbR, (t0 + s + 1) & 31);
+      const T bp = HAS_P ? shfl(nextw ? rbPn : rbP, (t0 + s + 1) & 31) : T(0);
 #pragma unroll
       for (int k = 0; k < KS; ++k) {
         dg[k] = up[k];
@@ -305,30 +314,48 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
       up[0] = shfl_up1_rot(lane == 31 ? bv : Rn[0]);
       if (HAS_P) Pu[0] = shfl_up1_rot(lane == 31 ? bp : Pn[0]);
     }
+
+    if (wrapw) {
+      // lanes hold the bottom row for columns t0 - 23 - 32 KS + lane
+      const int scx = t0 - 23 - 32 * KS + lane;
+      if (scx >= 0) {
+        const int j = scx - (scx / p.L) * p.L;
+        dlR[j] = wbR;
+        if (HAS_P) dlP[j] = wbP;
+      }
+      __syncwarp();
+      rbR = rbRn;
+      rbRn = row_above(dlR, t0 + TILE + 32 + lane, p, wi, big);
+      if (HAS_P) {
+        rbP = rbPn;
+        rbPn = row_above(dlP, t0 + TILE + 32 + lane, p, wi, T(0));
+      }
+    }
   }
   cp_async_wait<0>();
+
+  // R[N-1, M-1] of each pair, read back from this lane's own saved stream
+  const int kstar = ((p.N - 1) % rows) / 32, lstar = (p.N - 1) % 32;
+  if (lane == lstar) {
+    for (int i = 0; i < wi.npairs; ++i) {
+      const long long ct = (long long)(i * p.NB + (p.N - 1) / rows) * p.L + (p.M - 1) +
+                           32 * kstar + lstar;
+      const T v = a.sR[woff + (ct * KS + kstar) * 32 + lane];
+      a.out_r[wi.p0 + i] = v >= big * T(0.5) ? T(INFINITY) : v * a.inv_kappa;
+      if (HAS_P) a.out_p[wi.p0 + i] = a.sP[woff + (ct * KS + kstar) * 32 + lane];
+    }
+  }
 }
 
 // ---------------------------------------------------------------- backward
 
-// Copy saved rows [8c, 8c+8) (contiguous: 8*KS*32 elements) into slot c&3.
+// This lane's saved values of stream row r (one per sub-band); rows before
+// the stream start read as +Big (R) / 0 (P).
 template <typename T, int KS>
-__device__ __forceinline__ void load_saved_chunk(const T* __restrict__ src_warp, T* ring, int c,
-                                                 int lane) {
-  if (c < 0) return;
-  constexpr int ELEMS = TILE * KS * 32;
-  constexpr int PER = 16 / (int)sizeof(T);
-  const T* src = src_warp + (long long)c * ELEMS;
-  T* dst = ring + (c & 3) * ELEMS;
+__device__ __forceinline__ void load_saved_row(const T* __restrict__ s_lane, int r, T fill,
+                                               T (&out)[KS]) {
 #pragma unroll
-  for (int i = lane; i < ELEMS / PER; i += 32) cp_async16(dst + i * PER, src + i * PER, 16);
-}
-
-template <typename T, int KS>
-__device__ __forceinline__ T saved_at(const T* ring, int row, int k, int lane, T big) {
-  constexpr int ELEMS = TILE * KS * 32;
-  if (row < 0) return big;
-  return ring[((row >> 3) & 3) * ELEMS + ((row & 7) * KS + k) * 32 + lane];
+  for (int k = 0; k < KS; ++k) out[k] = r >= 0 ? s_lane[((long long)r * KS + k) * 32] : fill;
 }
 
 // Row -1 value lane 0 of sub-band 0 used at stream column sc in the forward
@@ -346,14 +373,17 @@ __device__ __forceinline__ T row_above_saved(const T* s_warp, int sc, const Stre
 }
 
 // Adjoint pushed into the bottom row of the band at stream column sc from the
-// next band's top row (delay line); zero when the next band starts a new pair.
+// next band's top row (delay line); zero when the next band starts a new pair,
+// and zero on padding columns (j >= M), which carry no adjoint.  (The top row
+// of a pair's first band hands the adjoint of its virtual corner R(-1,-1) one
+// column back, into the previous pass's last padding column; it must stop there.)
 template <typename T>
 __device__ __forceinline__ T push_from_below(const T* dl, int sc, const StreamPlan& p,
                                              const WarpInfo& wi) {
   if (sc < 0) return T(0);
   const int q = sc / p.L;
   const int j = sc - q * p.L;
-  if (q + 1 >= wi.Q || (q + 1) % p.NB == 0) return T(0);
+  if (j >= p.M || q + 1 >= wi.Q || (q + 1) % p.NB == 0) return T(0);
   return dl[j];
 }
 
@@ -389,24 +419,18 @@ __device__ __forceinline__ void cell_backward(T Rl, T Ru, T Rd, T Pl, T Pu, T Pd
   }
 }
 
-// Write this lane's row of flush tile u (8 stream columns) from the staging
+// Write this lane's row of flush tile c (8 stream columns) from the staging
 // ring to dC (natural layout), data columns only.
 template <typename T, int KS>
-__device__ __forceinline__ void flush_row_tile(T* __restrict__ dst_base, const T* ring_row, int u,
-                                               int k, const StreamPlan& p, const WarpInfo& wi,
-                                               int vec) {
-  if (u < 0) return;
-  const int sc0 = u * TILE;
-  const int q = sc0 / p.L;
-  if (q >= wi.Q) return;
-  const int j0 = sc0 - q * p.L;
-  if (j0 >= p.M) return;
-  const int pq = q / p.NB;
-  const int band = q - pq * p.NB;
-  const int row = band * 32 * KS + 32 * k + wi.lane;
+__device__ __forceinline__ void flush_row_tile(T* __restrict__ dst_base, const T* ring_row,
+                                               const Cursor& c, int k, const StreamPlan& p,
+                                               const WarpInfo& wi, int vec) {
+  if (c.q < 0 || c.q >= wi.Q || c.j0 >= p.M) return;
+  const int j0 = c.j0;
+  const int row = c.band * 32 * KS + 32 * k + wi.lane;
   if (row >= p.N) return;
-  const T* src = ring_row + (sc0 & (RING - 1));
-  T* dst = dst_base + ((long long)(wi.p0 + pq) * p.N + row) * p.M + j0;
+  const T* src = ring_row + ((c.u * TILE) & (RING - 1));
+  T* dst = dst_base + ((long long)(wi.p0 + c.pq) * p.N + row) * p.M + j0;
   if (vec && j0 + TILE <= p.M) {
     constexpr int PER = 16 / (int)sizeof(T);
 #pragma unroll
@@ -422,18 +446,15 @@ template <typename T, int KS, bool HAS_P>
 __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
   constexpr int S = RingStride<T>::value;
   constexpr int RW = KS * 32 * S;
-  constexpr int SW = 4 * TILE * KS * 32;  // saved staging per operand
   const StreamPlan& p = a.p;
   WarpInfo wi;
   if (!warp_setup(p, KS, wi)) return;
   const int lane = wi.lane;
   const T big = Big<T>::value;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  T* base = reinterpret_cast<T*>(smem_raw) + (size_t)wi.wib * (RW + SW) * (HAS_P ? 2 : 1);
+  T* base = reinterpret_cast<T*>(smem_raw) + (size_t)wi.wib * RW * (HAS_P ? 2 : 1);
   T* outC = base;
   T* outQ = base + RW;
-  T* stR = base + RW * (HAS_P ? 2 : 1);
-  T* stP = stR + SW;
   T* myC = outC + lane * S;
   T* myQ = outQ + lane * S;
 
@@ -442,18 +463,21 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
   const T* sPw = HAS_P ? a.sP + woff : nullptr;
   const int Tend = (wi.Tw + TILE - 1) / TILE * TILE;
   const int btop = Tend / TILE - 1;
+  const T* sRl = sRw + lane;
+  const T* sPl = HAS_P ? sPw + lane : nullptr;
 
-#pragma unroll 1
-  for (int c = btop; c > btop - 3; --c) {
-    load_saved_chunk<T, KS>(sRw, stR, c, lane);
-    if (HAS_P) load_saved_chunk<T, KS>(sPw, stP, c, lane);
-    cp_async_commit();
+  // F holds saved rows 8b-2 .. 8b+5 of the current block b (row t-2 of
+  // iteration t = 8b + s is F[s]); G prefetches the next block's rows.
+  T F[TILE][KS], G[TILE][KS], FP[TILE][KS], GP[TILE][KS];
+#pragma unroll
+  for (int s = 0; s < TILE; ++s) {
+    load_saved_row<T, KS>(sRl, TILE * btop - 2 + s, big, F[s]);
+    if (HAS_P) load_saved_row<T, KS>(sPl, TILE * btop - 2 + s, T(0), FP[s]);
   }
 
   T* dlR = a.dlR + (long long)wi.w * p.L;
   T* dlP = HAS_P ? a.dlP + (long long)wi.w * p.L : nullptr;
 
-  // iteration state
   T accL[KS], accB[KS], dgp[KS], Qacc[KS], QaccB[KS], dgq[KS];
   T cur[KS], Xc[KS], Pcur[KS], PXc[KS];
 #pragma unroll
@@ -461,16 +485,11 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
     accL[k] = accB[k] = dgp[k] = Qacc[k] = QaccB[k] = dgq[k] = T(0);
   }
 
-  // rows t-1 and X(t) for t = Tend - 1 need the chunk btop landed
-  cp_async_wait<2>();
-  __syncwarp();
   const int t_first = Tend - 1;
-  // boundary windows (values of row -1 for lane 0 / sub-band 0), keyed by stream column
-  // A window holds 32 consecutive stream columns [32m, 32m+32), one per lane;
-  // the loop moves to the next lower window when its column hits 32m+31.  If
-  // the first column is already such a top, start one window higher.
-  const int c_b = t_first - 1;  // first column needing a row -1 value
-  int bw = floor_div(c_b, 32) + (pos_mod(c_b, 32) == 31 ? 1 : 0);
+  // Row -1 values (lane 0 / sub-band 0) by stream column, 32 per window: bR
+  // covers the window of column t-1 for iterations t of the current block
+  // except t = 32m (its t-1 is in the next lower window, bRn).
+  int bw = (t_first - 1) >> 5;
   T bR = row_above_saved<T, KS>(sRw, 32 * bw + lane, p, wi, big);
   T bRn = row_above_saved<T, KS>(sRw, 32 * (bw - 1) + lane, p, wi, big);
   T bP = T(0), bPn = T(0);
@@ -478,26 +497,25 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
     bP = row_above_saved<T, KS>(sPw, 32 * bw + lane, p, wi, T(0));
     bPn = row_above_saved<T, KS>(sPw, 32 * (bw - 1) + lane, p, wi, T(0));
   }
-  // push windows (adjoint from the band below), keyed by the bottom row's column
-  const int c_d = t_first - 1 - 32 * (KS - 1) - 31;
-  int dwin = floor_div(c_d, 32) + (pos_mod(c_d, 32) == 31 ? 1 : 0);
-  T dR = push_from_below(dlR, 32 * dwin + lane, p, wi);
-  T dRn = push_from_below(dlR, 32 * (dwin - 1) + lane, p, wi);
+  // Adjoint from the band below, by the bottom row's column t - 32 KS at
+  // iteration t (used one iteration later); a block never straddles windows.
+  int dw = (TILE * btop - 32 * KS) >> 5;
+  T dR = push_from_below(dlR, 32 * dw + lane, p, wi);
+  T dRn = push_from_below(dlR, 32 * (dw - 1) + lane, p, wi);
   T dP = T(0), dPn = T(0);
   if (HAS_P) {
-    dP = push_from_below(dlP, 32 * dwin + lane, p, wi);
-    dPn = push_from_below(dlP, 32 * (dwin - 1) + lane, p, wi);
+    dP = push_from_below(dlP, 32 * dw + lane, p, wi);
+    dPn = push_from_below(dlP, 32 * (dw - 1) + lane, p, wi);
   }
-  T wdR = T(0), wdP = T(0);
+  T wdR = T(0), wdP = T(0);  // top-row sends collected for the delay line
 
   {  // cur = saved row t_first - 1, Xc = X(t_first)
     const T b0 = row_above_saved<T, KS>(sRw, t_first, p, wi, big);
     const T b0p = HAS_P ? row_above_saved<T, KS>(sPw, t_first, p, wi, T(0)) : T(0);
+    load_saved_row<T, KS>(sRl, t_first - 1, big, cur);
 #pragma unroll
-    for (int k = 0; k < KS; ++k) {
-      cur[k] = saved_at<T, KS>(stR, t_first - 1, k, lane, big);
-      Pcur[k] = HAS_P ? saved_at<T, KS>(stP, t_first - 1, k, lane, T(0)) : T(0);
-    }
+    for (int k = 0; k < KS; ++k) Pcur[k] = T(0);
+    if (HAS_P) load_saved_row<T, KS>(sPl, t_first - 1, T(0), Pcur);
 #pragma unroll
     for (int k = KS - 1; k >= 1; --k) {
       Xc[k] = shfl_up1_rot(lane == 31 ? cur[k - 1] : cur[k]);
@@ -509,50 +527,48 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
 
   const int rows = 32 * KS;
   const int kstar = ((p.N - 1) % rows) / 32, lstar = (p.N - 1) % 32;
-  const long long NBL = (long long)p.NB * p.L;
+  const int NBL = p.NB * p.L;
   int cap_i = wi.npairs - 1;
-  long long cap_t = (long long)cap_i * NBL + (long long)((p.N - 1) / rows) * p.L + (p.M - 1) +
-                    32 * kstar + lstar;
+  int cap_t = cap_i * NBL + ((p.N - 1) / rows) * p.L + (p.M - 1) + 32 * kstar + lstar;
+  T seed_r = a.grad_r[wi.p0 + cap_i];
+  T seed_p = HAS_P ? a.grad_p[wi.p0 + cap_i] : T(0);
+
+  // tile completed by this lane in block b: u = b - 4k - lane/8
+  Cursor fl[KS];
+#pragma unroll
+  for (int k = 0; k < KS; ++k) fl[k] = cursor_at(btop - 4 * k - (lane >> 3), p);
 
 #pragma unroll 1
   for (int b = btop; b >= 0; --b) {
-    load_saved_chunk<T, KS>(sRw, stR, b - 3, lane);
-    if (HAS_P) load_saved_chunk<T, KS>(sPw, stP, b - 3, lane);
-    cp_async_commit();
-    cp_async_wait<2>();
-    __syncwarp();
+    const int t0 = TILE * b;
+#pragma unroll
+    for (int s = 0; s < TILE; ++s) {
+      load_saved_row<T, KS>(sRl, TILE * (b - 1) - 2 + s, big, G[s]);
+      if (HAS_P) load_saved_row<T, KS>(sPl, TILE * (b - 1) - 2 + s, T(0), GP[s]);
+    }
+    const bool lowb = (t0 & 31) == 0;  // iteration t0 reads row -1 of column t0-1 from bRn
+    const bool seedhere = cap_t >= t0 && cap_t < t0 + TILE;
 
 #pragma unroll
     for (int s = TILE - 1; s >= 0; --s) {
-      const int t = b * TILE + s;
-      if (t == cap_t) {
-        const int pi = wi.p0 + cap_i;
-        const T gr = a.grad_r[pi];
-        const T gp = HAS_P ? a.grad_p[pi] : T(0);
-        if (lane == lstar) {
+      const int t = t0 + s;
+      // the end cell of a pair receives dL/dR (and dL/dP) as its adjoint
+      const bool inj = seedhere && t == cap_t && lane == lstar;
 #pragma unroll
-          for (int k = 0; k < KS; ++k)
-            if (k == kstar) { accL[k] += gr; if (HAS_P) Qacc[k] += gp; }
-        }
-        --cap_i;
-        cap_t = cap_i >= 0 ? cap_t - NBL : -1;
+      for (int k = 0; k < KS; ++k) {
+        const bool kk = inj && k == kstar;
+        accL[k] += kk ? seed_r : T(0);
+        if (HAS_P) Qacc[k] += kk ? seed_p : T(0);
       }
-      // next predecessor rows: saved row t-2 and X(t-1)
-      if ((pos_mod(t - 1, 32)) == 31) {
-        bR = bRn;
-        bRn = row_above_saved<T, KS>(sRw, t - 1 - 63 + lane, p, wi, big);
-        if (HAS_P) {
-          bP = bPn;
-          bPn = row_above_saved<T, KS>(sPw, t - 1 - 63 + lane, p, wi, T(0));
-        }
-      }
-      const T bv = shfl(bR, pos_mod(t - 1, 32));
-      const T bvp = HAS_P ? shfl(bP, pos_mod(t - 1, 32)) : T(0);
+      // predecessor rows: saved row t-2 and X(t-1)
+      const bool loww = (s == 0) && lowb;
+      const T bv = shfl(loww ? bRn : bR, (t - 1) & 31);
+      const T bvp = HAS_P ? shfl(loww ? bPn : bP, (t - 1) & 31) : T(0);
       T nxt[KS], Pnxt[KS], Xn[KS], PXn[KS];
 #pragma unroll
       for (int k = 0; k < KS; ++k) {
-        nxt[k] = saved_at<T, KS>(stR, t - 2, k, lane, big);
-        Pnxt[k] = HAS_P ? saved_at<T, KS>(stP, t - 2, k, lane, T(0)) : T(0);
+        nxt[k] = F[s][k];
+        Pnxt[k] = HAS_P ? FP[s][k] : T(0);
       }
 #pragma unroll
       for (int k = KS - 1; k >= 1; --k) {
@@ -583,31 +599,15 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
           dgq[k] = qd;
         }
       }
-
-      {  // top row of the band -> delay line (adjoint for the band above)
-        const T v = shfl(send[0], 0);
-        const T vq = HAS_P ? shfl(sendq[0], 0) : T(0);
-        if ((t & 31) == lane) { wdR = v; wdP = vq; }
-        if ((t & 31) == 0) {
-          const int scx = t + lane;
-          const int j = scx - (scx / p.L) * p.L;
-          dlR[j] = wdR;
-          if (HAS_P) dlP[j] = wdP;
-          __syncwarp();
-        }
-      }
+      // top row's send (column t) is kept by lane t mod 32
+      const T v = shfl(send[0], 0);
+      const T vq = HAS_P ? shfl(sendq[0], 0) : T(0);
+      const bool mine = lane == (t & 31);
+      wdR = mine ? v : wdR;
+      if (HAS_P) wdP = mine ? vq : wdP;
       // adjoint arriving at the bottom row (lane 31, sub-band KS-1) at t-1
-      const int scd = t - 1 - 32 * (KS - 1) - 31;
-      if (pos_mod(scd, 32) == 31) {
-        dR = dRn;
-        dRn = push_from_below(dlR, scd - 63 + lane, p, wi);
-        if (HAS_P) {
-          dP = dPn;
-          dPn = push_from_below(dlP, scd - 63 + lane, p, wi);
-        }
-      }
-      const T dv = shfl(dR, pos_mod(scd, 32));
-      const T dvq = HAS_P ? shfl(dP, pos_mod(scd, 32)) : T(0);
+      const T dv = shfl(dR, (t - 32 * KS) & 31);
+      const T dvq = HAS_P ? shfl(dP, (t - 32 * KS) & 31) : T(0);
 #pragma unroll
       for (int k = 0; k < KS - 1; ++k) {
         accB[k] = shfl_dn1_rot(lane == 0 ? send[k + 1] : send[k]);
@@ -615,7 +615,6 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
       }
       accB[KS - 1] = shfl_dn1_rot(lane == 0 ? dv : send[KS - 1]);
       if (HAS_P) QaccB[KS - 1] = shfl_dn1_rot(lane == 0 ? dvq : sendq[KS - 1]);
-
 #pragma unroll
       for (int k = 0; k < KS; ++k) {
         cur[k] = nxt[k];
@@ -623,14 +622,54 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
         if (HAS_P) { Pcur[k] = Pnxt[k]; PXc[k] = PXn[k]; }
       }
     }
-    // tiles completed in this block: u = b - 4k - lane/8
+
+    // ---- between blocks
+#pragma unroll
+    for (int s = 0; s < TILE; ++s)
+#pragma unroll
+      for (int k = 0; k < KS; ++k) {
+        F[s][k] = G[s][k];
+        if (HAS_P) FP[s][k] = GP[s][k];
+      }
 #pragma unroll
     for (int k = 0; k < KS; ++k) {
-      flush_row_tile<T, KS>(a.dC, myC + k * 32 * S, b - 4 * k - (lane >> 3), k, p, wi, a.vec);
-      if (HAS_P) flush_row_tile<T, KS>(a.dQ, myQ + k * 32 * S, b - 4 * k - (lane >> 3), k, p, wi, a.vec);
+      flush_row_tile<T, KS>(a.dC, myC + k * 32 * S, fl[k], k, p, wi, a.vec);
+      if (HAS_P) flush_row_tile<T, KS>(a.dQ, myQ + k * 32 * S, fl[k], k, p, wi, a.vec);
+      cursor_prev(fl[k], p);
+    }
+    if (seedhere) {
+      --cap_i;
+      cap_t = cap_i >= 0 ? cap_t - NBL : -1;
+      if (cap_i >= 0) {
+        seed_r = a.grad_r[wi.p0 + cap_i];
+        if (HAS_P) seed_p = a.grad_p[wi.p0 + cap_i];
+      }
+    }
+    if (lowb) {
+      // the window [t0, t0+32) of top-row sends is complete
+      const int j = (t0 + lane) - ((t0 + lane) / p.L) * p.L;
+      dlR[j] = wdR;
+      if (HAS_P) dlP[j] = wdP;
+      __syncwarp();
+      bR = bRn;
+      bRn = row_above_saved<T, KS>(sRw, t0 - 64 + lane, p, wi, big);
+      if (HAS_P) {
+        bP = bPn;
+        bPn = row_above_saved<T, KS>(sPw, t0 - 64 + lane, p, wi, T(0));
+      }
+    }
+    // the next block (t0 - 8) may open a new window of bottom-row columns
+    const int dwn = (t0 - TILE - 32 * KS) >> 5;
+    if (dwn != dw) {
+      dw = dwn;
+      dR = dRn;
+      dRn = push_from_below(dlR, 32 * (dw - 1) + lane, p, wi);
+      if (HAS_P) {
+        dP = dPn;
+        dPn = push_from_below(dlP, 32 * (dw - 1) + lane, p, wi);
+      }
     }
   }
-  cp_async_wait<0>();
 }
 
 template <typename T, int KS, bool HAS_P, bool HAS_BAND>
@@ -672,36 +711,49 @@ int bwd_ks(const SdtwArgs<T>& a, bool has_p, cudaStream_t st) {
 
 }  // namespace
 
+static int env_int(const char* name, int fallback) {
+  const char* v = getenv(name);
+  return (v && *v) ? atoi(v) : fallback;
+}
+
 StreamPlan make_stream_plan(int B, int N, int M, int eb, bool has_p, int sms) {
   StreamPlan p;
   p.B = B;
   p.N = N;
   p.M = M;
-  p.KS = N <= 32 ? 1 : (N <= 64 ? 2 : 4);
+  // Sub-bands per warp: ILP inside a warp.  Thread-level parallelism (warps
+  // per SM) is what hides the soft-min's latency, and every sub-band costs a
+  // ring of shared memory, so two sub-bands by default.
+  int ks = env_int("TW_STREAM_KS", N <= 32 ? 1 : 2);
+  p.KS = ks >= 4 ? 4 : (ks >= 2 ? 2 : 1);
   const int rows = 32 * p.KS;
   p.NB = (N + rows - 1) / rows;
-  const int L = M + 1 > rows + 128 ? M + 1 : rows + 128;
+  // The band-to-band delay line needs L >= 32*KS + 128 (see row_above); a
+  // single-band pair has no delay line and only needs the padding column.
+  int L = M + 1;
+  if (p.NB > 1 && L < rows + 128) L = rows + 128;
   p.L = (L + TILE - 1) / TILE * TILE;
   const int S = eb == 4 ? RingStride<float>::value : RingStride<double>::value;
-  const size_t ring = (size_t)p.KS * 32 * S * eb;
-  const size_t stage = (size_t)4 * TILE * p.KS * 32 * eb;
-  const size_t fwd_w = ring * (has_p ? 2 : 1);
-  const size_t bwd_w = (ring + stage) * (has_p ? 2 : 1);
-  const size_t per_w = fwd_w > bwd_w ? fwd_w : bwd_w;
-  int wps = (int)((size_t)(200 * 1024) / per_w);
-  wps = wps < 1 ? 1 : (wps > 16 ? 16 : wps);
-  p.wpc = wps < 4 ? wps : 4;
-  const int cps = wps / p.wpc > 0 ? wps / p.wpc : 1;
-  const int maxw = sms * cps * p.wpc;
-  p.warps = B < maxw ? B : maxw;
-  if (p.warps < 1) p.warps = 1;
+  const size_t per_w = (size_t)p.KS * 32 * S * eb * (has_p ? 2 : 1);
+  int wps = (int)((size_t)(208 * 1024) / per_w);
+  wps = wps < 1 ? 1 : (wps > 24 ? 24 : wps);
+  const int cap = env_int("TW_STREAM_WPS", 0);
+  if (cap > 0 && cap < wps) wps = cap;
+  int wpc = wps < 4 ? wps : 4;
+  if (wpc > B) wpc = B > 0 ? B : 1;
+  const int cps = wps / wpc > 0 ? wps / wpc : 1;
+  int ctas = sms * cps;
+  const int ctas_needed = B / wpc > 0 ? B / wpc : 1;
+  if (ctas > ctas_needed) ctas = ctas_needed;
+  p.wpc = wpc;
+  p.warps = ctas * wpc;
   p.base = B / p.warps;
   p.rem = B % p.warps;
   const long long maxpairs = p.base + (p.rem ? 1 : 0);
   const long long Tw = maxpairs * p.NB * p.L + 32 * p.KS - 1;
   p.tmax = (Tw + TILE - 1) / TILE * TILE;
-  p.smem_fwd = fwd_w * p.wpc;
-  p.smem_bwd = bwd_w * p.wpc;
+  p.smem_fwd = per_w * p.wpc;
+  p.smem_bwd = per_w * p.wpc;
   return p;
 }
 
