@@ -127,6 +127,69 @@ int tw_udtw_features_grad_f64(const double* X, const double* Y, const double* vx
                               double eps, double* dX, double* dY, double* dvx, double* dvy,
                               void* stream);
 
+/* ---------------------------------------------------------------------
+ * JEANIE on a cost [B, K1, K2, T, U] (one viewpoint axis: K2 = 1).
+ *   s1, s2: viewpoint shifts (already clamped to K-1 by the caller).
+ *   out [B]: soft-min over viewpoints of R[:, T-1, U-1];
+ *   R [B, K1, K2, T, U]: the accumulator (saved state of the backward).
+ * Replaces jeanie_forward() src/torchwarp/csrc/jeanie_cuda.cu:564-588 (and
+ * the diagonal-major relayout of jeanie/_ops.py:68-79: layouts are natural).
+ * ------------------------------------------------------------------- */
+int tw_jeanie_forward_f32(const float* cost, int B, int K1, int K2, int T, int U, int s1, int s2,
+                          double gamma, float* out, float* R, void* stream);
+int tw_jeanie_forward_f64(const double* cost, int B, int K1, int K2, int T, int U, int s1, int s2,
+                          double gamma, double* out, double* R, void* stream);
+/* Backward for L = sum_b grad_out[b] out[b] + <grad_R, R> (grad_R may be NULL).
+ * Replaces jeanie_backward() src/torchwarp/csrc/jeanie_cuda.cu:590-619. */
+int tw_jeanie_backward_f32(const float* cost, const float* R, const float* grad_out,
+                           const float* grad_R, int B, int K1, int K2, int T, int U, int s1,
+                           int s2, double gamma, float* d_cost, void* stream);
+int tw_jeanie_backward_f64(const double* cost, const double* R, const double* grad_out,
+                           const double* grad_R, int B, int K1, int K2, int T, int U, int s1,
+                           int s2, double gamma, double* d_cost, void* stream);
+
+/* Query/support base cost: query [B, R, D] (R = K*T rows in (n, t) order),
+ * support [B, U, D] -> cost [B, R, U]; metric 0 = squared Euclidean
+ * (clamped at 0), 1 = Euclidean.  Replaces the bmm + relayout of
+ * jeanie/_ops.py:159-167 feeding jeanie_fused_forward (jeanie_cuda.cu:621-648)
+ * and the torch cost of jeanie/distances.py:25-38. */
+int tw_qs_cost_f32(const float* query, const float* support, int B, int R, int U, int D,
+                   int metric, float* cost, void* stream);
+int tw_qs_cost_f64(const double* query, const double* support, int B, int R, int U, int D,
+                   int metric, double* cost, void* stream);
+/* Gradient of that cost given d_cost [B, R, U]: d_query [B, R, D],
+ * d_support [B, U, D] (no gradient through sq <= 0, as torch.clamp_min /
+ * sqrt at 0).  Replaces jeanie_fused_backward's chain rule + bmm
+ * (jeanie_cuda.cu:650-683, jeanie/_ops.py:208-215); deterministic. */
+int tw_qs_cost_grad_f32(const float* query, const float* support, const float* cost,
+                        const float* d_cost, int B, int R, int U, int D, int metric,
+                        float* d_query, float* d_support, void* stream);
+int tw_qs_cost_grad_f64(const double* query, const double* support, const double* cost,
+                        const double* d_cost, int B, int R, int U, int D, int metric,
+                        double* d_query, double* d_support, void* stream);
+
+/* FVM viewpoint soft-min: cost [B, Kf, TU] -> temporal [B, TU] =
+ * -gamma logsumexp_n(-cost / gamma), and its backward d_cost = softmax_n *
+ * d_temporal.  Replaces jeanie/fvm.py:36-37 (torch logsumexp). */
+int tw_fvm_softmin_f32(const float* cost, int B, int Kf, int TU, double gamma, float* temporal,
+                       void* stream);
+int tw_fvm_softmin_f64(const double* cost, int B, int Kf, int TU, double gamma,
+                       double* temporal, void* stream);
+int tw_fvm_softmin_backward_f32(const float* cost, const float* d_temporal, int B, int Kf,
+                                int TU, double gamma, float* d_cost, void* stream);
+int tw_fvm_softmin_backward_f64(const double* cost, const double* d_temporal, int B, int Kf,
+                                int TU, double gamma, double* d_cost, void* stream);
+
+/* Hard alignment path (gamma -> 0) of cost [B, K, T, U] (float64), with the
+ * tie-break of src/torchwarp/paths.py:85-117 (viewpoint ascending, then
+ * (t-1,u-1), (t-1,u), (t,u-1), strict <; end viewpoint = first argmin);
+ * start_view < 0 means a free start.  Workspaces r_ws (double) and back_ws
+ * (int) hold B*K*T*U each; path [B, T+U-1, 3] gets (t, u, k) from (0,0) to
+ * (T-1,U-1) and length [B] its number of cells.  Replaces _optimal_3d. */
+int tw_optimal_path_f64(const double* cost, int B, int K, int T, int U, int max_shift,
+                        int start_view, double* r_ws, int* back_ws, int* path, int* length,
+                        void* stream);
+
 #ifdef __cplusplus
 }
 #endif

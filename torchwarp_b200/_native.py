@@ -40,6 +40,21 @@ SIGNATURES = {
                                 _c_p, _c_p]),
     "tw_udtw_features_grad_f32": (_c_i, [_c_p] * 7 + [_c_i] * 4 + [_c_d, _c_d] + [_c_p] * 5),
     "tw_udtw_features_grad_f64": (_c_i, [_c_p] * 7 + [_c_i] * 4 + [_c_d, _c_d] + [_c_p] * 5),
+    "tw_jeanie_forward_f32": (_c_i, [_c_p, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_d, _c_p,
+                                     _c_p, _c_p]),
+    "tw_jeanie_forward_f64": (_c_i, [_c_p, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_d, _c_p,
+                                     _c_p, _c_p]),
+    "tw_jeanie_backward_f32": (_c_i, [_c_p, _c_p, _c_p, _c_p] + [_c_i] * 7 + [_c_d, _c_p, _c_p]),
+    "tw_jeanie_backward_f64": (_c_i, [_c_p, _c_p, _c_p, _c_p] + [_c_i] * 7 + [_c_d, _c_p, _c_p]),
+    "tw_qs_cost_f32": (_c_i, [_c_p, _c_p] + [_c_i] * 5 + [_c_p, _c_p]),
+    "tw_qs_cost_f64": (_c_i, [_c_p, _c_p] + [_c_i] * 5 + [_c_p, _c_p]),
+    "tw_qs_cost_grad_f32": (_c_i, [_c_p] * 4 + [_c_i] * 5 + [_c_p, _c_p, _c_p]),
+    "tw_qs_cost_grad_f64": (_c_i, [_c_p] * 4 + [_c_i] * 5 + [_c_p, _c_p, _c_p]),
+    "tw_fvm_softmin_f32": (_c_i, [_c_p, _c_i, _c_i, _c_i, _c_d, _c_p, _c_p]),
+    "tw_fvm_softmin_f64": (_c_i, [_c_p, _c_i, _c_i, _c_i, _c_d, _c_p, _c_p]),
+    "tw_fvm_softmin_backward_f32": (_c_i, [_c_p, _c_p, _c_i, _c_i, _c_i, _c_d, _c_p, _c_p]),
+    "tw_fvm_softmin_backward_f64": (_c_i, [_c_p, _c_p, _c_i, _c_i, _c_i, _c_d, _c_p, _c_p]),
+    "tw_optimal_path_f64": (_c_i, [_c_p] + [_c_i] * 6 + [_c_p] * 5),
 }
 
 _LIB = None

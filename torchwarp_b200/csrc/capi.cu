@@ -142,6 +142,30 @@ int udtw_grad_f64(const double*, const double*, const double*, const double*, co
                   const double*, const double*, int, int, int, int, double, double, double*,
                   double*, double*, double*, cudaStream_t);
 
+template <typename T>
+int jeanie_forward(const T*, int, int, int, int, int, int, int, double, T*, T*, cudaStream_t);
+template <typename T>
+int jeanie_backward(const T*, const T*, const T*, const T*, int, int, int, int, int, int, int,
+                    double, T*, cudaStream_t);
+template <typename T>
+int qs_cost(const T*, const T*, int, int, int, int, int, T*, cudaStream_t);
+template <typename T>
+int qs_grad(const T*, const T*, const T*, const T*, int, int, int, int, int, T*, T*, cudaStream_t);
+template <typename T>
+int fvm_softmin(const T*, int, int, int, double, T*, cudaStream_t);
+template <typename T>
+int fvm_softmin_bwd(const T*, const T*, int, int, int, double, T*, cudaStream_t);
+int optimal_path(const double*, int, int, int, int, int, int, double*, int*, int*, int*,
+                 cudaStream_t);
+
+static int check_jeanie(const char* who, int B, int K1, int K2, int T, int U, int s1, int s2,
+                        double gamma) {
+  if (B < 0 || K1 <= 0 || K2 <= 0 || T <= 0 || U <= 0 || s1 < 0 || s2 < 0 || !(gamma > 0))
+    return set_error(kInvalid, "%s: invalid arguments (B=%d K1=%d K2=%d T=%d U=%d s=%d,%d)", who,
+                     B, K1, K2, T, U, s1, s2);
+  return kOk;
+}
+
 }  // namespace tw
 
 using namespace tw;
@@ -231,6 +255,76 @@ int tw_udtw_features_grad_f64(const double* X, const double* Y, const double* vx
     return set_error(kInvalid, "tw_udtw_features_grad: invalid arguments");
   return udtw_grad_f64(X, Y, vx, vy, cost, d_cost, d_penalty, B, N, M, D, beta, eps, dX, dY, dvx,
                        dvy, (cudaStream_t)stream);
+}
+
+
+#define TW_JEANIE_ENTRIES(SUF, T)                                                                \
+  int tw_jeanie_forward_##SUF(const T* cost, int B, int K1, int K2, int Tn, int U, int s1,      \
+                              int s2, double gamma, T* out, T* R, void* stream) {               \
+    g_err[0] = 0;                                                                               \
+    if (int e = check_jeanie("tw_jeanie_forward", B, K1, K2, Tn, U, s1, s2, gamma)) return e;   \
+    if (B && (!cost || !out || !R)) return set_error(kInvalid, "tw_jeanie_forward: null pointer"); \
+    return jeanie_forward<T>(cost, B, K1, K2, Tn, U, s1, s2, gamma, out, R,                    \
+                             (cudaStream_t)stream);                                              \
+  }                                                                                             \
+  int tw_jeanie_backward_##SUF(const T* cost, const T* R, const T* grad_out, const T* grad_R,   \
+                               int B, int K1, int K2, int Tn, int U, int s1, int s2,            \
+                               double gamma, T* d_cost, void* stream) {                         \
+    g_err[0] = 0;                                                                               \
+    if (int e = check_jeanie("tw_jeanie_backward", B, K1, K2, Tn, U, s1, s2, gamma)) return e;  \
+    if (B && (!cost || !R || !grad_out || !d_cost))                                              \
+      return set_error(kInvalid, "tw_jeanie_backward: null pointer");                          \
+    return jeanie_backward<T>(cost, R, grad_out, grad_R, B, K1, K2, Tn, U, s1, s2, gamma, d_cost, \
+                              (cudaStream_t)stream);                                             \
+  }                                                                                             \
+  int tw_qs_cost_##SUF(const T* query, const T* support, int B, int R, int U, int D,           \
+                       int metric, T* cost, void* stream) {                                     \
+    g_err[0] = 0;                                                                               \
+    if (B < 0 || R <= 0 || U <= 0 || D <= 0 || (metric != 0 && metric != 1))                  \
+      return set_error(kInvalid, "tw_qs_cost: invalid arguments");                             \
+    if (B && (!query || !support || !cost)) return set_error(kInvalid, "tw_qs_cost: null pointer"); \
+    return qs_cost<T>(query, support, B, R, U, D, metric, cost, (cudaStream_t)stream);         \
+  }                                                                                             \
+  int tw_qs_cost_grad_##SUF(const T* query, const T* support, const T* cost, const T* d_cost,  \
+                            int B, int R, int U, int D, int metric, T* d_query, T* d_support,   \
+                            void* stream) {                                                     \
+    g_err[0] = 0;                                                                               \
+    if (B < 0 || R <= 0 || U <= 0 || D <= 0 || (metric != 0 && metric != 1))                  \
+      return set_error(kInvalid, "tw_qs_cost_grad: invalid arguments");                        \
+    if (B && (!query || !support || !cost || !d_cost || !d_query || !d_support))              \
+      return set_error(kInvalid, "tw_qs_cost_grad: null pointer");                             \
+    return qs_grad<T>(query, support, cost, d_cost, B, R, U, D, metric, d_query, d_support,    \
+                      (cudaStream_t)stream);                                                     \
+  }                                                                                             \
+  int tw_fvm_softmin_##SUF(const T* cost, int B, int Kf, int TU, double gamma, T* temporal,    \
+                           void* stream) {                                                      \
+    g_err[0] = 0;                                                                               \
+    if (B < 0 || Kf <= 0 || TU <= 0 || !(gamma > 0))                                           \
+      return set_error(kInvalid, "tw_fvm_softmin: invalid arguments");                         \
+    return fvm_softmin<T>(cost, B, Kf, TU, gamma, temporal, (cudaStream_t)stream);             \
+  }                                                                                             \
+  int tw_fvm_softmin_backward_##SUF(const T* cost, const T* d_temporal, int B, int Kf, int TU, \
+                                    double gamma, T* d_cost, void* stream) {                    \
+    g_err[0] = 0;                                                                               \
+    if (B < 0 || Kf <= 0 || TU <= 0 || !(gamma > 0))                                           \
+      return set_error(kInvalid, "tw_fvm_softmin_backward: invalid arguments");                \
+    return fvm_softmin_bwd<T>(cost, d_temporal, B, Kf, TU, gamma, d_cost, (cudaStream_t)stream); \
+  }
+
+TW_JEANIE_ENTRIES(f32, float)
+TW_JEANIE_ENTRIES(f64, double)
+#undef TW_JEANIE_ENTRIES
+
+int tw_optimal_path_f64(const double* cost, int B, int K, int T, int U, int max_shift,
+                        int start_view, double* r_ws, int* back_ws, int* path, int* length,
+                        void* stream) {
+  g_err[0] = 0;
+  if (B < 0 || K <= 0 || T <= 0 || U <= 0 || max_shift < 0 || start_view >= K)
+    return set_error(kInvalid, "tw_optimal_path: invalid arguments");
+  if (B && (!cost || !r_ws || !back_ws || !path || !length))
+    return set_error(kInvalid, "tw_optimal_path: null pointer");
+  return optimal_path(cost, B, K, T, U, max_shift, start_view, r_ws, back_ws, path, length,
+                      (cudaStream_t)stream);
 }
 
 }  // extern "C"

@@ -1,0 +1,243 @@
+"""JEANIE, FVM and the query/support cost as torch custom operators over the C ABI.
+
+Mirrors the reference op layer (hibana2077/torchwarp src/torchwarp/jeanie/_ops.py:
+``dp``/``dp_backward`` :110-139, ``features``/``features_backward`` :155-230,
+autograd Functions :299-447) with native sm_100a kernels only:
+
+* ``torchwarp_b200::jeanie_dp(cost5, s1, s2, gamma)`` -> (out [B], R): the
+  DP on a [B, K1, K2, T, U] cost; R (natural layout) is both the saved state
+  and the differentiable accumulator.
+* ``torchwarp_b200::jeanie_dp_backward(cost5, R, grad_out, grad_R?, ...)``.
+* ``torchwarp_b200::qs_cost(query, support, metric)`` -> cost [B, R, U] and
+  its backward, the (squared) Euclidean query/support cost that replaces the
+  reference's bmm + relayout + fused kernel cost.
+* ``torchwarp_b200::fvm_softmin(cost, gamma)`` -> temporal [B, T, U] and its
+  backward (FVM's viewpoint soft-min).
+
+Each op has a fake implementation (torch.compile) and runs in float32 under
+autocast; the backward ops are first-order only.
+"""
+
+from typing import Optional, Tuple
+
+import torch
+from torch import Tensor
+
+from .. import _native as nat
+
+
+def _register_autocast(op):
+    for device in ("cuda", "cpu"):
+        torch.library.register_autocast(op, device, torch.float32)
+
+
+def _fn(name, dtype):
+    return getattr(nat.lib(), name + "_" + nat.suffix(dtype))
+
+
+# ------------------------------------------------------------ JEANIE DP
+
+@torch.library.custom_op("torchwarp_b200::jeanie_dp", mutates_args=())
+def jeanie_dp(cost: Tensor, s1: int, s2: int, gamma: float) -> Tuple[Tensor, Tensor]:
+    nat.require_cuda(cost)
+    B, K1, K2, T, U = cost.shape
+    cost = cost.contiguous()
+    out = cost.new_empty(B)
+    R = torch.empty_like(cost)
+    if B:
+        with torch.cuda.device(cost.device):
+            nat.check(nat.call("jeanie_forward", _fn("tw_jeanie_forward", cost.dtype),
+                               nat.ptr(cost), B, K1, K2, T, U, int(s1), int(s2), float(gamma),
+                               nat.ptr(out), nat.ptr(R), nat.stream_of(cost)), "tw_jeanie_forward")
+    return out, R
+
+
+@jeanie_dp.register_fake
+def _(cost, s1, s2, gamma):
+    return cost.new_empty(cost.shape[0]), torch.empty_like(cost)
+
+
+@torch.library.custom_op("torchwarp_b200::jeanie_dp_backward", mutates_args=())
+def jeanie_dp_backward(cost: Tensor, R: Tensor, grad_out: Tensor, grad_R: Optional[Tensor], s1: int,
+                       s2: int, gamma: float) -> Tensor:
+    nat.require_cuda(cost)
+    B, K1, K2, T, U = cost.shape
+    cost, R = cost.contiguous(), R.contiguous()
+    grad_out = grad_out.to(cost.dtype).contiguous()
+    gR = None if grad_R is None else grad_R.to(cost.dtype).contiguous()
+    d_cost = torch.empty_like(cost)
+    if B:
+        with torch.cuda.device(cost.device):
+            nat.check(nat.call("jeanie_backward", _fn("tw_jeanie_backward", cost.dtype),
+                               nat.ptr(cost), nat.ptr(R), nat.ptr(grad_out), nat.ptr(gR), B, K1,
+                               K2, T, U, int(s1), int(s2), float(gamma), nat.ptr(d_cost),
+                               nat.stream_of(cost)), "tw_jeanie_backward")
+    return d_cost
+
+
+@jeanie_dp_backward.register_fake
+def _(cost, R, grad_out, grad_R, s1, s2, gamma):
+    return torch.empty_like(cost)
+
+
+_register_autocast(jeanie_dp)
+_register_autocast(jeanie_dp_backward)
+
+
+class JeanieDP(torch.autograd.Function):
+    """cost5 -> (out, R); both differentiable."""
+
+    @staticmethod
+    def forward(cost, s1, s2, gamma):
+        return jeanie_dp(cost, s1, s2, gamma)
+
+    @staticmethod
+    def setup_context(ctx, inputs, output):
+        cost, s1, s2, gamma = inputs
+        ctx.set_materialize_grads(False)
+        ctx.save_for_backward(cost, output[1])
+        ctx.args = (s1, s2, gamma)
+
+    @staticmethod
+    @torch.autograd.function.once_differentiable
+    def backward(ctx, g_out, g_R):
+        cost, R = ctx.saved_tensors
+        s1, s2, gamma = ctx.args
+        if g_out is None:
+            g_out = cost.new_zeros(cost.shape[0])
+        return jeanie_dp_backward(cost, R, g_out, g_R, s1, s2, gamma), None, None, None
+
+
+# ------------------------------------------------------ query/support cost
+
+@torch.library.custom_op("torchwarp_b200::qs_cost", mutates_args=())
+def qs_cost(query: Tensor, support: Tensor, metric: int) -> Tensor:
+    nat.require_cuda(query, support)
+    B, Rr, D = query.shape
+    U = support.shape[1]
+    query, support = query.contiguous(), support.contiguous()
+    cost = query.new_empty(B, Rr, U)
+    if B and Rr and U:
+        with torch.cuda.device(query.device):
+            nat.check(nat.call("qs_cost", _fn("tw_qs_cost", query.dtype), nat.ptr(query),
+                               nat.ptr(support), B, Rr, U, D, int(metric), nat.ptr(cost),
+                               nat.stream_of(query)), "tw_qs_cost")
+    return cost
+
+
+@qs_cost.register_fake
+def _(query, support, metric):
+    return query.new_empty(query.shape[0], query.shape[1], support.shape[1])
+
+
+@torch.library.custom_op("torchwarp_b200::qs_cost_backward", mutates_args=())
+def qs_cost_backward(query: Tensor, support: Tensor, cost: Tensor, d_cost: Tensor,
+                     metric: int) -> Tuple[Tensor, Tensor]:
+    nat.require_cuda(query, support)
+    B, Rr, D = query.shape
+    U = support.shape[1]
+    query, support, cost = query.contiguous(), support.contiguous(), cost.contiguous()
+    d_cost = d_cost.to(query.dtype).contiguous()
+    dq, ds = torch.empty_like(query), torch.empty_like(support)
+    if B and Rr and U:
+        with torch.cuda.device(query.device):
+            nat.check(nat.call("qs_cost_grad", _fn("tw_qs_cost_grad", query.dtype),
+                               nat.ptr(query), nat.ptr(support), nat.ptr(cost), nat.ptr(d_cost),
+                               B, Rr, U, D, int(metric), nat.ptr(dq), nat.ptr(ds),
+                               nat.stream_of(query)), "tw_qs_cost_grad")
+    return dq, ds
+
+
+@qs_cost_backward.register_fake
+def _(query, support, cost, d_cost, metric):
+    return torch.empty_like(query), torch.empty_like(support)
+
+
+_register_autocast(qs_cost)
+_register_autocast(qs_cost_backward)
+
+
+class QSCost(torch.autograd.Function):
+    """(query [B,R,D], support [B,U,D]) -> cost [B,R,U]."""
+
+    @staticmethod
+    def forward(query, support, metric):
+        return qs_cost(query, support, metric)
+
+    @staticmethod
+    def setup_context(ctx, inputs, output):
+        query, support, metric = inputs
+        ctx.save_for_backward(query, support, output)
+        ctx.metric = metric
+
+    @staticmethod
+    @torch.autograd.function.once_differentiable
+    def backward(ctx, g):
+        query, support, cost = ctx.saved_tensors
+        dq, ds = qs_cost_backward(query, support, cost, g, ctx.metric)
+        return dq, ds, None
+
+
+# ------------------------------------------------------------ FVM soft-min
+
+@torch.library.custom_op("torchwarp_b200::fvm_softmin", mutates_args=())
+def fvm_softmin(cost: Tensor, gamma: float) -> Tensor:
+    nat.require_cuda(cost)
+    B, Kf, T, U = cost.shape
+    cost = cost.contiguous()
+    out = cost.new_empty(B, T, U)
+    if B:
+        with torch.cuda.device(cost.device):
+            nat.check(nat.call("fvm_softmin", _fn("tw_fvm_softmin", cost.dtype), nat.ptr(cost), B,
+                               Kf, T * U, float(gamma), nat.ptr(out), nat.stream_of(cost)),
+                      "tw_fvm_softmin")
+    return out
+
+
+@fvm_softmin.register_fake
+def _(cost, gamma):
+    return cost.new_empty(cost.shape[0], cost.shape[2], cost.shape[3])
+
+
+@torch.library.custom_op("torchwarp_b200::fvm_softmin_backward", mutates_args=())
+def fvm_softmin_backward(cost: Tensor, d_temporal: Tensor, gamma: float) -> Tensor:
+    nat.require_cuda(cost)
+    B, Kf, T, U = cost.shape
+    cost = cost.contiguous()
+    d_temporal = d_temporal.to(cost.dtype).contiguous()
+    d_cost = torch.empty_like(cost)
+    if B:
+        with torch.cuda.device(cost.device):
+            nat.check(nat.call("fvm_softmin_backward", _fn("tw_fvm_softmin_backward", cost.dtype),
+                               nat.ptr(cost), nat.ptr(d_temporal), B, Kf, T * U, float(gamma),
+                               nat.ptr(d_cost), nat.stream_of(cost)), "tw_fvm_softmin_backward")
+    return d_cost
+
+
+@fvm_softmin_backward.register_fake
+def _(cost, d_temporal, gamma):
+    return torch.empty_like(cost)
+
+
+_register_autocast(fvm_softmin)
+_register_autocast(fvm_softmin_backward)
+
+
+class FvmSoftmin(torch.autograd.Function):
+    """cost [B,Kf,T,U] -> temporal [B,T,U]."""
+
+    @staticmethod
+    def forward(cost, gamma):
+        return fvm_softmin(cost, gamma)
+
+    @staticmethod
+    def setup_context(ctx, inputs, output):
+        cost, gamma = inputs
+        ctx.save_for_backward(cost)
+        ctx.gamma = gamma
+
+    @staticmethod
+    @torch.autograd.function.once_differentiable
+    def backward(ctx, g):
+        (cost,) = ctx.saved_tensors
+        return fvm_softmin_backward(cost, g, ctx.gamma), None
