@@ -50,6 +50,11 @@ extern "C" {
 int tw_version(void);
 /* Message of the last error on this host thread ("" if none). */
 const char* tw_last_error(void);
+/* Reads and clears the device-side error word of the tensor-core kernels
+ * (0: none; TW_ERR_TIMEOUT: a bounded pipeline wait ran out; TW_ERR_LAUNCH:
+ * unaligned shared memory).  Synchronises with the device.  No counterpart
+ * in the reference, whose kernels have no device-side waits. */
+int tw_device_error(void);
 
 /* ---------------------------------------------------------------------
  * Soft-min DP on a precomputed cost (soft-DTW / uDTW), natural layout.
@@ -104,7 +109,11 @@ int tw_sdtw_backward_f64(const double* grad_r, const double* grad_p, int B, int 
  *   var_ij = max(0.5 (vx_i + vy_j), eps)
  *   cost_ij = sq_ij / var_ij,  penalty_ij = beta * log(var_ij)
  * X [B,N,D], Y [B,M,D], vx [B,N], vy [B,M] (vx/vy NULL: variance 1, no penalty).
- * cost, penalty: [B,N,M] outputs (penalty may be NULL). */
+ * cost, penalty: [B,N,M] outputs (penalty may be NULL).
+ * fp32 with D >= 64, D and M multiples of 4 and 16-byte aligned pointers runs
+ * the x.y contraction on tcgen05 tensor cores (3xTF32, fp32 accumulate);
+ * other shapes, and fp64, use SIMT kernels.  Setting the environment
+ * variable TW_COST_SIMT=1 forces the SIMT kernels (for testing). */
 int tw_udtw_cost_f32(const float* X, const float* Y, const float* vx, const float* vy, int B,
                      int N, int M, int D, double beta, double eps, float* cost, float* penalty,
                      void* stream);

@@ -22,6 +22,7 @@ _c_sz = ctypes.c_size_t
 SIGNATURES = {
     "tw_version": (_c_i, []),
     "tw_last_error": (ctypes.c_char_p, []),
+    "tw_device_error": (_c_i, []),
     "tw_sdtw_saved_bytes": (_c_sz, [_c_i, _c_i, _c_i, _c_i, _c_i]),
     "tw_sdtw_workspace_bytes": (_c_sz, [_c_i, _c_i, _c_i, _c_i, _c_i]),
     "tw_sdtw_forward_f32": (_c_i, [_c_p, _c_p, _c_i, _c_i, _c_i, _c_d, _c_d, _c_p, _c_p, _c_p,

@@ -131,6 +131,7 @@ static int sdtw_bwd(const T* grad_r, const T* grad_p, int B, int N, int M, doubl
 template int sdtw_fwd<float>(const float*, const float*, int, int, int, double, double, float*,
                              float*, void*, size_t, void*, size_t, cudaStream_t);
 
+int tc_take_device_error();
 int udtw_cost_f32(const float*, const float*, const float*, const float*, int, int, int, int,
                   double, double, float*, float*, cudaStream_t);
 int udtw_cost_f64(const double*, const double*, const double*, const double*, int, int, int, int,
@@ -175,6 +176,11 @@ extern "C" {
 int tw_version(void) { return 100; }
 
 const char* tw_last_error(void) { return g_err; }
+
+int tw_device_error(void) {
+  if (cudaDeviceSynchronize() != cudaSuccess) return set_error(kLaunch, "device synchronize failed");
+  return tc_take_device_error();
+}
 
 size_t tw_sdtw_saved_bytes(int B, int N, int M, int dtype_bytes, int has_penalty) {
   if (!dims_ok(B, N, M) || B == 0 || (dtype_bytes != 4 && dtype_bytes != 8)) return 0;

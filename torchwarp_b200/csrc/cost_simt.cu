@@ -11,6 +11,7 @@
 //   dvx = 0.5 rowsum(dvar), dvy = 0.5 colsum(dvar)
 // One CTA owns a 64 x 64 tile of (i, j) cells (cost) or a 64-row / 64-column
 // strip (gradients); no atomics, so every result is bitwise reproducible.
+// fp32 with D >= 64 goes to the tensor-core kernels of tc_gemm.cu instead.
 #include "common.cuh"
 
 namespace tw {
@@ -203,8 +204,21 @@ int grad_launch(const T* X, const T* Y, const T* vx, const T* vy, const T* C, co
 
 }  // namespace
 
+// Tensor-core forms (tc_gemm.cu), used for fp32 when they apply.
+bool tc_cost_eligible(const float* X, const float* Y, const float* vx, const float* vy, int N,
+                      int M, int D, const float* C, const float* Q);
+int tc_cost_f32(const float* X, const float* Y, const float* vx, const float* vy, int B, int N,
+                int M, int D, double beta, double eps, float* C, float* Q, cudaStream_t st);
+bool tc_grad_eligible(const float* X, const float* Y, const float* C, const float* dC,
+                      const float* dQ, const float* dX, const float* dY, int M, int D);
+int tc_grad_f32(const float* X, const float* Y, const float* vx, const float* vy, const float* C,
+                const float* dC, const float* dQ, int B, int N, int M, int D, double beta,
+                double eps, float* dX, float* dY, float* dvx, float* dvy, cudaStream_t st);
+
 int udtw_cost_f32(const float* X, const float* Y, const float* vx, const float* vy, int B, int N,
                   int M, int D, double beta, double eps, float* C, float* Q, cudaStream_t st) {
+  if (tc_cost_eligible(X, Y, vx, vy, N, M, D, C, Q))
+    return tc_cost_f32(X, Y, vx, vy, B, N, M, D, beta, eps, C, Q, st);
   return cost_launch(X, Y, vx, vy, B, N, M, D, beta, eps, C, Q, st);
 }
 int udtw_cost_f64(const double* X, const double* Y, const double* vx, const double* vy, int B,
@@ -215,6 +229,8 @@ int udtw_cost_f64(const double* X, const double* Y, const double* vx, const doub
 int udtw_grad_f32(const float* X, const float* Y, const float* vx, const float* vy, const float* C,
                   const float* dC, const float* dQ, int B, int N, int M, int D, double beta,
                   double eps, float* dX, float* dY, float* dvx, float* dvy, cudaStream_t st) {
+  if (tc_grad_eligible(X, Y, C, dC, dQ, dX, dY, M, D))
+    return tc_grad_f32(X, Y, vx, vy, C, dC, dQ, B, N, M, D, beta, eps, dX, dY, dvx, dvy, st);
   return grad_launch(X, Y, vx, vy, C, dC, dQ, B, N, M, D, beta, eps, dX, dY, dvx, dvy, st);
 }
 int udtw_grad_f64(const double* X, const double* Y, const double* vx, const double* vy,

@@ -1,0 +1,817 @@
+// Tensor-core (tcgen05, 3xTF32, fp32 accumulate in TMEM) forms of the
+// pairwise cost and of its feature chain rule, for fp32 features with
+// D >= 64 (the contraction is then worth a tensor core; smaller D stays on
+// the SIMT kernels of cost_simt.cu).
+//
+// Cost (hibana2077/torchwarp src/torchwarp/csrc/udtw_cuda.cu:379-387,
+// src/torchwarp/udtw/_autograd.py:24-29, jeanie/distances.py:15-27):
+//   G = X Y^T on tensor cores, sq = max(|x_i|^2 + |y_j|^2 - 2 G_ij, 0),
+//   var = max(0.5 (vx_i + vy_j), eps), C = sq / var, Q = beta log(var).
+//
+// Each CTA is persistent (one per SM) and walks output tiles of 128 x 128
+// cells.  Warp roles:
+//   warps 0-3  epilogue: TMEM -> registers -> cost -> swizzled smem -> TMA store
+//   warps 4-7  split:    fp32 tile -> (hi, lo) TF32 pair in place, row norms
+//   warp  8    TMA producer of the X / Y feature chunks (32 features each)
+//   warp  9    MMA issuer: hi*hi + hi*lo + lo*hi per 8-feature step
+// Two TMEM accumulators (2 x 128 columns) let the epilogue of one tile
+// overlap the MMAs of the next.  No atomics: results are reproducible.
+#include <cstdlib>
+#include <mutex>
+
+#include "tc_common.cuh"
+
+namespace tw {
+
+namespace {
+
+__device__ int g_tc_error;
+
+using namespace tc;
+
+constexpr int BM = 128;            // rows (i) per tile
+constexpr int BN = 128;            // columns (j) per tile
+constexpr int KC = 32;             // features per chunk: one 128-byte swizzle line
+constexpr int STAGES = 3;
+constexpr int TILE_A = BM * KC * 4;                       // 16 KB
+constexpr int TILE_B = BN * KC * 4;                       // 16 KB
+constexpr int STAGE_BYTES = 2 * TILE_A + 2 * TILE_B;      // hi and lo of A and B
+constexpr int STG_BYTES = BM * 32 * 4;                    // one 128 x 32 output chunk
+constexpr int COST_THREADS = 320;
+constexpr uint32_t COST_TMEM_COLS = 2 * BN;
+
+struct CostShared {
+  float x2[2][BM];
+  float y2[2][BN];
+  uint64_t full[STAGES], empty[STAGES], conv[STAGES];
+  uint64_t accf[2], acce[2], nfull[2], nempty[2];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort;
+};
+
+constexpr size_t COST_SMEM = (size_t)STAGES * STAGE_BYTES + 2 * STG_BYTES + sizeof(CostShared);
+
+__device__ __forceinline__ void record_timeout(volatile int* abort) {
+  *abort = 1;
+  atomicExch(&g_tc_error, kTimeout);
+}
+
+struct TileCoord {
+  int b, ib, jb;
+};
+
+__device__ __forceinline__ TileCoord tile_of(int t, int nI, int nJ) {
+  const int per = nI * nJ;
+  TileCoord c;
+  c.b = t / per;
+  const int r = t - c.b * per;
+  c.ib = r / nJ;
+  c.jb = r - c.ib * nJ;
+  return c;
+}
+
+// Splits one 128-byte line (32 fp32) of a swizzled box in place into its
+// TF32 hi part, writing the lo part at the same offset of `lo_base`.
+// Returns the sum of squares of the original values.
+__device__ __forceinline__ float split_line(uint8_t* hi_base, uint8_t* lo_base, int line) {
+  float ss = 0.f;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const uint32_t off = sw128_chunk(line, q);
+    float4 v = *reinterpret_cast<float4*>(hi_base + off);
+    ss = fmaf(v.x, v.x, ss);
+    ss = fmaf(v.y, v.y, ss);
+    ss = fmaf(v.z, v.z, ss);
+    ss = fmaf(v.w, v.w, ss);
+    float4 h, l;
+    split_tf32(v.x, h.x, l.x);
+    split_tf32(v.y, h.y, l.y);
+    split_tf32(v.z, h.z, l.z);
+    split_tf32(v.w, h.w, l.w);
+    *reinterpret_cast<float4*>(hi_base + off) = h;
+    *reinterpret_cast<float4*>(lo_base + off) = l;
+  }
+  return ss;
+}
+
+template <bool VAR>
+__global__ void __launch_bounds__(COST_THREADS, 1)
+    tc_cost_kernel(const __grid_constant__ CUtensorMap mapX, const __grid_constant__ CUtensorMap mapY,
+                   const __grid_constant__ CUtensorMap mapC, const __grid_constant__ CUtensorMap mapQ,
+                   const float* __restrict__ vx, const float* __restrict__ vy, int B, int N, int M,
+                   int D, float beta, float eps, int write_q) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint8_t* stage_base = smem;
+  uint8_t* stg_base = smem + (size_t)STAGES * STAGE_BYTES;
+  CostShared& sh = *reinterpret_cast<CostShared*>(stg_base + 2 * STG_BYTES);
+  volatile int* abort = &sh.abort;
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int nI = (N + BM - 1) / BM, nJ = (M + BN - 1) / BN, nK = (D + KC - 1) / KC;
+  const int total = B * nI * nJ;
+
+  if (tid == 0) {
+    if ((smem_u32(smem) & 1023u) != 0) {
+      atomicExch(&g_tc_error, kLaunch);
+      sh.abort = 1;
+    } else {
+      sh.abort = 0;
+    }
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&sh.full[s], 1);
+      mbar_init(&sh.empty[s], 1);
+      mbar_init(&sh.conv[s], 128);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&sh.accf[a], 1);
+      mbar_init(&sh.acce[a], 128);
+      mbar_init(&sh.nfull[a], 128);
+      mbar_init(&sh.nempty[a], 128);
+    }
+    mbar_init(&sh.mma_done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 8 && lane == 0) {
+    prefetch_map(&mapX);
+    prefetch_map(&mapY);
+    prefetch_map(&mapC);
+    if (VAR) prefetch_map(&mapQ);
+  }
+  if (warp == 9) tmem_alloc(&sh.tmem_base, COST_TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh.tmem_base;
+  const bool dead = sh.abort != 0;
+
+  if (!dead && warp == 8 && lane == 0) {
+    // ------------------------------------------------ TMA producer
+    int it = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      const TileCoord c = tile_of(t, nI, nJ);
+      for (int kc = 0; kc < nK; ++kc, ++it) {
+        const int s = it % STAGES;
+        const unsigned ph = (unsigned)(it / STAGES) & 1u;
+        if (!mbar_wait(&sh.empty[s], ph ^ 1u, abort)) { record_timeout(abort); goto producer_drain; }
+        uint8_t* st = stage_base + (size_t)s * STAGE_BYTES;
+        mbar_arrive_expect_tx(&sh.full[s], TILE_A + TILE_B);
+        tma_load_3d(st, &mapX, &sh.full[s], kc * KC, c.ib * BM, c.b);
+        tma_load_3d(st + 2 * TILE_A, &mapY, &sh.full[s], kc * KC, c.jb * BN, c.b);
+      }
+    }
+  producer_drain:
+    // every load issued lands before the CTA exits
+    for (int k = (it > STAGES ? it - STAGES : 0); k < it; ++k) {
+      const int s = k % STAGES;
+      for (unsigned n = 0; n < kSpinLimit; ++n)
+        if (mbar_try_wait(&sh.full[s], (unsigned)(k / STAGES) & 1u)) break;
+    }
+  } else if (!dead && warp >= 4 && warp < 8) {
+    // ------------------------------------------------ TF32 split + norms
+    const int ct = tid - 128;
+    int it = 0, ti = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++ti) {
+      float sa = 0.f, sb = 0.f;
+      for (int kc = 0; kc < nK; ++kc, ++it) {
+        const int s = it % STAGES;
+        const unsigned ph = (unsigned)(it / STAGES) & 1u;
+        if (!mbar_wait(&sh.full[s], ph, abort)) { record_timeout(abort); goto split_done; }
+        uint8_t* st = stage_base + (size_t)s * STAGE_BYTES;
+        sa += split_line(st, st + TILE_A, ct);
+        sb += split_line(st + 2 * TILE_A, st + 2 * TILE_A + TILE_B, ct);
+        fence_async_smem();
+        mbar_arrive(&sh.conv[s]);
+      }
+      const int a = ti & 1;
+      if (!mbar_wait(&sh.nempty[a], ((unsigned)(ti >> 1) & 1u) ^ 1u, abort)) {
+        record_timeout(abort);
+        goto split_done;
+      }
+      sh.x2[a][ct] = sa;
+      sh.y2[a][ct] = sb;
+      mbar_arrive(&sh.nfull[a]);
+    }
+  split_done:;
+  } else if (!dead && warp == 9) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t IDESC = idesc_tf32(BM, BN, 0, 0);
+      int it = 0, ti = 0;
+      for (int t = blockIdx.x; t < total; t += gridDim.x, ++ti) {
+        const int a = ti & 1;
+        if (!mbar_wait(&sh.acce[a], ((unsigned)(ti >> 1) & 1u) ^ 1u, abort)) {
+          record_timeout(abort);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + (uint32_t)(a * BN);
+        bool ok = true;
+        for (int kc = 0; kc < nK; ++kc, ++it) {
+          const int s = it % STAGES;
+          const unsigned ph = (unsigned)(it / STAGES) & 1u;
+          if (!mbar_wait(&sh.conv[s], ph, abort)) { record_timeout(abort); ok = false; break; }
+          tc_fence_after();
+          const uint32_t ah = smem_u32(stage_base + (size_t)s * STAGE_BYTES);
+          const uint32_t al = ah + TILE_A, bh = ah + 2 * TILE_A, bl = bh + TILE_B;
+#pragma unroll
+          for (int kk = 0; kk < KC / 8; ++kk) {
+            const uint64_t dah = smem_desc_sw128(ah + kk * 32, 16, 1024);
+            const uint64_t dal = smem_desc_sw128(al + kk * 32, 16, 1024);
+            const uint64_t dbh = smem_desc_sw128(bh + kk * 32, 16, 1024);
+            const uint64_t dbl = smem_desc_sw128(bl + kk * 32, 16, 1024);
+            mma_tf32(d_tmem, dal, dbh, IDESC, (kc | kk) != 0);
+            mma_tf32(d_tmem, dah, dbl, IDESC, 1);
+            mma_tf32(d_tmem, dah, dbh, IDESC, 1);
+          }
+          mma_commit(&sh.empty[s]);
+        }
+        if (!ok) break;
+        mma_commit(&sh.accf[a]);
+      }
+      // every MMA issued has finished before TMEM is released
+      mma_commit(&sh.mma_done);
+      for (unsigned n = 0; n < kSpinLimit; ++n)
+        if (mbar_try_wait(&sh.mma_done, 0)) break;
+    }
+    __syncwarp();
+  } else if (!dead && warp < 4) {
+    // ------------------------------------------------ epilogue
+    const int row = tid;  // TMEM lane == tile row
+    int ti = 0, si = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++ti) {
+      const TileCoord c = tile_of(t, nI, nJ);
+      const int a = ti & 1;
+      const unsigned ph = (unsigned)(ti >> 1) & 1u;
+      const bool ok = mbar_wait(&sh.accf[a], ph, abort) && mbar_wait(&sh.nfull[a], ph, abort);
+      if (!ok) record_timeout(abort);
+      if (named_bar_or(1, 128, !ok)) break;  // the four warps stop together
+      tc_fence_after();
+      const int i = c.ib * BM + row;
+      const float x2 = sh.x2[a][row];
+      float vxi = 0.f;
+      if (VAR) vxi = i < N ? vx[(long long)c.b * N + i] : 1.f;
+#pragma unroll 1
+      for (int cc = 0; cc < BN / 32; ++cc) {
+        float v[32];
+        tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(a * BN + 32 * cc), v);
+        if (cc == BN / 32 - 1) {
+          tc_fence_before();
+          mbar_arrive(&sh.acce[a]);
+        }
+        const int j0 = c.jb * BN + 32 * cc;
+        float qv[32];
+#pragma unroll
+        for (int q = 0; q < 32; ++q) {
+          float sq = (x2 + sh.y2[a][32 * cc + q]) - 2.f * v[q];
+          sq = sq > 0.f ? sq : 0.f;
+          if (VAR) {
+            const int j = j0 + q;
+            const float vyj = j < M ? vy[(long long)c.b * M + j] : 1.f;
+            float var = 0.5f * (vxi + vyj);
+            var = var > eps ? var : eps;
+            v[q] = sq / var;
+            qv[q] = beta * logf(var);
+          } else {
+            v[q] = sq;
+          }
+        }
+        if (cc == BN / 32 - 1) mbar_arrive(&sh.nempty[a]);
+        // C chunk (and Q chunk) through the two staging buffers
+#pragma unroll
+        for (int which = 0; which < (VAR ? 2 : 1); ++which) {
+          if (which == 1 && !write_q) break;
+          uint8_t* buf = stg_base + (size_t)(si & 1) * STG_BYTES;
+          if (row == 0) bulk_wait_read<1>();
+          named_bar(1, 128);
+          const float* src = which == 0 ? v : qv;
+#pragma unroll
+          for (int q4 = 0; q4 < 8; ++q4)
+            *reinterpret_cast<float4*>(buf + sw128_chunk(row, q4)) =
+                make_float4(src[4 * q4], src[4 * q4 + 1], src[4 * q4 + 2], src[4 * q4 + 3]);
+          fence_async_smem();
+          named_bar(1, 128);
+          if (row == 0) {
+            tma_store_3d(which == 0 ? &mapC : &mapQ, buf, j0, c.ib * BM, c.b);
+            bulk_commit();
+          }
+          ++si;
+        }
+      }
+    }
+    if (row == 0) bulk_wait_all();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 9) tmem_dealloc(tmem, COST_TMEM_COLS);
+}
+
+// ----------------------------------------------------------------------
+// Chain rule of the cost on tensor cores (udtw_cuda.cu:557-568,
+// udtw/_ops.py:179-183):
+//   S = dsq = dC / var where C > 0 (else 0)
+//   dX = -2 S Y + 2 X rowsum(S)        (SIDE 0: unit = 128 rows i of a pair,
+//                                        K = j in chunks of 32)
+//   dY = -2 S^T X + 2 Y colsum(S)      (SIDE 1: unit = 128 rows j of a pair,
+//                                        K = i in chunks of 32)
+//   dvx = 0.5 rowsum(dvar), dvy = 0.5 colsum(dvar),
+//   dvar = (beta dQ - dC C) / var where var_raw > eps.
+// The split warps turn each 32-wide chunk of (dC, C[, dQ]) into S in place
+// (hi over dC, lo over C) and accumulate the row (column) sums of S and
+// dvar in registers; the MMA contracts S (K-major for SIDE 0, MN-major for
+// SIDE 1) with the other side's features (MN-major) into a 128 x BD TMEM
+// accumulator; the epilogue adds 2 A rowsum and stores through TMA.
+// MN-major TF32 operands are only valid in the 32-byte-granule swizzle
+// (a standard 128-byte-swizzle MN-major descriptor yields no product), so
+// those boxes are loaded with that swizzle.
+
+constexpr int GRAD_THREADS = 320;
+constexpr int GRAD_MAX_STAGES = 4;
+constexpr int SBOX = 128 * 32 * 4;  // one 16 KB slice of dC / C / dQ per stage
+
+struct GradShared {
+  float rs[2][128];
+  uint64_t full[GRAD_MAX_STAGES], empty[GRAD_MAX_STAGES], conv[GRAD_MAX_STAGES];
+  uint64_t accf[2], acce[2], nfull[2], nempty[2];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort;
+};
+
+struct GradGeom {
+  int nF;           // 32-feature boxes (BD = 32 nF)
+  int stages;
+  int off_dq, off_fh, off_fl, stage_bytes, tx_bytes;
+  uint32_t tmem_cols;
+};
+
+template <int SIDE, bool VAR>
+__global__ void __launch_bounds__(GRAD_THREADS, 1)
+    tc_grad_kernel(const __grid_constant__ CUtensorMap mapDC, const __grid_constant__ CUtensorMap mapC,
+                   const __grid_constant__ CUtensorMap mapDQ, const __grid_constant__ CUtensorMap mapF,
+                   const __grid_constant__ CUtensorMap mapOut, const float* __restrict__ A,
+                   const float* __restrict__ va, const float* __restrict__ vb,
+                   float* __restrict__ dva, int B, int N, int M, int D, float beta, float eps,
+                   int has_dq, GradGeom g) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint8_t* stage_base = smem;
+  uint8_t* stg_base = smem + (size_t)g.stages * g.stage_bytes;
+  GradShared& sh = *reinterpret_cast<GradShared*>(stg_base + 2 * STG_BYTES);
+  volatile int* abort = &sh.abort;
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int R = SIDE == 0 ? N : M;   // rows of the gradient (own side)
+  const int S = SIDE == 0 ? M : N;   // summed extent
+  const int nBlk = (R + 127) / 128, nK = (S + 31) / 32;
+  const int total = B * nBlk;
+  const int BD = 32 * g.nF;
+  const int stages = g.stages;
+
+  if (tid == 0) {
+    if ((smem_u32(smem) & 1023u) != 0) {
+      atomicExch(&g_tc_error, kLaunch);
+      sh.abort = 1;
+    } else {
+      sh.abort = 0;
+    }
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&sh.full[s], 1);
+      mbar_init(&sh.empty[s], 1);
+      mbar_init(&sh.conv[s], 128);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&sh.accf[a], 1);
+      mbar_init(&sh.acce[a], 128);
+      mbar_init(&sh.nfull[a], 128);
+      mbar_init(&sh.nempty[a], 128);
+    }
+    mbar_init(&sh.mma_done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 8 && lane == 0) {
+    prefetch_map(&mapDC);
+    prefetch_map(&mapC);
+    if (VAR && has_dq) prefetch_map(&mapDQ);
+    prefetch_map(&mapF);
+    prefetch_map(&mapOut);
+  }
+  if (warp == 9) tmem_alloc(&sh.tmem_base, g.tmem_cols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh.tmem_base;
+  const bool dead = sh.abort != 0;
+
+  if (!dead && warp == 8 && lane == 0) {
+    // ------------------------------------------------ TMA producer
+    int it = 0;
+    for (int u = blockIdx.x; u < total; u += gridDim.x) {
+      const int b = u / nBlk, blk = u - b * nBlk;
+      for (int kc = 0; kc < nK; ++kc, ++it) {
+        const int s = it % stages;
+        const unsigned ph = (unsigned)(it / stages) & 1u;
+        if (!mbar_wait(&sh.empty[s], ph ^ 1u, abort)) { record_timeout(abort); goto producer_drain; }
+        uint8_t* st = stage_base + (size_t)s * g.stage_bytes;
+        mbar_arrive_expect_tx(&sh.full[s], g.tx_bytes);
+        if (SIDE == 0) {
+          // S slice: 128 rows i x 32 columns j
+          tma_load_3d(st, &mapDC, &sh.full[s], kc * 32, blk * 128, b);
+          tma_load_3d(st + SBOX, &mapC, &sh.full[s], kc * 32, blk * 128, b);
+          if (VAR && has_dq) tma_load_3d(st + g.off_dq, &mapDQ, &sh.full[s], kc * 32, blk * 128, b);
+        } else {
+          // S slice: 32 rows i x 128 columns j, as four 32 x 32 boxes
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            tma_load_3d(st + q * 4096, &mapDC, &sh.full[s], blk * 128 + 32 * q, kc * 32, b);
+            tma_load_3d(st + SBOX + q * 4096, &mapC, &sh.full[s], blk * 128 + 32 * q, kc * 32, b);
+            if (VAR && has_dq)
+              tma_load_3d(st + g.off_dq + q * 4096, &mapDQ, &sh.full[s], blk * 128 + 32 * q,
+                          kc * 32, b);
+          }
+        }
+        // the other side's features: 32 summed rows x BD features
+        for (int f = 0; f < g.nF; ++f)
+          tma_load_3d(st + g.off_fh + f * 4096, &mapF, &sh.full[s], 32 * f, kc * 32, b);
+      }
+    }
+  producer_drain:
+    for (int k = (it > stages ? it - stages : 0); k < it; ++k) {
+      const int s = k % stages;
+      for (unsigned n = 0; n < kSpinLimit; ++n)
+        if (mbar_try_wait(&sh.full[s], (unsigned)(k / stages) & 1u)) break;
+    }
+  } else if (!dead && warp >= 4 && warp < 8) {
+    // ------------------------------------------------ S = dsq, split, sums
+    const int ct = tid - 128;
+    int it = 0, ti = 0;
+    for (int u = blockIdx.x; u < total; u += gridDim.x, ++ti) {
+      const int b = u / nBlk, blk = u - b * nBlk;
+      const int r = blk * 128 + ct;  // own row (i for SIDE 0, j for SIDE 1)
+      const float va_r = VAR ? (r < R ? va[(long long)b * R + r] : 1.f) : 0.f;
+      const float* vb_b = VAR ? vb + (long long)b * S : nullptr;
+      float rsum = 0.f, vsum = 0.f;
+      for (int kc = 0; kc < nK; ++kc, ++it) {
+        const int s = it % stages;
+        const unsigned ph = (unsigned)(it / stages) & 1u;
+        if (!mbar_wait(&sh.full[s], ph, abort)) { record_timeout(abort); goto split_done; }
+        uint8_t* st = stage_base + (size_t)s * g.stage_bytes;
+        uint8_t* dcb = st;
+        uint8_t* cb = st + SBOX;
+        uint8_t* dqb = st + g.off_dq;
+        if (SIDE == 0) {
+#pragma unroll 2
+          for (int q = 0; q < 8; ++q) {
+            const uint32_t off = sw128_chunk(ct, q);
+            const float4 g4 = *reinterpret_cast<const float4*>(dcb + off);
+            const float4 c4 = *reinterpret_cast<const float4*>(cb + off);
+            float4 q4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (VAR && has_dq) q4 = *reinterpret_cast<const float4*>(dqb + off);
+            const float ge[4] = {g4.x, g4.y, g4.z, g4.w}, ce[4] = {c4.x, c4.y, c4.z, c4.w},
+                        qe[4] = {q4.x, q4.y, q4.z, q4.w};
+            float he[4], le[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              float var = 1.f, var_raw = 1.f;
+              if (VAR) {
+                const int j = kc * 32 + 4 * q + e;
+                var_raw = 0.5f * (va_r + (j < S ? __ldg(vb_b + j) : 1.f));
+                var = var_raw > eps ? var_raw : eps;
+              }
+              const float sv = ce[e] > 0.f ? (VAR ? ge[e] / var : ge[e]) : 0.f;
+              rsum += sv;
+              if (VAR && var_raw > eps) vsum += (beta * qe[e] - ge[e] * ce[e]) / var;
+              split_tf32(sv, he[e], le[e]);
+            }
+            *reinterpret_cast<float4*>(dcb + off) = make_float4(he[0], he[1], he[2], he[3]);
+            *reinterpret_cast<float4*>(cb + off) = make_float4(le[0], le[1], le[2], le[3]);
+          }
+        } else {
+          const int box = ct >> 5, w = ct & 31;
+#pragma unroll 4
+          for (int rr = 0; rr < 32; ++rr) {
+            const uint32_t off = box * 4096 + sw128b32_elem(rr, w);
+            const float gv = *reinterpret_cast<const float*>(dcb + off);
+            const float cv = *reinterpret_cast<const float*>(cb + off);
+            const float qv = (VAR && has_dq) ? *reinterpret_cast<const float*>(dqb + off) : 0.f;
+            float var = 1.f, var_raw = 1.f;
+            if (VAR) {
+              const int i = kc * 32 + rr;
+              var_raw = 0.5f * ((i < S ? __ldg(vb_b + i) : 1.f) + va_r);
+              var = var_raw > eps ? var_raw : eps;
+            }
+            const float sv = cv > 0.f ? (VAR ? gv / var : gv) : 0.f;
+            rsum += sv;
+            if (VAR && var_raw > eps) vsum += (beta * qv - gv * cv) / var;
+            float h, l;
+            split_tf32(sv, h, l);
+            *reinterpret_cast<float*>(dcb + off) = h;
+            *reinterpret_cast<float*>(cb + off) = l;
+          }
+        }
+        // the other side's features: elementwise split of the whole slab
+        {
+          float4* fh = reinterpret_cast<float4*>(st + g.off_fh);
+          float4* fl = reinterpret_cast<float4*>(st + g.off_fl);
+          const int n4 = g.nF * 256;
+          for (int k = ct; k < n4; k += 128) {
+            const float4 v = fh[k];
+            float4 h, l;
+            split_tf32(v.x, h.x, l.x);
+            split_tf32(v.y, h.y, l.y);
+            split_tf32(v.z, h.z, l.z);
+            split_tf32(v.w, h.w, l.w);
+            fh[k] = h;
+            fl[k] = l;
+          }
+        }
+        fence_async_smem();
+        mbar_arrive(&sh.conv[s]);
+      }
+      if (VAR && dva != nullptr && r < R) dva[(long long)b * R + r] = 0.5f * vsum;
+      const int a = ti & 1;
+      if (!mbar_wait(&sh.nempty[a], ((unsigned)(ti >> 1) & 1u) ^ 1u, abort)) {
+        record_timeout(abort);
+        goto split_done;
+      }
+      sh.rs[a][ct] = rsum;
+      mbar_arrive(&sh.nfull[a]);
+    }
+  split_done:;
+  } else if (!dead && warp == 9) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_tf32(128, BD, SIDE == 1 ? 1 : 0, 1);
+      int it = 0, ti = 0;
+      for (int u = blockIdx.x; u < total; u += gridDim.x, ++ti) {
+        const int a = ti & 1;
+        if (!mbar_wait(&sh.acce[a], ((unsigned)(ti >> 1) & 1u) ^ 1u, abort)) {
+          record_timeout(abort);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + (uint32_t)(a * BD);
+        bool ok = true;
+        for (int kc = 0; kc < nK; ++kc, ++it) {
+          const int s = it % stages;
+          const unsigned ph = (unsigned)(it / stages) & 1u;
+          if (!mbar_wait(&sh.conv[s], ph, abort)) { record_timeout(abort); ok = false; break; }
+          tc_fence_after();
+          const uint32_t st = smem_u32(stage_base + (size_t)s * g.stage_bytes);
+          const uint32_t ah = st, al = st + SBOX, fh = st + g.off_fh, fl = st + g.off_fl;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            uint64_t dah, dal;
+            if (SIDE == 0) {
+              dah = smem_desc_sw128(ah + kk * 32, 16, 1024);
+              dal = smem_desc_sw128(al + kk * 32, 16, 1024);
+            } else {
+              dah = smem_desc(ah + kk * 1024, 4096, 512, kLayoutSW128Base32);
+              dal = smem_desc(al + kk * 1024, 4096, 512, kLayoutSW128Base32);
+            }
+            const uint64_t dbh = smem_desc(fh + kk * 1024, 4096, 512, kLayoutSW128Base32);
+            const uint64_t dbl = smem_desc(fl + kk * 1024, 4096, 512, kLayoutSW128Base32);
+            mma_tf32(d_tmem, dal, dbh, idesc, (kc | kk) != 0);
+            mma_tf32(d_tmem, dah, dbl, idesc, 1);
+            mma_tf32(d_tmem, dah, dbh, idesc, 1);
+          }
+          mma_commit(&sh.empty[s]);
+        }
+        if (!ok) break;
+        mma_commit(&sh.accf[a]);
+      }
+      mma_commit(&sh.mma_done);
+      for (unsigned n = 0; n < kSpinLimit; ++n)
+        if (mbar_try_wait(&sh.mma_done, 0)) break;
+    }
+    __syncwarp();
+  } else if (!dead && warp < 4) {
+    // ------------------------------------------------ epilogue
+    int ti = 0, si = 0;
+    for (int u = blockIdx.x; u < total; u += gridDim.x, ++ti) {
+      const int b = u / nBlk, blk = u - b * nBlk;
+      const int a = ti & 1;
+      const unsigned ph = (unsigned)(ti >> 1) & 1u;
+      const bool ok = mbar_wait(&sh.accf[a], ph, abort) && mbar_wait(&sh.nfull[a], ph, abort);
+      if (!ok) record_timeout(abort);
+      if (named_bar_or(1, 128, !ok)) break;
+      tc_fence_after();
+      const int r = blk * 128 + tid;
+      const float rs2 = 2.f * sh.rs[a][tid];
+      const float* Ar = A + ((long long)b * R + (r < R ? r : 0)) * D;
+#pragma unroll 1
+      for (int cc = 0; cc < g.nF; ++cc) {
+        float v[32];
+        tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(a * BD + 32 * cc), v);
+        if (cc == g.nF - 1) {
+          tc_fence_before();
+          mbar_arrive(&sh.acce[a]);
+          mbar_arrive(&sh.nempty[a]);
+        }
+#pragma unroll
+        for (int q4 = 0; q4 < 8; ++q4) {
+          const int d = 32 * cc + 4 * q4;
+          float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (r < R && d < D) x = __ldg(reinterpret_cast<const float4*>(Ar + d));
+          v[4 * q4] = -2.f * v[4 * q4] + x.x * rs2;
+          v[4 * q4 + 1] = -2.f * v[4 * q4 + 1] + x.y * rs2;
+          v[4 * q4 + 2] = -2.f * v[4 * q4 + 2] + x.z * rs2;
+          v[4 * q4 + 3] = -2.f * v[4 * q4 + 3] + x.w * rs2;
+        }
+        uint8_t* buf = stg_base + (size_t)(si & 1) * STG_BYTES;
+        if (tid == 0) bulk_wait_read<1>();
+        named_bar(1, 128);
+#pragma unroll
+        for (int q4 = 0; q4 < 8; ++q4)
+          *reinterpret_cast<float4*>(buf + sw128_chunk(tid, q4)) =
+              make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
+        fence_async_smem();
+        named_bar(1, 128);
+        if (tid == 0) {
+          tma_store_3d(&mapOut, buf, 32 * cc, blk * 128, b);
+          bulk_commit();
+        }
+        ++si;
+      }
+    }
+    if (tid == 0) bulk_wait_all();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 9) tmem_dealloc(tmem, g.tmem_cols);
+}
+
+int sm_count() {
+  static int n = 0;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  });
+  return n;
+}
+
+bool aligned16(const void* p) { return p == nullptr || ((uintptr_t)p & 15u) == 0; }
+
+}  // namespace
+
+// ------------------------------------------------------------------ host
+
+int make_map_3d_f32(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1,
+                    uint64_t dim2, uint32_t box0, uint32_t box1, bool granule32) {
+  using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+  static EncodeFn encode = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      encode = reinterpret_cast<EncodeFn>(fn);
+  });
+  if (encode == nullptr) return set_error(kUnsupported, "cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[3] = {dim0, dim1, dim2};
+  const cuuint64_t strides[2] = {dim0 * 4, dim0 * dim1 * 4};
+  const cuuint32_t box[3] = {box0, box1, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims,
+                            strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            granule32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                                      : CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(kUnsupported, "tensor map rejected (CUresult %d)", (int)r);
+  return kOk;
+}
+
+int tc_take_device_error() {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_tc_error, sizeof(int)) != cudaSuccess) return kLaunch;
+  if (v != 0) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_tc_error, &zero, sizeof(int));
+  }
+  return v;
+}
+
+// True when the tensor-core cost path applies: fp32 features with D >= 64,
+// 16-byte aligned rows (D, M multiples of 4) and base pointers.  The
+// TW_COST_SIMT environment variable (any value but "0") forces the SIMT path.
+bool tc_cost_eligible(const float* X, const float* Y, const float* vx, const float* vy, int N,
+                      int M, int D, const float* C, const float* Q) {
+  const char* env = std::getenv("TW_COST_SIMT");
+  if (env != nullptr && env[0] != '\0' && env[0] != '0') return false;
+  (void)vx;
+  (void)vy;
+  (void)N;
+  return D >= 64 && D % 4 == 0 && M % 4 == 0 && aligned16(X) && aligned16(Y) && aligned16(C) &&
+         aligned16(Q);
+}
+
+int tc_cost_f32(const float* X, const float* Y, const float* vx, const float* vy, int B, int N,
+                int M, int D, double beta, double eps, float* C, float* Q, cudaStream_t st) {
+  if (B == 0 || N == 0 || M == 0) return kOk;
+  CUtensorMap mX, mY, mC, mQ;
+  int rc;
+  if ((rc = make_map_3d_f32(&mX, X, D, N, B, KC, BM)) != kOk) return rc;
+  if ((rc = make_map_3d_f32(&mY, Y, D, M, B, KC, BN)) != kOk) return rc;
+  if ((rc = make_map_3d_f32(&mC, C, M, N, B, 32, BM)) != kOk) return rc;
+  mQ = mC;
+  if (Q != nullptr && (rc = make_map_3d_f32(&mQ, Q, M, N, B, 32, BM)) != kOk) return rc;
+  const long long tiles = (long long)B * ((N + BM - 1) / BM) * ((M + BN - 1) / BN);
+  const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
+  const bool var = vx != nullptr;
+  auto kern = var ? tc_cost_kernel<true> : tc_cost_kernel<false>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)COST_SMEM);
+  kern<<<grid, COST_THREADS, COST_SMEM, st>>>(mX, mY, mC, mQ, vx, vy, B, N, M, D, (float)beta,
+                                              (float)eps, Q != nullptr ? 1 : 0);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(kLaunch, "tc cost launch: %s", cudaGetErrorString(e));
+  return kOk;
+}
+
+namespace {
+
+template <int SIDE, bool VAR>
+int grad_side(const float* A, const float* F, const float* va, const float* vb, const float* C,
+              const float* dC, const float* dQ, int B, int N, int M, int D, double beta,
+              double eps, float* dA, float* dva, cudaStream_t st) {
+  const int R = SIDE == 0 ? N : M, S = SIDE == 0 ? M : N;
+  CUtensorMap mDC, mC, mDQ, mF, mOut;
+  int rc;
+  // SIDE 0 reads S as a K-major operand (16-byte granules), SIDE 1 as an
+  // MN-major one (32-byte granules); the features are always MN-major.
+  const uint32_t sbox_rows = SIDE == 0 ? 128 : 32;
+  const bool s_g32 = SIDE == 1;
+  if ((rc = make_map_3d_f32(&mDC, dC, M, N, B, 32, sbox_rows, s_g32)) != kOk) return rc;
+  if ((rc = make_map_3d_f32(&mC, C, M, N, B, 32, sbox_rows, s_g32)) != kOk) return rc;
+  mDQ = mC;
+  const bool has_dq = VAR && dQ != nullptr;
+  if (has_dq && (rc = make_map_3d_f32(&mDQ, dQ, M, N, B, 32, sbox_rows, s_g32)) != kOk) return rc;
+  if ((rc = make_map_3d_f32(&mF, F, D, S, B, 32, 32, true)) != kOk) return rc;
+  if ((rc = make_map_3d_f32(&mOut, dA, D, R, B, 32, 128)) != kOk) return rc;
+  GradGeom g;
+  g.nF = (D + 31) / 32;
+  g.off_dq = 2 * SBOX;
+  g.off_fh = (VAR ? 3 : 2) * SBOX;
+  g.off_fl = g.off_fh + g.nF * 4096;
+  g.stage_bytes = g.off_fl + g.nF * 4096;
+  g.tx_bytes = 2 * SBOX + (has_dq ? SBOX : 0) + g.nF * 4096;
+  const int avail = 232448 - 2 * STG_BYTES - (int)sizeof(GradShared);
+  g.stages = avail / g.stage_bytes;
+  if (g.stages > GRAD_MAX_STAGES) g.stages = GRAD_MAX_STAGES;
+  if (g.stages < 1) return set_error(kUnsupported, "tc grad: D=%d needs too much shared memory", D);
+  uint32_t cols = 32;
+  while (cols < (uint32_t)(2 * 32 * g.nF)) cols <<= 1;
+  g.tmem_cols = cols;
+  const size_t smem = (size_t)g.stages * g.stage_bytes + 2 * STG_BYTES + sizeof(GradShared);
+  const long long units = (long long)B * ((R + 127) / 128);
+  const int grid = (int)(units < sm_count() ? units : sm_count());
+  auto kern = tc_grad_kernel<SIDE, VAR>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  kern<<<grid, GRAD_THREADS, smem, st>>>(mDC, mC, mDQ, mF, mOut, A, va, vb, dva, B, N, M, D,
+                                         (float)beta, (float)eps, has_dq ? 1 : 0, g);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(kLaunch, "tc grad launch: %s", cudaGetErrorString(e));
+  return kOk;
+}
+
+}  // namespace
+
+// True when the tensor-core chain-rule path applies (same conditions as the
+// cost path, and D <= 256 so a 128 x D accumulator pair fits in TMEM).
+bool tc_grad_eligible(const float* X, const float* Y, const float* C, const float* dC,
+                      const float* dQ, const float* dX, const float* dY, int M, int D) {
+  return tc_cost_eligible(X, Y, nullptr, nullptr, 0, M, D, C, dC) && D <= 256 && aligned16(dQ) &&
+         aligned16(dX) && aligned16(dY);
+}
+
+int tc_grad_f32(const float* X, const float* Y, const float* vx, const float* vy, const float* C,
+                const float* dC, const float* dQ, int B, int N, int M, int D, double beta,
+                double eps, float* dX, float* dY, float* dvx, float* dvy, cudaStream_t st) {
+  if (B == 0 || N == 0 || M == 0) return kOk;
+  int rc;
+  if (vx != nullptr) {
+    if ((rc = grad_side<0, true>(X, Y, vx, vy, C, dC, dQ, B, N, M, D, beta, eps, dX, dvx, st)))
+      return rc;
+    return grad_side<1, true>(Y, X, vy, vx, C, dC, dQ, B, N, M, D, beta, eps, dY, dvy, st);
+  }
+  if ((rc = grad_side<0, false>(X, Y, nullptr, nullptr, C, dC, nullptr, B, N, M, D, beta, eps, dX,
+                                nullptr, st)))
+    return rc;
+  return grad_side<1, false>(Y, X, nullptr, nullptr, C, dC, nullptr, B, N, M, D, beta, eps, dY,
+                             nullptr, st);
+}
+
+}  // namespace tw
