@@ -10,7 +10,8 @@ implementation:
   (and uDTW penalty).  ``saved`` is the kernel's opaque saved stream
   (uint8), replacing the reference's diagonal-major R and P.
 * ``torchwarp_b200::sdtw_dp_backward(saved, grad_r, grad_p, N, M, gamma,
-  has_penalty)`` -> (d_cost, d_penalty).
+  has_penalty)`` -> (d_cost, d_penalty); d_penalty is an empty tensor when
+  has_penalty is False (nothing is written for a penalty that does not exist).
 * ``torchwarp_b200::udtw_fused(X, Y, vx?, vy?, gamma, beta, eps, bandwidth)``
   -> (out_r, out_p, saved, cost): cost built by the native cost kernel from
   the features, then the DP.  ``vx``/``vy`` None means unit variance and no
@@ -89,11 +90,13 @@ def _dp_forward(cost, penalty, gamma, bandwidth):
 
 
 def _dp_backward(saved, grad_r, grad_p, N, M, gamma, has_p):
+    """(d_cost [B,N,M], d_penalty): d_penalty is [B,N,M] with a penalty and an
+    empty [0] tensor without one (soft-DTW has no penalty input to feed)."""
     nat.require_cuda(grad_r)
     B = grad_r.shape[0]
     dtype = grad_r.dtype
     d_cost = grad_r.new_empty(B, N, M)
-    d_pen = grad_r.new_empty(B, N, M) if has_p else grad_r.new_zeros(B, N, M)
+    d_pen = grad_r.new_empty(B, N, M) if has_p else grad_r.new_empty(0)
     if B == 0:
         return d_cost, d_pen
     grad_r = grad_r.contiguous()
@@ -135,7 +138,8 @@ def sdtw_dp_backward(saved: Tensor, grad_r: Tensor, grad_p: Tensor, N: int, M: i
 @sdtw_dp_backward.register_fake
 def _(saved, grad_r, grad_p, N, M, gamma, has_penalty):
     B = grad_r.shape[0]
-    return grad_r.new_empty(B, N, M), grad_r.new_empty(B, N, M)
+    return grad_r.new_empty(B, N, M), (grad_r.new_empty(B, N, M) if has_penalty
+                                       else grad_r.new_empty(0))
 
 
 _register_autocast(sdtw_dp)
