@@ -14,9 +14,10 @@ Printed (rank 0), one JSON line:
             events between barriers, max over ranks;
   e2e       the same step with X, Y copied from pinned host memory and the
             distances copied back inside the timed region;
-  roofline  the dominant native kernel: algorithmic bytes per launch (cost
-            read or cost-gradient write, 4 B/cell) / its average CUDA-event
-            duration in the timed region, against MEASURED_PEAKS.json;
+  roofline  the dominant native kernel (longest average launch): its
+            algorithmic bytes per launch / its average CUDA-event duration in
+            the timed region, against MEASURED_PEAKS.json, with the DRAM
+            traffic ncu measured for that kernel (per cell, scaled);
   cpu_baseline  the float64 CPU oracle (oracle/, one thread) on a bounded
             sample of the same workload (rank 0, N=1 only).
 ``--impl reference`` times the CPU implementation of the reference's path
@@ -42,7 +43,22 @@ sys.path.insert(0, str(ROOT))
 METRIC = "fwd+bwd DP cells/s (soft-DTW B=4096 N=M=1024)"
 UNIT = "cells/s"
 ALGO_BYTES_PER_CELL = 8      # soft-DTW fwd+bwd: cost read + cost-gradient write
-KERNEL_BYTES_PER_CELL = 4    # one DP sweep: its cost read (fwd) or gradient write (bwd)
+
+# Per native call: (kernel launches per call, algorithmic bytes per cell of one
+# launch, DRAM bytes per cell of one launch measured by ncu).  Algorithmic:
+# the DP forward's cost read and the backward's cost-gradient write (the
+# 8 B/cell of the step split between them), the cost builder's cost write,
+# each chain-rule launch's cost + cost-gradient read.  Measured: DRAM read +
+# write per cell from the `ncu --set full` capture of the same kernels at
+# B=4096, N=M=256 (profiles/soft_dtw_b4096_n256_kernels_ncu.md), applied per
+# cell to the launch being timed; feature bytes (X, Y, dX, dY) are added at
+# the timed shape.
+CALLS = {
+    "udtw_cost": (1, 4, 4.0),            # + X, Y read
+    "sdtw_forward": (1, 4, 8.16),        # C read + saved R' write
+    "sdtw_backward": (1, 4, 9.57),       # saved R' read + dC write (+1.5 B/cell to find)
+    "udtw_features_grad": (2, 8, 8.96),  # C + dC read (+ other side's features via L2)
+}
 
 
 def parse():
@@ -63,7 +79,7 @@ def parse():
 def config(a, world):
     return {"workload": "soft_dtw fwd+bwd, squared-Euclidean cost, gamma={}".format(a.gamma),
             "global_batch": a.batch, "N": a.length, "M": a.length, "D": a.dim,
-            "per_gpu_batch": a.batch // world, "parallelism": "dp{}".format(world),
+            "per_gpu_batch": -(-a.batch // world), "parallelism": "dp{}".format(world),
             "l2": "inputs larger than L2 (X,Y {:.1f} GB, cost {:.1f} GB)".format(
                 2 * a.batch // world * a.length * a.dim * 4 / 1e9,
                 a.batch // world * a.length * a.length * 4 / 1e9)}
@@ -147,14 +163,13 @@ def run_ours(a):
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
-    if a.batch % world:
-        raise SystemExit("batch {} not divisible by {} GPUs".format(a.batch, world))
-    Bl, N, D = a.batch // world, a.length, a.dim
+    from torchwarp_b200.sharding import gather_pairs, shard_bounds
+    lo, hi = shard_bounds(a.batch, world, rank)
+    Bl, N, D = hi - lo, a.length, a.dim
     cells_total = a.batch * N * N
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
     X = torch.randn(Bl, N, D, device=dev, generator=g)
     Y = torch.randn(Bl, N, D, device=dev, generator=g)
-    gathered = [torch.empty(Bl, device=dev) for _ in range(world)]
 
     def step(x, y):
         x = x.detach().requires_grad_(True)
@@ -162,7 +177,7 @@ def run_ours(a):
         d = twb.functional.soft_dtw(x, y, gamma=a.gamma)
         d.sum().backward()
         if world > 1:
-            dist.all_gather(gathered, d.detach())
+            gather_pairs(d.detach(), a.batch)   # every rank gets all B distances
         return d, x.grad, y.grad
 
     def barrier():
@@ -196,38 +211,76 @@ def run_ours(a):
 
     e2e = None
     if not a.no_e2e:
+        # Host-resident inputs (pinned), copied to the device every step and
+        # the distances read back every step.  The copy of step k+1 runs on a
+        # copy stream while step k computes (double-buffered device inputs),
+        # as a training loop with a prefetching loader would.
         Xh = X.cpu().pin_memory()
         Yh = Y.cpu().pin_memory()
-        out_h = torch.empty(Bl, pin_memory=True)
+        out_h = torch.empty(2, Bl, pin_memory=True)
+        copy_stream = torch.cuda.Stream(dev)
+        bufs = [(torch.empty_like(X), torch.empty_like(Y)) for _ in range(2)]
+        ready = [torch.cuda.Event() for _ in range(2)]
+        free = [torch.cuda.Event() for _ in range(2)]
+        for e in free:
+            e.record()
 
-        def e2e_step():
-            x = Xh.to(dev, non_blocking=True)
-            y = Yh.to(dev, non_blocking=True)
-            d, _, _ = step(x, y)
-            out_h.copy_(d.detach(), non_blocking=True)
+        def issue_copy(k):
+            s = k % 2
+            with torch.cuda.stream(copy_stream):
+                copy_stream.wait_event(free[s])
+                bufs[s][0].copy_(Xh, non_blocking=True)
+                bufs[s][1].copy_(Yh, non_blocking=True)
+                ready[s].record(copy_stream)
 
-        e2e_step()
-        ms_e = timed(e2e_step, a.steps)
+        def e2e_run(steps):
+            issue_copy(0)
+            for k in range(steps):
+                if k + 1 < steps:
+                    issue_copy(k + 1)
+                s = k % 2
+                torch.cuda.current_stream().wait_event(ready[s])
+                d, _, _ = step(bufs[s][0], bufs[s][1])
+                out_h[s].copy_(d.detach(), non_blocking=True)
+                free[s].record()
+
+        e2e_run(2)
+        ms_e = timed(lambda: e2e_run(a.steps), 1)
+        del bufs
         e2e = {"value": cells_total / (ms_e / a.steps / 1e3), "unit": UNIT,
                "h2d_bytes_per_step": int((Xh.numel() + Yh.numel()) * 4 * world),
-               "d2h_bytes_per_step": int(Bl * 4 * world), "ms_per_step": ms_e / a.steps}
+               "d2h_bytes_per_step": int(Bl * 4 * world), "ms_per_step": ms_e / a.steps,
+               "copies": "pinned host -> device every step, overlapped with the previous "
+                         "step on a copy stream; distances read back every step"}
 
-    # dominant native kernel of the timed region
-    name, (launches, tot) = max(kern.items(), key=lambda kv: kv[1][1])
-    per_launch_ms = tot / launches
+    # dominant native kernel of the timed region (one C-ABI call may launch
+    # several kernels of equal work: the chain rule runs its dX and dY sides)
+    def per_launch(kv):
+        name, (calls, tot) = kv
+        return tot / (calls * CALLS.get(name, (1, 0, 0))[0])
+
+    name, (calls, tot) = max(kern.items(), key=per_launch)
+    launches_per_call, algo_pc, traffic_pc = CALLS.get(name, (1, 0, None))
+    per_launch_ms = tot / (calls * launches_per_call)
     peak, src = peaks()
     cells_local = Bl * N * N
-    if name in ("sdtw_forward", "sdtw_backward"):
-        algo = cells_local * KERNEL_BYTES_PER_CELL
-    elif name == "udtw_cost":
-        algo = cells_local * 4 + 2 * Bl * N * D * 4
-    else:  # udtw_features_grad: cost and cost-gradient read, dX/dY written
-        algo = cells_local * 8 + 2 * Bl * N * D * 4
+    feat = Bl * N * D * 4                 # one side's features
+    algo = cells_local * algo_pc
+    traffic = None if traffic_pc is None else cells_local * traffic_pc
+    if name == "udtw_cost":
+        algo += 2 * feat
+        traffic += 2 * feat
+    elif name == "udtw_features_grad":
+        algo += feat                      # each side writes its own gradient
+        traffic += feat
     achieved = algo / (per_launch_ms / 1e3) / 1e9
     roofline = {"bound": "hbm", "kernel": name, "achieved": achieved, "peak": peak,
                 "unit": "GB/s", "frac": achieved / peak, "peak_source": src,
-                "traffic": None, "algorithmic_bytes_per_launch": algo,
-                "avg_launch_ms": per_launch_ms,
+                "traffic": traffic,
+                "traffic_source": "ncu dram__bytes_read+write per cell of the B=4096 N=M=256 "
+                                  "capture, scaled to this launch's cells",
+                "algorithmic_bytes_per_launch": algo, "avg_launch_ms": per_launch_ms,
+                "launches_per_call": launches_per_call,
                 "step_frac": (cells_local * ALGO_BYTES_PER_CELL / (ms_step / 1e3) / 1e9) / peak,
                 "kernels_ms_per_step": {k: v[1] / a.steps for k, v in kern.items()}}
 
@@ -241,9 +294,7 @@ def run_ours(a):
     if rank != 0:
         return
     launches_per_step = sum(v[0] for v in kern.values()) // a.steps
-    kernels_per_call = {"udtw_cost": 1, "sdtw_forward": 1, "sdtw_backward": 1,
-                        "udtw_features_grad": 2}
-    gpu_launches = sum(kernels_per_call.get(k, 1) * v[0] for k, v in kern.items())
+    gpu_launches = sum(CALLS.get(k, (1,))[0] * v[0] for k, v in kern.items())
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
