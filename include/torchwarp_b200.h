@@ -137,6 +137,31 @@ int tw_udtw_features_grad_f64(const double* X, const double* Y, const double* vx
                               void* stream);
 
 /* ---------------------------------------------------------------------
+ * soft-DTW's squared-Euclidean cost with a positivity mask in place of the
+ * cost for the chain rule (cost path of sdtw.py:78-84, chain rule of
+ * udtw_cuda.cu:557-568 with unit variance):
+ *   cost_ij = max(|x_i|^2 + |y_j|^2 - 2 x_i.y_j, 0)   [B,N,M]
+ *   mask: uint32 words [B][ceil(M/32)][NP], NP = 4 ceil(N/4); bit (j & 31)
+ *         of word [b][j>>5][i] is set where the unclamped value is > 0 (bits
+ *         for j >= M and words of rows i >= N are 0).
+ * The chain rule reads the mask instead of the cost (1 bit instead of 4 or 8
+ * bytes per cell), so the cost can be freed after the DP forward:
+ *   dX = -2 S Y + 2 X rowsum(S), dY = -2 S^T X + 2 Y colsum(S),
+ *   S = d_cost where the mask bit is set, else 0.
+ * fp32 with D >= 64 (D, M multiples of 4, 16-byte aligned) runs on tcgen05
+ * tensor cores (3xTF32); other shapes and fp64 on SIMT kernels. */
+int tw_sqeuclid_cost_f32(const float* X, const float* Y, int B, int N, int M, int D, float* cost,
+                         uint32_t* mask, void* stream);
+int tw_sqeuclid_cost_f64(const double* X, const double* Y, int B, int N, int M, int D,
+                         double* cost, uint32_t* mask, void* stream);
+int tw_sqeuclid_grad_f32(const float* X, const float* Y, const uint32_t* mask,
+                         const float* d_cost, int B, int N, int M, int D, float* dX, float* dY,
+                         void* stream);
+int tw_sqeuclid_grad_f64(const double* X, const double* Y, const uint32_t* mask,
+                         const double* d_cost, int B, int N, int M, int D, double* dX,
+                         double* dY, void* stream);
+
+/* ---------------------------------------------------------------------
  * JEANIE on a cost [B, K1, K2, T, U] (one viewpoint axis: K2 = 1).
  *   s1, s2: viewpoint shifts (already clamped to K-1 by the caller).
  *   out [B]: soft-min over viewpoints of R[:, T-1, U-1];

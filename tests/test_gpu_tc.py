@@ -192,3 +192,79 @@ def test_soft_dtw_features_path_uses_tensor_cores(monkeypatch, orc):
     (tc_d, tc_x, tc_y), (si_d, si_x, si_y) = errs
     assert tc_d < 1e-5 and tc_x < 1e-4 and tc_y < 1e-4, errs
     assert tc_d <= 2 * si_d + 1e-7 and tc_x <= 2 * si_x + 1e-6 and tc_y <= 2 * si_y + 1e-6, errs
+
+
+# ------------------------------------------- squared-Euclidean cost + mask
+
+def _sq_cost(X, Y):
+    B, N, D = X.shape
+    M = Y.shape[1]
+    C = torch.empty(B, N, M, device="cuda", dtype=X.dtype)
+    mask = torch.empty(B, (M + 31) // 32, (N + 3) // 4 * 4, device="cuda", dtype=torch.int32)
+    fn = getattr(nat.lib(), "tw_sqeuclid_cost_" + nat.suffix(X.dtype))
+    nat.check(fn(nat.ptr(X), nat.ptr(Y), B, N, M, D, nat.ptr(C), nat.ptr(mask),
+                 nat.stream_of(X)), "tw_sqeuclid_cost")
+    torch.cuda.synchronize()
+    return C, mask
+
+
+def _pack_positive(C):
+    """[B, N, M] cost -> [B, ceil(M/32), 4 ceil(N/4)] words with bit j&31 set
+    where C > 0 (padding rows zero)."""
+    B, N, M = C.shape
+    MW = (M + 31) // 32
+    NP = (N + 3) // 4 * 4
+    pos = torch.zeros(B, NP, MW * 32, dtype=torch.int64, device=C.device)
+    pos[:, :N, :M] = (C > 0).long()
+    w = (pos.view(B, NP, MW, 32) << torch.arange(32, device=C.device)).sum(-1)
+    w = torch.where(w >= 2 ** 31, w - 2 ** 32, w).to(torch.int32)
+    return w.transpose(1, 2).contiguous()
+
+
+@pytest.mark.parametrize("shape", SHAPES + [(2, 70, 45, 8), (3, 33, 100, 3)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64])
+@pytest.mark.parametrize("simt", [False, True])
+def test_sq_cost_and_mask(shape, dtype, simt, monkeypatch):
+    if dtype == torch.float64 and simt:
+        pytest.skip("float64 always runs the SIMT kernels")
+    _env(monkeypatch, simt)
+    X, Y, _, _ = _inputs(*shape, seed=3 * sum(shape))
+    X, Y = X.to(dtype), Y.to(dtype)
+    # exact duplicates: sq_raw <= 0 there, so the mask has zeros to find
+    n = min(X.shape[1], Y.shape[1])
+    Y[:, : n // 2] = X[:, : n // 2]
+    C, mask = _sq_cost(X, Y)
+    assert nat.lib().tw_device_error() == 0
+    Cu, _ = _cost(X.float(), Y.float(), None, None, 0.0, 1e-8) if dtype == torch.float32 else (
+        None, None)
+    if Cu is not None:
+        assert torch.equal(C, Cu)
+    assert torch.equal(mask, _pack_positive(C))
+
+
+@pytest.mark.parametrize("shape", SHAPES + [(2, 70, 45, 8)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64])
+def test_sq_grad_mask_equals_cost_path(shape, dtype, monkeypatch):
+    """The chain rule from the mask is bit-identical to the one from the cost."""
+    _env(monkeypatch, False)
+    B, N, M, D = shape
+    X, Y, _, _ = _inputs(*shape, seed=5 * sum(shape))
+    X, Y = X.to(dtype), Y.to(dtype)
+    n = min(N, M)
+    Y[:, : n // 3] = X[:, : n // 3]
+    C, mask = _sq_cost(X, Y)
+    dC = torch.randn(B, N, M, device="cuda", dtype=dtype)
+    dX = torch.empty_like(X)
+    dY = torch.empty_like(Y)
+    fn = getattr(nat.lib(), "tw_sqeuclid_grad_" + nat.suffix(dtype))
+    nat.check(fn(nat.ptr(X), nat.ptr(Y), nat.ptr(mask), nat.ptr(dC), B, N, M, D, nat.ptr(dX),
+                 nat.ptr(dY), nat.stream_of(X)), "tw_sqeuclid_grad")
+    fn2 = getattr(nat.lib(), "tw_udtw_features_grad_" + nat.suffix(dtype))
+    rX = torch.empty_like(X)
+    rY = torch.empty_like(Y)
+    nat.check(fn2(nat.ptr(X), nat.ptr(Y), None, None, nat.ptr(C), nat.ptr(dC), None, B, N, M, D,
+                  0.0, 1e-8, nat.ptr(rX), nat.ptr(rY), None, None, nat.stream_of(X)),
+              "tw_udtw_features_grad")
+    torch.cuda.synchronize()
+    assert nat.lib().tw_device_error() == 0
+    assert torch.equal(dX, rX) and torch.equal(dY, rY)

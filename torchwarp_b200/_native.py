@@ -41,6 +41,12 @@ SIGNATURES = {
                                 _c_p, _c_p]),
     "tw_udtw_features_grad_f32": (_c_i, [_c_p] * 7 + [_c_i] * 4 + [_c_d, _c_d] + [_c_p] * 5),
     "tw_udtw_features_grad_f64": (_c_i, [_c_p] * 7 + [_c_i] * 4 + [_c_d, _c_d] + [_c_p] * 5),
+    "tw_sqeuclid_cost_f32": (_c_i, [_c_p, _c_p, _c_i, _c_i, _c_i, _c_i, _c_p, _c_p, _c_p]),
+    "tw_sqeuclid_cost_f64": (_c_i, [_c_p, _c_p, _c_i, _c_i, _c_i, _c_i, _c_p, _c_p, _c_p]),
+    "tw_sqeuclid_grad_f32": (_c_i, [_c_p, _c_p, _c_p, _c_p, _c_i, _c_i, _c_i, _c_i, _c_p, _c_p,
+                                    _c_p]),
+    "tw_sqeuclid_grad_f64": (_c_i, [_c_p, _c_p, _c_p, _c_p, _c_i, _c_i, _c_i, _c_i, _c_p, _c_p,
+                                    _c_p]),
     "tw_jeanie_forward_f32": (_c_i, [_c_p, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_d, _c_p,
                                      _c_p, _c_p]),
     "tw_jeanie_forward_f64": (_c_i, [_c_p, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_d, _c_p,

@@ -142,6 +142,13 @@ int udtw_grad_f32(const float*, const float*, const float*, const float*, const 
 int udtw_grad_f64(const double*, const double*, const double*, const double*, const double*,
                   const double*, const double*, int, int, int, int, double, double, double*,
                   double*, double*, double*, cudaStream_t);
+int sq_cost_f32(const float*, const float*, int, int, int, int, float*, uint32_t*, cudaStream_t);
+int sq_cost_f64(const double*, const double*, int, int, int, int, double*, uint32_t*,
+                cudaStream_t);
+int sq_grad_f32(const float*, const float*, const uint32_t*, const float*, int, int, int, int,
+                float*, float*, cudaStream_t);
+int sq_grad_f64(const double*, const double*, const uint32_t*, const double*, int, int, int, int,
+                double*, double*, cudaStream_t);
 
 template <typename T>
 int jeanie_forward(const T*, int, int, int, int, int, int, int, double, T*, T*, cudaStream_t);
@@ -250,6 +257,26 @@ int tw_udtw_features_grad_f32(const float* X, const float* Y, const float* vx, c
   return udtw_grad_f32(X, Y, vx, vy, cost, d_cost, d_penalty, B, N, M, D, beta, eps, dX, dY, dvx,
                        dvy, (cudaStream_t)stream);
 }
+#define TW_SQ_ENTRIES(SUF, T)                                                                    \
+  int tw_sqeuclid_cost_##SUF(const T* X, const T* Y, int B, int N, int M, int D, T* cost,       \
+                             uint32_t* mask, void* stream) {                                     \
+    g_err[0] = 0;                                                                               \
+    if (B < 0 || N <= 0 || M <= 0 || D <= 0 || (B && (!X || !Y || !cost || !mask)))             \
+      return set_error(kInvalid, "tw_sqeuclid_cost: invalid arguments");                        \
+    return sq_cost_##SUF(X, Y, B, N, M, D, cost, mask, (cudaStream_t)stream);                   \
+  }                                                                                             \
+  int tw_sqeuclid_grad_##SUF(const T* X, const T* Y, const uint32_t* mask, const T* d_cost,     \
+                             int B, int N, int M, int D, T* dX, T* dY, void* stream) {          \
+    g_err[0] = 0;                                                                               \
+    if (B < 0 || N <= 0 || M <= 0 || D <= 0 ||                                                  \
+        (B && (!X || !Y || !mask || !d_cost || !dX || !dY)))                                    \
+      return set_error(kInvalid, "tw_sqeuclid_grad: invalid arguments");                        \
+    return sq_grad_##SUF(X, Y, mask, d_cost, B, N, M, D, dX, dY, (cudaStream_t)stream);         \
+  }
+
+TW_SQ_ENTRIES(f32, float)
+TW_SQ_ENTRIES(f64, double)
+
 int tw_udtw_features_grad_f64(const double* X, const double* Y, const double* vx,
                               const double* vy, const double* cost, const double* d_cost,
                               const double* d_penalty, int B, int N, int M, int D, double beta,

@@ -26,9 +26,11 @@ __global__ void __launch_bounds__(256) udtw_cost_kernel(const T* __restrict__ X,
                                                         const T* __restrict__ vx,
                                                         const T* __restrict__ vy, int N, int M,
                                                         int D, T beta, T eps, T* __restrict__ C,
-                                                        T* __restrict__ Q) {
+                                                        T* __restrict__ Q,
+                                                        uint32_t* __restrict__ mask) {
   __shared__ T Xs[TM][KC + 1];
   __shared__ T Ys[TM][KC + 1];
+  __shared__ uint32_t pos[TM][TM / 32];  // positivity bits of the tile's cells
   const int b = blockIdx.z;
   const int i0 = blockIdx.y * TM, j0 = blockIdx.x * TM;
   const int tid = threadIdx.x;
@@ -63,6 +65,10 @@ __global__ void __launch_bounds__(256) udtw_cost_kernel(const T* __restrict__ X,
     }
     __syncthreads();
   }
+  if (mask != nullptr) {
+    if (tid < TM * TM / 32) pos[tid >> 1][tid & 1] = 0u;
+    __syncthreads();
+  }
   for (int a = 0; a < 4; ++a) {
     const int i = i0 + ty * 4 + a;
     if (i >= N) continue;
@@ -70,6 +76,8 @@ __global__ void __launch_bounds__(256) udtw_cost_kernel(const T* __restrict__ X,
       const int j = j0 + tx * 4 + c;
       if (j >= M) continue;
       T sq = (x2[a] + y2[c]) - T(2) * acc[a][c];
+      if (mask != nullptr && sq > T(0))
+        atomicOr(&pos[ty * 4 + a][(tx * 4 + c) >> 5], 1u << ((tx * 4 + c) & 31));
       sq = sq > T(0) ? sq : T(0);
       T var = T(1);
       if (vx != nullptr) {
@@ -79,6 +87,17 @@ __global__ void __launch_bounds__(256) udtw_cost_kernel(const T* __restrict__ X,
       const long long o = ((long long)b * N + i) * M + j;
       C[o] = sq / var;
       if (Q != nullptr) Q[o] = beta * log(var);
+    }
+  }
+  if (mask != nullptr) {
+    // words [b][j0/32 + w][i] (rows padded to NP = 4 ceil(N/4), padding rows
+    // zero): j0 is a multiple of 64, so each tile owns 2 words per row
+    __syncthreads();
+    const int MW = (M + 31) >> 5, NP = (N + 3) & ~3;
+    if (tid < TM * TM / 32) {
+      const int r = tid >> 1, w = tid & 1;
+      const int i = i0 + r, jw = (j0 >> 5) + w;
+      if (i < NP && jw < MW) mask[((long long)b * MW + jw) * NP + i] = pos[r][w];
     }
   }
 }
@@ -91,7 +110,7 @@ __global__ void __launch_bounds__(256) udtw_grad_strip_kernel(
     const T* __restrict__ A, const T* __restrict__ Bf, const T* __restrict__ va,
     const T* __restrict__ vb, const T* __restrict__ C, const T* __restrict__ dC,
     const T* __restrict__ dQ, int N, int M, int D, T beta, T eps, T* __restrict__ dA,
-    T* __restrict__ dva) {
+    T* __restrict__ dva, const uint32_t* __restrict__ mask) {
   constexpr int TS = 32;
   __shared__ T Gs[TM][TS + 1];   // dsq [strip row][summed index]
   __shared__ T Bs[TS][TM + 1];   // other side's features [summed index][feature]
@@ -124,8 +143,17 @@ __global__ void __launch_bounds__(256) udtw_grad_strip_kernel(
           var_raw = T(0.5) * (vi + vj);
           var = var_raw > eps ? var_raw : eps;
         }
-        const T cc = C[o], dc = dC[o];
-        g = cc > T(0) ? dc / var : T(0);
+        const T dc = dC[o];
+        bool positive;
+        T cc = T(0);
+        if (mask != nullptr) {
+          const int MW = (M + 31) >> 5, NP = (N + 3) & ~3;
+          positive = (mask[((long long)b * MW + (j >> 5)) * NP + i] >> (j & 31)) & 1u;
+        } else {
+          cc = C[o];
+          positive = cc > T(0);
+        }
+        g = positive ? dc / var : T(0);
         if (va != nullptr && var_raw > eps) {
           const T dq = dQ != nullptr ? dQ[o] : T(0);
           vsum += (beta * dq - dc * cc) / var;
@@ -177,10 +205,10 @@ __global__ void __launch_bounds__(256) udtw_grad_strip_kernel(
 
 template <typename T>
 int cost_launch(const T* X, const T* Y, const T* vx, const T* vy, int B, int N, int M, int D,
-                double beta, double eps, T* C, T* Q, cudaStream_t st) {
+                double beta, double eps, T* C, T* Q, cudaStream_t st, uint32_t* mask = nullptr) {
   if (B == 0 || N == 0 || M == 0) return kOk;
   dim3 grid((M + TM - 1) / TM, (N + TM - 1) / TM, B);
-  udtw_cost_kernel<T><<<grid, 256, 0, st>>>(X, Y, vx, vy, N, M, D, (T)beta, (T)eps, C, Q);
+  udtw_cost_kernel<T><<<grid, 256, 0, st>>>(X, Y, vx, vy, N, M, D, (T)beta, (T)eps, C, Q, mask);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(kLaunch, "udtw cost launch: %s", cudaGetErrorString(e));
   return kOk;
@@ -189,14 +217,14 @@ int cost_launch(const T* X, const T* Y, const T* vx, const T* vy, int B, int N, 
 template <typename T>
 int grad_launch(const T* X, const T* Y, const T* vx, const T* vy, const T* C, const T* dC,
                 const T* dQ, int B, int N, int M, int D, double beta, double eps, T* dX, T* dY,
-                T* dvx, T* dvy, cudaStream_t st) {
+                T* dvx, T* dvy, cudaStream_t st, const uint32_t* mask = nullptr) {
   if (B == 0 || N == 0 || M == 0) return kOk;
   const int fch = (D + TM - 1) / TM;
   dim3 gx(fch, (N + TM - 1) / TM, B), gy(fch, (M + TM - 1) / TM, B);
   udtw_grad_strip_kernel<T, 0><<<gx, 256, 0, st>>>(X, Y, vx, vy, C, dC, dQ, N, M, D, (T)beta,
-                                                    (T)eps, dX, vx ? dvx : nullptr);
+                                                    (T)eps, dX, vx ? dvx : nullptr, mask);
   udtw_grad_strip_kernel<T, 1><<<gy, 256, 0, st>>>(Y, X, vy, vx, C, dC, dQ, N, M, D, (T)beta,
-                                                    (T)eps, dY, vx ? dvy : nullptr);
+                                                    (T)eps, dY, vx ? dvy : nullptr, mask);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(kLaunch, "udtw grad launch: %s", cudaGetErrorString(e));
   return kOk;
@@ -208,7 +236,10 @@ int grad_launch(const T* X, const T* Y, const T* vx, const T* vy, const T* C, co
 bool tc_cost_eligible(const float* X, const float* Y, const float* vx, const float* vy, int N,
                       int M, int D, const float* C, const float* Q);
 int tc_cost_f32(const float* X, const float* Y, const float* vx, const float* vy, int B, int N,
-                int M, int D, double beta, double eps, float* C, float* Q, cudaStream_t st);
+                int M, int D, double beta, double eps, float* C, float* Q, uint32_t* mask,
+                cudaStream_t st);
+int tc_sq_grad_f32(const float* X, const float* Y, const uint32_t* mask, const float* dC, int B,
+                   int N, int M, int D, float* dX, float* dY, cudaStream_t st);
 bool tc_grad_eligible(const float* X, const float* Y, const float* C, const float* dC,
                       const float* dQ, const float* dX, const float* dY, int M, int D);
 int tc_grad_f32(const float* X, const float* Y, const float* vx, const float* vy, const float* C,
@@ -218,7 +249,7 @@ int tc_grad_f32(const float* X, const float* Y, const float* vx, const float* vy
 int udtw_cost_f32(const float* X, const float* Y, const float* vx, const float* vy, int B, int N,
                   int M, int D, double beta, double eps, float* C, float* Q, cudaStream_t st) {
   if (tc_cost_eligible(X, Y, vx, vy, N, M, D, C, Q))
-    return tc_cost_f32(X, Y, vx, vy, B, N, M, D, beta, eps, C, Q, st);
+    return tc_cost_f32(X, Y, vx, vy, B, N, M, D, beta, eps, C, Q, nullptr, st);
   return cost_launch(X, Y, vx, vy, B, N, M, D, beta, eps, C, Q, st);
 }
 int udtw_cost_f64(const double* X, const double* Y, const double* vx, const double* vy, int B,
@@ -238,6 +269,32 @@ int udtw_grad_f64(const double* X, const double* Y, const double* vx, const doub
                   double beta, double eps, double* dX, double* dY, double* dvx, double* dvy,
                   cudaStream_t st) {
   return grad_launch(X, Y, vx, vy, C, dC, dQ, B, N, M, D, beta, eps, dX, dY, dvx, dvy, st);
+}
+
+// Squared-Euclidean cost with its positivity mask (bit j & 31 of word
+// [b][j >> 5][i] set where sq_raw > 0; rows padded to 4 ceil(N/4)), and the
+// chain rule that takes the mask in place of the cost.
+int sq_cost_f32(const float* X, const float* Y, int B, int N, int M, int D, float* C,
+                uint32_t* mask, cudaStream_t st) {
+  if (tc_cost_eligible(X, Y, nullptr, nullptr, N, M, D, C, nullptr))
+    return tc_cost_f32(X, Y, nullptr, nullptr, B, N, M, D, 0.0, 1e-8, C, nullptr, mask, st);
+  return cost_launch<float>(X, Y, nullptr, nullptr, B, N, M, D, 0.0, 1e-8, C, nullptr, st, mask);
+}
+int sq_cost_f64(const double* X, const double* Y, int B, int N, int M, int D, double* C,
+                uint32_t* mask, cudaStream_t st) {
+  return cost_launch<double>(X, Y, nullptr, nullptr, B, N, M, D, 0.0, 1e-8, C, nullptr, st, mask);
+}
+int sq_grad_f32(const float* X, const float* Y, const uint32_t* mask, const float* dC, int B,
+                int N, int M, int D, float* dX, float* dY, cudaStream_t st) {
+  if (tc_grad_eligible(X, Y, dC, dC, nullptr, dX, dY, M, D))
+    return tc_sq_grad_f32(X, Y, mask, dC, B, N, M, D, dX, dY, st);
+  return grad_launch<float>(X, Y, nullptr, nullptr, nullptr, dC, nullptr, B, N, M, D, 0.0, 1e-8,
+                            dX, dY, nullptr, nullptr, st, mask);
+}
+int sq_grad_f64(const double* X, const double* Y, const uint32_t* mask, const double* dC, int B,
+                int N, int M, int D, double* dX, double* dY, cudaStream_t st) {
+  return grad_launch<double>(X, Y, nullptr, nullptr, nullptr, dC, nullptr, B, N, M, D, 0.0, 1e-8,
+                             dX, dY, nullptr, nullptr, st, mask);
 }
 
 }  // namespace tw

@@ -100,7 +100,7 @@ __global__ void __launch_bounds__(COST_THREADS, 1)
     tc_cost_kernel(const __grid_constant__ CUtensorMap mapX, const __grid_constant__ CUtensorMap mapY,
                    const __grid_constant__ CUtensorMap mapC, const __grid_constant__ CUtensorMap mapQ,
                    const float* __restrict__ vx, const float* __restrict__ vy, int B, int N, int M,
-                   int D, float beta, float eps, int write_q) {
+                   int D, float beta, float eps, int write_q, uint32_t* __restrict__ mask) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* stage_base = smem;
   uint8_t* stg_base = smem + (size_t)STAGES * STAGE_BYTES;
@@ -262,9 +262,11 @@ __global__ void __launch_bounds__(COST_THREADS, 1)
         }
         const int j0 = c.jb * BN + 32 * cc;
         float qv[32];
+        uint32_t pos = 0;  // bit q: sq_raw > 0 at column j0 + q
 #pragma unroll
         for (int q = 0; q < 32; ++q) {
           float sq = (x2 + sh.y2[a][32 * cc + q]) - 2.f * v[q];
+          pos |= (sq > 0.f ? 1u : 0u) << q;
           sq = sq > 0.f ? sq : 0.f;
           if (VAR) {
             const int j = j0 + q;
@@ -278,6 +280,16 @@ __global__ void __launch_bounds__(COST_THREADS, 1)
           }
         }
         if (cc == BN / 32 - 1) mbar_arrive(&sh.nempty[a]);
+        if (mask != nullptr && j0 < M) {
+          // words [b][j >> 5][i] with the row count padded to NP = 4 ceil(N/4)
+          const int NP = (N + 3) & ~3;
+          if (i < NP) {
+            const int left = M - j0;
+            const uint32_t valid = left >= 32 ? 0xFFFFFFFFu : ((1u << left) - 1u);
+            const int MW = (M + 31) >> 5;
+            mask[((long long)c.b * MW + (j0 >> 5)) * NP + i] = i < N ? (pos & valid) : 0u;
+          }
+        }
         // C chunk (and Q chunk) through the two staging buffers
 #pragma unroll
         for (int which = 0; which < (VAR ? 2 : 1); ++which) {
@@ -312,29 +324,37 @@ __global__ void __launch_bounds__(COST_THREADS, 1)
 // ----------------------------------------------------------------------
 // Chain rule of the cost on tensor cores (udtw_cuda.cu:557-568,
 // udtw/_ops.py:179-183):
-//   S = dsq = dC / var where C > 0 (else 0)
+//   S = dsq = dC / var where sq_raw > 0 (C > 0, or the cost's positivity
+//       mask), else 0
 //   dX = -2 S Y + 2 X rowsum(S)        (SIDE 0: unit = 128 rows i of a pair,
 //                                        K = j in chunks of 32)
 //   dY = -2 S^T X + 2 Y colsum(S)      (SIDE 1: unit = 128 rows j of a pair,
 //                                        K = i in chunks of 32)
 //   dvx = 0.5 rowsum(dvar), dvy = 0.5 colsum(dvar),
 //   dvar = (beta dQ - dC C) / var where var_raw > eps.
-// The split warps turn each 32-wide chunk of (dC, C[, dQ]) into S in place
-// (hi over dC, lo over C) and accumulate the row (column) sums of S and
-// dvar in registers; the MMA contracts S (K-major for SIDE 0, MN-major for
-// SIDE 1) with the other side's features (MN-major) into a 128 x BD TMEM
-// accumulator; the epilogue adds 2 A rowsum and stores through TMA.
-// MN-major TF32 operands are only valid in the 32-byte-granule swizzle
-// (a standard 128-byte-swizzle MN-major descriptor yields no product), so
-// those boxes are loaded with that swizzle.
+// Two rings of shared memory: a deep landing ring that TMA fills with raw
+// chunks (dC [, C] [, dQ], the other side's 32 feature rows, the mask words)
+// so that enough bytes are in flight to cover HBM latency, and a two-deep
+// ring of converted operands: the split warps read a landing chunk, write S
+// and the features as TF32 (hi, lo) pairs into a converted slot (same
+// swizzled positions) and release the landing slot at once.  The MMA
+// contracts S (K-major for SIDE 0, MN-major for SIDE 1) with the features
+// (MN-major) into a 128 x BD TMEM accumulator; the epilogue adds 2 A rowsum
+// and stores through TMA.  MN-major TF32 operands are only valid in the
+// 32-byte-granule swizzle (a standard 128-byte-swizzle MN-major descriptor
+// yields no product), so those boxes are loaded with that swizzle.
 
 constexpr int GRAD_THREADS = 320;
-constexpr int GRAD_MAX_STAGES = 4;
-constexpr int SBOX = 128 * 32 * 4;  // one 16 KB slice of dC / C / dQ per stage
+constexpr int GRAD_MAX_LAND = 6;
+constexpr int GRAD_MAX_CONV = 2;
+constexpr int SBOX = 128 * 32 * 4;  // one 16 KB chunk of dC / C / dQ
 
 struct GradShared {
   float rs[2][128];
-  uint64_t full[GRAD_MAX_STAGES], empty[GRAD_MAX_STAGES], conv[GRAD_MAX_STAGES];
+  float red[4][128];  // SIDE 1: per-row-group partial column sums
+  float redv[4][128];
+  uint64_t lfull[GRAD_MAX_LAND], lempty[GRAD_MAX_LAND];
+  uint64_t cfull[GRAD_MAX_CONV], cempty[GRAD_MAX_CONV];
   uint64_t accf[2], acce[2], nfull[2], nempty[2];
   uint64_t mma_done;
   uint32_t tmem_base;
@@ -343,23 +363,37 @@ struct GradShared {
 
 struct GradGeom {
   int nF;           // 32-feature boxes (BD = 32 nF)
-  int stages;
-  int off_dq, off_fh, off_fl, stage_bytes, tx_bytes;
+  int mw;           // positivity-mask words per row: ceil(M / 32)
+  int np;           // mask row count, padded: 4 ceil(N / 4)
+  int lstages, cstages;
+  int l_c, l_dq, l_f, l_mask, l_bytes;  // landing slot layout (dC at 0)
+  int c_bytes;      // converted slot: S hi 0, S lo SBOX, F hi 2 SBOX, F lo 2 SBOX + 4096 nF
+  int tx_fixed;     // landing bytes per chunk other than the mask
   uint32_t tmem_cols;
 };
 
-template <int SIDE, bool VAR>
+__device__ __forceinline__ float4 split4(float4 v, float4& lo) {
+  float4 hi;
+  split_tf32(v.x, hi.x, lo.x);
+  split_tf32(v.y, hi.y, lo.y);
+  split_tf32(v.z, hi.z, lo.z);
+  split_tf32(v.w, hi.w, lo.w);
+  return hi;
+}
+
+template <int SIDE, bool VAR, bool MASKED>
 __global__ void __launch_bounds__(GRAD_THREADS, 1)
     tc_grad_kernel(const __grid_constant__ CUtensorMap mapDC, const __grid_constant__ CUtensorMap mapC,
                    const __grid_constant__ CUtensorMap mapDQ, const __grid_constant__ CUtensorMap mapF,
                    const __grid_constant__ CUtensorMap mapOut, const float* __restrict__ A,
                    const float* __restrict__ va, const float* __restrict__ vb,
                    float* __restrict__ dva, int B, int N, int M, int D, float beta, float eps,
-                   int has_dq, GradGeom g) {
+                   int has_dq, GradGeom g, const uint32_t* __restrict__ mask) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  uint8_t* stage_base = smem;
-  uint8_t* stg_base = smem + (size_t)g.stages * g.stage_bytes;
-  GradShared& sh = *reinterpret_cast<GradShared*>(stg_base + 2 * STG_BYTES);
+  uint8_t* land_base = smem;
+  uint8_t* conv_base = smem + (size_t)g.lstages * g.l_bytes;
+  uint8_t* stg_base = conv_base + (size_t)g.cstages * g.c_bytes;  // one staging buffer
+  GradShared& sh = *reinterpret_cast<GradShared*>(stg_base + STG_BYTES);
   volatile int* abort = &sh.abort;
 
   const int tid = threadIdx.x;
@@ -369,7 +403,7 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
   const int nBlk = (R + 127) / 128, nK = (S + 31) / 32;
   const int total = B * nBlk;
   const int BD = 32 * g.nF;
-  const int stages = g.stages;
+  const int LS = g.lstages, CS = g.cstages;
 
   if (tid == 0) {
     if ((smem_u32(smem) & 1023u) != 0) {
@@ -378,10 +412,13 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
     } else {
       sh.abort = 0;
     }
-    for (int s = 0; s < stages; ++s) {
-      mbar_init(&sh.full[s], 1);
-      mbar_init(&sh.empty[s], 1);
-      mbar_init(&sh.conv[s], 128);
+    for (int s = 0; s < LS; ++s) {
+      mbar_init(&sh.lfull[s], 1);
+      mbar_init(&sh.lempty[s], 128);
+    }
+    for (int s = 0; s < CS; ++s) {
+      mbar_init(&sh.cfull[s], 128);
+      mbar_init(&sh.cempty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&sh.accf[a], 1);
@@ -394,7 +431,7 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
   }
   if (warp == 8 && lane == 0) {
     prefetch_map(&mapDC);
-    prefetch_map(&mapC);
+    if (!MASKED) prefetch_map(&mapC);
     if (VAR && has_dq) prefetch_map(&mapDQ);
     prefetch_map(&mapF);
     prefetch_map(&mapOut);
@@ -412,135 +449,228 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
     for (int u = blockIdx.x; u < total; u += gridDim.x) {
       const int b = u / nBlk, blk = u - b * nBlk;
       for (int kc = 0; kc < nK; ++kc, ++it) {
-        const int s = it % stages;
-        const unsigned ph = (unsigned)(it / stages) & 1u;
-        if (!mbar_wait(&sh.empty[s], ph ^ 1u, abort)) { record_timeout(abort); goto producer_drain; }
-        uint8_t* st = stage_base + (size_t)s * g.stage_bytes;
-        mbar_arrive_expect_tx(&sh.full[s], g.tx_bytes);
+        const int s = it % LS;
+        const unsigned ph = (unsigned)(it / LS) & 1u;
+        if (!mbar_wait(&sh.lempty[s], ph ^ 1u, abort)) { record_timeout(abort); goto producer_drain; }
+        uint8_t* st = land_base + (size_t)s * g.l_bytes;
+        unsigned tx = g.tx_fixed;
+        const uint32_t* msrc[4] = {nullptr, nullptr, nullptr, nullptr};
+        unsigned mbytes[4] = {0, 0, 0, 0};
+        if (MASKED) {
+          // SIDE 0: word row kc, rows blk*128 ..; SIDE 1: word rows blk*4 + q, rows kc*32 ..
+          if (SIDE == 0) {
+            const int r0 = blk * 128, n = min(128, g.np - r0);
+            msrc[0] = mask + ((long long)b * g.mw + kc) * g.np + r0;
+            mbytes[0] = (unsigned)n * 4u;
+          } else {
+            const int r0 = kc * 32, n = min(32, g.np - r0);
+            for (int q = 0; q < 4; ++q) {
+              const int jw = blk * 4 + q;
+              if (jw < g.mw) {
+                msrc[q] = mask + ((long long)b * g.mw + jw) * g.np + r0;
+                mbytes[q] = (unsigned)n * 4u;
+              }
+            }
+          }
+          tx += mbytes[0] + mbytes[1] + mbytes[2] + mbytes[3];
+        }
+        mbar_arrive_expect_tx(&sh.lfull[s], tx);
+        if (MASKED) {
+          for (int q = 0; q < 4; ++q)
+            if (mbytes[q]) bulk_load(st + g.l_mask + q * 128, msrc[q], mbytes[q], &sh.lfull[s]);
+        }
         if (SIDE == 0) {
-          // S slice: 128 rows i x 32 columns j
-          tma_load_3d(st, &mapDC, &sh.full[s], kc * 32, blk * 128, b);
-          tma_load_3d(st + SBOX, &mapC, &sh.full[s], kc * 32, blk * 128, b);
-          if (VAR && has_dq) tma_load_3d(st + g.off_dq, &mapDQ, &sh.full[s], kc * 32, blk * 128, b);
+          // S chunk: 128 rows i x 32 columns j
+          tma_load_3d(st, &mapDC, &sh.lfull[s], kc * 32, blk * 128, b);
+          if (!MASKED) tma_load_3d(st + g.l_c, &mapC, &sh.lfull[s], kc * 32, blk * 128, b);
+          if (VAR && has_dq) tma_load_3d(st + g.l_dq, &mapDQ, &sh.lfull[s], kc * 32, blk * 128, b);
         } else {
-          // S slice: 32 rows i x 128 columns j, as four 32 x 32 boxes
+          // S chunk: 32 rows i x 128 columns j, as four 32 x 32 boxes
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            tma_load_3d(st + q * 4096, &mapDC, &sh.full[s], blk * 128 + 32 * q, kc * 32, b);
-            tma_load_3d(st + SBOX + q * 4096, &mapC, &sh.full[s], blk * 128 + 32 * q, kc * 32, b);
+            const int x = blk * 128 + 32 * q;
+            tma_load_3d(st + q * 4096, &mapDC, &sh.lfull[s], x, kc * 32, b);
+            if (!MASKED) tma_load_3d(st + g.l_c + q * 4096, &mapC, &sh.lfull[s], x, kc * 32, b);
             if (VAR && has_dq)
-              tma_load_3d(st + g.off_dq + q * 4096, &mapDQ, &sh.full[s], blk * 128 + 32 * q,
-                          kc * 32, b);
+              tma_load_3d(st + g.l_dq + q * 4096, &mapDQ, &sh.lfull[s], x, kc * 32, b);
           }
         }
         // the other side's features: 32 summed rows x BD features
         for (int f = 0; f < g.nF; ++f)
-          tma_load_3d(st + g.off_fh + f * 4096, &mapF, &sh.full[s], 32 * f, kc * 32, b);
+          tma_load_3d(st + g.l_f + f * 4096, &mapF, &sh.lfull[s], 32 * f, kc * 32, b);
       }
     }
   producer_drain:
-    for (int k = (it > stages ? it - stages : 0); k < it; ++k) {
-      const int s = k % stages;
+    // every load issued lands before the CTA exits
+    for (int k = (it > LS ? it - LS : 0); k < it; ++k) {
+      const int s = k % LS;
       for (unsigned n = 0; n < kSpinLimit; ++n)
-        if (mbar_try_wait(&sh.full[s], (unsigned)(k / stages) & 1u)) break;
+        if (mbar_try_wait(&sh.lfull[s], (unsigned)(k / LS) & 1u)) break;
     }
   } else if (!dead && warp >= 4 && warp < 8) {
     // ------------------------------------------------ S = dsq, split, sums
     const int ct = tid - 128;
+    const int rg = ct >> 5;          // SIDE 1: row group (8 of the 32 chunk rows)
+    const int cq = ct & 31;          // SIDE 1: column quad (4 consecutive columns)
     int it = 0, ti = 0;
-    for (int u = blockIdx.x; u < total; u += gridDim.x, ++ti) {
+    bool ok = true;
+    for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++ti) {
       const int b = u / nBlk, blk = u - b * nBlk;
-      const int r = blk * 128 + ct;  // own row (i for SIDE 0, j for SIDE 1)
-      const float va_r = VAR ? (r < R ? va[(long long)b * R + r] : 1.f) : 0.f;
+      // SIDE 0: thread ct owns row r = blk*128 + ct.  SIDE 1: thread owns the
+      // 4 columns j = blk*128 + 4 cq + e of rows rg*8 .. rg*8+7 of each chunk.
+      float va_r[4] = {0.f, 0.f, 0.f, 0.f};
       const float* vb_b = VAR ? vb + (long long)b * S : nullptr;
-      float rsum = 0.f, vsum = 0.f;
-      for (int kc = 0; kc < nK; ++kc, ++it) {
-        const int s = it % stages;
-        const unsigned ph = (unsigned)(it / stages) & 1u;
-        if (!mbar_wait(&sh.full[s], ph, abort)) { record_timeout(abort); goto split_done; }
-        uint8_t* st = stage_base + (size_t)s * g.stage_bytes;
-        uint8_t* dcb = st;
-        uint8_t* cb = st + SBOX;
-        uint8_t* dqb = st + g.off_dq;
+      if (VAR) {
         if (SIDE == 0) {
+          const int r = blk * 128 + ct;
+          va_r[0] = r < R ? va[(long long)b * R + r] : 1.f;
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int j = blk * 128 + 4 * cq + e;
+            va_r[e] = j < R ? va[(long long)b * R + j] : 1.f;
+          }
+        }
+      }
+      float rsum[4] = {0.f, 0.f, 0.f, 0.f}, vsum[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int kc = 0; kc < nK; ++kc, ++it) {
+        const int s = it % LS, cs = it % CS;
+        if (!mbar_wait(&sh.lfull[s], (unsigned)(it / LS) & 1u, abort) ||
+            !mbar_wait(&sh.cempty[cs], ((unsigned)(it / CS) & 1u) ^ 1u, abort)) {
+          record_timeout(abort);
+          ok = false;
+          break;
+        }
+        const uint8_t* ld = land_base + (size_t)s * g.l_bytes;
+        uint8_t* cv = conv_base + (size_t)cs * g.c_bytes;
+        if (SIDE == 0) {
+          const uint32_t mword =
+              MASKED ? reinterpret_cast<const uint32_t*>(ld + g.l_mask)[ct] : 0u;
 #pragma unroll 2
           for (int q = 0; q < 8; ++q) {
             const uint32_t off = sw128_chunk(ct, q);
-            const float4 g4 = *reinterpret_cast<const float4*>(dcb + off);
-            const float4 c4 = *reinterpret_cast<const float4*>(cb + off);
+            const float4 g4 = *reinterpret_cast<const float4*>(ld + off);
+            float ce[4];
+            if (MASKED) {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) ce[e] = (mword >> (4 * q + e)) & 1u ? 1.f : 0.f;
+            } else {
+              const float4 c4 = *reinterpret_cast<const float4*>(ld + g.l_c + off);
+              ce[0] = c4.x; ce[1] = c4.y; ce[2] = c4.z; ce[3] = c4.w;
+            }
             float4 q4 = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (VAR && has_dq) q4 = *reinterpret_cast<const float4*>(dqb + off);
-            const float ge[4] = {g4.x, g4.y, g4.z, g4.w}, ce[4] = {c4.x, c4.y, c4.z, c4.w},
-                        qe[4] = {q4.x, q4.y, q4.z, q4.w};
-            float he[4], le[4];
+            if (VAR && has_dq) q4 = *reinterpret_cast<const float4*>(ld + g.l_dq + off);
+            const float ge[4] = {g4.x, g4.y, g4.z, g4.w}, qe[4] = {q4.x, q4.y, q4.z, q4.w};
+            float sv[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               float var = 1.f, var_raw = 1.f;
               if (VAR) {
                 const int j = kc * 32 + 4 * q + e;
-                var_raw = 0.5f * (va_r + (j < S ? __ldg(vb_b + j) : 1.f));
+                var_raw = 0.5f * (va_r[0] + (j < S ? __ldg(vb_b + j) : 1.f));
                 var = var_raw > eps ? var_raw : eps;
               }
-              const float sv = ce[e] > 0.f ? (VAR ? ge[e] / var : ge[e]) : 0.f;
-              rsum += sv;
-              if (VAR && var_raw > eps) vsum += (beta * qe[e] - ge[e] * ce[e]) / var;
-              split_tf32(sv, he[e], le[e]);
+              sv[e] = ce[e] > 0.f ? (VAR ? ge[e] / var : ge[e]) : 0.f;
+              rsum[0] += sv[e];
+              if (VAR && var_raw > eps) vsum[0] += (beta * qe[e] - ge[e] * ce[e]) / var;
             }
-            *reinterpret_cast<float4*>(dcb + off) = make_float4(he[0], he[1], he[2], he[3]);
-            *reinterpret_cast<float4*>(cb + off) = make_float4(le[0], le[1], le[2], le[3]);
+            float4 lo;
+            const float4 hi = split4(make_float4(sv[0], sv[1], sv[2], sv[3]), lo);
+            *reinterpret_cast<float4*>(cv + off) = hi;
+            *reinterpret_cast<float4*>(cv + SBOX + off) = lo;
           }
         } else {
-          const int box = ct >> 5, w = ct & 31;
-#pragma unroll 4
-          for (int rr = 0; rr < 32; ++rr) {
-            const uint32_t off = box * 4096 + sw128b32_elem(rr, w);
-            const float gv = *reinterpret_cast<const float*>(dcb + off);
-            const float cv = *reinterpret_cast<const float*>(cb + off);
-            const float qv = (VAR && has_dq) ? *reinterpret_cast<const float*>(dqb + off) : 0.f;
-            float var = 1.f, var_raw = 1.f;
+          // 4 columns (one 16-byte piece of a 32-byte granule) of 8 rows
+          const int box = cq >> 3, gq = (cq & 7) >> 1, half = cq & 1;
+          const int jw = blk * 4 + box;
+#pragma unroll 2
+          for (int k8 = 0; k8 < 8; ++k8) {
+            const int rr = rg * 8 + k8;
+            const uint32_t off =
+                box * 4096 + rr * 128 + (uint32_t)(((gq ^ (rr & 3)) << 5) + half * 16);
+            const float4 g4 = *reinterpret_cast<const float4*>(ld + off);
+            float ce[4];
+            if (MASKED) {
+              const uint32_t w = (jw < g.mw)
+                                     ? reinterpret_cast<const uint32_t*>(ld + g.l_mask)[box * 32 + rr]
+                                     : 0u;
+#pragma unroll
+              for (int e = 0; e < 4; ++e) ce[e] = (w >> (4 * (cq & 7) + e)) & 1u ? 1.f : 0.f;
+            } else {
+              const float4 c4 = *reinterpret_cast<const float4*>(ld + g.l_c + off);
+              ce[0] = c4.x; ce[1] = c4.y; ce[2] = c4.z; ce[3] = c4.w;
+            }
+            float4 q4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (VAR && has_dq) q4 = *reinterpret_cast<const float4*>(ld + g.l_dq + off);
+            const float ge[4] = {g4.x, g4.y, g4.z, g4.w}, qe[4] = {q4.x, q4.y, q4.z, q4.w};
+            float vbi = 0.f;
             if (VAR) {
               const int i = kc * 32 + rr;
-              var_raw = 0.5f * ((i < S ? __ldg(vb_b + i) : 1.f) + va_r);
-              var = var_raw > eps ? var_raw : eps;
+              vbi = i < S ? __ldg(vb_b + i) : 1.f;
             }
-            const float sv = cv > 0.f ? (VAR ? gv / var : gv) : 0.f;
-            rsum += sv;
-            if (VAR && var_raw > eps) vsum += (beta * qv - gv * cv) / var;
-            float h, l;
-            split_tf32(sv, h, l);
-            *reinterpret_cast<float*>(dcb + off) = h;
-            *reinterpret_cast<float*>(cb + off) = l;
+            float sv[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              float var = 1.f, var_raw = 1.f;
+              if (VAR) {
+                var_raw = 0.5f * (vbi + va_r[e]);
+                var = var_raw > eps ? var_raw : eps;
+              }
+              sv[e] = ce[e] > 0.f ? (VAR ? ge[e] / var : ge[e]) : 0.f;
+              rsum[e] += sv[e];
+              if (VAR && var_raw > eps) vsum[e] += (beta * qe[e] - ge[e] * ce[e]) / var;
+            }
+            float4 lo;
+            const float4 hi = split4(make_float4(sv[0], sv[1], sv[2], sv[3]), lo);
+            *reinterpret_cast<float4*>(cv + off) = hi;
+            *reinterpret_cast<float4*>(cv + SBOX + off) = lo;
           }
         }
         // the other side's features: elementwise split of the whole slab
         {
-          float4* fh = reinterpret_cast<float4*>(st + g.off_fh);
-          float4* fl = reinterpret_cast<float4*>(st + g.off_fl);
+          const float4* fr = reinterpret_cast<const float4*>(ld + g.l_f);
+          float4* fh = reinterpret_cast<float4*>(cv + 2 * SBOX);
+          float4* fl = reinterpret_cast<float4*>(cv + 2 * SBOX + g.nF * 4096);
           const int n4 = g.nF * 256;
           for (int k = ct; k < n4; k += 128) {
-            const float4 v = fh[k];
-            float4 h, l;
-            split_tf32(v.x, h.x, l.x);
-            split_tf32(v.y, h.y, l.y);
-            split_tf32(v.z, h.z, l.z);
-            split_tf32(v.w, h.w, l.w);
-            fh[k] = h;
-            fl[k] = l;
+            float4 lo;
+            fh[k] = split4(fr[k], lo);
+            fl[k] = lo;
           }
         }
+        mbar_arrive(&sh.lempty[s]);   // landing slot read completely
         fence_async_smem();
-        mbar_arrive(&sh.conv[s]);
+        mbar_arrive(&sh.cfull[cs]);
       }
-      if (VAR && dva != nullptr && r < R) dva[(long long)b * R + r] = 0.5f * vsum;
       const int a = ti & 1;
+      float rfin, vfin;
+      if (SIDE == 0) {
+        if (!ok) break;
+        rfin = rsum[0];
+        vfin = vsum[0];
+      } else {
+        // combine the four row groups' partial column sums: thread ct ends
+        // with column j = blk*128 + ct (the four warps decide together)
+        if (named_bar_or(2, 128, !ok)) break;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          sh.red[rg][4 * cq + e] = rsum[e];
+          if (VAR) sh.redv[rg][4 * cq + e] = vsum[e];
+        }
+        named_bar(2, 128);
+        rfin = (sh.red[0][ct] + sh.red[1][ct]) + (sh.red[2][ct] + sh.red[3][ct]);
+        vfin = VAR ? (sh.redv[0][ct] + sh.redv[1][ct]) + (sh.redv[2][ct] + sh.redv[3][ct]) : 0.f;
+        named_bar(2, 128);
+      }
+      const int r = blk * 128 + ct;
+      if (VAR && dva != nullptr && r < R) dva[(long long)b * R + r] = 0.5f * vfin;
       if (!mbar_wait(&sh.nempty[a], ((unsigned)(ti >> 1) & 1u) ^ 1u, abort)) {
         record_timeout(abort);
-        goto split_done;
+        break;
       }
-      sh.rs[a][ct] = rsum;
+      sh.rs[a][ct] = rfin;
       mbar_arrive(&sh.nfull[a]);
     }
-  split_done:;
   } else if (!dead && warp == 9) {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
@@ -556,12 +686,15 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
         const uint32_t d_tmem = tmem + (uint32_t)(a * BD);
         bool ok = true;
         for (int kc = 0; kc < nK; ++kc, ++it) {
-          const int s = it % stages;
-          const unsigned ph = (unsigned)(it / stages) & 1u;
-          if (!mbar_wait(&sh.conv[s], ph, abort)) { record_timeout(abort); ok = false; break; }
+          const int cs = it % CS;
+          if (!mbar_wait(&sh.cfull[cs], (unsigned)(it / CS) & 1u, abort)) {
+            record_timeout(abort);
+            ok = false;
+            break;
+          }
           tc_fence_after();
-          const uint32_t st = smem_u32(stage_base + (size_t)s * g.stage_bytes);
-          const uint32_t ah = st, al = st + SBOX, fh = st + g.off_fh, fl = st + g.off_fl;
+          const uint32_t st = smem_u32(conv_base + (size_t)cs * g.c_bytes);
+          const uint32_t ah = st, al = st + SBOX, fh = st + 2 * SBOX, fl = fh + g.nF * 4096;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             uint64_t dah, dal;
@@ -578,7 +711,7 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
             mma_tf32(d_tmem, dah, dbl, idesc, 1);
             mma_tf32(d_tmem, dah, dbh, idesc, 1);
           }
-          mma_commit(&sh.empty[s]);
+          mma_commit(&sh.cempty[cs]);
         }
         if (!ok) break;
         mma_commit(&sh.accf[a]);
@@ -590,7 +723,7 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
     __syncwarp();
   } else if (!dead && warp < 4) {
     // ------------------------------------------------ epilogue
-    int ti = 0, si = 0;
+    int ti = 0;
     for (int u = blockIdx.x; u < total; u += gridDim.x, ++ti) {
       const int b = u / nBlk, blk = u - b * nBlk;
       const int a = ti & 1;
@@ -621,8 +754,8 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
           v[4 * q4 + 2] = -2.f * v[4 * q4 + 2] + x.z * rs2;
           v[4 * q4 + 3] = -2.f * v[4 * q4 + 3] + x.w * rs2;
         }
-        uint8_t* buf = stg_base + (size_t)(si & 1) * STG_BYTES;
-        if (tid == 0) bulk_wait_read<1>();
+        uint8_t* buf = stg_base;
+        if (tid == 0) bulk_wait_read<0>();   // the previous store has read the buffer
         named_bar(1, 128);
 #pragma unroll
         for (int q4 = 0; q4 < 8; ++q4)
@@ -634,7 +767,6 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
           tma_store_3d(&mapOut, buf, 32 * cc, blk * 128, b);
           bulk_commit();
         }
-        ++si;
       }
     }
     if (tid == 0) bulk_wait_all();
@@ -720,7 +852,8 @@ bool tc_cost_eligible(const float* X, const float* Y, const float* vx, const flo
 }
 
 int tc_cost_f32(const float* X, const float* Y, const float* vx, const float* vy, int B, int N,
-                int M, int D, double beta, double eps, float* C, float* Q, cudaStream_t st) {
+                int M, int D, double beta, double eps, float* C, float* Q, uint32_t* mask,
+                cudaStream_t st) {
   if (B == 0 || N == 0 || M == 0) return kOk;
   CUtensorMap mX, mY, mC, mQ;
   int rc;
@@ -735,7 +868,7 @@ int tc_cost_f32(const float* X, const float* Y, const float* vx, const float* vy
   auto kern = var ? tc_cost_kernel<true> : tc_cost_kernel<false>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)COST_SMEM);
   kern<<<grid, COST_THREADS, COST_SMEM, st>>>(mX, mY, mC, mQ, vx, vy, B, N, M, D, (float)beta,
-                                              (float)eps, Q != nullptr ? 1 : 0);
+                                              (float)eps, Q != nullptr ? 1 : 0, mask);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(kLaunch, "tc cost launch: %s", cudaGetErrorString(e));
   return kOk;
@@ -743,10 +876,11 @@ int tc_cost_f32(const float* X, const float* Y, const float* vx, const float* vy
 
 namespace {
 
-template <int SIDE, bool VAR>
+template <int SIDE, bool VAR, bool MASKED = false>
 int grad_side(const float* A, const float* F, const float* va, const float* vb, const float* C,
               const float* dC, const float* dQ, int B, int N, int M, int D, double beta,
-              double eps, float* dA, float* dva, cudaStream_t st) {
+              double eps, float* dA, float* dva, cudaStream_t st,
+              const uint32_t* mask = nullptr) {
   const int R = SIDE == 0 ? N : M, S = SIDE == 0 ? M : N;
   CUtensorMap mDC, mC, mDQ, mF, mOut;
   int rc;
@@ -755,7 +889,8 @@ int grad_side(const float* A, const float* F, const float* va, const float* vb, 
   const uint32_t sbox_rows = SIDE == 0 ? 128 : 32;
   const bool s_g32 = SIDE == 1;
   if ((rc = make_map_3d_f32(&mDC, dC, M, N, B, 32, sbox_rows, s_g32)) != kOk) return rc;
-  if ((rc = make_map_3d_f32(&mC, C, M, N, B, 32, sbox_rows, s_g32)) != kOk) return rc;
+  mC = mDC;  // C is not read when the positivity mask replaces it
+  if (!MASKED && (rc = make_map_3d_f32(&mC, C, M, N, B, 32, sbox_rows, s_g32)) != kOk) return rc;
   mDQ = mC;
   const bool has_dq = VAR && dQ != nullptr;
   if (has_dq && (rc = make_map_3d_f32(&mDQ, dQ, M, N, B, 32, sbox_rows, s_g32)) != kOk) return rc;
@@ -763,25 +898,42 @@ int grad_side(const float* A, const float* F, const float* va, const float* vb, 
   if ((rc = make_map_3d_f32(&mOut, dA, D, R, B, 32, 128)) != kOk) return rc;
   GradGeom g;
   g.nF = (D + 31) / 32;
-  g.off_dq = 2 * SBOX;
-  g.off_fh = (VAR ? 3 : 2) * SBOX;
-  g.off_fl = g.off_fh + g.nF * 4096;
-  g.stage_bytes = g.off_fl + g.nF * 4096;
-  g.tx_bytes = 2 * SBOX + (has_dq ? SBOX : 0) + g.nF * 4096;
-  const int avail = 232448 - 2 * STG_BYTES - (int)sizeof(GradShared);
-  g.stages = avail / g.stage_bytes;
-  if (g.stages > GRAD_MAX_STAGES) g.stages = GRAD_MAX_STAGES;
-  if (g.stages < 1) return set_error(kUnsupported, "tc grad: D=%d needs too much shared memory", D);
+  g.mw = (M + 31) / 32;
+  g.np = (N + 3) & ~3;
+  if (MASKED && ((uintptr_t)mask & 15u) != 0)
+    return set_error(kUnsupported, "tc grad: mask not 16-byte aligned");
+  int off = SBOX;                       // dC at 0
+  g.l_c = MASKED ? -1 : off;
+  if (!MASKED) off += SBOX;
+  g.l_dq = has_dq ? off : -1;
+  if (has_dq) off += SBOX;
+  g.l_f = off;
+  off += g.nF * 4096;
+  g.l_mask = off;
+  if (MASKED) off += 512;
+  g.l_bytes = (off + 1023) & ~1023;
+  g.tx_fixed = SBOX * (MASKED ? 1 : 2) + (has_dq ? SBOX : 0) + g.nF * 4096;
+  g.c_bytes = 2 * SBOX + 2 * g.nF * 4096;
+  const int budget = 232448 - STG_BYTES - (int)sizeof(GradShared);
+  g.cstages = GRAD_MAX_CONV;
+  g.lstages = (budget - g.cstages * g.c_bytes) / g.l_bytes;
+  if (g.lstages < 2) {
+    g.cstages = 1;
+    g.lstages = (budget - g.c_bytes) / g.l_bytes;
+  }
+  if (g.lstages > GRAD_MAX_LAND) g.lstages = GRAD_MAX_LAND;
+  if (g.lstages < 1) return set_error(kUnsupported, "tc grad: D=%d needs too much shared memory", D);
   uint32_t cols = 32;
   while (cols < (uint32_t)(2 * 32 * g.nF)) cols <<= 1;
   g.tmem_cols = cols;
-  const size_t smem = (size_t)g.stages * g.stage_bytes + 2 * STG_BYTES + sizeof(GradShared);
+  const size_t smem = (size_t)g.lstages * g.l_bytes + (size_t)g.cstages * g.c_bytes +
+                      STG_BYTES + sizeof(GradShared);
   const long long units = (long long)B * ((R + 127) / 128);
   const int grid = (int)(units < sm_count() ? units : sm_count());
-  auto kern = tc_grad_kernel<SIDE, VAR>;
+  auto kern = tc_grad_kernel<SIDE, VAR, MASKED>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   kern<<<grid, GRAD_THREADS, smem, st>>>(mDC, mC, mDQ, mF, mOut, A, va, vb, dva, B, N, M, D,
-                                         (float)beta, (float)eps, has_dq ? 1 : 0, g);
+                                         (float)beta, (float)eps, has_dq ? 1 : 0, g, mask);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(kLaunch, "tc grad launch: %s", cudaGetErrorString(e));
   return kOk;
@@ -812,6 +964,19 @@ int tc_grad_f32(const float* X, const float* Y, const float* vx, const float* vy
     return rc;
   return grad_side<1, false>(Y, X, nullptr, nullptr, C, dC, nullptr, B, N, M, D, beta, eps, dY,
                              nullptr, st);
+}
+
+// Squared-Euclidean chain rule with the positivity mask of the cost kernel in
+// place of the cost: S = dC where sq_raw > 0.
+int tc_sq_grad_f32(const float* X, const float* Y, const uint32_t* mask, const float* dC, int B,
+                   int N, int M, int D, float* dX, float* dY, cudaStream_t st) {
+  if (B == 0 || N == 0 || M == 0) return kOk;
+  int rc;
+  if ((rc = grad_side<0, false, true>(X, Y, nullptr, nullptr, nullptr, dC, nullptr, B, N, M, D,
+                                      0.0, 1e-8, dX, nullptr, st, mask)))
+    return rc;
+  return grad_side<1, false, true>(Y, X, nullptr, nullptr, nullptr, dC, nullptr, B, N, M, D, 0.0,
+                                   1e-8, dY, nullptr, st, mask);
 }
 
 }  // namespace tw

@@ -15,7 +15,7 @@ import torch.nn as nn
 
 from .udtw import _ops as _udtw_ops
 from .udtw.functional import (_BACKENDS, _check_backend, _check_band_reached, _float,
-                              _udtw_fused, udtw_from_cost)
+                              _sdtw_fused, udtw_from_cost)
 
 
 def softmin(x: torch.Tensor, gamma: float, dim: Optional[int] = None) -> torch.Tensor:
@@ -102,7 +102,7 @@ def soft_dtw(X: torch.Tensor, Y: torch.Tensor, *, gamma: float = 1.0, normalize:
             if A.shape[1] == 0 or Bq.shape[1] == 0:
                 raise ValueError("sequence lengths must be non-zero")
             # unit variance, no penalty: cost = max(|x|^2 + |y|^2 - 2 x.y, 0)
-            return _udtw_fused(A, Bq, None, None, 0.0, gamma, bandwidth, 1e-8).distance
+            return _sdtw_fused(A, Bq, gamma, bandwidth)
         cost = dist_func(A, Bq)
         return udtw_from_cost(cost, torch.zeros_like(cost), gamma=gamma, bandwidth=bandwidth,
                               backend=backend).distance

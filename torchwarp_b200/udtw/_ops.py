@@ -17,6 +17,11 @@ implementation:
   the features, then the DP.  ``vx``/``vy`` None means unit variance and no
   penalty (soft-DTW).
 * ``torchwarp_b200::udtw_fused_backward(...)`` -> (dX, dY, dvx, dvy).
+* ``torchwarp_b200::sdtw_fused(X, Y, gamma, bandwidth)`` -> (out_r, saved,
+  mask) and ``sdtw_fused_backward(X, Y, mask, saved, grad_r, gamma)`` ->
+  (dX, dY): soft-DTW on features.  The backward keeps the cost's positivity
+  mask (1 bit per cell) instead of the cost, which is freed after the DP
+  forward.
 
 Each op has a fake (meta) implementation for torch.compile, a vmap rule that
 folds the vmapped dimension into the batch, and runs in float32 under
@@ -212,6 +217,73 @@ _register_autocast(udtw_fused)
 _register_autocast(udtw_fused_backward)
 
 
+# ----------- soft-DTW from features: positivity mask instead of the saved cost
+
+def _mask_words(M):
+    return (M + 31) // 32
+
+
+def _mask_rows(N):
+    return (N + 3) // 4 * 4
+
+
+@torch.library.custom_op("torchwarp_b200::sdtw_fused", mutates_args=())
+def sdtw_fused(X: Tensor, Y: Tensor, gamma: float, bandwidth: float) -> Tuple[Tensor, Tensor,
+                                                                              Tensor]:
+    """soft-DTW on features: squared-Euclidean cost (tw_sqeuclid_cost) and the
+    DP forward.  Returns (out_r [B], saved, mask [B, ceil(M/32), N] int32).
+    The cost itself is dropped when the op returns: the backward needs only
+    the saved stream and the cost's positivity mask."""
+    nat.require_cuda(X, Y)
+    B, N, D = X.shape
+    M = Y.shape[1]
+    X, Y = X.contiguous(), Y.contiguous()
+    cost = X.new_empty(B, N, M)
+    mask = torch.empty(B, _mask_words(M), _mask_rows(N), dtype=torch.int32, device=X.device)
+    if B:
+        with torch.cuda.device(X.device):
+            fn = getattr(nat.lib(), "tw_sqeuclid_cost_" + nat.suffix(X.dtype))
+            nat.check(nat.call("udtw_cost", fn, nat.ptr(X), nat.ptr(Y), B, N, M, D,
+                               nat.ptr(cost), nat.ptr(mask), nat.stream_of(X)),
+                      "tw_sqeuclid_cost")
+    out_r, _, saved = _dp_forward(cost, None, gamma, bandwidth)
+    return out_r, saved, mask
+
+
+@sdtw_fused.register_fake
+def _(X, Y, gamma, bandwidth):
+    B, N, M = X.shape[0], X.shape[1], Y.shape[1]
+    nbytes = _saved_bytes(B, N, M, X.dtype, False) if B else 0
+    return (X.new_empty(B), X.new_empty(nbytes, dtype=torch.uint8),
+            X.new_empty(B, _mask_words(M), _mask_rows(N), dtype=torch.int32))
+
+
+@torch.library.custom_op("torchwarp_b200::sdtw_fused_backward", mutates_args=())
+def sdtw_fused_backward(X: Tensor, Y: Tensor, mask: Tensor, saved: Tensor, grad_r: Tensor,
+                        gamma: float) -> Tuple[Tensor, Tensor]:
+    B, N, D = X.shape
+    M = Y.shape[1]
+    d_cost, _ = _dp_backward(saved, grad_r, grad_r, N, M, gamma, False)
+    X, Y = X.contiguous(), Y.contiguous()
+    dX, dY = torch.empty_like(X), torch.empty_like(Y)
+    if B:
+        with torch.cuda.device(X.device):
+            fn = getattr(nat.lib(), "tw_sqeuclid_grad_" + nat.suffix(X.dtype))
+            nat.check(nat.call("udtw_features_grad", fn, nat.ptr(X), nat.ptr(Y), nat.ptr(mask),
+                               nat.ptr(d_cost), B, N, M, D, nat.ptr(dX), nat.ptr(dY),
+                               nat.stream_of(X)), "tw_sqeuclid_grad")
+    return dX, dY
+
+
+@sdtw_fused_backward.register_fake
+def _(X, Y, mask, saved, grad_r, gamma):
+    return torch.empty_like(X), torch.empty_like(Y)
+
+
+_register_autocast(sdtw_fused)
+_register_autocast(sdtw_fused_backward)
+
+
 # ------------------------------------------------------- autograd Functions
 
 def _zeros_if_none(g, like, B):
@@ -275,6 +347,34 @@ class Fused(torch.autograd.Function):
                                                eps)
         has_p = vx is not None
         return dX, dY, (dvx if has_p else None), (dvy if has_p else None), None, None, None, None
+
+
+class SdtwFused(torch.autograd.Function):
+    """(X, Y) -> (distance, saved, mask): soft-DTW with squared-Euclidean cost."""
+
+    @staticmethod
+    def forward(X, Y, gamma, bandwidth):
+        return sdtw_fused(X, Y, gamma, bandwidth)
+
+    @staticmethod
+    def setup_context(ctx, inputs, output):
+        X, Y, gamma, bandwidth = inputs
+        ctx.mark_non_differentiable(output[1], output[2])
+        ctx.set_materialize_grads(False)
+        ctx.save_for_backward(X, Y, output[2], output[1])
+        ctx.gamma = gamma
+
+    @staticmethod
+    @torch.autograd.function.once_differentiable
+    def backward(ctx, g_r, _g_saved, _g_mask):
+        X, Y, mask, saved = ctx.saved_tensors
+        g_r = _zeros_if_none(g_r, X, X.shape[0])
+        dX, dY = sdtw_fused_backward(X, Y, mask, saved, g_r, ctx.gamma)
+        return dX, dY, None, None
+
+
+def sdtw_fused_apply(X, Y, gamma, bandwidth):
+    return SdtwFused.apply(X, Y, gamma, bandwidth)
 
 
 def dp_apply(cost, penalty, gamma, bandwidth):

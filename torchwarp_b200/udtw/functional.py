@@ -156,6 +156,20 @@ def _udtw_fused(X, Y, sigma_x, sigma_y, beta, gamma, bandwidth, eps):
     return UDTWOutput(distance, pen)
 
 
+def _sdtw_fused(X, Y, gamma, bandwidth):
+    """soft-DTW distance with the squared-Euclidean cost built natively (uDTW
+    with unit variance and no penalty, sdtw.py:78-84); the backward keeps the
+    cost's positivity mask instead of the cost."""
+    if X.shape[1] > Y.shape[1]:
+        X, Y = Y, X
+    dtype = X.dtype if X.dtype in (torch.float32, torch.float64) else torch.float32
+    X, Y = X.to(dtype), Y.to(dtype)
+    band = 0.0 if bandwidth is None else float(bandwidth)
+    distance, _, _ = _ops.sdtw_fused_apply(X, Y, float(gamma), band)
+    _check_band_reached(distance, band)
+    return distance
+
+
 def udtw(X, Y, sigma_x, sigma_y, *, beta=1.0, gamma=1.0, normalize=False, bandwidth=None,
          method="gemm", eps=1e-8, backend="auto"):
     """Uncertainty-DTW between two batches of sequences.
