@@ -344,15 +344,19 @@ __global__ void __launch_bounds__(COST_THREADS, 1)
 // 32-byte-granule swizzle (a standard 128-byte-swizzle MN-major descriptor
 // yields no product), so those boxes are loaded with that swizzle.
 
-constexpr int GRAD_THREADS = 320;
+// Warp roles: 0-3 epilogue (TMEM lanes 32 w ..), 4-11 split, 12 TMA, 13 MMA.
+constexpr int GRAD_CONV = 256;            // split threads
+constexpr int GRAD_PROD_WARP = 4 + GRAD_CONV / 32;
+constexpr int GRAD_MMA_WARP = GRAD_PROD_WARP + 1;
+constexpr int GRAD_THREADS = 32 * (GRAD_MMA_WARP + 1);
 constexpr int GRAD_MAX_LAND = 6;
 constexpr int GRAD_MAX_CONV = 2;
 constexpr int SBOX = 128 * 32 * 4;  // one 16 KB chunk of dC / C / dQ
 
 struct GradShared {
   float rs[2][128];
-  float red[4][128];  // SIDE 1: per-row-group partial column sums
-  float redv[4][128];
+  float red[8][128];  // partial row / column sums of the split threads
+  float redv[8][128];
   uint64_t lfull[GRAD_MAX_LAND], lempty[GRAD_MAX_LAND];
   uint64_t cfull[GRAD_MAX_CONV], cempty[GRAD_MAX_CONV];
   uint64_t accf[2], acce[2], nfull[2], nempty[2];
@@ -414,10 +418,10 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
     }
     for (int s = 0; s < LS; ++s) {
       mbar_init(&sh.lfull[s], 1);
-      mbar_init(&sh.lempty[s], 128);
+      mbar_init(&sh.lempty[s], GRAD_CONV);
     }
     for (int s = 0; s < CS; ++s) {
-      mbar_init(&sh.cfull[s], 128);
+      mbar_init(&sh.cfull[s], GRAD_CONV);
       mbar_init(&sh.cempty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -429,21 +433,21 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
     mbar_init(&sh.mma_done, 1);
     fence_barrier_init();
   }
-  if (warp == 8 && lane == 0) {
+  if (warp == GRAD_PROD_WARP && lane == 0) {
     prefetch_map(&mapDC);
     if (!MASKED) prefetch_map(&mapC);
     if (VAR && has_dq) prefetch_map(&mapDQ);
     prefetch_map(&mapF);
     prefetch_map(&mapOut);
   }
-  if (warp == 9) tmem_alloc(&sh.tmem_base, g.tmem_cols);
+  if (warp == GRAD_MMA_WARP) tmem_alloc(&sh.tmem_base, g.tmem_cols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sh.tmem_base;
   const bool dead = sh.abort != 0;
 
-  if (!dead && warp == 8 && lane == 0) {
+  if (!dead && warp == GRAD_PROD_WARP && lane == 0) {
     // ------------------------------------------------ TMA producer
     int it = 0;
     for (int u = blockIdx.x; u < total; u += gridDim.x) {
@@ -507,22 +511,26 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
       for (unsigned n = 0; n < kSpinLimit; ++n)
         if (mbar_try_wait(&sh.lfull[s], (unsigned)(k / LS) & 1u)) break;
     }
-  } else if (!dead && warp >= 4 && warp < 8) {
+  } else if (!dead && warp >= 4 && warp < GRAD_PROD_WARP) {
     // ------------------------------------------------ S = dsq, split, sums
+    // SIDE 0: thread ct owns row (ct & 127) of the 128-row chunk, 16-byte
+    // pieces 4h .. 4h+3 of its 128-byte line (h = ct >> 7).
+    // SIDE 1: thread ct owns the 4 columns 4 cq .. 4 cq + 3 (cq = ct & 31) of
+    // the chunk rows 4 rg .. 4 rg + 3 (rg = ct >> 5).
+    // Partial sums meet in shared memory at the end of a unit; thread
+    // ct < 128 then holds the sums of gradient row ct.
     const int ct = tid - 128;
-    const int rg = ct >> 5;          // SIDE 1: row group (8 of the 32 chunk rows)
-    const int cq = ct & 31;          // SIDE 1: column quad (4 consecutive columns)
+    const int h = ct >> 7, row = ct & 127;
+    const int rg = ct >> 5, cq = ct & 31;
     int it = 0, ti = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++ti) {
+    for (int u = blockIdx.x; u < total; u += gridDim.x, ++ti) {
       const int b = u / nBlk, blk = u - b * nBlk;
-      // SIDE 0: thread ct owns row r = blk*128 + ct.  SIDE 1: thread owns the
-      // 4 columns j = blk*128 + 4 cq + e of rows rg*8 .. rg*8+7 of each chunk.
       float va_r[4] = {0.f, 0.f, 0.f, 0.f};
       const float* vb_b = VAR ? vb + (long long)b * S : nullptr;
       if (VAR) {
         if (SIDE == 0) {
-          const int r = blk * 128 + ct;
+          const int r = blk * 128 + row;
           va_r[0] = r < R ? va[(long long)b * R + r] : 1.f;
         } else {
 #pragma unroll
@@ -533,7 +541,7 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
         }
       }
       float rsum[4] = {0.f, 0.f, 0.f, 0.f}, vsum[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int kc = 0; kc < nK; ++kc, ++it) {
+      for (int kc = 0; kc < nK && ok; ++kc, ++it) {
         const int s = it % LS, cs = it % CS;
         if (!mbar_wait(&sh.lfull[s], (unsigned)(it / LS) & 1u, abort) ||
             !mbar_wait(&sh.cempty[cs], ((unsigned)(it / CS) & 1u) ^ 1u, abort)) {
@@ -545,22 +553,29 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
         uint8_t* cv = conv_base + (size_t)cs * g.c_bytes;
         if (SIDE == 0) {
           const uint32_t mword =
-              MASKED ? reinterpret_cast<const uint32_t*>(ld + g.l_mask)[ct] : 0u;
-#pragma unroll 2
-          for (int q = 0; q < 8; ++q) {
-            const uint32_t off = sw128_chunk(ct, q);
-            const float4 g4 = *reinterpret_cast<const float4*>(ld + off);
+              MASKED ? reinterpret_cast<const uint32_t*>(ld + g.l_mask)[row] : 0u;
+          float4 g4[4], c4[4], q4[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t off = sw128_chunk(row, 4 * h + k);
+            g4[k] = *reinterpret_cast<const float4*>(ld + off);
+            if (!MASKED) c4[k] = *reinterpret_cast<const float4*>(ld + g.l_c + off);
+            q4[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (VAR && has_dq) q4[k] = *reinterpret_cast<const float4*>(ld + g.l_dq + off);
+          }
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int q = 4 * h + k;
+            const uint32_t off = sw128_chunk(row, q);
             float ce[4];
             if (MASKED) {
 #pragma unroll
               for (int e = 0; e < 4; ++e) ce[e] = (mword >> (4 * q + e)) & 1u ? 1.f : 0.f;
             } else {
-              const float4 c4 = *reinterpret_cast<const float4*>(ld + g.l_c + off);
-              ce[0] = c4.x; ce[1] = c4.y; ce[2] = c4.z; ce[3] = c4.w;
+              ce[0] = c4[k].x; ce[1] = c4[k].y; ce[2] = c4[k].z; ce[3] = c4[k].w;
             }
-            float4 q4 = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (VAR && has_dq) q4 = *reinterpret_cast<const float4*>(ld + g.l_dq + off);
-            const float ge[4] = {g4.x, g4.y, g4.z, g4.w}, qe[4] = {q4.x, q4.y, q4.z, q4.w};
+            const float ge[4] = {g4[k].x, g4[k].y, g4[k].z, g4[k].w};
+            const float qe[4] = {q4[k].x, q4[k].y, q4[k].z, q4[k].w};
             float sv[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
@@ -580,29 +595,39 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
             *reinterpret_cast<float4*>(cv + SBOX + off) = lo;
           }
         } else {
-          // 4 columns (one 16-byte piece of a 32-byte granule) of 8 rows
+          // 4 columns (one 16-byte piece of a 32-byte granule) of 4 rows
           const int box = cq >> 3, gq = (cq & 7) >> 1, half = cq & 1;
           const int jw = blk * 4 + box;
-#pragma unroll 2
-          for (int k8 = 0; k8 < 8; ++k8) {
-            const int rr = rg * 8 + k8;
+          float4 g4[4], c4[4], q4[4];
+          uint32_t mw4[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int rr = rg * 4 + k;
             const uint32_t off =
                 box * 4096 + rr * 128 + (uint32_t)(((gq ^ (rr & 3)) << 5) + half * 16);
-            const float4 g4 = *reinterpret_cast<const float4*>(ld + off);
+            g4[k] = *reinterpret_cast<const float4*>(ld + off);
+            if (!MASKED) c4[k] = *reinterpret_cast<const float4*>(ld + g.l_c + off);
+            q4[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (VAR && has_dq) q4[k] = *reinterpret_cast<const float4*>(ld + g.l_dq + off);
+            mw4[k] = (MASKED && jw < g.mw)
+                         ? reinterpret_cast<const uint32_t*>(ld + g.l_mask)[box * 32 + rr]
+                         : 0u;
+          }
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int rr = rg * 4 + k;
+            const uint32_t off =
+                box * 4096 + rr * 128 + (uint32_t)(((gq ^ (rr & 3)) << 5) + half * 16);
             float ce[4];
             if (MASKED) {
-              const uint32_t w = (jw < g.mw)
-                                     ? reinterpret_cast<const uint32_t*>(ld + g.l_mask)[box * 32 + rr]
-                                     : 0u;
 #pragma unroll
-              for (int e = 0; e < 4; ++e) ce[e] = (w >> (4 * (cq & 7) + e)) & 1u ? 1.f : 0.f;
+              for (int e = 0; e < 4; ++e)
+                ce[e] = (mw4[k] >> (4 * (cq & 7) + e)) & 1u ? 1.f : 0.f;
             } else {
-              const float4 c4 = *reinterpret_cast<const float4*>(ld + g.l_c + off);
-              ce[0] = c4.x; ce[1] = c4.y; ce[2] = c4.z; ce[3] = c4.w;
+              ce[0] = c4[k].x; ce[1] = c4[k].y; ce[2] = c4[k].z; ce[3] = c4[k].w;
             }
-            float4 q4 = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (VAR && has_dq) q4 = *reinterpret_cast<const float4*>(ld + g.l_dq + off);
-            const float ge[4] = {g4.x, g4.y, g4.z, g4.w}, qe[4] = {q4.x, q4.y, q4.z, q4.w};
+            const float ge[4] = {g4[k].x, g4[k].y, g4[k].z, g4[k].w};
+            const float qe[4] = {q4[k].x, q4[k].y, q4[k].z, q4[k].w};
             float vbi = 0.f;
             if (VAR) {
               const int i = kc * 32 + rr;
@@ -632,7 +657,8 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
           float4* fh = reinterpret_cast<float4*>(cv + 2 * SBOX);
           float4* fl = reinterpret_cast<float4*>(cv + 2 * SBOX + g.nF * 4096);
           const int n4 = g.nF * 256;
-          for (int k = ct; k < n4; k += 128) {
+#pragma unroll 2
+          for (int k = ct; k < n4; k += GRAD_CONV) {
             float4 lo;
             fh[k] = split4(fr[k], lo);
             fl[k] = lo;
@@ -642,36 +668,45 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
         fence_async_smem();
         mbar_arrive(&sh.cfull[cs]);
       }
+      // the eight split warps decide together whether to go on
+      if (named_bar_or(2, GRAD_CONV, !ok)) break;
       const int a = ti & 1;
-      float rfin, vfin;
       if (SIDE == 0) {
-        if (!ok) break;
-        rfin = rsum[0];
-        vfin = vsum[0];
+        sh.red[h][row] = rsum[0];
+        if (VAR) sh.redv[h][row] = vsum[0];
       } else {
-        // combine the four row groups' partial column sums: thread ct ends
-        // with column j = blk*128 + ct (the four warps decide together)
-        if (named_bar_or(2, 128, !ok)) break;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           sh.red[rg][4 * cq + e] = rsum[e];
           if (VAR) sh.redv[rg][4 * cq + e] = vsum[e];
         }
-        named_bar(2, 128);
-        rfin = (sh.red[0][ct] + sh.red[1][ct]) + (sh.red[2][ct] + sh.red[3][ct]);
-        vfin = VAR ? (sh.redv[0][ct] + sh.redv[1][ct]) + (sh.redv[2][ct] + sh.redv[3][ct]) : 0.f;
-        named_bar(2, 128);
       }
-      const int r = blk * 128 + ct;
-      if (VAR && dva != nullptr && r < R) dva[(long long)b * R + r] = 0.5f * vfin;
-      if (!mbar_wait(&sh.nempty[a], ((unsigned)(ti >> 1) & 1u) ^ 1u, abort)) {
-        record_timeout(abort);
-        break;
+      named_bar(2, GRAD_CONV);
+      if (ct < 128) {
+        float rfin, vfin = 0.f;
+        if (SIDE == 0) {
+          rfin = sh.red[0][ct] + sh.red[1][ct];
+          if (VAR) vfin = sh.redv[0][ct] + sh.redv[1][ct];
+        } else {
+          rfin = ((sh.red[0][ct] + sh.red[1][ct]) + (sh.red[2][ct] + sh.red[3][ct])) +
+                 ((sh.red[4][ct] + sh.red[5][ct]) + (sh.red[6][ct] + sh.red[7][ct]));
+          if (VAR)
+            vfin = ((sh.redv[0][ct] + sh.redv[1][ct]) + (sh.redv[2][ct] + sh.redv[3][ct])) +
+                   ((sh.redv[4][ct] + sh.redv[5][ct]) + (sh.redv[6][ct] + sh.redv[7][ct]));
+        }
+        const int r = blk * 128 + ct;
+        if (VAR && dva != nullptr && r < R) dva[(long long)b * R + r] = 0.5f * vfin;
+        if (mbar_wait(&sh.nempty[a], ((unsigned)(ti >> 1) & 1u) ^ 1u, abort)) {
+          sh.rs[a][ct] = rfin;
+          mbar_arrive(&sh.nfull[a]);
+        } else {
+          record_timeout(abort);
+          ok = false;
+        }
       }
-      sh.rs[a][ct] = rfin;
-      mbar_arrive(&sh.nfull[a]);
+      named_bar(2, GRAD_CONV);  // red[] is free for the next unit
     }
-  } else if (!dead && warp == 9) {
+  } else if (!dead && warp == GRAD_MMA_WARP) {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = idesc_tf32(128, BD, SIDE == 1 ? 1 : 0, 1);
@@ -775,7 +810,7 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 9) tmem_dealloc(tmem, g.tmem_cols);
+  if (warp == GRAD_MMA_WARP) tmem_dealloc(tmem, g.tmem_cols);
 }
 
 int sm_count() {
