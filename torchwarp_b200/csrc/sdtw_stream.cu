@@ -11,6 +11,9 @@
 //             its Pbar; w_p is recomputed from the saved R' of the predecessors.
 #include <climits>
 #include <cstdlib>
+#include <map>
+#include <mutex>
+#include <tuple>
 
 #include "sdtw_stream.cuh"
 
@@ -18,15 +21,19 @@ namespace tw {
 namespace {
 
 template <typename T> struct RingStride;
-// Row stride (elements) of the per-lane cost rings: lane l reads column
-// (t - l) of row l, so the bank of its word is (l*(S-1) + t) mod 32; S-1 odd
-// (and S*elem a multiple of 16 bytes for cp.async) makes the read conflict-free.
-template <> struct RingStride<float> { static constexpr int value = 68; };
-template <> struct RingStride<double> { static constexpr int value = 66; };
+// Row stride (elements) of the per-lane rings: lane l reads column (t - l)
+// of row l, so the bank of its word is (l*(S-1) + t) mod 32; S-1 odd (and
+// S*elem a multiple of 16 bytes for cp.async) makes the access conflict-free.
+template <> struct RingStride<float> { static constexpr int value = 36; };
+template <> struct RingStride<double> { static constexpr int value = 34; };
 
-constexpr int RING = 64;   // stream columns a lane row can hold
+// Each lane streams its own row: at block u it works in tiles cur-1 and cur
+// (cur = u - 4k - lane/8) and has tiles cur+1 .. cur+LEAD in flight, so a
+// ring of LEAD + 2 tiles per lane row suffices.
+constexpr int RING = 32;   // stream columns a lane row can hold
 constexpr int TILE = 8;    // columns per copy tile / flush tile
-constexpr int LEAD = 3;    // forward: cost tiles issued ahead of use
+constexpr int LEAD = 2;    // forward: cost tiles issued ahead of use
+static_assert(TILE * (LEAD + 2) <= RING, "ring too small for the lead");
 
 __device__ __forceinline__ int floor_div(int a, int b) {
   const int q = a / b;
@@ -197,10 +204,10 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
   T* myC = ringC + lane * S;
   T* myQ = ringQ + lane * S;
 
-  Cursor ld[KS], pt[KS];  // next tile to load / to patch, per sub-band
+  Cursor ld[KS], pt[KS];  // next tile to load / to patch, per sub-band (lane-dependent)
 #pragma unroll
   for (int k = 0; k < KS; ++k) {
-    ld[k] = cursor_at(-4 * k, p);
+    ld[k] = cursor_at(-4 * k - (lane >> 3), p);
     pt[k] = ld[k];
   }
 #pragma unroll 1
@@ -272,7 +279,7 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
       T Rn[KS], Pn[KS];
 #pragma unroll
       for (int k = 0; k < KS; ++k) {
-        const int off = k * 32 * S + ((k & 1) ? (ia ^ 32) : ia);
+        const int off = k * 32 * S + ia;  // column t - 32k - lane of sub-band k
         const T c = myC[off] * kap;
         const T qv = HAS_P ? myQ[off] : T(0);
         cell_forward<T, HAS_P>(c, qv, left[k], up[k], dg[k], Pl[k], Pu[k], Pd[k], Rn[k], Pn[k]);
@@ -584,7 +591,7 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
       for (int k = 0; k < KS; ++k) {
         const T rbar = accL[k] + accB[k];
         const T pbar = HAS_P ? Qacc[k] + QaccB[k] : T(0);
-        const int off = k * 32 * S + ((k & 1) ? (ia ^ 32) : ia);
+        const int off = k * 32 * S + ia;
         myC[off] = rbar;
         if (HAS_P) myQ[off] = pbar;
         T pl, pu, pd, ql, qu, qd;
@@ -709,6 +716,53 @@ int bwd_ks(const SdtwArgs<T>& a, bool has_p, cudaStream_t st) {
   return has_p ? launch_bwd<T, KS, true>(a, st) : launch_bwd<T, KS, false>(a, st);
 }
 
+// Blocks of `wpc` warps per SM that both sweeps of a plan can keep resident
+// with `smem` bytes each (registers and shared memory), or -1 when the
+// device cannot be asked (no GPU: the shared-memory bound alone is used).
+template <typename T, int KS, bool HAS_P>
+int resident_blocks(int wpc, size_t smem) {
+  const void* kerns[3] = {(const void*)sdtw_fwd_kernel<T, KS, HAS_P, false>,
+                          (const void*)sdtw_fwd_kernel<T, KS, HAS_P, true>,
+                          (const void*)sdtw_bwd_kernel<T, KS, HAS_P>};
+  int best = INT_MAX;
+  for (const void* k : kerns) {
+    int n = 0;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+            cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, 32 * wpc, smem) != cudaSuccess) {
+      cudaGetLastError();
+      return -1;
+    }
+    best = n < best ? n : best;
+  }
+  return best;
+}
+
+int resident_blocks_any(int eb, int KS, bool has_p, int wpc, size_t smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, bool, int, size_t>, int> cache;
+  const auto key = std::make_tuple(eb, KS, has_p, wpc, smem);
+  {
+    std::lock_guard<std::mutex> g(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  int n = -1;
+#define TW_RB(TT, K)                                                                          \
+  n = has_p ? resident_blocks<TT, K, true>(wpc, smem) : resident_blocks<TT, K, false>(wpc, smem)
+  if (eb == 4) {
+    if (KS == 1) TW_RB(float, 1); else if (KS == 2) TW_RB(float, 2); else TW_RB(float, 4);
+  } else {
+    if (KS == 1) TW_RB(double, 1); else if (KS == 2) TW_RB(double, 2); else TW_RB(double, 4);
+  }
+#undef TW_RB
+  if (n >= 0) {
+    std::lock_guard<std::mutex> g(mu);
+    cache[key] = n;
+  }
+  return n;
+}
+
 }  // namespace
 
 static int env_int(const char* name, int fallback) {
@@ -735,16 +789,25 @@ StreamPlan make_stream_plan(int B, int N, int M, int eb, bool has_p, int sms) {
   p.L = (L + TILE - 1) / TILE * TILE;
   const int S = eb == 4 ? RingStride<float>::value : RingStride<double>::value;
   const size_t per_w = (size_t)p.KS * 32 * S * eb * (has_p ? 2 : 1);
-  int wps = (int)((size_t)(208 * 1024) / per_w);
-  wps = wps < 1 ? 1 : (wps > 24 ? 24 : wps);
+  // Warps per SM: bounded by shared memory (the per-lane rings), by the
+  // registers of the heavier of the two sweeps, and by 32.
+  int wps = (int)((size_t)(216 * 1024) / per_w);
+  wps = wps < 1 ? 1 : (wps > 32 ? 32 : wps);
   const int cap = env_int("TW_STREAM_WPS", 0);
   if (cap > 0 && cap < wps) wps = cap;
   int wpc = wps < 4 ? wps : 4;
   if (wpc > B) wpc = B > 0 ? B : 1;
-  const int cps = wps / wpc > 0 ? wps / wpc : 1;
-  int ctas = sms * cps;
-  const int ctas_needed = B / wpc > 0 ? B / wpc : 1;
-  if (ctas > ctas_needed) ctas = ctas_needed;
+  int cps = wps / wpc > 0 ? wps / wpc : 1;
+  const int resident = resident_blocks_any(eb, p.KS, has_p, wpc, per_w * wpc);
+  if (resident > 0 && resident < cps) cps = resident;
+  // Every warp carries whole pairs, so the sweep lasts as long as the warp
+  // with the most pairs.  Take the fewest pairs per warp the resident warps
+  // allow, then the fewest warps that still achieve it (equal loads).
+  const long long cap_warps = (long long)sms * cps * wpc;
+  const long long per_warp = B > 0 ? (B + cap_warps - 1) / cap_warps : 1;
+  const long long warps_needed = B > 0 ? (B + per_warp - 1) / per_warp : 1;
+  int ctas = (int)((warps_needed + wpc - 1) / wpc);
+  if (ctas < 1) ctas = 1;
   p.wpc = wpc;
   p.warps = ctas * wpc;
   p.base = B / p.warps;
