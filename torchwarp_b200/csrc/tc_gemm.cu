@@ -350,7 +350,7 @@ constexpr int GRAD_PROD_WARP = 4 + GRAD_CONV / 32;
 constexpr int GRAD_MMA_WARP = GRAD_PROD_WARP + 1;
 constexpr int GRAD_THREADS = 32 * (GRAD_MMA_WARP + 1);
 constexpr int GRAD_MAX_LAND = 6;
-constexpr int GRAD_MAX_CONV = 2;
+constexpr int GRAD_MAX_CONV = 4;
 constexpr int SBOX = 128 * 32 * 4;  // one 16 KB chunk of dC / C / dQ
 
 struct GradShared {
@@ -371,9 +371,11 @@ struct GradGeom {
   int np;           // mask row count, padded: 4 ceil(N / 4)
   int lstages, cstages;
   int l_c, l_dq, l_f, l_mask, l_bytes;  // landing slot layout (dC at 0)
-  int c_bytes;      // converted slot: S hi 0, S lo SBOX, F hi 2 SBOX, F lo 2 SBOX + 4096 nF
+  int c_bytes;      // converted slot (shared memory)
+  int c_fh, c_fl;   // features hi / lo in a converted slot (S hi / lo at 0 / SBOX unless in TMEM)
   int tx_fixed;     // landing bytes per chunk other than the mask
   uint32_t tmem_cols;
+  uint32_t a_col0;  // S in TMEM: first column of the (hi 32 | lo 32) x cstages ring
 };
 
 __device__ __forceinline__ float4 split4(float4 v, float4& lo) {
@@ -385,7 +387,7 @@ __device__ __forceinline__ float4 split4(float4 v, float4& lo) {
   return hi;
 }
 
-template <int SIDE, bool VAR, bool MASKED>
+template <int SIDE, bool VAR, bool MASKED, bool TA>
 __global__ void __launch_bounds__(GRAD_THREADS, 1)
     tc_grad_kernel(const __grid_constant__ CUtensorMap mapDC, const __grid_constant__ CUtensorMap mapC,
                    const __grid_constant__ CUtensorMap mapDQ, const __grid_constant__ CUtensorMap mapF,
@@ -511,7 +513,148 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
       for (unsigned n = 0; n < kSpinLimit; ++n)
         if (mbar_try_wait(&sh.lfull[s], (unsigned)(k / LS) & 1u)) break;
     }
-  } else if (!dead && warp >= 4 && warp < GRAD_PROD_WARP) {
+  } else if (TA && !dead && warp >= 4 && warp < GRAD_PROD_WARP) {
+    // ------------------------------------------- S = dsq, split into TMEM, sums
+    // S goes to TMEM as the MMA's A operand (lane = own row, column = summed
+    // index), so neither its hi / lo halves nor the MMA's A reads touch
+    // shared memory.  Warp w writes TMEM lanes 32 (w % 4) ..; thread ct owns
+    // own-row ct & 127 and the 16 summed columns 16 hh .. of each chunk.
+    const int ct = tid - 128;
+    const int own = ct & 127, hh = ct >> 7;
+    const int sub = warp & 3;
+    const uint32_t lane_base = (uint32_t)(32 * sub) << 16;
+    int it = 0, ti = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < total; u += gridDim.x, ++ti) {
+      const int b = u / nBlk, blk = u - b * nBlk;
+      const int r = blk * 128 + own;
+      const float va_r = VAR ? (r < R ? va[(long long)b * R + r] : 1.f) : 0.f;
+      const float* vb_b = VAR ? vb + (long long)b * S : nullptr;
+      float rsum = 0.f, vsum = 0.f;
+      for (int kc = 0; kc < nK && ok; ++kc, ++it) {
+        const int s = it % LS, cs = it % CS;
+        if (!mbar_wait(&sh.lfull[s], (unsigned)(it / LS) & 1u, abort) ||
+            !mbar_wait(&sh.cempty[cs], ((unsigned)(it / CS) & 1u) ^ 1u, abort)) {
+          record_timeout(abort);
+          ok = false;
+          break;
+        }
+        tc_fence_after();  // the MMAs that read this TMEM slot have completed
+        const uint8_t* ld = land_base + (size_t)s * g.l_bytes;
+        uint8_t* cv = conv_base + (size_t)cs * g.c_bytes;
+        float sv[16];
+        if (SIDE == 0) {
+          const uint32_t mword =
+              MASKED ? reinterpret_cast<const uint32_t*>(ld + g.l_mask)[own] : 0u;
+          float4 g4[4], c4[4], q4[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t off = sw128_chunk(own, 4 * hh + k);
+            g4[k] = *reinterpret_cast<const float4*>(ld + off);
+            if (!MASKED) c4[k] = *reinterpret_cast<const float4*>(ld + g.l_c + off);
+            q4[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (VAR && has_dq) q4[k] = *reinterpret_cast<const float4*>(ld + g.l_dq + off);
+          }
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float ge[4] = {g4[k].x, g4[k].y, g4[k].z, g4[k].w};
+            const float qe[4] = {q4[k].x, q4[k].y, q4[k].z, q4[k].w};
+            float ce[4];
+            if (!MASKED) { ce[0] = c4[k].x; ce[1] = c4[k].y; ce[2] = c4[k].z; ce[3] = c4[k].w; }
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int jj = 16 * hh + 4 * k + e;  // summed column within the chunk
+              if (MASKED) ce[e] = (mword >> jj) & 1u ? 1.f : 0.f;
+              float var = 1.f, var_raw = 1.f;
+              if (VAR) {
+                const int j = kc * 32 + jj;
+                var_raw = 0.5f * (va_r + (j < S ? __ldg(vb_b + j) : 1.f));
+                var = var_raw > eps ? var_raw : eps;
+              }
+              const float v = ce[e] > 0.f ? (VAR ? ge[e] / var : ge[e]) : 0.f;
+              rsum += v;
+              if (VAR && var_raw > eps) vsum += (beta * qe[e] - ge[e] * ce[e]) / var;
+              sv[4 * k + e] = v;
+            }
+          }
+        } else {
+          // own column j = blk*128 + 32 sub + lane: box `sub`, element `lane`
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            const int rr = 16 * hh + k;
+            const uint32_t off = sub * 4096 + sw128b32_elem(rr, lane);
+            const float gv = *reinterpret_cast<const float*>(ld + off);
+            float cvv;
+            if (MASKED) {
+              const int jw = blk * 4 + sub;
+              const uint32_t w =
+                  jw < g.mw ? reinterpret_cast<const uint32_t*>(ld + g.l_mask)[sub * 32 + rr] : 0u;
+              cvv = (w >> lane) & 1u ? 1.f : 0.f;
+            } else {
+              cvv = *reinterpret_cast<const float*>(ld + g.l_c + off);
+            }
+            const float qv = (VAR && has_dq) ? *reinterpret_cast<const float*>(ld + g.l_dq + off)
+                                             : 0.f;
+            float var = 1.f, var_raw = 1.f;
+            if (VAR) {
+              const int i = kc * 32 + rr;
+              var_raw = 0.5f * ((i < S ? __ldg(vb_b + i) : 1.f) + va_r);
+              var = var_raw > eps ? var_raw : eps;
+            }
+            const float v = cvv > 0.f ? (VAR ? gv / var : gv) : 0.f;
+            rsum += v;
+            if (VAR && var_raw > eps) vsum += (beta * qv - gv * cvv) / var;
+            sv[k] = v;
+          }
+        }
+        {
+          float hi[16], lo[16];
+#pragma unroll
+          for (int k = 0; k < 16; ++k) split_tf32(sv[k], hi[k], lo[k]);
+          const uint32_t a_hi = tmem + lane_base + g.a_col0 + (uint32_t)(cs * 64 + 16 * hh);
+          tmem_st16(a_hi, hi);
+          tmem_st16(a_hi + 32, lo);
+        }
+        // the other side's features: elementwise split into shared memory
+        {
+          const float4* fr = reinterpret_cast<const float4*>(ld + g.l_f);
+          float4* fh = reinterpret_cast<float4*>(cv + g.c_fh);
+          float4* fl = reinterpret_cast<float4*>(cv + g.c_fl);
+          const int n4 = g.nF * 256;
+#pragma unroll 2
+          for (int k = ct; k < n4; k += GRAD_CONV) {
+            float4 lo;
+            fh[k] = split4(fr[k], lo);
+            fl[k] = lo;
+          }
+        }
+        tmem_st_wait();
+        mbar_arrive(&sh.lempty[s]);
+        fence_async_smem();
+        tc_fence_before();
+        mbar_arrive(&sh.cfull[cs]);
+      }
+      if (named_bar_or(2, GRAD_CONV, !ok)) break;
+      const int a = ti & 1;
+      sh.red[hh][own] = rsum;
+      if (VAR) sh.redv[hh][own] = vsum;
+      named_bar(2, GRAD_CONV);
+      if (ct < 128) {
+        const float rfin = sh.red[0][ct] + sh.red[1][ct];
+        const float vfin = VAR ? sh.redv[0][ct] + sh.redv[1][ct] : 0.f;
+        const int rr = blk * 128 + ct;
+        if (VAR && dva != nullptr && rr < R) dva[(long long)b * R + rr] = 0.5f * vfin;
+        if (mbar_wait(&sh.nempty[a], ((unsigned)(ti >> 1) & 1u) ^ 1u, abort)) {
+          sh.rs[a][ct] = rfin;
+          mbar_arrive(&sh.nfull[a]);
+        } else {
+          record_timeout(abort);
+          ok = false;
+        }
+      }
+      named_bar(2, GRAD_CONV);
+    }
+  } else if (!TA && !dead && warp >= 4 && warp < GRAD_PROD_WARP) {
     // ------------------------------------------------ S = dsq, split, sums
     // SIDE 0: thread ct owns row (ct & 127) of the 128-row chunk, 16-byte
     // pieces 4h .. 4h+3 of its 128-byte line (h = ct >> 7).
@@ -654,8 +797,8 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
         // the other side's features: elementwise split of the whole slab
         {
           const float4* fr = reinterpret_cast<const float4*>(ld + g.l_f);
-          float4* fh = reinterpret_cast<float4*>(cv + 2 * SBOX);
-          float4* fl = reinterpret_cast<float4*>(cv + 2 * SBOX + g.nF * 4096);
+          float4* fh = reinterpret_cast<float4*>(cv + g.c_fh);
+          float4* fl = reinterpret_cast<float4*>(cv + g.c_fl);
           const int n4 = g.nF * 256;
 #pragma unroll 2
           for (int k = ct; k < n4; k += GRAD_CONV) {
@@ -709,7 +852,7 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
   } else if (!dead && warp == GRAD_MMA_WARP) {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = idesc_tf32(128, BD, SIDE == 1 ? 1 : 0, 1);
+      const uint32_t idesc = idesc_tf32(128, BD, (SIDE == 1 && !TA) ? 1 : 0, 1);
       int it = 0, ti = 0;
       for (int u = blockIdx.x; u < total; u += gridDim.x, ++ti) {
         const int a = ti & 1;
@@ -729,7 +872,19 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
           }
           tc_fence_after();
           const uint32_t st = smem_u32(conv_base + (size_t)cs * g.c_bytes);
-          const uint32_t ah = st, al = st + SBOX, fh = st + 2 * SBOX, fl = fh + g.nF * 4096;
+          const uint32_t ah = st, al = st + SBOX, fh = st + g.c_fh, fl = st + g.c_fl;
+          if constexpr (TA) {
+            const uint32_t ta = tmem + g.a_col0 + (uint32_t)(cs * 64);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t dbh = smem_desc(fh + kk * 1024, 4096, 512, kLayoutSW128Base32);
+              const uint64_t dbl = smem_desc(fl + kk * 1024, 4096, 512, kLayoutSW128Base32);
+              mma_tf32_ts(d_tmem, ta + 32 + 8 * kk, dbh, idesc, (kc | kk) != 0);
+              mma_tf32_ts(d_tmem, ta + 8 * kk, dbl, idesc, 1);
+              mma_tf32_ts(d_tmem, ta + 8 * kk, dbh, idesc, 1);
+            }
+            mma_commit(&sh.cempty[cs]);
+          } else {
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             uint64_t dah, dal;
@@ -747,6 +902,7 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
             mma_tf32(d_tmem, dah, dbh, idesc, 1);
           }
           mma_commit(&sh.cempty[cs]);
+          }
         }
         if (!ok) break;
         mma_commit(&sh.accf[a]);
@@ -911,11 +1067,11 @@ int tc_cost_f32(const float* X, const float* Y, const float* vx, const float* vy
 
 namespace {
 
-template <int SIDE, bool VAR, bool MASKED = false>
-int grad_side(const float* A, const float* F, const float* va, const float* vb, const float* C,
-              const float* dC, const float* dQ, int B, int N, int M, int D, double beta,
-              double eps, float* dA, float* dva, cudaStream_t st,
-              const uint32_t* mask = nullptr) {
+template <int SIDE, bool VAR, bool MASKED, bool TA>
+int grad_side_impl(const float* A, const float* F, const float* va, const float* vb,
+                   const float* C, const float* dC, const float* dQ, int B, int N, int M, int D,
+                   double beta, double eps, float* dA, float* dva, cudaStream_t st,
+                   const uint32_t* mask) {
   const int R = SIDE == 0 ? N : M, S = SIDE == 0 ? M : N;
   CUtensorMap mDC, mC, mDQ, mF, mOut;
   int rc;
@@ -948,30 +1104,64 @@ int grad_side(const float* A, const float* F, const float* va, const float* vb, 
   if (MASKED) off += 512;
   g.l_bytes = (off + 1023) & ~1023;
   g.tx_fixed = SBOX * (MASKED ? 1 : 2) + (has_dq ? SBOX : 0) + g.nF * 4096;
-  g.c_bytes = 2 * SBOX + 2 * g.nF * 4096;
+  const int BD = 32 * g.nF;
   const int budget = 232448 - STG_BYTES - (int)sizeof(GradShared);
-  g.cstages = GRAD_MAX_CONV;
-  g.lstages = (budget - g.cstages * g.c_bytes) / g.l_bytes;
-  if (g.lstages < 2) {
-    g.cstages = 1;
-    g.lstages = (budget - g.c_bytes) / g.l_bytes;
+  if (TA) {
+    // S in TMEM after the two accumulators: (hi 32 | lo 32) columns per slot
+    g.c_fh = 0;
+    g.c_fl = g.nF * 4096;
+    g.c_bytes = 2 * g.nF * 4096;
+    g.a_col0 = (uint32_t)(2 * BD);
+    g.cstages = (512 - 2 * BD) / 64;
+    if (g.cstages > GRAD_MAX_CONV) g.cstages = GRAD_MAX_CONV;
+    if (g.cstages < 1) return set_error(kUnsupported, "tc grad: D=%d too wide for S in TMEM", D);
+    g.lstages = (budget - g.cstages * g.c_bytes) / g.l_bytes;
+  } else {
+    g.c_fh = 2 * SBOX;
+    g.c_fl = 2 * SBOX + g.nF * 4096;
+    g.c_bytes = 2 * SBOX + 2 * g.nF * 4096;
+    g.a_col0 = 0;
+    g.cstages = 2;
+    g.lstages = (budget - g.cstages * g.c_bytes) / g.l_bytes;
+    if (g.lstages < 2) {
+      g.cstages = 1;
+      g.lstages = (budget - g.c_bytes) / g.l_bytes;
+    }
   }
   if (g.lstages > GRAD_MAX_LAND) g.lstages = GRAD_MAX_LAND;
   if (g.lstages < 1) return set_error(kUnsupported, "tc grad: D=%d needs too much shared memory", D);
+  uint32_t need = (uint32_t)(2 * BD) + (TA ? (uint32_t)(64 * g.cstages) : 0u);
   uint32_t cols = 32;
-  while (cols < (uint32_t)(2 * 32 * g.nF)) cols <<= 1;
+  while (cols < need) cols <<= 1;
   g.tmem_cols = cols;
   const size_t smem = (size_t)g.lstages * g.l_bytes + (size_t)g.cstages * g.c_bytes +
                       STG_BYTES + sizeof(GradShared);
   const long long units = (long long)B * ((R + 127) / 128);
   const int grid = (int)(units < sm_count() ? units : sm_count());
-  auto kern = tc_grad_kernel<SIDE, VAR, MASKED>;
+  auto kern = tc_grad_kernel<SIDE, VAR, MASKED, TA>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   kern<<<grid, GRAD_THREADS, smem, st>>>(mDC, mC, mDQ, mF, mOut, A, va, vb, dva, B, N, M, D,
                                          (float)beta, (float)eps, has_dq ? 1 : 0, g, mask);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(kLaunch, "tc grad launch: %s", cudaGetErrorString(e));
   return kOk;
+}
+
+// S goes to TMEM (no shared-memory traffic for it) whenever the two
+// accumulators leave room for it: D <= 192.  TW_GRAD_SMEM_S=1 keeps S in
+// shared memory (for comparisons).
+template <int SIDE, bool VAR, bool MASKED = false>
+int grad_side(const float* A, const float* F, const float* va, const float* vb, const float* C,
+              const float* dC, const float* dQ, int B, int N, int M, int D, double beta,
+              double eps, float* dA, float* dva, cudaStream_t st,
+              const uint32_t* mask = nullptr) {
+  const char* env = std::getenv("TW_GRAD_SMEM_S");
+  const bool smem_s = env != nullptr && env[0] != '\0' && env[0] != '0';
+  if (!smem_s && 2 * 32 * ((D + 31) / 32) + 64 <= 512)
+    return grad_side_impl<SIDE, VAR, MASKED, true>(A, F, va, vb, C, dC, dQ, B, N, M, D, beta, eps,
+                                                   dA, dva, st, mask);
+  return grad_side_impl<SIDE, VAR, MASKED, false>(A, F, va, vb, C, dC, dQ, B, N, M, D, beta, eps,
+                                                  dA, dva, st, mask);
 }
 
 }  // namespace
