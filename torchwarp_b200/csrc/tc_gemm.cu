@@ -13,8 +13,9 @@
 //   warps 0-3  epilogue: TMEM -> registers -> cost -> swizzled smem -> TMA store
 //   warps 4-7  split:    fp32 tile -> (hi, lo) TF32 pair in place, row norms
 //   warp  8    TMA producer of the X / Y feature chunks (32 features each)
-//   warp  9    MMA issuer: hi*hi + hi*lo + lo*hi per 8-feature step
-// Two TMEM accumulators (2 x 128 columns) let the epilogue of one tile
+//   warp  9    MMA issuer: per 8-feature step two N = 256 MMAs, A_hi [B_hi; B_lo]
+//              and A_lo [B_hi; B_lo] (all four TF32 products)
+// Two TMEM accumulators (2 x 256 columns) let the epilogue of one tile
 // overlap the MMAs of the next.  No atomics: results are reproducible.
 #include <cstdlib>
 #include <mutex>
@@ -38,7 +39,11 @@ constexpr int TILE_B = BN * KC * 4;                       // 16 KB
 constexpr int STAGE_BYTES = 2 * TILE_A + 2 * TILE_B;      // hi and lo of A and B
 constexpr int STG_BYTES = BM * 32 * 4;                    // one 128 x 32 output chunk
 constexpr int COST_THREADS = 320;
-constexpr uint32_t COST_TMEM_COLS = 2 * BN;
+// Per tile a 128 x 2BN accumulator: columns [0, BN) take A * B_hi products,
+// [BN, 2BN) A * B_lo (B_hi and B_lo are contiguous in shared memory, so one
+// N = 256 MMA covers both); two tiles in flight fill all 512 columns.
+constexpr uint32_t COST_ACC_COLS = 2 * BN;
+constexpr uint32_t COST_TMEM_COLS = 2 * COST_ACC_COLS;
 
 struct CostShared {
   float x2[2][BM];
@@ -197,7 +202,7 @@ __global__ void __launch_bounds__(COST_THREADS, 1)
   } else if (!dead && warp == 9) {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t IDESC = idesc_tf32(BM, BN, 0, 0);
+      constexpr uint32_t IDESC = idesc_tf32(BM, 2 * BN, 0, 0);
       int it = 0, ti = 0;
       for (int t = blockIdx.x; t < total; t += gridDim.x, ++ti) {
         const int a = ti & 1;
@@ -206,7 +211,7 @@ __global__ void __launch_bounds__(COST_THREADS, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem + (uint32_t)(a * BN);
+        const uint32_t d_tmem = tmem + (uint32_t)(a * COST_ACC_COLS);
         bool ok = true;
         for (int kc = 0; kc < nK; ++kc, ++it) {
           const int s = it % STAGES;
@@ -214,16 +219,15 @@ __global__ void __launch_bounds__(COST_THREADS, 1)
           if (!mbar_wait(&sh.conv[s], ph, abort)) { record_timeout(abort); ok = false; break; }
           tc_fence_after();
           const uint32_t ah = smem_u32(stage_base + (size_t)s * STAGE_BYTES);
-          const uint32_t al = ah + TILE_A, bh = ah + 2 * TILE_A, bl = bh + TILE_B;
+          const uint32_t al = ah + TILE_A, bh = ah + 2 * TILE_A;
 #pragma unroll
           for (int kk = 0; kk < KC / 8; ++kk) {
+            // B = [B_hi; B_lo] (256 rows): A_hi B -> hi.hi | hi.lo, A_lo B -> lo.hi | lo.lo
             const uint64_t dah = smem_desc_sw128(ah + kk * 32, 16, 1024);
             const uint64_t dal = smem_desc_sw128(al + kk * 32, 16, 1024);
-            const uint64_t dbh = smem_desc_sw128(bh + kk * 32, 16, 1024);
-            const uint64_t dbl = smem_desc_sw128(bl + kk * 32, 16, 1024);
-            mma_tf32(d_tmem, dal, dbh, IDESC, (kc | kk) != 0);
-            mma_tf32(d_tmem, dah, dbl, IDESC, 1);
-            mma_tf32(d_tmem, dah, dbh, IDESC, 1);
+            const uint64_t db = smem_desc_sw128(bh + kk * 32, 16, 1024);
+            mma_tf32(d_tmem, dah, db, IDESC, (kc | kk) != 0);
+            mma_tf32(d_tmem, dal, db, IDESC, 1);
           }
           mma_commit(&sh.empty[s]);
         }
@@ -254,12 +258,16 @@ __global__ void __launch_bounds__(COST_THREADS, 1)
       if (VAR) vxi = i < N ? vx[(long long)c.b * N + i] : 1.f;
 #pragma unroll 1
       for (int cc = 0; cc < BN / 32; ++cc) {
-        float v[32];
-        tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(a * BN + 32 * cc), v);
+        float v[32], w[32];
+        const uint32_t tcol = tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(a * COST_ACC_COLS + 32 * cc);
+        tmem_ld32(tcol, v);
+        tmem_ld32(tcol + BN, w);
         if (cc == BN / 32 - 1) {
           tc_fence_before();
           mbar_arrive(&sh.acce[a]);
         }
+#pragma unroll
+        for (int q = 0; q < 32; ++q) v[q] += w[q];  // (hi.hi + lo.hi) + (hi.lo + lo.lo)
         const int j0 = c.jb * BN + 32 * cc;
         float qv[32];
         uint32_t pos = 0;  // bit q: sq_raw > 0 at column j0 + q
@@ -387,7 +395,7 @@ __device__ __forceinline__ float4 split4(float4 v, float4& lo) {
   return hi;
 }
 
-template <int SIDE, bool VAR, bool MASKED, bool TA>
+template <int SIDE, bool VAR, bool MASKED, bool TA, bool WIDE>
 __global__ void __launch_bounds__(GRAD_THREADS, 1)
     tc_grad_kernel(const __grid_constant__ CUtensorMap mapDC, const __grid_constant__ CUtensorMap mapC,
                    const __grid_constant__ CUtensorMap mapDQ, const __grid_constant__ CUtensorMap mapF,
@@ -852,7 +860,9 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
   } else if (!dead && warp == GRAD_MMA_WARP) {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = idesc_tf32(128, BD, (SIDE == 1 && !TA) ? 1 : 0, 1);
+      // WIDE: B = [F_hi | F_lo] along N (2 BD columns), two MMAs per K step
+      const int ACC = WIDE ? 2 * BD : BD;
+      const uint32_t idesc = idesc_tf32(128, ACC, (SIDE == 1 && !TA) ? 1 : 0, 1);
       int it = 0, ti = 0;
       for (int u = blockIdx.x; u < total; u += gridDim.x, ++ti) {
         const int a = ti & 1;
@@ -861,7 +871,7 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem + (uint32_t)(a * BD);
+        const uint32_t d_tmem = tmem + (uint32_t)(a * ACC);
         bool ok = true;
         for (int kc = 0; kc < nK; ++kc, ++it) {
           const int cs = it % CS;
@@ -878,10 +888,15 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
               const uint64_t dbh = smem_desc(fh + kk * 1024, 4096, 512, kLayoutSW128Base32);
-              const uint64_t dbl = smem_desc(fl + kk * 1024, 4096, 512, kLayoutSW128Base32);
-              mma_tf32_ts(d_tmem, ta + 32 + 8 * kk, dbh, idesc, (kc | kk) != 0);
-              mma_tf32_ts(d_tmem, ta + 8 * kk, dbl, idesc, 1);
-              mma_tf32_ts(d_tmem, ta + 8 * kk, dbh, idesc, 1);
+              if (WIDE) {
+                mma_tf32_ts(d_tmem, ta + 8 * kk, dbh, idesc, (kc | kk) != 0);
+                mma_tf32_ts(d_tmem, ta + 32 + 8 * kk, dbh, idesc, 1);
+              } else {
+                const uint64_t dbl = smem_desc(fl + kk * 1024, 4096, 512, kLayoutSW128Base32);
+                mma_tf32_ts(d_tmem, ta + 32 + 8 * kk, dbh, idesc, (kc | kk) != 0);
+                mma_tf32_ts(d_tmem, ta + 8 * kk, dbl, idesc, 1);
+                mma_tf32_ts(d_tmem, ta + 8 * kk, dbh, idesc, 1);
+              }
             }
             mma_commit(&sh.cempty[cs]);
           } else {
@@ -896,10 +911,15 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
               dal = smem_desc(al + kk * 1024, 4096, 512, kLayoutSW128Base32);
             }
             const uint64_t dbh = smem_desc(fh + kk * 1024, 4096, 512, kLayoutSW128Base32);
-            const uint64_t dbl = smem_desc(fl + kk * 1024, 4096, 512, kLayoutSW128Base32);
-            mma_tf32(d_tmem, dal, dbh, idesc, (kc | kk) != 0);
-            mma_tf32(d_tmem, dah, dbl, idesc, 1);
-            mma_tf32(d_tmem, dah, dbh, idesc, 1);
+            if (WIDE) {
+              mma_tf32(d_tmem, dah, dbh, idesc, (kc | kk) != 0);
+              mma_tf32(d_tmem, dal, dbh, idesc, 1);
+            } else {
+              const uint64_t dbl = smem_desc(fl + kk * 1024, 4096, 512, kLayoutSW128Base32);
+              mma_tf32(d_tmem, dal, dbh, idesc, (kc | kk) != 0);
+              mma_tf32(d_tmem, dah, dbl, idesc, 1);
+              mma_tf32(d_tmem, dah, dbh, idesc, 1);
+            }
           }
           mma_commit(&sh.cempty[cs]);
           }
@@ -929,7 +949,15 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
 #pragma unroll 1
       for (int cc = 0; cc < g.nF; ++cc) {
         float v[32];
-        tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(a * BD + 32 * cc), v);
+        const uint32_t tcol =
+            tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(a * (WIDE ? 2 * BD : BD) + 32 * cc);
+        tmem_ld32(tcol, v);
+        if (WIDE) {
+          float w[32];
+          tmem_ld32(tcol + BD, w);
+#pragma unroll
+          for (int q = 0; q < 32; ++q) v[q] += w[q];  // (hi.hi + lo.hi) + (hi.lo + lo.lo)
+        }
         if (cc == g.nF - 1) {
           tc_fence_before();
           mbar_arrive(&sh.acce[a]);
@@ -1067,7 +1095,7 @@ int tc_cost_f32(const float* X, const float* Y, const float* vx, const float* vy
 
 namespace {
 
-template <int SIDE, bool VAR, bool MASKED, bool TA>
+template <int SIDE, bool VAR, bool MASKED, bool TA, bool WIDE>
 int grad_side_impl(const float* A, const float* F, const float* va, const float* vb,
                    const float* C, const float* dC, const float* dQ, int B, int N, int M, int D,
                    double beta, double eps, float* dA, float* dva, cudaStream_t st,
@@ -1111,8 +1139,8 @@ int grad_side_impl(const float* A, const float* F, const float* va, const float*
     g.c_fh = 0;
     g.c_fl = g.nF * 4096;
     g.c_bytes = 2 * g.nF * 4096;
-    g.a_col0 = (uint32_t)(2 * BD);
-    g.cstages = (512 - 2 * BD) / 64;
+    g.a_col0 = (uint32_t)(2 * (WIDE ? 2 * BD : BD));
+    g.cstages = (512 - (int)g.a_col0) / 64;
     if (g.cstages > GRAD_MAX_CONV) g.cstages = GRAD_MAX_CONV;
     if (g.cstages < 1) return set_error(kUnsupported, "tc grad: D=%d too wide for S in TMEM", D);
     g.lstages = (budget - g.cstages * g.c_bytes) / g.l_bytes;
@@ -1130,7 +1158,8 @@ int grad_side_impl(const float* A, const float* F, const float* va, const float*
   }
   if (g.lstages > GRAD_MAX_LAND) g.lstages = GRAD_MAX_LAND;
   if (g.lstages < 1) return set_error(kUnsupported, "tc grad: D=%d needs too much shared memory", D);
-  uint32_t need = (uint32_t)(2 * BD) + (TA ? (uint32_t)(64 * g.cstages) : 0u);
+  uint32_t need = (uint32_t)(2 * (WIDE ? 2 * BD : BD)) + (TA ? (uint32_t)(64 * g.cstages) : 0u);
+  if (need > 512) return set_error(kUnsupported, "tc grad: D=%d needs %u TMEM columns", D, need);
   uint32_t cols = 32;
   while (cols < need) cols <<= 1;
   g.tmem_cols = cols;
@@ -1138,7 +1167,7 @@ int grad_side_impl(const float* A, const float* F, const float* va, const float*
                       STG_BYTES + sizeof(GradShared);
   const long long units = (long long)B * ((R + 127) / 128);
   const int grid = (int)(units < sm_count() ? units : sm_count());
-  auto kern = tc_grad_kernel<SIDE, VAR, MASKED, TA>;
+  auto kern = tc_grad_kernel<SIDE, VAR, MASKED, TA, WIDE>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   kern<<<grid, GRAD_THREADS, smem, st>>>(mDC, mC, mDQ, mF, mOut, A, va, vb, dva, B, N, M, D,
                                          (float)beta, (float)eps, has_dq ? 1 : 0, g, mask);
@@ -1148,8 +1177,8 @@ int grad_side_impl(const float* A, const float* F, const float* va, const float*
 }
 
 // S goes to TMEM (no shared-memory traffic for it) whenever the two
-// accumulators leave room for it: D <= 192.  TW_GRAD_SMEM_S=1 keeps S in
-// shared memory (for comparisons).
+// accumulators leave room for it.  TW_GRAD_SMEM_S=1 keeps S in shared
+// memory (for comparisons).
 template <int SIDE, bool VAR, bool MASKED = false>
 int grad_side(const float* A, const float* F, const float* va, const float* vb, const float* C,
               const float* dC, const float* dQ, int B, int N, int M, int D, double beta,
@@ -1157,11 +1186,17 @@ int grad_side(const float* A, const float* F, const float* va, const float* vb, 
               const uint32_t* mask = nullptr) {
   const char* env = std::getenv("TW_GRAD_SMEM_S");
   const bool smem_s = env != nullptr && env[0] != '\0' && env[0] != '0';
-  if (!smem_s && 2 * 32 * ((D + 31) / 32) + 64 <= 512)
-    return grad_side_impl<SIDE, VAR, MASKED, true>(A, F, va, vb, C, dC, dQ, B, N, M, D, beta, eps,
-                                                   dA, dva, st, mask);
-  return grad_side_impl<SIDE, VAR, MASKED, false>(A, F, va, vb, C, dC, dQ, B, N, M, D, beta, eps,
-                                                  dA, dva, st, mask);
+  const int BD = 32 * ((D + 31) / 32);
+  // S in TMEM with wide MMAs while 2 x 2BD accumulator columns + one S slot
+  // fit in 512 (D <= 96); wide MMAs with S in shared memory up to D = 128.
+  if (!smem_s && 4 * BD + 64 <= 512)
+    return grad_side_impl<SIDE, VAR, MASKED, true, true>(A, F, va, vb, C, dC, dQ, B, N, M, D,
+                                                         beta, eps, dA, dva, st, mask);
+  if (2 * BD <= 256)
+    return grad_side_impl<SIDE, VAR, MASKED, false, true>(A, F, va, vb, C, dC, dQ, B, N, M, D,
+                                                          beta, eps, dA, dva, st, mask);
+  return grad_side_impl<SIDE, VAR, MASKED, false, false>(A, F, va, vb, C, dC, dQ, B, N, M, D,
+                                                         beta, eps, dA, dva, st, mask);
 }
 
 }  // namespace
