@@ -100,6 +100,87 @@ __device__ __forceinline__ float split_line(uint8_t* hi_base, uint8_t* lo_base, 
   return ss;
 }
 
+// Epilogue of one 128 x BN cost tile (accumulator a): TMEM -> registers ->
+// cost (and penalty, positivity mask) -> swizzled staging -> TMA store.
+// Called by the four epilogue warps; `si` counts staging-buffer uses.
+template <bool VAR>
+__device__ __forceinline__ void cost_epilogue_tile(
+    const TileCoord& c, int a, uint32_t tmem, int warp, int row, const float* x2s,
+    const float* y2s, uint64_t* acce, uint64_t* nempty, uint8_t* stg_base,
+    const CUtensorMap* mapC, const CUtensorMap* mapQ, const float* __restrict__ vx,
+    const float* __restrict__ vy, int N, int M, float beta, float eps, int write_q,
+    uint32_t* __restrict__ mask, int& si) {
+  tc_fence_after();
+  const int i = c.ib * BM + row;
+  const float x2 = x2s[row];
+  float vxi = 0.f;
+  if (VAR) vxi = i < N ? vx[(long long)c.b * N + i] : 1.f;
+#pragma unroll 1
+  for (int cc = 0; cc < BN / 32; ++cc) {
+    float v[32], w[32];
+    const uint32_t tcol =
+        tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(a * COST_ACC_COLS + 32 * cc);
+    tmem_ld32(tcol, v);
+    tmem_ld32(tcol + BN, w);
+    if (cc == BN / 32 - 1) {
+      tc_fence_before();
+      mbar_arrive(acce);
+    }
+#pragma unroll
+    for (int q = 0; q < 32; ++q) v[q] += w[q];  // (hi.hi + lo.hi) + (hi.lo + lo.lo)
+    const int j0 = c.jb * BN + 32 * cc;
+    float qv[32];
+    uint32_t pos = 0;  // bit q: sq_raw > 0 at column j0 + q
+#pragma unroll
+    for (int q = 0; q < 32; ++q) {
+      float sq = (x2 + y2s[32 * cc + q]) - 2.f * v[q];
+      pos |= (sq > 0.f ? 1u : 0u) << q;
+      sq = sq > 0.f ? sq : 0.f;
+      if (VAR) {
+        const int j = j0 + q;
+        const float vyj = j < M ? vy[(long long)c.b * M + j] : 1.f;
+        float var = 0.5f * (vxi + vyj);
+        var = var > eps ? var : eps;
+        v[q] = sq / var;
+        qv[q] = beta * logf(var);
+      } else {
+        v[q] = sq;
+      }
+    }
+    if (cc == BN / 32 - 1) mbar_arrive(nempty);
+    if (mask != nullptr && j0 < M) {
+      // words [b][j >> 5][i] with the row count padded to NP = 4 ceil(N/4)
+      const int NP = (N + 3) & ~3;
+      if (i < NP) {
+        const int left = M - j0;
+        const uint32_t valid = left >= 32 ? 0xFFFFFFFFu : ((1u << left) - 1u);
+        const int MW = (M + 31) >> 5;
+        mask[((long long)c.b * MW + (j0 >> 5)) * NP + i] = i < N ? (pos & valid) : 0u;
+      }
+    }
+    // C chunk (and Q chunk) through the two staging buffers
+#pragma unroll
+    for (int which = 0; which < (VAR ? 2 : 1); ++which) {
+      if (which == 1 && !write_q) break;
+      uint8_t* buf = stg_base + (size_t)(si & 1) * STG_BYTES;
+      if (row == 0) bulk_wait_read<1>();
+      named_bar(1, 128);
+      const float* src = which == 0 ? v : qv;
+#pragma unroll
+      for (int q4 = 0; q4 < 8; ++q4)
+        *reinterpret_cast<float4*>(buf + sw128_chunk(row, q4)) =
+            make_float4(src[4 * q4], src[4 * q4 + 1], src[4 * q4 + 2], src[4 * q4 + 3]);
+      fence_async_smem();
+      named_bar(1, 128);
+      if (row == 0) {
+        tma_store_3d(which == 0 ? mapC : mapQ, buf, j0, c.ib * BM, c.b);
+        bulk_commit();
+      }
+      ++si;
+    }
+  }
+}
+
 template <bool VAR>
 __global__ void __launch_bounds__(COST_THREADS, 1)
     tc_cost_kernel(const __grid_constant__ CUtensorMap mapX, const __grid_constant__ CUtensorMap mapY,
@@ -251,73 +332,262 @@ __global__ void __launch_bounds__(COST_THREADS, 1)
       const bool ok = mbar_wait(&sh.accf[a], ph, abort) && mbar_wait(&sh.nfull[a], ph, abort);
       if (!ok) record_timeout(abort);
       if (named_bar_or(1, 128, !ok)) break;  // the four warps stop together
-      tc_fence_after();
-      const int i = c.ib * BM + row;
-      const float x2 = sh.x2[a][row];
-      float vxi = 0.f;
-      if (VAR) vxi = i < N ? vx[(long long)c.b * N + i] : 1.f;
-#pragma unroll 1
-      for (int cc = 0; cc < BN / 32; ++cc) {
-        float v[32], w[32];
-        const uint32_t tcol = tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(a * COST_ACC_COLS + 32 * cc);
-        tmem_ld32(tcol, v);
-        tmem_ld32(tcol + BN, w);
-        if (cc == BN / 32 - 1) {
-          tc_fence_before();
-          mbar_arrive(&sh.acce[a]);
-        }
-#pragma unroll
-        for (int q = 0; q < 32; ++q) v[q] += w[q];  // (hi.hi + lo.hi) + (hi.lo + lo.lo)
-        const int j0 = c.jb * BN + 32 * cc;
-        float qv[32];
-        uint32_t pos = 0;  // bit q: sq_raw > 0 at column j0 + q
-#pragma unroll
-        for (int q = 0; q < 32; ++q) {
-          float sq = (x2 + sh.y2[a][32 * cc + q]) - 2.f * v[q];
-          pos |= (sq > 0.f ? 1u : 0u) << q;
-          sq = sq > 0.f ? sq : 0.f;
-          if (VAR) {
-            const int j = j0 + q;
-            const float vyj = j < M ? vy[(long long)c.b * M + j] : 1.f;
-            float var = 0.5f * (vxi + vyj);
-            var = var > eps ? var : eps;
-            v[q] = sq / var;
-            qv[q] = beta * logf(var);
-          } else {
-            v[q] = sq;
+      cost_epilogue_tile<VAR>(c, a, tmem, warp, row, sh.x2[a], sh.y2[a], &sh.acce[a],
+                              &sh.nempty[a], stg_base, &mapC, &mapQ, vx, vy, N, M, beta, eps,
+                              write_q, mask, si);
+    }
+    if (row == 0) bulk_wait_all();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 9) tmem_dealloc(tmem, COST_TMEM_COLS);
+}
+
+// ----------------------------------------------------------------------
+// Cost with the X row block resident: a work unit is one pair's 128 rows
+// (b, ib) against all its column tiles.  The X chunks of the unit are loaded
+// and split into TF32 (hi, lo) once (XB buffers, so the next unit's X loads
+// while this one is in use) and serve every column tile; only Y streams
+// through the YS-deep ring.  Same roles, tiles and epilogue as
+// tc_cost_kernel.
+constexpr int XR_MAX_YS = 4;
+constexpr int XR_CHUNK = 2 * TILE_A;   // hi + lo of one 128 x 32 chunk (32 KB)
+
+struct CostXRShared {
+  float x2[2][BM];
+  float y2[2][BN];
+  uint64_t full[XR_MAX_YS], empty[XR_MAX_YS], conv[XR_MAX_YS];
+  uint64_t xfull[2], xempty[2], xconv[2];
+  uint64_t accf[2], acce[2], nfull[2], nempty[2];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort;
+};
+
+struct CostXRGeom {
+  int nK;   // 32-feature chunks
+  int XB;   // X buffers (1 or 2)
+  int YS;   // Y stages
+};
+
+template <bool VAR>
+__global__ void __launch_bounds__(COST_THREADS, 1)
+    tc_cost_xr_kernel(const __grid_constant__ CUtensorMap mapX,
+                      const __grid_constant__ CUtensorMap mapY,
+                      const __grid_constant__ CUtensorMap mapC,
+                      const __grid_constant__ CUtensorMap mapQ, const float* __restrict__ vx,
+                      const float* __restrict__ vy, int B, int N, int M, int D, float beta,
+                      float eps, int write_q, uint32_t* __restrict__ mask, CostXRGeom g) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int nK = g.nK, XB = g.XB, YS = g.YS;
+  uint8_t* x_base = smem;                                        // XB x nK chunks
+  uint8_t* y_base = smem + (size_t)XB * nK * XR_CHUNK;            // YS chunks
+  uint8_t* stg_base = y_base + (size_t)YS * XR_CHUNK;
+  CostXRShared& sh = *reinterpret_cast<CostXRShared*>(stg_base + 2 * STG_BYTES);
+  volatile int* abort = &sh.abort;
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int nI = (N + BM - 1) / BM, nJ = (M + BN - 1) / BN;
+  const int units = B * nI;
+
+  if (tid == 0) {
+    if ((smem_u32(smem) & 1023u) != 0) {
+      atomicExch(&g_tc_error, kLaunch);
+      sh.abort = 1;
+    } else {
+      sh.abort = 0;
+    }
+    for (int s = 0; s < YS; ++s) {
+      mbar_init(&sh.full[s], 1);
+      mbar_init(&sh.empty[s], 1);
+      mbar_init(&sh.conv[s], 128);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&sh.xfull[a], 1);
+      mbar_init(&sh.xempty[a], 1);
+      mbar_init(&sh.xconv[a], 128);
+      mbar_init(&sh.accf[a], 1);
+      mbar_init(&sh.acce[a], 128);
+      mbar_init(&sh.nfull[a], 128);
+      mbar_init(&sh.nempty[a], 128);
+    }
+    mbar_init(&sh.mma_done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 8 && lane == 0) {
+    prefetch_map(&mapX);
+    prefetch_map(&mapY);
+    prefetch_map(&mapC);
+    if (VAR) prefetch_map(&mapQ);
+  }
+  if (warp == 9) tmem_alloc(&sh.tmem_base, COST_TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh.tmem_base;
+  const bool dead = sh.abort != 0;
+
+  if (!dead && warp == 8 && lane == 0) {
+    // ------------------------------------------------ TMA producer
+    int it = 0, ui = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++ui) {
+      const int b = u / nI, ib = u - b * nI;
+      const int xb = ui % XB;
+      if (!mbar_wait(&sh.xempty[xb], ((unsigned)(ui / XB) & 1u) ^ 1u, abort)) {
+        record_timeout(abort);
+        goto producer_drain;
+      }
+      mbar_arrive_expect_tx(&sh.xfull[xb], nK * TILE_A);
+      for (int kc = 0; kc < nK; ++kc)
+        tma_load_3d(x_base + (size_t)(xb * nK + kc) * XR_CHUNK, &mapX, &sh.xfull[xb], kc * KC,
+                    ib * BM, b);
+      for (int jb = 0; jb < nJ; ++jb) {
+        for (int kc = 0; kc < nK; ++kc, ++it) {
+          const int s = it % YS;
+          if (!mbar_wait(&sh.empty[s], ((unsigned)(it / YS) & 1u) ^ 1u, abort)) {
+            record_timeout(abort);
+            goto producer_drain;
           }
+          mbar_arrive_expect_tx(&sh.full[s], TILE_B);
+          tma_load_3d(y_base + (size_t)s * XR_CHUNK, &mapY, &sh.full[s], kc * KC, jb * BN, b);
         }
-        if (cc == BN / 32 - 1) mbar_arrive(&sh.nempty[a]);
-        if (mask != nullptr && j0 < M) {
-          // words [b][j >> 5][i] with the row count padded to NP = 4 ceil(N/4)
-          const int NP = (N + 3) & ~3;
-          if (i < NP) {
-            const int left = M - j0;
-            const uint32_t valid = left >= 32 ? 0xFFFFFFFFu : ((1u << left) - 1u);
-            const int MW = (M + 31) >> 5;
-            mask[((long long)c.b * MW + (j0 >> 5)) * NP + i] = i < N ? (pos & valid) : 0u;
+      }
+    }
+  producer_drain:
+    // every load issued lands before the CTA exits
+    for (int k = (it > YS ? it - YS : 0); k < it; ++k) {
+      const int s = k % YS;
+      for (unsigned n = 0; n < kSpinLimit; ++n)
+        if (mbar_try_wait(&sh.full[s], (unsigned)(k / YS) & 1u)) break;
+    }
+    for (int k = (ui > XB ? ui - XB : 0); k < ui; ++k) {
+      const int xb = k % XB;
+      for (unsigned n = 0; n < kSpinLimit; ++n)
+        if (mbar_try_wait(&sh.xfull[xb], (unsigned)(k / XB) & 1u)) break;
+    }
+  } else if (!dead && warp >= 4 && warp < 8) {
+    // ------------------------------------------------ TF32 split + norms
+    const int ct = tid - 128;
+    int it = 0, ti = 0, ui = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++ui) {
+      const int xb = ui % XB;
+      if (!mbar_wait(&sh.xfull[xb], (unsigned)(ui / XB) & 1u, abort)) {
+        record_timeout(abort);
+        goto split_done;
+      }
+      float sa = 0.f;
+      for (int kc = 0; kc < nK; ++kc) {
+        uint8_t* xc = x_base + (size_t)(xb * nK + kc) * XR_CHUNK;
+        sa += split_line(xc, xc + TILE_A, ct);
+      }
+      fence_async_smem();
+      mbar_arrive(&sh.xconv[xb]);
+      for (int jb = 0; jb < nJ; ++jb, ++ti) {
+        float sb = 0.f;
+        for (int kc = 0; kc < nK; ++kc, ++it) {
+          const int s = it % YS;
+          if (!mbar_wait(&sh.full[s], (unsigned)(it / YS) & 1u, abort)) {
+            record_timeout(abort);
+            goto split_done;
           }
-        }
-        // C chunk (and Q chunk) through the two staging buffers
-#pragma unroll
-        for (int which = 0; which < (VAR ? 2 : 1); ++which) {
-          if (which == 1 && !write_q) break;
-          uint8_t* buf = stg_base + (size_t)(si & 1) * STG_BYTES;
-          if (row == 0) bulk_wait_read<1>();
-          named_bar(1, 128);
-          const float* src = which == 0 ? v : qv;
-#pragma unroll
-          for (int q4 = 0; q4 < 8; ++q4)
-            *reinterpret_cast<float4*>(buf + sw128_chunk(row, q4)) =
-                make_float4(src[4 * q4], src[4 * q4 + 1], src[4 * q4 + 2], src[4 * q4 + 3]);
+          uint8_t* yc = y_base + (size_t)s * XR_CHUNK;
+          sb += split_line(yc, yc + TILE_B, ct);
           fence_async_smem();
-          named_bar(1, 128);
-          if (row == 0) {
-            tma_store_3d(which == 0 ? &mapC : &mapQ, buf, j0, c.ib * BM, c.b);
-            bulk_commit();
-          }
-          ++si;
+          mbar_arrive(&sh.conv[s]);
         }
+        const int a = ti & 1;
+        if (!mbar_wait(&sh.nempty[a], ((unsigned)(ti >> 1) & 1u) ^ 1u, abort)) {
+          record_timeout(abort);
+          goto split_done;
+        }
+        sh.x2[a][ct] = sa;
+        sh.y2[a][ct] = sb;
+        mbar_arrive(&sh.nfull[a]);
+      }
+    }
+  split_done:;
+  } else if (!dead && warp == 9) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t IDESC = idesc_tf32(BM, 2 * BN, 0, 0);
+      int it = 0, ti = 0, ui = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++ui) {
+        const int xb = ui % XB;
+        if (!mbar_wait(&sh.xconv[xb], (unsigned)(ui / XB) & 1u, abort)) {
+          record_timeout(abort);
+          break;
+        }
+        tc_fence_after();
+        for (int jb = 0; jb < nJ && ok; ++jb, ++ti) {
+          const int a = ti & 1;
+          if (!mbar_wait(&sh.acce[a], ((unsigned)(ti >> 1) & 1u) ^ 1u, abort)) {
+            record_timeout(abort);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d_tmem = tmem + (uint32_t)(a * COST_ACC_COLS);
+          for (int kc = 0; kc < nK; ++kc, ++it) {
+            const int s = it % YS;
+            if (!mbar_wait(&sh.conv[s], (unsigned)(it / YS) & 1u, abort)) {
+              record_timeout(abort);
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t ah = smem_u32(x_base + (size_t)(xb * nK + kc) * XR_CHUNK);
+            const uint32_t al = ah + TILE_A;
+            const uint32_t bh = smem_u32(y_base + (size_t)s * XR_CHUNK);
+#pragma unroll
+            for (int kk = 0; kk < KC / 8; ++kk) {
+              // B = [B_hi; B_lo] (256 rows): A_hi B -> hi.hi | hi.lo, A_lo B -> lo.hi | lo.lo
+              const uint64_t dah = smem_desc_sw128(ah + kk * 32, 16, 1024);
+              const uint64_t dal = smem_desc_sw128(al + kk * 32, 16, 1024);
+              const uint64_t db = smem_desc_sw128(bh + kk * 32, 16, 1024);
+              mma_tf32(d_tmem, dah, db, IDESC, (kc | kk) != 0);
+              mma_tf32(d_tmem, dal, db, IDESC, 1);
+            }
+            mma_commit(&sh.empty[s]);
+          }
+          if (!ok) break;
+          mma_commit(&sh.accf[a]);
+        }
+        if (!ok) break;
+        mma_commit(&sh.xempty[xb]);   // this unit's X chunks are free once its MMAs finish
+      }
+      // every MMA issued has finished before TMEM is released
+      mma_commit(&sh.mma_done);
+      for (unsigned n = 0; n < kSpinLimit; ++n)
+        if (mbar_try_wait(&sh.mma_done, 0)) break;
+    }
+    __syncwarp();
+  } else if (!dead && warp < 4) {
+    // ------------------------------------------------ epilogue
+    const int row = tid;  // TMEM lane == tile row
+    int ti = 0, si = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      const int b = u / nI, ib = u - b * nI;
+      for (int jb = 0; jb < nJ; ++jb, ++ti) {
+        TileCoord c;
+        c.b = b;
+        c.ib = ib;
+        c.jb = jb;
+        const int a = ti & 1;
+        const unsigned ph = (unsigned)(ti >> 1) & 1u;
+        const bool good = mbar_wait(&sh.accf[a], ph, abort) && mbar_wait(&sh.nfull[a], ph, abort);
+        if (!good) record_timeout(abort);
+        if (named_bar_or(1, 128, !good)) {  // the four warps stop together
+          ok = false;
+          break;
+        }
+        cost_epilogue_tile<VAR>(c, a, tmem, warp, row, sh.x2[a], sh.y2[a], &sh.acce[a],
+                                &sh.nempty[a], stg_base, &mapC, &mapQ, vx, vy, N, M, beta, eps,
+                                write_q, mask, si);
       }
     }
     if (row == 0) bulk_wait_all();
@@ -1081,9 +1351,30 @@ int tc_cost_f32(const float* X, const float* Y, const float* vx, const float* vy
   if ((rc = make_map_3d_f32(&mC, C, M, N, B, 32, BM)) != kOk) return rc;
   mQ = mC;
   if (Q != nullptr && (rc = make_map_3d_f32(&mQ, Q, M, N, B, 32, BM)) != kOk) return rc;
+  const bool var = vx != nullptr;
+  // X-resident form while one row block's X chunks and at least two Y stages
+  // fit in shared memory (D <= 128); otherwise every tile streams X and Y.
+  const int nK = (D + KC - 1) / KC;
+  const int budget = 232448 - 2 * STG_BYTES - (int)sizeof(CostXRShared);
+  for (int XB = 2; XB >= 1; --XB) {
+    int YS = (budget - XB * nK * XR_CHUNK) / XR_CHUNK;
+    if (YS > XR_MAX_YS) YS = XR_MAX_YS;
+    if (YS < 2) continue;
+    const CostXRGeom g{nK, XB, YS};
+    const size_t smem =
+        (size_t)(XB * nK + YS) * XR_CHUNK + 2 * STG_BYTES + sizeof(CostXRShared);
+    const long long units = (long long)B * ((N + BM - 1) / BM);
+    const int grid = (int)(units < sm_count() ? units : sm_count());
+    auto kern = var ? tc_cost_xr_kernel<true> : tc_cost_xr_kernel<false>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    kern<<<grid, COST_THREADS, smem, st>>>(mX, mY, mC, mQ, vx, vy, B, N, M, D, (float)beta,
+                                           (float)eps, Q != nullptr ? 1 : 0, mask, g);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(kLaunch, "tc cost launch: %s", cudaGetErrorString(e));
+    return kOk;
+  }
   const long long tiles = (long long)B * ((N + BM - 1) / BM) * ((M + BN - 1) / BN);
   const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
-  const bool var = vx != nullptr;
   auto kern = var ? tc_cost_kernel<true> : tc_cost_kernel<false>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)COST_SMEM);
   kern<<<grid, COST_THREADS, COST_SMEM, st>>>(mX, mY, mC, mQ, vx, vy, B, N, M, D, (float)beta,
