@@ -194,8 +194,10 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
   const int lane = wi.lane;
   const T big = Big<T>::value;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  T* ringC = reinterpret_cast<T*>(smem_raw) + (size_t)wi.wib * RW * (HAS_P ? 2 : 1);
+  T* ringC = reinterpret_cast<T*>(smem_raw) + (size_t)wi.wib * (RW * (HAS_P ? 2 : 1) + 64);
   T* ringQ = ringC + RW;
+  // bottom-row values of the current 32-step window: R at [0, 32), P at [32, 64)
+  T* coll = ringC + RW * (HAS_P ? 2 : 1);
   for (int i = lane; i < RW; i += 32) {
     ringC[i] = a.pad_raw;
     if (HAS_P) ringQ[i] = T(0);
@@ -246,7 +248,6 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
     rbP = row_above(dlP, lane, p, wi, T(0));
     rbPn = row_above(dlP, 32 + lane, p, wi, T(0));
   }
-  T wbR = T(0), wbP = T(0);  // bottom-row values collected for the delay line
 
   const long long woff = (long long)wi.w * p.tmax * KS * 32;
   const T kap = a.kappa;
@@ -270,6 +271,7 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
     cp_async_commit();
 
     const bool wrapw = ((t0 + TILE) & 31) == 0;  // column t0+8 opens the next window
+    T* coll8 = coll + (t0 & 24);                 // slot of step t0 + s is coll8[s]
     T* srow = a.sR + woff + lane + (long long)t0 * KS * 32;
     T* prow = HAS_P ? a.sP + woff + lane + (long long)t0 * KS * 32 : nullptr;
     const int c0 = (t0 - lane) & (RING - 1);
@@ -297,12 +299,11 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
         srow[(s * KS + k) * 32] = Rn[k];
         if (HAS_P) prow[(s * KS + k) * 32] = Pn[k];
       }
-      // bottom row (column t - 32 KS + 1) is kept by lane t mod 32
-      const T v = shfl(Rn[KS - 1], 31);
-      const T vp = HAS_P ? shfl(Pn[KS - 1], 31) : T(0);
-      const bool mine = lane == ((t0 + s) & 31);
-      wbR = mine ? v : wbR;
-      if (HAS_P) wbP = mine ? vp : wbP;
+      // bottom row (column t - 32 KS + 1): lane 31 files it under step t mod 32
+      if (lane == 31) {
+        coll8[s] = Rn[KS - 1];
+        if (HAS_P) coll8[32 + s] = Pn[KS - 1];
+      }
       // row -1 value for the next step (column t + 1)
       const bool nextw = (s == TILE - 1) && wrapw;
       const T bv = shfl(nextw ? rbRn : rbR, (t0 + s + 1) & 31);
@@ -323,7 +324,11 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
     }
 
     if (wrapw) {
-      // lanes hold the bottom row for columns t0 - 23 - 32 KS + lane
+      // lane l takes the bottom row of step l of the window: column
+      // t0 - 23 - 32 KS + lane
+      __syncwarp();
+      const T wbR = coll[lane];
+      const T wbP = HAS_P ? coll[32 + lane] : T(0);
       const int scx = t0 - 23 - 32 * KS + lane;
       if (scx >= 0) {
         const int j = scx - (scx / p.L) * p.L;
@@ -405,11 +410,13 @@ __device__ __forceinline__ void cell_backward(T Rl, T Ru, T Rd, T Pl, T Pu, T Pd
   const T inv = rcp(add_rn(add_rn(T(1), e1), e2));
   const bool p1 = Rl <= Ru;
   const bool p2 = m1 <= Rd;
+  // unnormalised weights of the left / up / diagonal predecessors
   const T wm1 = p2 ? T(1) : e2;
-  const T wd = (p2 ? e2 : T(1)) * inv;
-  const T wl = (p1 ? wm1 : e1) * inv;
-  const T wu = (p1 ? e1 : wm1) * inv;
+  const T ud = p2 ? e2 : T(1);
+  const T ul = p1 ? wm1 : e1;
+  const T uu = p1 ? e1 : wm1;
   if constexpr (HAS_P) {
+    const T wd = ud * inv, wl = ul * inv, wu = uu * inv;
     const T A = wl * Pl + wu * Pu + wd * Pd;
     const T pg = pbar * inv_gamma;
     pl = wl * (rbar - pg * (Pl - A));
@@ -419,9 +426,10 @@ __device__ __forceinline__ void cell_backward(T Rl, T Ru, T Rd, T Pl, T Pu, T Pd
     qu = wu * pbar;
     qd = wd * pbar;
   } else {
-    pl = wl * rbar;
-    pu = wu * rbar;
-    pd = wd * rbar;
+    const T ri = rbar * inv;  // adjoint over the soft-min normaliser
+    pl = ul * ri;
+    pu = uu * ri;
+    pd = ud * ri;
     ql = qu = qd = T(0);
   }
 }
@@ -459,9 +467,11 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
   const int lane = wi.lane;
   const T big = Big<T>::value;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  T* base = reinterpret_cast<T*>(smem_raw) + (size_t)wi.wib * RW * (HAS_P ? 2 : 1);
+  T* base = reinterpret_cast<T*>(smem_raw) + (size_t)wi.wib * (RW * (HAS_P ? 2 : 1) + 64);
   T* outC = base;
   T* outQ = base + RW;
+  // top-row sends of the current 32-step window: R at [0, 32), P at [32, 64)
+  T* coll = base + RW * (HAS_P ? 2 : 1);
   T* myC = outC + lane * S;
   T* myQ = outQ + lane * S;
 
@@ -514,7 +524,6 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
     dP = push_from_below(dlP, 32 * dw + lane, p, wi);
     dPn = push_from_below(dlP, 32 * (dw - 1) + lane, p, wi);
   }
-  T wdR = T(0), wdP = T(0);  // top-row sends collected for the delay line
 
   {  // cur = saved row t_first - 1, Xc = X(t_first)
     const T b0 = row_above_saved<T, KS>(sRw, t_first, p, wi, big);
@@ -537,8 +546,19 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
   const int NBL = p.NB * p.L;
   int cap_i = wi.npairs - 1;
   int cap_t = cap_i * NBL + ((p.N - 1) / rows) * p.L + (p.M - 1) + 32 * kstar + lstar;
-  T seed_r = a.grad_r[wi.p0 + cap_i];
-  T seed_p = HAS_P ? a.grad_p[wi.p0 + cap_i] : T(0);
+  // adjoint seeds dL/dR (dL/dP) of the current pair's end cell, held by the
+  // lane and sub-band that own it
+  const bool seed_lane = lane == lstar;
+  T sdR[KS], sdP[KS];
+  {
+    const T sr = a.grad_r[wi.p0 + cap_i];
+    const T sp = HAS_P ? a.grad_p[wi.p0 + cap_i] : T(0);
+#pragma unroll
+    for (int k = 0; k < KS; ++k) {
+      sdR[k] = (seed_lane && k == kstar) ? sr : T(0);
+      sdP[k] = (seed_lane && k == kstar) ? sp : T(0);
+    }
+  }
 
   // tile completed by this lane in block b: u = b - 4k - lane/8
   Cursor fl[KS];
@@ -555,17 +575,19 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
     }
     const bool lowb = (t0 & 31) == 0;  // iteration t0 reads row -1 of column t0-1 from bRn
     const bool seedhere = cap_t >= t0 && cap_t < t0 + TILE;
+    const int s_inj = seedhere ? cap_t - t0 : -1;  // step of this block that seeds
+    T* coll8 = coll + (t0 & 24);                   // slot of step t0 + s is coll8[s]
 
 #pragma unroll
     for (int s = TILE - 1; s >= 0; --s) {
       const int t = t0 + s;
       // the end cell of a pair receives dL/dR (and dL/dP) as its adjoint
-      const bool inj = seedhere && t == cap_t && lane == lstar;
+      if (s == s_inj) {
 #pragma unroll
-      for (int k = 0; k < KS; ++k) {
-        const bool kk = inj && k == kstar;
-        accL[k] += kk ? seed_r : T(0);
-        if (HAS_P) Qacc[k] += kk ? seed_p : T(0);
+        for (int k = 0; k < KS; ++k) {
+          accL[k] += sdR[k];
+          if (HAS_P) Qacc[k] += sdP[k];
+        }
       }
       // predecessor rows: saved row t-2 and X(t-1)
       const bool loww = (s == 0) && lowb;
@@ -606,12 +628,11 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
           dgq[k] = qd;
         }
       }
-      // top row's send (column t) is kept by lane t mod 32
-      const T v = shfl(send[0], 0);
-      const T vq = HAS_P ? shfl(sendq[0], 0) : T(0);
-      const bool mine = lane == (t & 31);
-      wdR = mine ? v : wdR;
-      if (HAS_P) wdP = mine ? vq : wdP;
+      // top row's send (column t): lane 0 files it under step t mod 32
+      if (lane == 0) {
+        coll8[s] = send[0];
+        if (HAS_P) coll8[32 + s] = sendq[0];
+      }
       // adjoint arriving at the bottom row (lane 31, sub-band KS-1) at t-1
       const T dv = shfl(dR, (t - 32 * KS) & 31);
       const T dvq = HAS_P ? shfl(dP, (t - 32 * KS) & 31) : T(0);
@@ -648,12 +669,21 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
       --cap_i;
       cap_t = cap_i >= 0 ? cap_t - NBL : -1;
       if (cap_i >= 0) {
-        seed_r = a.grad_r[wi.p0 + cap_i];
-        if (HAS_P) seed_p = a.grad_p[wi.p0 + cap_i];
+        const T sr = a.grad_r[wi.p0 + cap_i];
+        const T sp = HAS_P ? a.grad_p[wi.p0 + cap_i] : T(0);
+#pragma unroll
+        for (int k = 0; k < KS; ++k) {
+          sdR[k] = (seed_lane && k == kstar) ? sr : T(0);
+          sdP[k] = (seed_lane && k == kstar) ? sp : T(0);
+        }
       }
     }
     if (lowb) {
-      // the window [t0, t0+32) of top-row sends is complete
+      // the window [t0, t0+32) of top-row sends is complete: lane l takes
+      // the send of step t0 + l
+      __syncwarp();
+      const T wdR = coll[lane];
+      const T wdP = HAS_P ? coll[32 + lane] : T(0);
       const int j = (t0 + lane) - ((t0 + lane) / p.L) * p.L;
       dlR[j] = wdR;
       if (HAS_P) dlP[j] = wdP;
@@ -788,7 +818,7 @@ StreamPlan make_stream_plan(int B, int N, int M, int eb, bool has_p, int sms) {
   if (p.NB > 1 && L < rows + 128) L = rows + 128;
   p.L = (L + TILE - 1) / TILE * TILE;
   const int S = eb == 4 ? RingStride<float>::value : RingStride<double>::value;
-  const size_t per_w = (size_t)p.KS * 32 * S * eb * (has_p ? 2 : 1);
+  const size_t per_w = ((size_t)p.KS * 32 * S * (has_p ? 2 : 1) + 64) * eb;
   // Warps per SM: bounded by shared memory (the per-lane rings), by the
   // registers of the heavier of the two sweeps, and by 32.
   int wps = (int)((size_t)(216 * 1024) / per_w);
