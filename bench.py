@@ -48,16 +48,16 @@ ALGO_BYTES_PER_CELL = 8      # soft-DTW fwd+bwd: cost read + cost-gradient write
 # launch, DRAM bytes per cell of one launch measured by ncu).  Algorithmic:
 # the DP forward's cost read and the backward's cost-gradient write (the
 # 8 B/cell of the step split between them), the cost builder's cost write,
-# each chain-rule launch's cost + cost-gradient read.  Measured: DRAM read +
+# each chain-rule launch's cost-gradient read.  Measured: DRAM read +
 # write per cell from the `ncu --set full` capture of the same kernels at
 # B=4096, N=M=256 (profiles/soft_dtw_b4096_n256_kernels_ncu.md), applied per
 # cell to the launch being timed; feature bytes (X, Y, dX, dY) are added at
 # the timed shape.
 CALLS = {
-    "udtw_cost": (1, 4, 4.0),            # + X, Y read
-    "sdtw_forward": (1, 4, 8.16),        # C read + saved R' write
-    "sdtw_backward": (1, 4, 9.57),       # saved R' read + dC write (+1.5 B/cell to find)
-    "udtw_features_grad": (2, 8, 8.96),  # C + dC read (+ other side's features via L2)
+    "udtw_cost": (1, 4, 4.0),            # C write (+ mask), + X, Y read
+    "sdtw_forward": (1, 4, 8.19),        # C read + saved R' write
+    "sdtw_backward": (1, 4, 9.72),       # saved R' read + dC write (+1.6 B/cell to find)
+    "udtw_features_grad": (2, 4, 4.1),   # dC (+ positivity mask) read per side
 }
 
 
@@ -73,6 +73,10 @@ def parse():
     ap.add_argument("--gamma", type=float, default=0.01)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--workload", default="cfg5",
+                    choices=["cfg5", "cfg5-udtw", "cfg1", "cfg2", "cfg3", "cfg4", "cfg4-cost"],
+                    help="cfg5 (default) is the headline line; the others time the remaining "
+                         "configurations on one GPU (secondary lines, same JSON shape)")
     return ap.parse_args()
 
 
@@ -390,10 +394,117 @@ def run_reference(a):
     print(json.dumps(line))
 
 
+# ------------------------------------------------- secondary workloads
+
+def _secondary(a):
+    """One GPU, inputs resident, fwd+bwd per step, CUDA-event timed; the
+    configurations of the other SURVEY configs (seeded synthetic inputs with
+    their shapes) and the uDTW variant of cfg5.  Algorithmic bytes follow the
+    byte accounting of each configuration."""
+    import torchwarp_b200 as twb
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(4321)
+    w = a.workload
+
+    def rn(*shape):
+        return torch.randn(*shape, device=dev, generator=g)
+
+    if w == "cfg5-udtw":
+        B, N, D = a.batch, a.length, a.dim
+        X, Y = rn(B, N, D), rn(B, N, D)
+        sx = torch.rand(B, N, 1, device=dev, generator=g) + 0.5
+        sy = torch.rand(B, N, 1, device=dev, generator=g) + 0.5
+        cells, algo = B * N * N, 16 * B * N * N
+        metric = "fwd+bwd DP cells/s (uDTW B={} N=M={} D={}, beta=1)".format(B, N, D)
+
+        def step():
+            x, y = X.detach().requires_grad_(True), Y.detach().requires_grad_(True)
+            a_, b_ = sx.detach().requires_grad_(True), sy.detach().requires_grad_(True)
+            out = twb.functional.udtw(x, y, a_, b_, gamma=a.gamma, beta=1.0)
+            (out.distance + out.penalty).sum().backward()
+    elif w == "cfg1":
+        X, Y = rn(64, 30, 8), rn(64, 40, 8)
+        sx = torch.rand(64, 30, 1, device=dev, generator=g) + 0.5
+        sy = torch.rand(64, 40, 1, device=dev, generator=g) + 0.5
+        cells, algo = 64 * 30 * 40, 16 * 64 * 30 * 40
+        metric = "fwd+bwd DP cells/s (uDTW B=64 N=30 M=40 D=8)"
+
+        def step():
+            x, y = X.detach().requires_grad_(True), Y.detach().requires_grad_(True)
+            a_, b_ = sx.detach().requires_grad_(True), sy.detach().requires_grad_(True)
+            out = twb.functional.udtw(x, y, a_, b_, gamma=1.0, beta=1.0)
+            (out.distance + out.penalty).mean().backward()
+    elif w == "cfg2":
+        def series():
+            s_ = torch.cumsum(0.1 * rn(500, 140, 1), dim=1)
+            return (s_ - s_.mean(1, keepdim=True)) / s_.std(1, keepdim=True)
+        X, Y = series(), series()
+        cells, algo = 500 * 140 * 140, 8 * 500 * 140 * 140
+        metric = "fwd+bwd DP cells/s (soft-DTW B=500 N=M=140 D=1)"
+
+        def step():
+            x = X.detach().requires_grad_(True)
+            twb.functional.soft_dtw(x, Y, gamma=0.1).sum().backward()
+    elif w == "cfg3":
+        Q, S_ = rn(1024, 15, 10, 256), rn(1024, 10, 256)
+        cells, algo = 1024 * 15 * 10 * 10, 335544320
+        metric = "fwd+bwd DP cells/s (JEANIE B=1024 K=15 T=U=10 D=256)"
+
+        def step():
+            q, s_ = Q.detach().requires_grad_(True), S_.detach().requires_grad_(True)
+            twb.functional.jeanie(q, s_, gamma=0.1, max_shift=1).sum().backward()
+    elif w == "cfg4":
+        Q, S_ = rn(1024, 7, 7, 10, 256), rn(1024, 10, 256)
+        cells, algo = 1024 * 49 * 10 * 10, 1048576000
+        metric = "fwd+bwd DP cells/s (FVM B=1024 K1=K2=7 T=U=10 D=256)"
+
+        def step():
+            q, s_ = Q.detach().requires_grad_(True), S_.detach().requires_grad_(True)
+            twb.functional.fvm(q, s_, gamma=0.1).sum().backward()
+    else:  # cfg4-cost
+        Cc = rn(1024, 7, 7, 10, 10).abs()
+        cells, algo = 1024 * 49 * 10 * 10, 40140800
+        metric = "fwd+bwd DP cells/s (fvm_from_cost B=1024 K1=K2=7 T=U=10)"
+
+        def step():
+            c = Cc.detach().requires_grad_(True)
+            twb.functional.fvm_from_cost(c, gamma=0.1).sum().backward()
+
+    from torchwarp_b200 import _native
+    for _ in range(a.warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / a.steps
+    with _native.LaunchTimer() as lt:   # per native call, in a separate untimed pass
+        step()
+    torch.cuda.synchronize()
+    calls = {k: round(v[1], 4) for k, v in lt.totals().items()}
+    peak, src = peaks()
+    achieved = algo / (ms / 1e3) / 1e9
+    print(json.dumps({"metric": metric, "value": cells / (ms / 1e3), "unit": UNIT, "n_gpus": 1,
+                      "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms,
+                      "higher_is_better": True, "dtype": "f32", "data": "synthetic",
+                      "config": {"workload": w},
+                      "roofline": {"bound": "hbm", "kernel": "whole step",
+                                   "algorithmic_bytes_per_step": algo, "achieved": achieved,
+                                   "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                                   "peak_source": src},
+                      "native_calls_ms": calls}))
+
+
 def main():
     a = parse()
     if a.impl == "reference":
         run_reference(a)
+    elif a.workload != "cfg5":
+        _secondary(a)
     else:
         run_ours(a)
 

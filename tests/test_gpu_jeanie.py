@@ -293,3 +293,51 @@ def test_path_matrix_is_gradient(tw):
         p = a.optimal_path[b]
         assert p[0] == (0, 0) and p[-1] == (8, 11)
         assert float(a.path_matrix[b, 0, 0]) == pytest.approx(1.0, abs=1e-6)
+
+
+# ------------------------- fp32 warp-per-row query/support cost and gradient
+
+def _qs_ref(q, s, metric):
+    q, s = q.double(), s.double()
+    raw = (q * q).sum(-1)[:, :, None] + (s * s).sum(-1)[:, None, :] - 2 * q @ s.transpose(1, 2)
+    sq = raw.clamp_min(0)
+    return torch.where(raw > 0, sq.sqrt(), torch.zeros_like(sq)) if metric == 1 else sq
+
+
+@pytest.mark.parametrize("R,U,D", [(150, 10, 256), (490, 10, 256), (37, 3, 64), (64, 16, 128),
+                                   (20, 12, 100), (9, 7, 252), (33, 10, 36)])
+@pytest.mark.parametrize("metric", [0, 1])
+def test_qs_fast_fp32(R, U, D, metric):
+    """The fp32 query/support cost and its chain rule (warp-per-row kernels for
+    U <= 16, D <= 256) against a float64 torch evaluation of the same formulas
+    (jeanie/distances.py:15-38; zero gradient where the cost is 0)."""
+    from torchwarp_b200 import _native as nat
+    B = 6
+    g = torch.Generator(device=DEV).manual_seed(R + U + D)
+    q = torch.randn(B, R, D, device=DEV, generator=g)
+    s = torch.randn(B, U, D, device=DEV, generator=g)
+    q[:, 0] = s[:, 0]  # an exactly zero cost
+    cost = torch.empty(B, R, U, device=DEV)
+    st = nat.stream_of(q)
+    nat.check(nat.lib().tw_qs_cost_f32(nat.ptr(q), nat.ptr(s), B, R, U, D, metric,
+                                       nat.ptr(cost), st), "qs cost")
+    torch.cuda.synchronize()
+    ref = _qs_ref(q, s, metric)
+    # fp32 rounding of |q|^2 + |s|^2 - 2 q.s is ~1e-4 here; its square root (metric 1)
+    # near a zero distance is ~1e-2
+    torch.testing.assert_close(cost.double(), ref, rtol=1e-5, atol=2e-2 if metric else 1e-3 * D / 8)
+    dcost = torch.randn(B, R, U, device=DEV, generator=g)
+    dq, ds = torch.empty_like(q), torch.empty_like(s)
+    nat.check(nat.lib().tw_qs_cost_grad_f32(nat.ptr(q), nat.ptr(s), nat.ptr(cost), nat.ptr(dcost),
+                                            B, R, U, D, metric, nat.ptr(dq), nat.ptr(ds), st),
+              "qs grad")
+    torch.cuda.synchronize()
+    c64 = cost.double()
+    dc = dcost.double()
+    dsq = torch.where(c64 > 0, dc * 0.5 / c64 if metric == 1 else dc, torch.zeros_like(dc))
+    q64, s64 = q.double(), s.double()
+    rdq = 2 * q64 * dsq.sum(2, keepdim=True) - 2 * dsq @ s64
+    rds = 2 * s64 * dsq.sum(1)[:, :, None] - 2 * dsq.transpose(1, 2) @ q64
+    for got, want in ((dq, rdq), (ds, rds)):
+        scale = float(want.abs().max()) + 1.0
+        torch.testing.assert_close(got.double(), want, rtol=1e-4, atol=1e-5 * scale)

@@ -320,6 +320,263 @@ __global__ void fvm_softmin_bwd_kernel(const T* __restrict__ cost, const T* __re
   for (int n = 0; n < Kf; ++n) dc[(long long)n * TU] = g * ex2(m - c[(long long)n * TU] * kap);
 }
 
+// ---------------------------------------------------------------------------
+// Warp-per-row forms of the query/support cost and its chain rule for fp32,
+// U <= 16 support frames and D <= 256 features (the JEANIE / FVM shapes).
+// Lanes split the features (4 per lane per 128-feature chunk), so every q row
+// is read with coalesced 16-byte loads; the pair's support rows (and, in the
+// backward, the partial ds accumulators) stay in registers, and the U dot
+// products of a row meet in a shuffle butterfly.  Row sums and the ds
+// partials of the warps are combined in a fixed order: results are
+// bitwise reproducible.
+
+constexpr int QW = 4;  // warps per CTA
+
+template <int CU>
+__device__ __forceinline__ void warp_allreduce(float (&v)[CU]) {
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1)
+#pragma unroll
+    for (int u = 0; u < CU; ++u) v[u] += __shfl_xor_sync(0xffffffffu, v[u], m);
+}
+
+__device__ __forceinline__ float dot4(float4 a, float4 b) {
+  return fmaf(a.x, b.x, fmaf(a.y, b.y, fmaf(a.z, b.z, a.w * b.w)));
+}
+
+template <int NCH, int CU>
+__global__ void __launch_bounds__(32 * QW) qs_cost_fast_kernel(const float* __restrict__ q,
+                                                                const float* __restrict__ s,
+                                                                int Rr, int U, int D, int metric,
+                                                                float* __restrict__ cost) {
+  const int b = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* sb = s + (long long)b * U * D;
+  const float* qb = q + (long long)b * Rr * D;
+  float4 sv[NCH][CU];
+  float s2[CU];
+#pragma unroll
+  for (int u = 0; u < CU; ++u) {
+    s2[u] = 0.f;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int d = c * 128 + 4 * lane;
+      sv[c][u] = (u < U && d < D) ? __ldg(reinterpret_cast<const float4*>(sb + (long long)u * D + d))
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+      s2[u] += dot4(sv[c][u], sv[c][u]);
+    }
+  }
+  warp_allreduce<CU>(s2);
+  float s2u = s2[0];
+#pragma unroll
+  for (int u = 1; u < CU; ++u) s2u = lane == u ? s2[u] : s2u;
+  // two rows per iteration (r and r + step): independent loads and butterflies
+  const int step = gridDim.x * QW;
+  for (int r = blockIdx.x * QW + warp; r < Rr; r += 2 * step) {
+    const int r2 = r + step;
+    const bool has2 = r2 < Rr;
+    float acc[2][CU + 1];
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int u = 0; u <= CU; ++u) acc[h][u] = 0.f;
+    float4 qv[2][NCH];
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int d = c * 128 + 4 * lane;
+      qv[0][c] = d < D ? __ldg(reinterpret_cast<const float4*>(qb + (long long)r * D + d))
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
+      qv[1][c] = (d < D && has2)
+                     ? __ldg(reinterpret_cast<const float4*>(qb + (long long)r2 * D + d))
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int c = 0; c < NCH; ++c)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        acc[h][CU] += dot4(qv[h][c], qv[h][c]);
+#pragma unroll
+        for (int u = 0; u < CU; ++u) acc[h][u] += dot4(qv[h][c], sv[c][u]);
+      }
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1)
+#pragma unroll
+      for (int u = 0; u <= CU; ++u) {
+        acc[0][u] += __shfl_xor_sync(0xffffffffu, acc[0][u], m);
+        acc[1][u] += __shfl_xor_sync(0xffffffffu, acc[1][u], m);
+      }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      // lane u writes column u
+      float mine = acc[h][0];
+#pragma unroll
+      for (int u = 1; u < CU; ++u) mine = lane == u ? acc[h][u] : mine;
+      const int rr = h == 0 ? r : r2;
+      if (lane < U && (h == 0 || has2)) {
+        const float raw = (acc[h][CU] + s2u) - 2.f * mine;
+        const float sq = raw > 0.f ? raw : 0.f;
+        cost[((long long)b * Rr + rr) * U + lane] =
+            metric == 1 ? (raw > 0.f ? sqrtf(sq) : 0.f) : sq;
+      }
+    }
+  }
+}
+
+template <int NCH, int CU>
+__global__ void __launch_bounds__(32 * QW) qs_grad_fast_kernel(
+    const float* __restrict__ q, const float* __restrict__ s, const float* __restrict__ cost,
+    const float* __restrict__ dcost, int Rr, int U, int D, int metric, float* __restrict__ dq,
+    float* __restrict__ ds) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float4* part = reinterpret_cast<float4*>(smem_raw);  // [QW][NCH][CU][32] ds partials
+  float* csum = reinterpret_cast<float*>(part + QW * NCH * CU * 32);  // [QW][CU]
+  const int b = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* sb = s + (long long)b * U * D;
+  const float* qb = q + (long long)b * Rr * D;
+  float4 sv[NCH][CU], acc[NCH][CU];
+#pragma unroll
+  for (int u = 0; u < CU; ++u)
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int d = c * 128 + 4 * lane;
+      sv[c][u] = (u < U && d < D) ? __ldg(reinterpret_cast<const float4*>(sb + (long long)u * D + d))
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+      acc[c][u] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  float cs[CU];
+#pragma unroll
+  for (int u = 0; u < CU; ++u) cs[u] = 0.f;
+  // the next row's cost / dcost / q are loaded one iteration ahead
+  float cn = 0.f, dcn = 0.f;
+  float4 qn[NCH];
+  auto fetch = [&](int r) {
+    if (r < Rr) {
+      if (lane < U) {
+        const long long o = ((long long)b * Rr + r) * U + lane;
+        cn = __ldg(cost + o);
+        dcn = __ldg(dcost + o);
+      }
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        const int d = c * 128 + 4 * lane;
+        qn[c] = d < D ? __ldg(reinterpret_cast<const float4*>(qb + (long long)r * D + d))
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+  };
+  fetch(warp);
+  for (int r = warp; r < Rr; r += QW) {
+    const float c0 = cn, dc0 = dcn;
+    float4 qcur[NCH];
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) qcur[c] = qn[c];
+    fetch(r + QW);
+    // dsq of the row: dcost (metric 0) or dcost / (2 cost) (metric 1), 0
+    // where the cost is 0 (the clamp_min / sqrt-at-0 convention)
+    float gl = 0.f;
+    if (lane < U) gl = c0 > 0.f ? (metric == 1 ? dc0 * 0.5f / c0 : dc0) : 0.f;
+    float gu[CU];
+    float rs = 0.f;
+#pragma unroll
+    for (int u = 0; u < CU; ++u) {
+      gu[u] = __shfl_sync(0xffffffffu, gl, u);
+      rs += gu[u];
+      cs[u] += gu[u];
+    }
+    float* dqr = dq + ((long long)b * Rr + r) * D;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int d = c * 128 + 4 * lane;
+      if (d >= D) continue;
+      const float4 qv = qcur[c];
+      float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < CU; ++u) {
+        t.x = fmaf(gu[u], sv[c][u].x, t.x);
+        t.y = fmaf(gu[u], sv[c][u].y, t.y);
+        t.z = fmaf(gu[u], sv[c][u].z, t.z);
+        t.w = fmaf(gu[u], sv[c][u].w, t.w);
+        acc[c][u].x = fmaf(gu[u], qv.x, acc[c][u].x);
+        acc[c][u].y = fmaf(gu[u], qv.y, acc[c][u].y);
+        acc[c][u].z = fmaf(gu[u], qv.z, acc[c][u].z);
+        acc[c][u].w = fmaf(gu[u], qv.w, acc[c][u].w);
+      }
+      float4 o;
+      o.x = 2.f * qv.x * rs - 2.f * t.x;
+      o.y = 2.f * qv.y * rs - 2.f * t.y;
+      o.z = 2.f * qv.z * rs - 2.f * t.z;
+      o.w = 2.f * qv.w * rs - 2.f * t.w;
+      *reinterpret_cast<float4*>(dqr + d) = o;
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < NCH; ++c)
+#pragma unroll
+    for (int u = 0; u < CU; ++u) part[((warp * NCH + c) * CU + u) * 32 + lane] = acc[c][u];
+  if (lane == 0)
+#pragma unroll
+    for (int u = 0; u < CU; ++u) csum[warp * CU + u] = cs[u];
+  __syncthreads();
+  // ds[u][d] = 2 s_u[d] colsum_u - 2 sum_r dsq_ru q_r[d], warps summed in order
+  for (int e = threadIdx.x; e < NCH * CU * 32; e += 32 * QW) {
+    const int l = e & 31, cu = e >> 5, u = cu % CU, c = cu / CU;
+    const int d = c * 128 + 4 * l;
+    if (u >= U || d >= D) continue;
+    float4 a = part[(0 * NCH * CU + cu) * 32 + l];
+    float col = csum[u];
+#pragma unroll
+    for (int w = 1; w < QW; ++w) {
+      const float4 p = part[(w * NCH * CU + cu) * 32 + l];
+      a.x += p.x; a.y += p.y; a.z += p.z; a.w += p.w;
+      col += csum[w * CU + u];
+    }
+    const float4 sd = __ldg(reinterpret_cast<const float4*>(sb + (long long)u * D + d));
+    float4 o;
+    o.x = 2.f * sd.x * col - 2.f * a.x;
+    o.y = 2.f * sd.y * col - 2.f * a.y;
+    o.z = 2.f * sd.z * col - 2.f * a.z;
+    o.w = 2.f * sd.w * col - 2.f * a.w;
+    *reinterpret_cast<float4*>(ds + ((long long)b * U + u) * D + d) = o;
+  }
+}
+
+template <int NCH, int CU>
+int qs_fast_launch(const float* q, const float* s, const float* cost, const float* dcost, int B,
+                   int Rr, int U, int D, int metric, float* out_cost, float* dq, float* ds,
+                   cudaStream_t st) {
+  if (out_cost != nullptr) {
+    int gx = (Rr + 32 * QW - 1) / (32 * QW);  // about 32 rows per warp: the support load amortises
+    dim3 grid(gx, B);
+    qs_cost_fast_kernel<NCH, CU><<<grid, 32 * QW, 0, st>>>(q, s, Rr, U, D, metric, out_cost);
+  } else {
+    const size_t smem = (size_t)QW * NCH * CU * 32 * sizeof(float4) + (size_t)QW * CU * sizeof(float);
+    auto kern = qs_grad_fast_kernel<NCH, CU>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+      return set_error(kLaunch, "qs grad: shared memory");
+    kern<<<B, 32 * QW, smem, st>>>(q, s, cost, dcost, Rr, U, D, metric, dq, ds);
+  }
+  return kOk;
+}
+
+// Dispatch to the warp-per-row kernels when they apply; kUnsupported otherwise.
+int qs_fast(const float* q, const float* s, const float* cost, const float* dcost, int B, int Rr,
+            int U, int D, int metric, float* out_cost, float* dq, float* ds, cudaStream_t st) {
+  if (D % 4 != 0 || D > 256 || U > 16 || U < 1 || ((uintptr_t)q & 15u) || ((uintptr_t)s & 15u) ||
+      (dq && ((uintptr_t)dq & 15u)) || (ds && ((uintptr_t)ds & 15u)))
+    return kUnsupported;
+  const int nch = D > 128 ? 2 : 1;
+  const int cu = U <= 4 ? 4 : (U <= 8 ? 8 : (U <= 12 ? 12 : 16));
+#define TW_QS(NC, C)                                                                             \
+  if (nch == NC && cu == C)                                                                      \
+    return qs_fast_launch<NC, C>(q, s, cost, dcost, B, Rr, U, D, metric, out_cost, dq, ds, st);
+  TW_QS(1, 4) TW_QS(1, 8) TW_QS(1, 12) TW_QS(1, 16)
+  TW_QS(2, 4) TW_QS(2, 8) TW_QS(2, 12) TW_QS(2, 16)
+#undef TW_QS
+  return kUnsupported;
+}
+
 template <typename T>
 int check_launch(const char* what) {
   const cudaError_t e = cudaGetLastError();
@@ -353,6 +610,10 @@ template <typename T>
 int qs_cost(const T* q, const T* s, int B, int Rr, int U, int D, int metric, T* cost,
             cudaStream_t st) {
   if (B == 0 || Rr == 0) return kOk;
+  if constexpr (sizeof(T) == 4) {
+    if (qs_fast(q, s, nullptr, nullptr, B, Rr, U, D, metric, cost, nullptr, nullptr, st) == kOk)
+      return check_launch<T>("query/support cost");
+  }
   const size_t smem = (size_t)(CU * D + CU) * sizeof(T);
   if (smem > 200 * 1024) return set_error(kUnsupported, "feature dimension %d too large", D);
   auto kern = qs_cost_kernel<T>;
@@ -370,6 +631,10 @@ template <typename T>
 int qs_grad(const T* q, const T* s, const T* cost, const T* dcost, int B, int Rr, int U, int D,
             int metric, T* dq, T* ds, cudaStream_t st) {
   if (B == 0 || Rr == 0) return kOk;
+  if constexpr (sizeof(T) == 4) {
+    if (qs_fast(q, s, cost, dcost, B, Rr, U, D, metric, nullptr, dq, ds, st) == kOk)
+      return check_launch<T>("query/support gradient");
+  }
   const size_t smem = ((size_t)GR * GU + (size_t)GU * GF + (size_t)GR * GU * GF + GU) * sizeof(T);
   auto kern = qs_grad_kernel<T>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
