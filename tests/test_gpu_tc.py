@@ -75,8 +75,10 @@ def test_tc_cost(shape, var, monkeypatch):
     torch.testing.assert_close(C.double(), Cr, rtol=1e-5, atol=atol)
     torch.testing.assert_close(C, Cs, rtol=1e-5, atol=atol)
     if var:
-        torch.testing.assert_close(Q.double(), Qr, rtol=1e-6, atol=1e-6)
-        torch.testing.assert_close(Q, Qs, rtol=0, atol=0)
+        # the tensor-core epilogue takes beta ln(var) from the hardware log2
+        # (relative error ~2^-22); the SIMT kernel calls logf
+        torch.testing.assert_close(Q.double(), Qr, rtol=2e-6, atol=2e-6)
+        torch.testing.assert_close(Q, Qs, rtol=2e-6, atol=2e-6)
 
 
 def test_tc_cost_self_distance_is_zero_on_the_diagonal(monkeypatch):

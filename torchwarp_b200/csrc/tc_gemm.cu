@@ -33,7 +33,7 @@ using namespace tc;
 constexpr int BM = 128;            // rows (i) per tile
 constexpr int BN = 128;            // columns (j) per tile
 constexpr int KC = 32;             // features per chunk: one 128-byte swizzle line
-constexpr int STAGES = 3;
+constexpr int STAGES = 2;  // streaming form (D > 128); the X-resident form has its own ring
 constexpr int TILE_A = BM * KC * 4;                       // 16 KB
 constexpr int TILE_B = BN * KC * 4;                       // 16 KB
 constexpr int STAGE_BYTES = 2 * TILE_A + 2 * TILE_B;      // hi and lo of A and B
@@ -48,6 +48,7 @@ constexpr uint32_t COST_TMEM_COLS = 2 * COST_ACC_COLS;
 struct CostShared {
   float x2[2][BM];
   float y2[2][BN];
+  float vyt[2][BN];  // uDTW: the tile's column variances
   uint64_t full[STAGES], empty[STAGES], conv[STAGES];
   uint64_t accf[2], acce[2], nfull[2], nempty[2];
   uint64_t mma_done;
@@ -106,7 +107,7 @@ __device__ __forceinline__ float split_line(uint8_t* hi_base, uint8_t* lo_base, 
 template <bool VAR>
 __device__ __forceinline__ void cost_epilogue_tile(
     const TileCoord& c, int a, uint32_t tmem, int warp, int row, const float* x2s,
-    const float* y2s, uint64_t* acce, uint64_t* nempty, uint8_t* stg_base,
+    const float* y2s, const float* vys, uint64_t* acce, uint64_t* nempty, uint8_t* stg_base,
     const CUtensorMap* mapC, const CUtensorMap* mapQ, const float* __restrict__ vx,
     const float* __restrict__ vy, int N, int M, float beta, float eps, int write_q,
     uint32_t* __restrict__ mask, int& si) {
@@ -115,6 +116,7 @@ __device__ __forceinline__ void cost_epilogue_tile(
   const float x2 = x2s[row];
   float vxi = 0.f;
   if (VAR) vxi = i < N ? vx[(long long)c.b * N + i] : 1.f;
+  const float beta_ln2 = beta * 0.693147180559945309f;
 #pragma unroll 1
   for (int cc = 0; cc < BN / 32; ++cc) {
     float v[32], w[32];
@@ -137,12 +139,12 @@ __device__ __forceinline__ void cost_epilogue_tile(
       pos |= (sq > 0.f ? 1u : 0u) << q;
       sq = sq > 0.f ? sq : 0.f;
       if (VAR) {
-        const int j = j0 + q;
-        const float vyj = j < M ? vy[(long long)c.b * M + j] : 1.f;
-        float var = 0.5f * (vxi + vyj);
+        // var = max((vx_i + vy_j) / 2, eps); cost = sq / var through a
+        // correctly rounded reciprocal; penalty = beta ln(var) from log2
+        float var = 0.5f * (vxi + vys[32 * cc + q]);
         var = var > eps ? var : eps;
-        v[q] = sq / var;
-        qv[q] = beta * logf(var);
+        v[q] = sq * __frcp_rn(var);
+        qv[q] = beta_ln2 * lg2(var);
       } else {
         v[q] = sq;
       }
@@ -277,6 +279,11 @@ __global__ void __launch_bounds__(COST_THREADS, 1)
       }
       sh.x2[a][ct] = sa;
       sh.y2[a][ct] = sb;
+      if (VAR) {
+        const TileCoord c = tile_of(t, nI, nJ);
+        const int j = c.jb * BN + ct;
+        sh.vyt[a][ct] = j < M ? vy[(long long)c.b * M + j] : 1.f;
+      }
       mbar_arrive(&sh.nfull[a]);
     }
   split_done:;
@@ -332,9 +339,9 @@ __global__ void __launch_bounds__(COST_THREADS, 1)
       const bool ok = mbar_wait(&sh.accf[a], ph, abort) && mbar_wait(&sh.nfull[a], ph, abort);
       if (!ok) record_timeout(abort);
       if (named_bar_or(1, 128, !ok)) break;  // the four warps stop together
-      cost_epilogue_tile<VAR>(c, a, tmem, warp, row, sh.x2[a], sh.y2[a], &sh.acce[a],
-                              &sh.nempty[a], stg_base, &mapC, &mapQ, vx, vy, N, M, beta, eps,
-                              write_q, mask, si);
+      cost_epilogue_tile<VAR>(c, a, tmem, warp, row, sh.x2[a], sh.y2[a], sh.vyt[a],
+                              &sh.acce[a], &sh.nempty[a], stg_base, &mapC, &mapQ, vx, vy, N, M,
+                              beta, eps, write_q, mask, si);
     }
     if (row == 0) bulk_wait_all();
   }
@@ -358,6 +365,7 @@ constexpr int XR_CHUNK = 2 * TILE_A;   // hi + lo of one 128 x 32 chunk (32 KB)
 struct CostXRShared {
   float x2[2][BM];
   float y2[2][BN];
+  float vyt[2][BN];  // uDTW: the tile's column variances
   uint64_t full[XR_MAX_YS], empty[XR_MAX_YS], conv[XR_MAX_YS];
   uint64_t xfull[2], xempty[2], xconv[2];
   uint64_t accf[2], acce[2], nfull[2], nempty[2];
@@ -505,6 +513,10 @@ __global__ void __launch_bounds__(COST_THREADS, 1)
         }
         sh.x2[a][ct] = sa;
         sh.y2[a][ct] = sb;
+        if (VAR) {
+          const int j = jb * BN + ct;
+          sh.vyt[a][ct] = j < M ? vy[(long long)(u / nI) * M + j] : 1.f;
+        }
         mbar_arrive(&sh.nfull[a]);
       }
     }
@@ -585,9 +597,9 @@ __global__ void __launch_bounds__(COST_THREADS, 1)
           ok = false;
           break;
         }
-        cost_epilogue_tile<VAR>(c, a, tmem, warp, row, sh.x2[a], sh.y2[a], &sh.acce[a],
-                                &sh.nempty[a], stg_base, &mapC, &mapQ, vx, vy, N, M, beta, eps,
-                                write_q, mask, si);
+        cost_epilogue_tile<VAR>(c, a, tmem, warp, row, sh.x2[a], sh.y2[a], sh.vyt[a],
+                                &sh.acce[a], &sh.nempty[a], stg_base, &mapC, &mapQ, vx, vy, N,
+                                M, beta, eps, write_q, mask, si);
       }
     }
     if (row == 0) bulk_wait_all();
@@ -820,6 +832,12 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
         tc_fence_after();  // the MMAs that read this TMEM slot have completed
         const uint8_t* ld = land_base + (size_t)s * g.l_bytes;
         uint8_t* cv = conv_base + (size_t)cs * g.c_bytes;
+        // uDTW: lane l holds the other side's variance at summed index kc*32 + l
+        float vbl = 1.f;
+        if (VAR) {
+          const int idx = kc * 32 + lane;
+          vbl = idx < S ? __ldg(vb_b + idx) : 1.f;
+        }
         float sv[16];
         if (SIDE == 0) {
           const uint32_t mword =
@@ -843,15 +861,14 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
             for (int e = 0; e < 4; ++e) {
               const int jj = 16 * hh + 4 * k + e;  // summed column within the chunk
               if (MASKED) ce[e] = (mword >> jj) & 1u ? 1.f : 0.f;
-              float var = 1.f, var_raw = 1.f;
+              float inv = 1.f, var_raw = 1.f;
               if (VAR) {
-                const int j = kc * 32 + jj;
-                var_raw = 0.5f * (va_r + (j < S ? __ldg(vb_b + j) : 1.f));
-                var = var_raw > eps ? var_raw : eps;
+                var_raw = 0.5f * (va_r + __shfl_sync(0xffffffffu, vbl, jj));
+                inv = __frcp_rn(var_raw > eps ? var_raw : eps);
               }
-              const float v = ce[e] > 0.f ? (VAR ? ge[e] / var : ge[e]) : 0.f;
+              const float v = ce[e] > 0.f ? (VAR ? ge[e] * inv : ge[e]) : 0.f;
               rsum += v;
-              if (VAR && var_raw > eps) vsum += (beta * qe[e] - ge[e] * ce[e]) / var;
+              if (VAR && var_raw > eps) vsum += (beta * qe[e] - ge[e] * ce[e]) * inv;
               sv[4 * k + e] = v;
             }
           }
@@ -873,15 +890,14 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
             }
             const float qv = (VAR && has_dq) ? *reinterpret_cast<const float*>(ld + g.l_dq + off)
                                              : 0.f;
-            float var = 1.f, var_raw = 1.f;
+            float inv = 1.f, var_raw = 1.f;
             if (VAR) {
-              const int i = kc * 32 + rr;
-              var_raw = 0.5f * ((i < S ? __ldg(vb_b + i) : 1.f) + va_r);
-              var = var_raw > eps ? var_raw : eps;
+              var_raw = 0.5f * (__shfl_sync(0xffffffffu, vbl, rr) + va_r);
+              inv = __frcp_rn(var_raw > eps ? var_raw : eps);
             }
-            const float v = cvv > 0.f ? (VAR ? gv / var : gv) : 0.f;
+            const float v = cvv > 0.f ? (VAR ? gv * inv : gv) : 0.f;
             rsum += v;
-            if (VAR && var_raw > eps) vsum += (beta * qv - gv * cvv) / var;
+            if (VAR && var_raw > eps) vsum += (beta * qv - gv * cvv) * inv;
             sv[k] = v;
           }
         }
