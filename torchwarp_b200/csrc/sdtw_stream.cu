@@ -781,9 +781,15 @@ int resident_blocks_any(int eb, int KS, bool has_p, int wpc, size_t smem) {
 #define TW_RB(TT, K)                                                                          \
   n = has_p ? resident_blocks<TT, K, true>(wpc, smem) : resident_blocks<TT, K, false>(wpc, smem)
   if (eb == 4) {
-    if (KS == 1) TW_RB(float, 1); else if (KS == 2) TW_RB(float, 2); else TW_RB(float, 4);
+    if (KS == 1) TW_RB(float, 1);
+    else if (KS == 2) TW_RB(float, 2);
+    else if (KS == 3) TW_RB(float, 3);
+    else TW_RB(float, 4);
   } else {
-    if (KS == 1) TW_RB(double, 1); else if (KS == 2) TW_RB(double, 2); else TW_RB(double, 4);
+    if (KS == 1) TW_RB(double, 1);
+    else if (KS == 2) TW_RB(double, 2);
+    else if (KS == 3) TW_RB(double, 3);
+    else TW_RB(double, 4);
   }
 #undef TW_RB
   if (n >= 0) {
@@ -809,7 +815,7 @@ StreamPlan make_stream_plan(int B, int N, int M, int eb, bool has_p, int sms) {
   // per SM) is what hides the soft-min's latency, and every sub-band costs a
   // ring of shared memory, so two sub-bands by default.
   int ks = env_int("TW_STREAM_KS", N <= 32 ? 1 : 2);
-  p.KS = ks >= 4 ? 4 : (ks >= 2 ? 2 : 1);
+  p.KS = ks >= 4 ? 4 : (ks < 1 ? 1 : ks);
   const int rows = 32 * p.KS;
   p.NB = (N + rows - 1) / rows;
   // The band-to-band delay line needs L >= 32*KS + 128 (see row_above); a
@@ -825,11 +831,24 @@ StreamPlan make_stream_plan(int B, int N, int M, int eb, bool has_p, int sms) {
   wps = wps < 1 ? 1 : (wps > 32 ? 32 : wps);
   const int cap = env_int("TW_STREAM_WPS", 0);
   if (cap > 0 && cap < wps) wps = cap;
-  int wpc = wps < 4 ? wps : 4;
-  if (wpc > B) wpc = B > 0 ? B : 1;
-  int cps = wps / wpc > 0 ? wps / wpc : 1;
-  const int resident = resident_blocks_any(eb, p.KS, has_p, wpc, per_w * wpc);
-  if (resident > 0 && resident < cps) cps = resident;
+  // Warps per CTA: 4, or 2 when register-limited residency rounds better in
+  // pairs of warps (the heavier sub-band counts).
+  int wpc = 4, cps = 1;
+  {
+    int best = -1;
+    for (int cand = 4; cand >= 2; cand -= 2) {
+      int c = cand > wps ? wps : cand;
+      if (c > B) c = B > 0 ? B : 1;
+      int n = wps / c > 0 ? wps / c : 1;
+      const int resident = resident_blocks_any(eb, p.KS, has_p, c, per_w * c);
+      if (resident > 0 && resident < n) n = resident;
+      if (n * c > best) {
+        best = n * c;
+        wpc = c;
+        cps = n;
+      }
+    }
+  }
   // Every warp carries whole pairs, so the sweep lasts as long as the warp
   // with the most pairs.  Take the fewest pairs per warp the resident warps
   // allow, then the fewest warps that still achieve it (equal loads).
@@ -855,6 +874,7 @@ int sdtw_stream_forward(const SdtwArgs<T>& a, bool has_p, bool has_band, cudaStr
   switch (a.p.KS) {
     case 1: return fwd_ks<T, 1>(a, has_p, has_band, st);
     case 2: return fwd_ks<T, 2>(a, has_p, has_band, st);
+    case 3: return fwd_ks<T, 3>(a, has_p, has_band, st);
     case 4: return fwd_ks<T, 4>(a, has_p, has_band, st);
     default: return set_error(kUnsupported, "sdtw forward: unsupported sub-band count %d", a.p.KS);
   }
@@ -865,6 +885,7 @@ int sdtw_stream_backward(const SdtwArgs<T>& a, bool has_p, bool /*has_band*/, cu
   switch (a.p.KS) {
     case 1: return bwd_ks<T, 1>(a, has_p, st);
     case 2: return bwd_ks<T, 2>(a, has_p, st);
+    case 3: return bwd_ks<T, 3>(a, has_p, st);
     case 4: return bwd_ks<T, 4>(a, has_p, st);
     default: return set_error(kUnsupported, "sdtw backward: unsupported sub-band count %d", a.p.KS);
   }
