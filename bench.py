@@ -305,7 +305,7 @@ def run_ours(a):
             "config": config(a, world), "e2e": e2e, "roofline": roofline,
             "cpu_baseline": cpu, "clocks": clk.summary(), "gpu_launches": gpu_launches,
             "native_calls_per_step": launches_per_step}
-    print(json.dumps(line))
+    _emit(line)
 
 
 # --------------------------------------------------------------- CPU arms
@@ -391,7 +391,7 @@ def run_reference(a):
                                            pairs, a.length, a.dim, a.batch)},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
-    print(json.dumps(line))
+    _emit(line)
 
 
 # ------------------------------------------------- secondary workloads
@@ -488,19 +488,43 @@ def _secondary(a):
     calls = {k: round(v[1], 4) for k, v in lt.totals().items()}
     peak, src = peaks()
     achieved = algo / (ms / 1e3) / 1e9
-    print(json.dumps({"metric": metric, "value": cells / (ms / 1e3), "unit": UNIT, "n_gpus": 1,
-                      "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms,
-                      "higher_is_better": True, "dtype": "f32", "data": "synthetic",
-                      "config": {"workload": w},
-                      "roofline": {"bound": "hbm", "kernel": "whole step",
-                                   "algorithmic_bytes_per_step": algo, "achieved": achieved,
-                                   "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                                   "peak_source": src},
-                      "native_calls_ms": calls}))
+    _emit({"metric": metric, "value": cells / (ms / 1e3), "unit": UNIT, "n_gpus": 1,
+           "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms,
+           "higher_is_better": True, "dtype": "f32", "data": "synthetic",
+           "config": {"workload": w},
+           "roofline": {"bound": "hbm", "kernel": "whole step",
+                        "algorithmic_bytes_per_step": algo, "achieved": achieved,
+                        "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                        "peak_source": src},
+           "native_calls_ms": calls})
+
+
+_JSON_FD = None
+
+
+def _stdout_to_stderr():
+    """Point file descriptor 1 at stderr for the whole run, so that whatever a
+    library writes to stdout (NCCL's version banner, for one) lands on stderr,
+    and keep a duplicate of the original stdout for the single JSON line."""
+    global _JSON_FD
+    sys.stdout.flush()
+    _JSON_FD = os.dup(1)
+    os.dup2(2, 1)
+
+
+def _emit(obj):
+    """Write the result line, and nothing else, to the original stdout."""
+    data = (json.dumps(obj) + "\n").encode()
+    if _JSON_FD is None:
+        sys.stdout.write(data.decode())
+        sys.stdout.flush()
+        return
+    os.write(_JSON_FD, data)
 
 
 def main():
     a = parse()
+    _stdout_to_stderr()
     if a.impl == "reference":
         run_reference(a)
     elif a.workload != "cfg5":
