@@ -35,6 +35,15 @@ constexpr int TILE = 8;    // columns per copy tile / flush tile
 constexpr int LEAD = 2;    // forward: cost tiles issued ahead of use
 static_assert(TILE * (LEAD + 2) <= RING, "ring too small for the lead");
 
+// Shared memory of one warp, in elements: the per-lane rings (cost / penalty
+// in the forward, adjoint staging in the backward), 64 slots for band-edge
+// collection, and the 64-column circular buffers of row -1 values (both
+// sweeps) and of adjoints arriving from the band below (backward), one set
+// for R and one for P.
+__host__ __device__ constexpr int warp_smem_elems(int KS, int S, bool has_p) {
+  return KS * 32 * S * (has_p ? 2 : 1) + 64 + (has_p ? 256 : 128);
+}
+
 __device__ __forceinline__ int floor_div(int a, int b) {
   const int q = a / b;
   return (a % b != 0 && a < 0) ? q - 1 : q;
@@ -162,15 +171,17 @@ __device__ __forceinline__ T row_above(const T* dl, int sc, const StreamPlan& p,
   return v;
 }
 
+// c is the raw cost; kap = log2(e) / gamma scales it into the log2 domain
+// inside the final fused multiply-add.
 template <typename T, bool HAS_P>
-__device__ __forceinline__ void cell_forward(T c, T qv, T left, T up, T dg, T Pl, T Pu, T Pd,
-                                             T& r, T& pv) {
+__device__ __forceinline__ void cell_forward(T c, T kap, T qv, T left, T up, T dg, T Pl, T Pu,
+                                             T Pd, T& r, T& pv) {
   const T m1 = fmin(left, up), M1 = fmax(left, up);
   const T m = fmin(m1, dg), Mx = fmax(m1, dg);
   const T e1 = ex2(add_rn(m, -M1));
   const T e2 = ex2(add_rn(m, -Mx));
   const T s = add_rn(add_rn(T(1), e1), e2);
-  r = add_rn(c, add_rn(m, -lg2(s)));
+  r = fma(c, kap, add_rn(m, -lg2(s)));
   if constexpr (HAS_P) {
     const bool p1 = left <= up;
     const bool p2 = m1 <= dg;
@@ -194,10 +205,14 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
   const int lane = wi.lane;
   const T big = Big<T>::value;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  T* ringC = reinterpret_cast<T*>(smem_raw) + (size_t)wi.wib * (RW * (HAS_P ? 2 : 1) + 64);
+  T* ringC = reinterpret_cast<T*>(smem_raw) + (size_t)wi.wib * warp_smem_elems(KS, S, HAS_P);
   T* ringQ = ringC + RW;
   // bottom-row values of the current 32-step window: R at [0, 32), P at [32, 64)
   T* coll = ringC + RW * (HAS_P ? 2 : 1);
+  // row -1 values (lane 0 / sub-band 0) by stream column mod 64: the window
+  // of the current step and the next one
+  T* fb = coll + 64;
+  T* fbp = fb + 64;
   for (int i = lane; i < RW; i += 32) {
     ringC[i] = a.pad_raw;
     if (HAS_P) ringQ[i] = T(0);
@@ -241,16 +256,24 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
 
   T* dlR = a.dlR + (long long)wi.w * p.L;
   T* dlP = HAS_P ? a.dlP + (long long)wi.w * p.L : nullptr;
-  // row -1 values for lane 0 / sub-band 0, one 32-column window per register
-  T rbR = row_above(dlR, lane, p, wi, big), rbRn = row_above(dlR, 32 + lane, p, wi, big);
-  T rbP = T(0), rbPn = T(0);
+  fb[lane] = row_above(dlR, lane, p, wi, big);
+  fb[32 + lane] = row_above(dlR, 32 + lane, p, wi, big);
   if (HAS_P) {
-    rbP = row_above(dlP, lane, p, wi, T(0));
-    rbPn = row_above(dlP, 32 + lane, p, wi, T(0));
+    fbp[lane] = row_above(dlP, lane, p, wi, T(0));
+    fbp[32 + lane] = row_above(dlP, 32 + lane, p, wi, T(0));
   }
+  __syncwarp();
 
-  const long long woff = (long long)wi.w * p.tmax * KS * 32;
+  const long long woff = p.saved_offset(wi.w);
   const T kap = a.kappa;
+  // rows below the stream start read as +Big (R) / 0 (P) in the backward
+#pragma unroll 1
+  for (int r = -StreamPlan::kPreRows; r < 0; ++r)
+#pragma unroll
+    for (int k = 0; k < KS; ++k) {
+      a.sR[woff + ((long long)r * KS + k) * 32 + lane] = big;
+      if (HAS_P) a.sP[woff + ((long long)r * KS + k) * 32 + lane] = T(0);
+    }
 
   // The 8 steps of a block are straight-line code; every rare event (cost
   // tiles, delay-line flush, window change) happens between blocks.
@@ -275,6 +298,18 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
     T* srow = a.sR + woff + lane + (long long)t0 * KS * 32;
     T* prow = HAS_P ? a.sP + woff + lane + (long long)t0 * KS * 32 : nullptr;
     const int c0 = (t0 - lane) & (RING - 1);
+    // row -1 values of columns t0 + s + 1, read before the block's stores
+    T fbv[TILE], fbpv[TILE];
+    {
+      const T* fbs = fb + ((t0 + 1) & 63);
+      const T* fbps = fbp + ((t0 + 1) & 63);
+      const int c7 = (t0 + TILE) & 63;
+#pragma unroll
+      for (int s = 0; s < TILE; ++s) {
+        fbv[s] = s == TILE - 1 ? fb[c7] : fbs[s];
+        if (HAS_P) fbpv[s] = s == TILE - 1 ? fbp[c7] : fbps[s];
+      }
+    }
 #pragma unroll
     for (int s = 0; s < TILE; ++s) {
       const int ia = (c0 + s) & (RING - 1);
@@ -282,9 +317,9 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
 #pragma unroll
       for (int k = 0; k < KS; ++k) {
         const int off = k * 32 * S + ia;  // column t - 32k - lane of sub-band k
-        const T c = myC[off] * kap;
         const T qv = HAS_P ? myQ[off] : T(0);
-        cell_forward<T, HAS_P>(c, qv, left[k], up[k], dg[k], Pl[k], Pu[k], Pd[k], Rn[k], Pn[k]);
+        cell_forward<T, HAS_P>(myC[off], kap, qv, left[k], up[k], dg[k], Pl[k], Pu[k], Pd[k],
+                               Rn[k], Pn[k]);
         if constexpr (HAS_BAND) {
           const bool ok = fabs((T)(rowk[k] - jk[k])) <= a.band;
           Rn[k] = ok ? Rn[k] : big;
@@ -305,9 +340,8 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
         if (HAS_P) coll8[32 + s] = Pn[KS - 1];
       }
       // row -1 value for the next step (column t + 1)
-      const bool nextw = (s == TILE - 1) && wrapw;
-      const T bv = shfl(nextw ? rbRn : rbR, (t0 + s + 1) & 31);
-      const T bp = HAS_P ? shfl(nextw ? rbPn : rbP, (t0 + s + 1) & 31) : T(0);
+      const T bv = fbv[s];
+      const T bp = HAS_P ? fbpv[s] : T(0);
 #pragma unroll
       for (int k = 0; k < KS; ++k) {
         dg[k] = up[k];
@@ -336,12 +370,12 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
         if (HAS_P) dlP[j] = wbP;
       }
       __syncwarp();
-      rbR = rbRn;
-      rbRn = row_above(dlR, t0 + TILE + 32 + lane, p, wi, big);
-      if (HAS_P) {
-        rbP = rbPn;
-        rbPn = row_above(dlP, t0 + TILE + 32 + lane, p, wi, T(0));
-      }
+      // the window that just ended makes room for the one after next (the
+      // delay line was written a pass ago, so these loads hit L2)
+      const int cn = t0 + TILE + 32 + lane;
+      fb[cn & 63] = row_above(dlR, cn, p, wi, big);
+      if (HAS_P) fbp[cn & 63] = row_above(dlP, cn, p, wi, T(0));
+      __syncwarp();
     }
   }
   cp_async_wait<0>();
@@ -361,13 +395,12 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
 
 // ---------------------------------------------------------------- backward
 
-// This lane's saved values of stream row r (one per sub-band); rows before
-// the stream start read as +Big (R) / 0 (P).
+// This lane's saved values of stream row r (one per sub-band).  Rows down to
+// -kPreRows exist (the forward fills them with +Big / 0), so no guard.
 template <typename T, int KS>
-__device__ __forceinline__ void load_saved_row(const T* __restrict__ s_lane, int r, T fill,
-                                               T (&out)[KS]) {
+__device__ __forceinline__ void load_saved_row(const T* __restrict__ s_lane, int r, T (&out)[KS]) {
 #pragma unroll
-  for (int k = 0; k < KS; ++k) out[k] = r >= 0 ? s_lane[((long long)r * KS + k) * 32] : fill;
+  for (int k = 0; k < KS; ++k) out[k] = s_lane[((long long)r * KS + k) * 32];
 }
 
 // Row -1 value lane 0 of sub-band 0 used at stream column sc in the forward
@@ -403,18 +436,30 @@ template <typename T, bool HAS_P>
 __device__ __forceinline__ void cell_backward(T Rl, T Ru, T Rd, T Pl, T Pu, T Pd, T rbar, T pbar,
                                               T inv_gamma, T& pl, T& pu, T& pd, T& ql, T& qu,
                                               T& qd) {
-  const T m1 = fmin(Rl, Ru), M1 = fmax(Rl, Ru);
-  const T m = fmin(m1, Rd), Mx = fmax(m1, Rd);
-  const T e1 = ex2(add_rn(m, -M1));
-  const T e2 = ex2(add_rn(m, -Mx));
-  const T inv = rcp(add_rn(add_rn(T(1), e1), e2));
-  const bool p1 = Rl <= Ru;
-  const bool p2 = m1 <= Rd;
-  // unnormalised weights of the left / up / diagonal predecessors
-  const T wm1 = p2 ? T(1) : e2;
-  const T ud = p2 ? e2 : T(1);
-  const T ul = p1 ? wm1 : e1;
-  const T uu = p1 ? e1 : wm1;
+  // unnormalised soft-min weights of the left / up / diagonal predecessors
+  // (the smallest R' gets exactly 1) and the reciprocal of their sum
+  T ul, uu, ud, inv;
+  if constexpr (sizeof(T) == 4) {
+    // three exponentials and no selects: fewer issue slots than sorting
+    const T m = fmin(fmin(Rl, Ru), Rd);
+    ul = ex2(add_rn(m, -Rl));
+    uu = ex2(add_rn(m, -Ru));
+    ud = ex2(add_rn(m, -Rd));
+    inv = rcp(add_rn(add_rn(ul, uu), ud));
+  } else {
+    // double: exp2 is a long sequence, so evaluate two and place the 1
+    const T m1 = fmin(Rl, Ru), M1 = fmax(Rl, Ru);
+    const T m = fmin(m1, Rd), Mx = fmax(m1, Rd);
+    const T e1 = ex2(add_rn(m, -M1));
+    const T e2 = ex2(add_rn(m, -Mx));
+    inv = rcp(add_rn(add_rn(T(1), e1), e2));
+    const bool p1 = Rl <= Ru;
+    const bool p2 = m1 <= Rd;
+    const T wm1 = p2 ? T(1) : e2;
+    ud = p2 ? e2 : T(1);
+    ul = p1 ? wm1 : e1;
+    uu = p1 ? e1 : wm1;
+  }
   if constexpr (HAS_P) {
     const T wd = ud * inv, wl = ul * inv, wu = uu * inv;
     const T A = wl * Pl + wu * Pu + wd * Pd;
@@ -467,15 +512,22 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
   const int lane = wi.lane;
   const T big = Big<T>::value;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  T* base = reinterpret_cast<T*>(smem_raw) + (size_t)wi.wib * (RW * (HAS_P ? 2 : 1) + 64);
+  T* base = reinterpret_cast<T*>(smem_raw) + (size_t)wi.wib * warp_smem_elems(KS, S, HAS_P);
   T* outC = base;
   T* outQ = base + RW;
   // top-row sends of the current 32-step window: R at [0, 32), P at [32, 64)
   T* coll = base + RW * (HAS_P ? 2 : 1);
+  // by stream column mod 64 (two 32-column windows each): row -1 values of
+  // lane 0 / sub-band 0 (sb, sbp), and adjoints arriving at lane 31 of
+  // sub-band KS-1 from the band below (sd, sdp)
+  T* sb = coll + 64;
+  T* sbp = sb + 64;
+  T* sd = sb + (HAS_P ? 128 : 64);
+  T* sdp = sd + 64;
   T* myC = outC + lane * S;
   T* myQ = outQ + lane * S;
 
-  const long long woff = (long long)wi.w * p.tmax * KS * 32;
+  const long long woff = p.saved_offset(wi.w);
   const T* sRw = a.sR + woff;
   const T* sPw = HAS_P ? a.sP + woff : nullptr;
   const int Tend = (wi.Tw + TILE - 1) / TILE * TILE;
@@ -483,13 +535,16 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
   const T* sRl = sRw + lane;
   const T* sPl = HAS_P ? sPw + lane : nullptr;
 
-  // F holds saved rows 8b-2 .. 8b+5 of the current block b (row t-2 of
-  // iteration t = 8b + s is F[s]); G prefetches the next block's rows.
-  T F[TILE][KS], G[TILE][KS], FP[TILE][KS], GP[TILE][KS];
+  // Two register sets of saved rows, F and G: a block reads saved row t-2 of
+  // iteration t = 8b + s from one set (index s) and, at its start, loads the
+  // next block's rows into the other, so every load has 8 to 15 steps to
+  // land.  The block loop is unrolled by two so the sets swap roles without
+  // copies.
+  T F[TILE][KS], FP[TILE][KS], G[TILE][KS], GP[TILE][KS];
 #pragma unroll
   for (int s = 0; s < TILE; ++s) {
-    load_saved_row<T, KS>(sRl, TILE * btop - 2 + s, big, F[s]);
-    if (HAS_P) load_saved_row<T, KS>(sPl, TILE * btop - 2 + s, T(0), FP[s]);
+    load_saved_row<T, KS>(sRl, TILE * btop - 2 + s, F[s]);
+    if (HAS_P) load_saved_row<T, KS>(sPl, TILE * btop - 2 + s, FP[s]);
   }
 
   T* dlR = a.dlR + (long long)wi.w * p.L;
@@ -503,35 +558,35 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
   }
 
   const int t_first = Tend - 1;
-  // Row -1 values (lane 0 / sub-band 0) by stream column, 32 per window: bR
-  // covers the window of column t-1 for iterations t of the current block
-  // except t = 32m (its t-1 is in the next lower window, bRn).
-  int bw = (t_first - 1) >> 5;
-  T bR = row_above_saved<T, KS>(sRw, 32 * bw + lane, p, wi, big);
-  T bRn = row_above_saved<T, KS>(sRw, 32 * (bw - 1) + lane, p, wi, big);
-  T bP = T(0), bPn = T(0);
-  if (HAS_P) {
-    bP = row_above_saved<T, KS>(sPw, 32 * bw + lane, p, wi, T(0));
-    bPn = row_above_saved<T, KS>(sPw, 32 * (bw - 1) + lane, p, wi, T(0));
+  // Row -1 values by stream column: iteration t reads column t-1, so the
+  // first block needs the windows of t_first-1 and the one below.
+  {
+    const int bw = (t_first - 1) >> 5;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int c = 32 * (bw - h) + lane;
+      sb[c & 63] = row_above_saved<T, KS>(sRw, c, p, wi, big);
+      if (HAS_P) sbp[c & 63] = row_above_saved<T, KS>(sPw, c, p, wi, T(0));
+    }
   }
   // Adjoint from the band below, by the bottom row's column t - 32 KS at
   // iteration t (used one iteration later); a block never straddles windows.
   int dw = (TILE * btop - 32 * KS) >> 5;
-  T dR = push_from_below(dlR, 32 * dw + lane, p, wi);
-  T dRn = push_from_below(dlR, 32 * (dw - 1) + lane, p, wi);
-  T dP = T(0), dPn = T(0);
-  if (HAS_P) {
-    dP = push_from_below(dlP, 32 * dw + lane, p, wi);
-    dPn = push_from_below(dlP, 32 * (dw - 1) + lane, p, wi);
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int c = 32 * (dw - h) + lane;
+    sd[c & 63] = push_from_below(dlR, c, p, wi);
+    if (HAS_P) sdp[c & 63] = push_from_below(dlP, c, p, wi);
   }
+  __syncwarp();
 
   {  // cur = saved row t_first - 1, Xc = X(t_first)
     const T b0 = row_above_saved<T, KS>(sRw, t_first, p, wi, big);
     const T b0p = HAS_P ? row_above_saved<T, KS>(sPw, t_first, p, wi, T(0)) : T(0);
-    load_saved_row<T, KS>(sRl, t_first - 1, big, cur);
+    load_saved_row<T, KS>(sRl, t_first - 1, cur);
 #pragma unroll
     for (int k = 0; k < KS; ++k) Pcur[k] = T(0);
-    if (HAS_P) load_saved_row<T, KS>(sPl, t_first - 1, T(0), Pcur);
+    if (HAS_P) load_saved_row<T, KS>(sPl, t_first - 1, Pcur);
 #pragma unroll
     for (int k = KS - 1; k >= 1; --k) {
       Xc[k] = shfl_up1_rot(lane == 31 ? cur[k - 1] : cur[k]);
@@ -565,19 +620,37 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
 #pragma unroll
   for (int k = 0; k < KS; ++k) fl[k] = cursor_at(btop - 4 * k - (lane >> 3), p);
 
-#pragma unroll 1
-  for (int b = btop; b >= 0; --b) {
-    const int t0 = TILE * b;
+  // The 8 steps of block b, reading saved rows from Fc and loading the next
+  // block's rows into Fn.  A pair's seed enters at step s_inj (-1: none).
+  auto run_block = [&](const int t0, T (&Fc)[TILE][KS], T (&FPc)[TILE][KS], T (&Fn)[TILE][KS],
+                       T (&FPn)[TILE][KS]) {
 #pragma unroll
     for (int s = 0; s < TILE; ++s) {
-      load_saved_row<T, KS>(sRl, TILE * (b - 1) - 2 + s, big, G[s]);
-      if (HAS_P) load_saved_row<T, KS>(sPl, TILE * (b - 1) - 2 + s, T(0), GP[s]);
+      load_saved_row<T, KS>(sRl, t0 - TILE - 2 + s, Fn[s]);
+      if (HAS_P) load_saved_row<T, KS>(sPl, t0 - TILE - 2 + s, FPn[s]);
     }
-    const bool lowb = (t0 & 31) == 0;  // iteration t0 reads row -1 of column t0-1 from bRn
-    const bool seedhere = cap_t >= t0 && cap_t < t0 + TILE;
-    const int s_inj = seedhere ? cap_t - t0 : -1;  // step of this block that seeds
-    T* coll8 = coll + (t0 & 24);                   // slot of step t0 + s is coll8[s]
-
+    const int s_inj = (cap_t >= t0 && cap_t < t0 + TILE) ? cap_t - t0 : -1;
+    T* coll8 = coll + (t0 & 24);  // slot of step t0 + s is coll8[s]
+    // The block's row -1 values (column t-1) and adjoints from below (column
+    // t - 32 KS), read into registers before the block's first shared-memory
+    // store so that no step waits on a shared load.
+    T bvs[TILE], bvps[TILE], dvs[TILE], dvqs[TILE];
+    {
+      const int cb0 = (t0 - 1) & 63;
+      const T* sb1 = sb + (t0 & 63);
+      const T* sbp1 = sbp + (t0 & 63);
+      const T* sdb = sd + ((t0 - 32 * KS) & 63);
+      const T* sdpb = sdp + ((t0 - 32 * KS) & 63);
+#pragma unroll
+      for (int s = 0; s < TILE; ++s) {
+        bvs[s] = s == 0 ? sb[cb0] : sb1[s - 1];
+        dvs[s] = sdb[s];
+        if (HAS_P) {
+          bvps[s] = s == 0 ? sbp[cb0] : sbp1[s - 1];
+          dvqs[s] = sdpb[s];
+        }
+      }
+    }
 #pragma unroll
     for (int s = TILE - 1; s >= 0; --s) {
       const int t = t0 + s;
@@ -590,14 +663,13 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
         }
       }
       // predecessor rows: saved row t-2 and X(t-1)
-      const bool loww = (s == 0) && lowb;
-      const T bv = shfl(loww ? bRn : bR, (t - 1) & 31);
-      const T bvp = HAS_P ? shfl(loww ? bPn : bP, (t - 1) & 31) : T(0);
+      const T bv = bvs[s];
+      const T bvp = HAS_P ? bvps[s] : T(0);
       T nxt[KS], Pnxt[KS], Xn[KS], PXn[KS];
 #pragma unroll
       for (int k = 0; k < KS; ++k) {
-        nxt[k] = F[s][k];
-        Pnxt[k] = HAS_P ? FP[s][k] : T(0);
+        nxt[k] = Fc[s][k];
+        Pnxt[k] = HAS_P ? FPc[s][k] : T(0);
       }
 #pragma unroll
       for (int k = KS - 1; k >= 1; --k) {
@@ -634,8 +706,8 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
         if (HAS_P) coll8[32 + s] = sendq[0];
       }
       // adjoint arriving at the bottom row (lane 31, sub-band KS-1) at t-1
-      const T dv = shfl(dR, (t - 32 * KS) & 31);
-      const T dvq = HAS_P ? shfl(dP, (t - 32 * KS) & 31) : T(0);
+      const T dv = dvs[s];
+      const T dvq = HAS_P ? dvqs[s] : T(0);
 #pragma unroll
       for (int k = 0; k < KS - 1; ++k) {
         accB[k] = shfl_dn1_rot(lane == 0 ? send[k + 1] : send[k]);
@@ -650,15 +722,16 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
         if (HAS_P) { Pcur[k] = Pnxt[k]; PXc[k] = PXn[k]; }
       }
     }
+  };
+
+  bool pend_b = false, pend_d = false;  // refills waiting for their shared-memory store
+  int pbc = 0, pdc = 0;
+  T pbv = T(0), pbpv = T(0), pdv = T(0), pdpv = T(0);
+  // Work between block t0 and block t0 - 8.
+  auto between = [&](const int t0) {
+    const bool seedhere = cap_t >= t0 && cap_t < t0 + TILE;
 
     // ---- between blocks
-#pragma unroll
-    for (int s = 0; s < TILE; ++s)
-#pragma unroll
-      for (int k = 0; k < KS; ++k) {
-        F[s][k] = G[s][k];
-        if (HAS_P) FP[s][k] = GP[s][k];
-      }
 #pragma unroll
     for (int k = 0; k < KS; ++k) {
       flush_row_tile<T, KS>(a.dC, myC + k * 32 * S, fl[k], k, p, wi, a.vec);
@@ -678,7 +751,24 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
         }
       }
     }
-    if (lowb) {
+    // Window refills are loaded from global memory at the end of one block
+    // and stored to shared memory at the end of the next, so no warp waits
+    // for the load; the slots they fill are first read three blocks later.
+    if (pend_b) {
+      __syncwarp();
+      sb[pbc & 63] = pbv;
+      if (HAS_P) sbp[pbc & 63] = pbpv;
+      pend_b = false;
+      __syncwarp();
+    }
+    if (pend_d) {
+      __syncwarp();
+      sd[pdc & 63] = pdv;
+      if (HAS_P) sdp[pdc & 63] = pdpv;
+      pend_d = false;
+      __syncwarp();
+    }
+    if ((t0 & 31) == 0) {
       // the window [t0, t0+32) of top-row sends is complete: lane l takes
       // the send of step t0 + l
       __syncwarp();
@@ -688,24 +778,30 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
       dlR[j] = wdR;
       if (HAS_P) dlP[j] = wdP;
       __syncwarp();
-      bR = bRn;
-      bRn = row_above_saved<T, KS>(sRw, t0 - 64 + lane, p, wi, big);
-      if (HAS_P) {
-        bP = bPn;
-        bPn = row_above_saved<T, KS>(sPw, t0 - 64 + lane, p, wi, T(0));
-      }
+      // row -1 values two windows down replace the window just finished
+      pbc = t0 - 64 + lane;
+      pbv = row_above_saved<T, KS>(sRw, pbc, p, wi, big);
+      if (HAS_P) pbpv = row_above_saved<T, KS>(sPw, pbc, p, wi, T(0));
+      pend_b = true;
     }
     // the next block (t0 - 8) may open a new window of bottom-row columns
     const int dwn = (t0 - TILE - 32 * KS) >> 5;
     if (dwn != dw) {
       dw = dwn;
-      dR = dRn;
-      dRn = push_from_below(dlR, 32 * (dw - 1) + lane, p, wi);
-      if (HAS_P) {
-        dP = dPn;
-        dPn = push_from_below(dlP, 32 * (dw - 1) + lane, p, wi);
-      }
+      pdc = 32 * (dw - 1) + lane;
+      pdv = push_from_below(dlR, pdc, p, wi);
+      if (HAS_P) pdpv = push_from_below(dlP, pdc, p, wi);
+      pend_d = true;
     }
+  };
+
+#pragma unroll 1
+  for (int b = btop; b >= 0; b -= 2) {
+    run_block(TILE * b, F, FP, G, GP);
+    between(TILE * b);
+    if (b == 0) break;
+    run_block(TILE * (b - 1), G, GP, F, FP);
+    between(TILE * (b - 1));
   }
 }
 
@@ -801,6 +897,10 @@ int resident_blocks_any(int eb, int KS, bool has_p, int wpc, size_t smem) {
 
 }  // namespace
 
+#ifndef SLICE_ALIGN
+#define SLICE_ALIGN(x) (x)
+#endif
+
 static int env_int(const char* name, int fallback) {
   const char* v = getenv(name);
   return (v && *v) ? atoi(v) : fallback;
@@ -824,37 +924,44 @@ StreamPlan make_stream_plan(int B, int N, int M, int eb, bool has_p, int sms) {
   if (p.NB > 1 && L < rows + 128) L = rows + 128;
   p.L = (L + TILE - 1) / TILE * TILE;
   const int S = eb == 4 ? RingStride<float>::value : RingStride<double>::value;
-  const size_t per_w = ((size_t)p.KS * 32 * S * (has_p ? 2 : 1) + 64) * eb;
+  const size_t per_w = (size_t)warp_smem_elems(p.KS, S, has_p) * eb;
   // Warps per SM: bounded by shared memory (the per-lane rings), by the
   // registers of the heavier of the two sweeps, and by 32.
   int wps = (int)((size_t)(216 * 1024) / per_w);
   wps = wps < 1 ? 1 : (wps > 32 ? 32 : wps);
   const int cap = env_int("TW_STREAM_WPS", 0);
   if (cap > 0 && cap < wps) wps = cap;
-  // Warps per CTA: 4, or 2 when register-limited residency rounds better in
-  // pairs of warps (the heavier sub-band counts).
-  int wpc = 4, cps = 1;
-  {
-    int best = -1;
-    for (int cand = 4; cand >= 2; cand -= 2) {
-      int c = cand > wps ? wps : cand;
-      if (c > B) c = B > 0 ? B : 1;
-      int n = wps / c > 0 ? wps / c : 1;
-      const int resident = resident_blocks_any(eb, p.KS, has_p, c, per_w * c);
-      if (resident > 0 && resident < n) n = resident;
-      if (n * c > best) {
-        best = n * c;
-        wpc = c;
-        cps = n;
-      }
+  // Warps per CTA (4, 2 or 1) and pairs per warp.  Every warp carries whole
+  // pairs and every CTA is resident from the start, so a sweep lasts about
+  // (pairs per warp) x (warps on the fullest SM) warp-steps of issue.  Take
+  // the CTA size that minimises that product (ties: the larger CTA).  Small
+  // CTAs spread the warps evenly: 2048 warps in 4-warp CTAs put 16 warps on
+  // some SMs, in 2-warp CTAs at most 14.
+  int wpc = 1;
+  long long per_warp = 1, warps_needed = 1, best_cost = LLONG_MAX;
+  for (int c : {4, 2, 1}) {
+    if (c > wps) continue;
+    int n = wps / c;
+    const int resident = resident_blocks_any(eb, p.KS, has_p, c, per_w * c);
+    if (resident >= 0 && resident < n) n = resident;
+    if (n < 1) continue;
+    const long long cap = (long long)sms * n * c;
+    const long long pw = B > 0 ? (B + cap - 1) / cap : 1;
+    const long long wn = B > 0 ? (B + pw - 1) / pw : 1;
+    const long long ctas_c = (wn + c - 1) / c;
+    const long long fullest = c * ((ctas_c + sms - 1) / sms);
+    const long long cost = pw * fullest;
+    if (cost < best_cost) {
+      best_cost = cost;
+      wpc = c;
+      per_warp = pw;
+      warps_needed = wn;
     }
   }
-  // Every warp carries whole pairs, so the sweep lasts as long as the warp
-  // with the most pairs.  Take the fewest pairs per warp the resident warps
-  // allow, then the fewest warps that still achieve it (equal loads).
-  const long long cap_warps = (long long)sms * cps * wpc;
-  const long long per_warp = B > 0 ? (B + cap_warps - 1) / cap_warps : 1;
-  const long long warps_needed = B > 0 ? (B + per_warp - 1) / per_warp : 1;
+  if (best_cost == LLONG_MAX) {  // nothing fits the residency estimate: one warp per CTA
+    per_warp = B > 0 ? (B + sms - 1) / sms : 1;
+    warps_needed = B > 0 ? (B + per_warp - 1) / per_warp : 1;
+  }
   int ctas = (int)((warps_needed + wpc - 1) / wpc);
   if (ctas < 1) ctas = 1;
   p.wpc = wpc;
@@ -864,6 +971,7 @@ StreamPlan make_stream_plan(int B, int N, int M, int eb, bool has_p, int sms) {
   const long long maxpairs = p.base + (p.rem ? 1 : 0);
   const long long Tw = maxpairs * p.NB * p.L + 32 * p.KS - 1;
   p.tmax = (Tw + TILE - 1) / TILE * TILE;
+  p.tstride = SLICE_ALIGN(p.tmax + StreamPlan::kPreRows);
   p.smem_fwd = per_w * p.wpc;
   p.smem_bwd = per_w * p.wpc;
   return p;

@@ -38,7 +38,16 @@ struct StreamPlan {
   long long tmax = 0;      // saved rows per warp (multiple of 8)
   size_t smem_fwd = 0, smem_bwd = 0;   // dynamic shared memory per CTA
 
-  long long saved_elems() const { return (long long)warps * tmax * KS * 32; }
+  // Each warp's saved stream starts with kPreRows rows of +Big (R) / 0 (P),
+  // so the backward sweep reloads rows below the stream start unguarded.
+  // Warp slices are `tstride` rows apart (>= tmax + kPreRows).
+  static constexpr int kPreRows = 16;
+  long long tstride = 0;
+  long long saved_elems() const { return (long long)warps * tstride * KS * 32; }
+  // offset of warp w's stream row 0
+  __host__ __device__ long long saved_offset(int w) const {
+    return ((long long)w * tstride + kPreRows) * KS * 32;
+  }
   long long delay_elems() const { return (long long)warps * L; }
 };
 
