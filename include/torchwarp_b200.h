@@ -103,6 +103,20 @@ int tw_sdtw_backward_f64(const double* grad_r, const double* grad_p, int B, int 
                          double* d_cost, double* d_penalty, void* workspace, size_t ws_bytes,
                          void* stream);
 
+/* soft-DTW backward that also applies the positivity mask of
+ * tw_sqeuclid_cost_* (no penalty): writes d_cost[b,i,j] = dL/dcost[b,i,j] where
+ * the mask bit of (b,i,j) is set, else 0 -- the S operand of the squared-
+ * Euclidean chain rule, which tw_sqeuclid_grad_* then takes with mask = NULL.
+ * Same saved state, workspace and results as tw_sdtw_backward_* otherwise.
+ * Mask layout: see tw_sqeuclid_cost_f32.  (The reference multiplies by the
+ * clamp's derivative inside its chain rule, udtw_cuda.cu:557-568.) */
+int tw_sdtw_backward_masked_f32(const float* grad_r, int B, int N, int M, double gamma,
+                                const void* saved, size_t saved_bytes, const uint32_t* mask,
+                                float* d_cost, void* workspace, size_t ws_bytes, void* stream);
+int tw_sdtw_backward_masked_f64(const double* grad_r, int B, int N, int M, double gamma,
+                                const void* saved, size_t saved_bytes, const uint32_t* mask,
+                                double* d_cost, void* workspace, size_t ws_bytes, void* stream);
+
 /* ---------------------------------------------------------------------
  * uDTW / soft-DTW cost from features (uDTW Eqs. 8, 16):
  *   sq_ij  = max(|x_i|^2 + |y_j|^2 - 2 x_i.y_j, 0)
@@ -147,7 +161,8 @@ int tw_udtw_features_grad_f64(const double* X, const double* Y, const double* vx
  * The chain rule reads the mask instead of the cost (1 bit instead of 4 or 8
  * bytes per cell), so the cost can be freed after the DP forward:
  *   dX = -2 S Y + 2 X rowsum(S), dY = -2 S^T X + 2 Y colsum(S),
- *   S = d_cost where the mask bit is set, else 0.
+ *   S = d_cost where the mask bit is set, else 0; with mask = NULL, S = d_cost
+ *   (the mask was already applied, e.g. by tw_sdtw_backward_masked_*).
  * fp32 with D >= 64 (D, M multiples of 4, 16-byte aligned) runs on tcgen05
  * tensor cores (3xTF32); other shapes and fp64 on SIMT kernels. */
 int tw_sqeuclid_cost_f32(const float* X, const float* Y, int B, int N, int M, int D, float* cost,

@@ -244,6 +244,52 @@ def test_sq_cost_and_mask(shape, dtype, simt, monkeypatch):
     assert torch.equal(mask, _pack_positive(C))
 
 
+def _unpack_mask(mask, N, M):
+    w = mask.to(torch.int64) & 0xFFFFFFFF
+    j = torch.arange(M, device=mask.device)
+    bits = (w[:, j // 32, :N] >> (j % 32)[None, :, None]) & 1
+    return bits.transpose(1, 2).bool().contiguous()
+
+
+@pytest.mark.parametrize("shape", SHAPES + [(2, 70, 45, 8)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64])
+@pytest.mark.parametrize("smem_s", [False, True])
+def test_sq_grad_premasked(shape, dtype, smem_s, monkeypatch):
+    """With a null mask the chain rule takes d_cost as already masked; on
+    S = d_cost * mask it reproduces the mask path (float64 exactly, float32
+    within its accumulation rounding)."""
+    if dtype == torch.float64 and smem_s:
+        pytest.skip("float64 always runs the SIMT kernels")
+    _env(monkeypatch, False)
+    if smem_s:
+        monkeypatch.setenv("TW_GRAD_SMEM_S", "1")
+    B, N, M, D = shape
+    X, Y, _, _ = _inputs(*shape, seed=7 * sum(shape))
+    X, Y = X.to(dtype), Y.to(dtype)
+    n = min(N, M)
+    Y[:, : n // 3] = X[:, : n // 3]
+    C, mask = _sq_cost(X, Y)
+    dC = torch.randn(B, N, M, device="cuda", dtype=dtype)
+    S = torch.where(_unpack_mask(mask, N, M), dC, torch.zeros_like(dC)).contiguous()
+    fn = getattr(nat.lib(), "tw_sqeuclid_grad_" + nat.suffix(dtype))
+    outs = []
+    for m, d in ((mask, dC), (None, S)):
+        dX = torch.empty_like(X)
+        dY = torch.empty_like(Y)
+        nat.check(fn(nat.ptr(X), nat.ptr(Y), None if m is None else nat.ptr(m), nat.ptr(d), B, N,
+                     M, D, nat.ptr(dX), nat.ptr(dY), nat.stream_of(X)), "tw_sqeuclid_grad")
+        outs.append((dX, dY))
+    torch.cuda.synchronize()
+    assert nat.lib().tw_device_error() == 0
+    (aX, aY), (bX, bY) = outs
+    if dtype == torch.float64:
+        assert torch.equal(aX, bX) and torch.equal(aY, bY)
+    else:
+        for a, b in ((aX, bX), (aY, bY)):
+            err = ((a - b).abs() / (a.abs() + 1.0)).max().item()
+            assert err < 2e-6, err
+
+
 @pytest.mark.parametrize("shape", SHAPES + [(2, 70, 45, 8)])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float64])
 def test_sq_grad_mask_equals_cost_path(shape, dtype, monkeypatch):

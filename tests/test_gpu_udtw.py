@@ -215,3 +215,39 @@ def test_unreachable_band_raises(tw):
 def test_cpu_tensors_rejected(tw):
     with pytest.raises(RuntimeError, match="CUDA"):
         tw.functional.soft_dtw_from_cost(torch.rand(1, 3, 4), gamma=0.1)
+
+
+def _unpack_mask(mask, N, M):
+    """[B, ceil(M/32), NP] int32 words -> [B, N, M] bool (bit j & 31 of word j >> 5)."""
+    w = mask.to(torch.int64) & 0xFFFFFFFF
+    j = torch.arange(M, device=mask.device)
+    bits = (w[:, j // 32, :N] >> (j % 32)[None, :, None]) & 1
+    return bits.transpose(1, 2).bool().contiguous()
+
+
+@pytest.mark.parametrize("shape", [(3, 70, 45), (2, 200, 130), (5, 33, 64), (4, 1, 1),
+                                   (2, 129, 300), (1, 257, 9), (2, 70, 40), (1, 100, 296)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64])
+def test_sdtw_backward_masked(tw, shape, dtype):
+    """tw_sdtw_backward_masked writes the plain backward's d_cost with the
+    cells whose mask bit is clear set to zero, bit for bit."""
+    from torchwarp_b200 import _native as nat
+    from torchwarp_b200.udtw import _ops
+    B, N, M = shape
+    g = torch.Generator().manual_seed(N * 7 + M)
+    C = torch.rand(B, N, M, generator=g, dtype=torch.float64).to(DEV, dtype)
+    mask = torch.randint(-2 ** 31, 2 ** 31, (B, (M + 31) // 32, (N + 3) // 4 * 4), generator=g,
+                         dtype=torch.int64).to(torch.int32).to(DEV)
+    gamma = 0.1
+    out_r, _, saved = _ops._dp_forward(C, None, gamma, 0.0)
+    grad_r = torch.rand(B, generator=g, dtype=torch.float64).to(DEV, dtype) + 0.5
+    d_cost, _ = _ops._dp_backward(saved, grad_r, grad_r, N, M, gamma, False)
+    s_cost = torch.full_like(d_cost, float("nan"))
+    wb = _ops._ws_bytes(B, N, M, dtype, False)
+    ws = torch.empty(wb, dtype=torch.uint8, device=DEV)
+    fn = getattr(nat.lib(), "tw_sdtw_backward_masked_" + nat.suffix(dtype))
+    nat.check(fn(nat.ptr(grad_r), B, N, M, gamma, nat.ptr(saved), saved.numel(), nat.ptr(mask),
+                 nat.ptr(s_cost), nat.ptr(ws), wb, nat.stream_of(C)), "tw_sdtw_backward_masked")
+    torch.cuda.synchronize()
+    want = torch.where(_unpack_mask(mask, N, M), d_cost, torch.zeros_like(d_cost))
+    assert torch.equal(s_cost, want)

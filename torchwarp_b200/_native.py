@@ -35,6 +35,10 @@ SIGNATURES = {
                                     _c_p, _c_p, _c_sz, _c_p]),
     "tw_sdtw_backward_f64": (_c_i, [_c_p, _c_p, _c_i, _c_i, _c_i, _c_d, _c_i, _c_p, _c_sz, _c_p,
                                     _c_p, _c_p, _c_sz, _c_p]),
+    "tw_sdtw_backward_masked_f32": (_c_i, [_c_p, _c_i, _c_i, _c_i, _c_d, _c_p, _c_sz, _c_p, _c_p,
+                                           _c_p, _c_sz, _c_p]),
+    "tw_sdtw_backward_masked_f64": (_c_i, [_c_p, _c_i, _c_i, _c_i, _c_d, _c_p, _c_sz, _c_p, _c_p,
+                                           _c_p, _c_sz, _c_p]),
     "tw_udtw_cost_f32": (_c_i, [_c_p, _c_p, _c_p, _c_p, _c_i, _c_i, _c_i, _c_i, _c_d, _c_d, _c_p,
                                 _c_p, _c_p]),
     "tw_udtw_cost_f64": (_c_i, [_c_p, _c_p, _c_p, _c_p, _c_i, _c_i, _c_i, _c_i, _c_d, _c_d, _c_p,

@@ -95,7 +95,7 @@ int sdtw_fwd(const T* cost, const T* pen, int B, int N, int M, double gamma, dou
 template <typename T>
 static int sdtw_bwd(const T* grad_r, const T* grad_p, int B, int N, int M, double gamma,
                     int has_pen, const void* saved, size_t saved_bytes, T* d_cost, T* d_pen,
-                    void* ws, size_t ws_bytes, cudaStream_t st) {
+                    void* ws, size_t ws_bytes, cudaStream_t st, const uint32_t* mask = nullptr) {
   g_err[0] = 0;
   if (int e = check_dims("tw_sdtw_backward", B, N, M)) return e;
   if (!(gamma > 0)) return set_error(kInvalid, "tw_sdtw_backward: gamma must be > 0");
@@ -124,6 +124,8 @@ static int sdtw_bwd(const T* grad_r, const T* grad_p, int B, int N, int M, doubl
   a.inv_gamma = (T)(1.0 / gamma);
   a.vec = ((M * sizeof(T)) % 16 == 0) && ((uintptr_t)d_cost % 16 == 0) &&
           (!d_pen || (uintptr_t)d_pen % 16 == 0);
+  a.mask = mask;
+  a.mask_np = (N + 3) & ~3;
   a.p = p;
   return sdtw_stream_backward<T>(a, has_p, false, st);
 }
@@ -229,6 +231,21 @@ int tw_sdtw_backward_f64(const double* grad_r, const double* grad_p, int B, int 
                           d_cost, d_penalty, workspace, ws_bytes, (cudaStream_t)stream);
 }
 
+int tw_sdtw_backward_masked_f32(const float* grad_r, int B, int N, int M, double gamma,
+                                const void* saved, size_t saved_bytes, const uint32_t* mask,
+                                float* d_cost, void* workspace, size_t ws_bytes, void* stream) {
+  if (B > 0 && mask == nullptr) return set_error(kInvalid, "tw_sdtw_backward_masked: null mask");
+  return sdtw_bwd<float>(grad_r, nullptr, B, N, M, gamma, 0, saved, saved_bytes, d_cost, nullptr,
+                         workspace, ws_bytes, (cudaStream_t)stream, mask);
+}
+int tw_sdtw_backward_masked_f64(const double* grad_r, int B, int N, int M, double gamma,
+                                const void* saved, size_t saved_bytes, const uint32_t* mask,
+                                double* d_cost, void* workspace, size_t ws_bytes, void* stream) {
+  if (B > 0 && mask == nullptr) return set_error(kInvalid, "tw_sdtw_backward_masked: null mask");
+  return sdtw_bwd<double>(grad_r, nullptr, B, N, M, gamma, 0, saved, saved_bytes, d_cost, nullptr,
+                          workspace, ws_bytes, (cudaStream_t)stream, mask);
+}
+
 int tw_udtw_cost_f32(const float* X, const float* Y, const float* vx, const float* vy, int B,
                      int N, int M, int D, double beta, double eps, float* cost, float* penalty,
                      void* stream) {
@@ -269,7 +286,7 @@ int tw_udtw_features_grad_f32(const float* X, const float* Y, const float* vx, c
                              int B, int N, int M, int D, T* dX, T* dY, void* stream) {          \
     g_err[0] = 0;                                                                               \
     if (B < 0 || N <= 0 || M <= 0 || D <= 0 ||                                                  \
-        (B && (!X || !Y || !mask || !d_cost || !dX || !dY)))                                    \
+        (B && (!X || !Y || !d_cost || !dX || !dY)))                                             \
       return set_error(kInvalid, "tw_sqeuclid_grad: invalid arguments");                        \
     return sq_grad_##SUF(X, Y, mask, d_cost, B, N, M, D, dX, dY, (cudaStream_t)stream);         \
   }

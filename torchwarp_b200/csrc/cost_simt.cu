@@ -149,9 +149,11 @@ __global__ void __launch_bounds__(256) udtw_grad_strip_kernel(
         if (mask != nullptr) {
           const int MW = (M + 31) >> 5, NP = (N + 3) & ~3;
           positive = (mask[((long long)b * MW + (j >> 5)) * NP + i] >> (j & 31)) & 1u;
-        } else {
+        } else if (C != nullptr) {
           cc = C[o];
           positive = cc > T(0);
+        } else {
+          positive = true;  // dC already carries the positivity mask
         }
         g = positive ? dc / var : T(0);
         if (va != nullptr && var_raw > eps) {

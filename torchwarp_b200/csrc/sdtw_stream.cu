@@ -479,26 +479,54 @@ __device__ __forceinline__ void cell_backward(T Rl, T Ru, T Rd, T Pl, T Pu, T Pd
   }
 }
 
+// Positivity-mask words of this lane's row in the pass of cursor c: word jw
+// of the row is at [jw * np].  Outside the data (no pass, or a padding row)
+// it points at the mask's first row instead, so that every load stays in
+// bounds; the flush writes nothing there.
+template <int KS>
+__device__ __forceinline__ const uint32_t* mask_row(const uint32_t* mask, int np, const Cursor& c,
+                                                    int k, const StreamPlan& p,
+                                                    const WarpInfo& wi) {
+  const int row = c.band * 32 * KS + 32 * k + wi.lane;
+  if (c.q < 0 || c.q >= wi.Q || row >= p.N) return mask;
+  const int mw = (p.M + 31) >> 5;
+  return mask + (long long)(wi.p0 + c.pq) * mw * np + row;
+}
+
 // Write this lane's row of flush tile c (8 stream columns) from the staging
-// ring to dC (natural layout), data columns only.
+// ring to dC (natural layout), data columns only; with `masked`, columns
+// whose bit in `word` is clear are written as 0.
 template <typename T, int KS>
 __device__ __forceinline__ void flush_row_tile(T* __restrict__ dst_base, const T* ring_row,
                                                const Cursor& c, int k, const StreamPlan& p,
-                                               const WarpInfo& wi, int vec) {
+                                               const WarpInfo& wi, int vec, bool masked,
+                                               uint32_t word) {
   if (c.q < 0 || c.q >= wi.Q || c.j0 >= p.M) return;
   const int j0 = c.j0;
   const int row = c.band * 32 * KS + 32 * k + wi.lane;
   if (row >= p.N) return;
   const T* src = ring_row + ((c.u * TILE) & (RING - 1));
   T* dst = dst_base + ((long long)(wi.p0 + c.pq) * p.N + row) * p.M + j0;
+  const uint32_t bits = masked ? word >> (j0 & 31) : 0xffu;
   if (vec && j0 + TILE <= p.M) {
     constexpr int PER = 16 / (int)sizeof(T);
 #pragma unroll
-    for (int h = 0; h < TILE / PER; ++h)
-      *reinterpret_cast<int4*>(dst + h * PER) = *reinterpret_cast<const int4*>(src + h * PER);
+    for (int h = 0; h < TILE / PER; ++h) {
+      union {
+        int4 i;
+        T v[PER];
+      } u;
+      u.i = *reinterpret_cast<const int4*>(src + h * PER);
+      if (masked) {
+#pragma unroll
+        for (int e = 0; e < PER; ++e)
+          if (!((bits >> (h * PER + e)) & 1u)) u.v[e] = T(0);
+      }
+      *reinterpret_cast<int4*>(dst + h * PER) = u.i;
+    }
   } else {
     const int n = min(TILE, p.M - j0);
-    for (int h = 0; h < n; ++h) dst[h] = src[h];
+    for (int h = 0; h < n; ++h) dst[h] = ((bits >> h) & 1u) ? src[h] : T(0);
   }
 }
 
@@ -615,10 +643,19 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
     }
   }
 
-  // tile completed by this lane in block b: u = b - 4k - lane/8
+  // tile completed by this lane in block b: u = b - 4k - lane/8; with a
+  // positivity mask, its word is loaded a block before the flush
   Cursor fl[KS];
+  uint32_t mwd[KS];
+  const uint32_t* mrow[KS];
+  const bool masked = a.mask != nullptr;
+  const int mwl = ((p.M + 31) >> 5) - 1;  // last word of a mask row
 #pragma unroll
-  for (int k = 0; k < KS; ++k) fl[k] = cursor_at(btop - 4 * k - (lane >> 3), p);
+  for (int k = 0; k < KS; ++k) {
+    fl[k] = cursor_at(btop - 4 * k - (lane >> 3), p);
+    mrow[k] = masked ? mask_row<KS>(a.mask, a.mask_np, fl[k], k, p, wi) : nullptr;
+    mwd[k] = masked ? mrow[k][min(fl[k].j0 >> 5, mwl) * a.mask_np] : 0u;
+  }
 
   // The 8 steps of block b, reading saved rows from Fc and loading the next
   // block's rows into Fn.  A pair's seed enters at step s_inj (-1: none).
@@ -734,9 +771,15 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
     // ---- between blocks
 #pragma unroll
     for (int k = 0; k < KS; ++k) {
-      flush_row_tile<T, KS>(a.dC, myC + k * 32 * S, fl[k], k, p, wi, a.vec);
-      if (HAS_P) flush_row_tile<T, KS>(a.dQ, myQ + k * 32 * S, fl[k], k, p, wi, a.vec);
+      flush_row_tile<T, KS>(a.dC, myC + k * 32 * S, fl[k], k, p, wi, a.vec, masked, mwd[k]);
+      if (HAS_P)
+        flush_row_tile<T, KS>(a.dQ, myQ + k * 32 * S, fl[k], k, p, wi, a.vec, false, 0u);
+      const int oq = fl[k].q;
       cursor_prev(fl[k], p);
+      if (masked) {
+        if (fl[k].q != oq) mrow[k] = mask_row<KS>(a.mask, a.mask_np, fl[k], k, p, wi);
+        mwd[k] = mrow[k][min(fl[k].j0 >> 5, mwl) * a.mask_np];
+      }
     }
     if (seedhere) {
       --cap_i;

@@ -72,6 +72,10 @@ struct SdtwArgs {
   const T* grad_p = nullptr;  // [B] or null
   T* dC = nullptr;            // [B,N,M]
   T* dQ = nullptr;            // [B,N,M] or null
+  // positivity mask of the squared-Euclidean cost, uint32 words
+  // [B][ceil(M/32)][mask_np]: dC is written as dC * bit (null: no mask)
+  const uint32_t* mask = nullptr;
+  int mask_np = 0;
   // scalars
   T kappa = 1;      // log2(e) / gamma
   T inv_kappa = 1;  // gamma * ln 2

@@ -677,7 +677,9 @@ __device__ __forceinline__ float4 split4(float4 v, float4& lo) {
   return hi;
 }
 
-template <int SIDE, bool VAR, bool MASKED, bool TA, bool WIDE>
+// PRE: dC already carries the positivity mask (S = dC), so neither the cost
+// nor mask words are loaded and the split warps skip the mask test.
+template <int SIDE, bool VAR, bool MASKED, bool TA, bool WIDE, bool PRE = false>
 __global__ void __launch_bounds__(GRAD_THREADS, 1)
     tc_grad_kernel(const __grid_constant__ CUtensorMap mapDC, const __grid_constant__ CUtensorMap mapC,
                    const __grid_constant__ CUtensorMap mapDQ, const __grid_constant__ CUtensorMap mapF,
@@ -685,6 +687,7 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
                    const float* __restrict__ va, const float* __restrict__ vb,
                    float* __restrict__ dva, int B, int N, int M, int D, float beta, float eps,
                    int has_dq, GradGeom g, const uint32_t* __restrict__ mask) {
+  static_assert(!(PRE && (VAR || MASKED)), "PRE is the plain soft-DTW chain rule");
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* land_base = smem;
   uint8_t* conv_base = smem + (size_t)g.lstages * g.l_bytes;
@@ -778,7 +781,7 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
         if (SIDE == 0) {
           // S chunk: 128 rows i x 32 columns j
           tma_load_3d(st, &mapDC, &sh.lfull[s], kc * 32, blk * 128, b);
-          if (!MASKED) tma_load_3d(st + g.l_c, &mapC, &sh.lfull[s], kc * 32, blk * 128, b);
+          if (!MASKED && !PRE) tma_load_3d(st + g.l_c, &mapC, &sh.lfull[s], kc * 32, blk * 128, b);
           if (VAR && has_dq) tma_load_3d(st + g.l_dq, &mapDQ, &sh.lfull[s], kc * 32, blk * 128, b);
         } else {
           // S chunk: 32 rows i x 128 columns j, as four 32 x 32 boxes
@@ -786,7 +789,8 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
           for (int q = 0; q < 4; ++q) {
             const int x = blk * 128 + 32 * q;
             tma_load_3d(st + q * 4096, &mapDC, &sh.lfull[s], x, kc * 32, b);
-            if (!MASKED) tma_load_3d(st + g.l_c + q * 4096, &mapC, &sh.lfull[s], x, kc * 32, b);
+            if (!MASKED && !PRE)
+              tma_load_3d(st + g.l_c + q * 4096, &mapC, &sh.lfull[s], x, kc * 32, b);
             if (VAR && has_dq)
               tma_load_3d(st + g.l_dq + q * 4096, &mapDQ, &sh.lfull[s], x, kc * 32, b);
           }
@@ -847,7 +851,7 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
           for (int k = 0; k < 4; ++k) {
             const uint32_t off = sw128_chunk(own, 4 * hh + k);
             g4[k] = *reinterpret_cast<const float4*>(ld + off);
-            if (!MASKED) c4[k] = *reinterpret_cast<const float4*>(ld + g.l_c + off);
+            if (!MASKED && !PRE) c4[k] = *reinterpret_cast<const float4*>(ld + g.l_c + off);
             q4[k] = make_float4(0.f, 0.f, 0.f, 0.f);
             if (VAR && has_dq) q4[k] = *reinterpret_cast<const float4*>(ld + g.l_dq + off);
           }
@@ -855,8 +859,8 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
           for (int k = 0; k < 4; ++k) {
             const float ge[4] = {g4[k].x, g4[k].y, g4[k].z, g4[k].w};
             const float qe[4] = {q4[k].x, q4[k].y, q4[k].z, q4[k].w};
-            float ce[4];
-            if (!MASKED) { ce[0] = c4[k].x; ce[1] = c4[k].y; ce[2] = c4[k].z; ce[3] = c4[k].w; }
+            float ce[4] = {1.f, 1.f, 1.f, 1.f};
+            if (!MASKED && !PRE) { ce[0] = c4[k].x; ce[1] = c4[k].y; ce[2] = c4[k].z; ce[3] = c4[k].w; }
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const int jj = 16 * hh + 4 * k + e;  // summed column within the chunk
@@ -866,7 +870,7 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
                 var_raw = 0.5f * (va_r + __shfl_sync(0xffffffffu, vbl, jj));
                 inv = __frcp_rn(var_raw > eps ? var_raw : eps);
               }
-              const float v = ce[e] > 0.f ? (VAR ? ge[e] * inv : ge[e]) : 0.f;
+              const float v = PRE ? ge[e] : (ce[e] > 0.f ? (VAR ? ge[e] * inv : ge[e]) : 0.f);
               rsum += v;
               if (VAR && var_raw > eps) vsum += (beta * qe[e] - ge[e] * ce[e]) * inv;
               sv[4 * k + e] = v;
@@ -879,13 +883,13 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
             const int rr = 16 * hh + k;
             const uint32_t off = sub * 4096 + sw128b32_elem(rr, lane);
             const float gv = *reinterpret_cast<const float*>(ld + off);
-            float cvv;
+            float cvv = 1.f;
             if (MASKED) {
               const int jw = blk * 4 + sub;
               const uint32_t w =
                   jw < g.mw ? reinterpret_cast<const uint32_t*>(ld + g.l_mask)[sub * 32 + rr] : 0u;
               cvv = (w >> lane) & 1u ? 1.f : 0.f;
-            } else {
+            } else if (!PRE) {
               cvv = *reinterpret_cast<const float*>(ld + g.l_c + off);
             }
             const float qv = (VAR && has_dq) ? *reinterpret_cast<const float*>(ld + g.l_dq + off)
@@ -895,7 +899,7 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
               var_raw = 0.5f * (__shfl_sync(0xffffffffu, vbl, rr) + va_r);
               inv = __frcp_rn(var_raw > eps ? var_raw : eps);
             }
-            const float v = cvv > 0.f ? (VAR ? gv * inv : gv) : 0.f;
+            const float v = PRE ? gv : (cvv > 0.f ? (VAR ? gv * inv : gv) : 0.f);
             rsum += v;
             if (VAR && var_raw > eps) vsum += (beta * qv - gv * cvv) * inv;
             sv[k] = v;
@@ -996,7 +1000,7 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
           for (int k = 0; k < 4; ++k) {
             const uint32_t off = sw128_chunk(row, 4 * h + k);
             g4[k] = *reinterpret_cast<const float4*>(ld + off);
-            if (!MASKED) c4[k] = *reinterpret_cast<const float4*>(ld + g.l_c + off);
+            if (!MASKED && !PRE) c4[k] = *reinterpret_cast<const float4*>(ld + g.l_c + off);
             q4[k] = make_float4(0.f, 0.f, 0.f, 0.f);
             if (VAR && has_dq) q4[k] = *reinterpret_cast<const float4*>(ld + g.l_dq + off);
           }
@@ -1004,11 +1008,11 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
           for (int k = 0; k < 4; ++k) {
             const int q = 4 * h + k;
             const uint32_t off = sw128_chunk(row, q);
-            float ce[4];
+            float ce[4] = {1.f, 1.f, 1.f, 1.f};
             if (MASKED) {
 #pragma unroll
               for (int e = 0; e < 4; ++e) ce[e] = (mword >> (4 * q + e)) & 1u ? 1.f : 0.f;
-            } else {
+            } else if (!PRE) {
               ce[0] = c4[k].x; ce[1] = c4[k].y; ce[2] = c4[k].z; ce[3] = c4[k].w;
             }
             const float ge[4] = {g4[k].x, g4[k].y, g4[k].z, g4[k].w};
@@ -1022,7 +1026,7 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
                 var_raw = 0.5f * (va_r[0] + (j < S ? __ldg(vb_b + j) : 1.f));
                 var = var_raw > eps ? var_raw : eps;
               }
-              sv[e] = ce[e] > 0.f ? (VAR ? ge[e] / var : ge[e]) : 0.f;
+              sv[e] = PRE ? ge[e] : (ce[e] > 0.f ? (VAR ? ge[e] / var : ge[e]) : 0.f);
               rsum[0] += sv[e];
               if (VAR && var_raw > eps) vsum[0] += (beta * qe[e] - ge[e] * ce[e]) / var;
             }
@@ -1043,7 +1047,7 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
             const uint32_t off =
                 box * 4096 + rr * 128 + (uint32_t)(((gq ^ (rr & 3)) << 5) + half * 16);
             g4[k] = *reinterpret_cast<const float4*>(ld + off);
-            if (!MASKED) c4[k] = *reinterpret_cast<const float4*>(ld + g.l_c + off);
+            if (!MASKED && !PRE) c4[k] = *reinterpret_cast<const float4*>(ld + g.l_c + off);
             q4[k] = make_float4(0.f, 0.f, 0.f, 0.f);
             if (VAR && has_dq) q4[k] = *reinterpret_cast<const float4*>(ld + g.l_dq + off);
             mw4[k] = (MASKED && jw < g.mw)
@@ -1055,12 +1059,12 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
             const int rr = rg * 4 + k;
             const uint32_t off =
                 box * 4096 + rr * 128 + (uint32_t)(((gq ^ (rr & 3)) << 5) + half * 16);
-            float ce[4];
+            float ce[4] = {1.f, 1.f, 1.f, 1.f};
             if (MASKED) {
 #pragma unroll
               for (int e = 0; e < 4; ++e)
                 ce[e] = (mw4[k] >> (4 * (cq & 7) + e)) & 1u ? 1.f : 0.f;
-            } else {
+            } else if (!PRE) {
               ce[0] = c4[k].x; ce[1] = c4[k].y; ce[2] = c4[k].z; ce[3] = c4[k].w;
             }
             const float ge[4] = {g4[k].x, g4[k].y, g4[k].z, g4[k].w};
@@ -1078,7 +1082,7 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
                 var_raw = 0.5f * (vbi + va_r[e]);
                 var = var_raw > eps ? var_raw : eps;
               }
-              sv[e] = ce[e] > 0.f ? (VAR ? ge[e] / var : ge[e]) : 0.f;
+              sv[e] = PRE ? ge[e] : (ce[e] > 0.f ? (VAR ? ge[e] / var : ge[e]) : 0.f);
               rsum[e] += sv[e];
               if (VAR && var_raw > eps) vsum[e] += (beta * qe[e] - ge[e] * ce[e]) / var;
             }
@@ -1402,7 +1406,7 @@ int tc_cost_f32(const float* X, const float* Y, const float* vx, const float* vy
 
 namespace {
 
-template <int SIDE, bool VAR, bool MASKED, bool TA, bool WIDE>
+template <int SIDE, bool VAR, bool MASKED, bool TA, bool WIDE, bool PRE>
 int grad_side_impl(const float* A, const float* F, const float* va, const float* vb,
                    const float* C, const float* dC, const float* dQ, int B, int N, int M, int D,
                    double beta, double eps, float* dA, float* dva, cudaStream_t st,
@@ -1415,8 +1419,9 @@ int grad_side_impl(const float* A, const float* F, const float* va, const float*
   const uint32_t sbox_rows = SIDE == 0 ? 128 : 32;
   const bool s_g32 = SIDE == 1;
   if ((rc = make_map_3d_f32(&mDC, dC, M, N, B, 32, sbox_rows, s_g32)) != kOk) return rc;
-  mC = mDC;  // C is not read when the positivity mask replaces it
-  if (!MASKED && (rc = make_map_3d_f32(&mC, C, M, N, B, 32, sbox_rows, s_g32)) != kOk) return rc;
+  mC = mDC;  // C is not read when the positivity mask replaces it (or is already applied)
+  if (!MASKED && !PRE && (rc = make_map_3d_f32(&mC, C, M, N, B, 32, sbox_rows, s_g32)) != kOk)
+    return rc;
   mDQ = mC;
   const bool has_dq = VAR && dQ != nullptr;
   if (has_dq && (rc = make_map_3d_f32(&mDQ, dQ, M, N, B, 32, sbox_rows, s_g32)) != kOk) return rc;
@@ -1429,8 +1434,8 @@ int grad_side_impl(const float* A, const float* F, const float* va, const float*
   if (MASKED && ((uintptr_t)mask & 15u) != 0)
     return set_error(kUnsupported, "tc grad: mask not 16-byte aligned");
   int off = SBOX;                       // dC at 0
-  g.l_c = MASKED ? -1 : off;
-  if (!MASKED) off += SBOX;
+  g.l_c = (MASKED || PRE) ? -1 : off;
+  if (!MASKED && !PRE) off += SBOX;
   g.l_dq = has_dq ? off : -1;
   if (has_dq) off += SBOX;
   g.l_f = off;
@@ -1438,7 +1443,7 @@ int grad_side_impl(const float* A, const float* F, const float* va, const float*
   g.l_mask = off;
   if (MASKED) off += 512;
   g.l_bytes = (off + 1023) & ~1023;
-  g.tx_fixed = SBOX * (MASKED ? 1 : 2) + (has_dq ? SBOX : 0) + g.nF * 4096;
+  g.tx_fixed = SBOX * ((MASKED || PRE) ? 1 : 2) + (has_dq ? SBOX : 0) + g.nF * 4096;
   const int BD = 32 * g.nF;
   const int budget = 232448 - STG_BYTES - (int)sizeof(GradShared);
   if (TA) {
@@ -1474,7 +1479,7 @@ int grad_side_impl(const float* A, const float* F, const float* va, const float*
                       STG_BYTES + sizeof(GradShared);
   const long long units = (long long)B * ((R + 127) / 128);
   const int grid = (int)(units < sm_count() ? units : sm_count());
-  auto kern = tc_grad_kernel<SIDE, VAR, MASKED, TA, WIDE>;
+  auto kern = tc_grad_kernel<SIDE, VAR, MASKED, TA, WIDE, PRE>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   kern<<<grid, GRAD_THREADS, smem, st>>>(mDC, mC, mDQ, mF, mOut, A, va, vb, dva, B, N, M, D,
                                          (float)beta, (float)eps, has_dq ? 1 : 0, g, mask);
@@ -1486,7 +1491,7 @@ int grad_side_impl(const float* A, const float* F, const float* va, const float*
 // S goes to TMEM (no shared-memory traffic for it) whenever the two
 // accumulators leave room for it.  TW_GRAD_SMEM_S=1 keeps S in shared
 // memory (for comparisons).
-template <int SIDE, bool VAR, bool MASKED = false>
+template <int SIDE, bool VAR, bool MASKED = false, bool PRE = false>
 int grad_side(const float* A, const float* F, const float* va, const float* vb, const float* C,
               const float* dC, const float* dQ, int B, int N, int M, int D, double beta,
               double eps, float* dA, float* dva, cudaStream_t st,
@@ -1497,13 +1502,13 @@ int grad_side(const float* A, const float* F, const float* va, const float* vb, 
   // S in TMEM with wide MMAs while 2 x 2BD accumulator columns + one S slot
   // fit in 512 (D <= 96); wide MMAs with S in shared memory up to D = 128.
   if (!smem_s && 4 * BD + 64 <= 512)
-    return grad_side_impl<SIDE, VAR, MASKED, true, true>(A, F, va, vb, C, dC, dQ, B, N, M, D,
-                                                         beta, eps, dA, dva, st, mask);
+    return grad_side_impl<SIDE, VAR, MASKED, true, true, PRE>(A, F, va, vb, C, dC, dQ, B, N, M, D,
+                                                              beta, eps, dA, dva, st, mask);
   if (2 * BD <= 256)
-    return grad_side_impl<SIDE, VAR, MASKED, false, true>(A, F, va, vb, C, dC, dQ, B, N, M, D,
-                                                          beta, eps, dA, dva, st, mask);
-  return grad_side_impl<SIDE, VAR, MASKED, false, false>(A, F, va, vb, C, dC, dQ, B, N, M, D,
-                                                         beta, eps, dA, dva, st, mask);
+    return grad_side_impl<SIDE, VAR, MASKED, false, true, PRE>(A, F, va, vb, C, dC, dQ, B, N, M,
+                                                               D, beta, eps, dA, dva, st, mask);
+  return grad_side_impl<SIDE, VAR, MASKED, false, false, PRE>(A, F, va, vb, C, dC, dQ, B, N, M, D,
+                                                              beta, eps, dA, dva, st, mask);
 }
 
 }  // namespace
@@ -1534,11 +1539,19 @@ int tc_grad_f32(const float* X, const float* Y, const float* vx, const float* vy
 }
 
 // Squared-Euclidean chain rule with the positivity mask of the cost kernel in
-// place of the cost: S = dC where sq_raw > 0.
+// place of the cost: S = dC where sq_raw > 0; with mask == nullptr, dC
+// already carries the mask (S = dC).
 int tc_sq_grad_f32(const float* X, const float* Y, const uint32_t* mask, const float* dC, int B,
                    int N, int M, int D, float* dX, float* dY, cudaStream_t st) {
   if (B == 0 || N == 0 || M == 0) return kOk;
   int rc;
+  if (mask == nullptr) {
+    if ((rc = grad_side<0, false, false, true>(X, Y, nullptr, nullptr, nullptr, dC, nullptr, B, N,
+                                               M, D, 0.0, 1e-8, dX, nullptr, st)))
+      return rc;
+    return grad_side<1, false, false, true>(Y, X, nullptr, nullptr, nullptr, dC, nullptr, B, N, M,
+                                            D, 0.0, 1e-8, dY, nullptr, st);
+  }
   if ((rc = grad_side<0, false, true>(X, Y, nullptr, nullptr, nullptr, dC, nullptr, B, N, M, D,
                                       0.0, 1e-8, dX, nullptr, st, mask)))
     return rc;

@@ -261,16 +261,28 @@ def _(X, Y, gamma, bandwidth):
 @torch.library.custom_op("torchwarp_b200::sdtw_fused_backward", mutates_args=())
 def sdtw_fused_backward(X: Tensor, Y: Tensor, mask: Tensor, saved: Tensor, grad_r: Tensor,
                         gamma: float) -> Tuple[Tensor, Tensor]:
+    """(dX, dY).  The DP backward writes dL/dcost with the cost's positivity
+    mask applied (tw_sdtw_backward_masked), so the chain rule takes it as S
+    directly (tw_sqeuclid_grad with a null mask)."""
+    nat.require_cuda(X, Y, grad_r)
     B, N, D = X.shape
     M = Y.shape[1]
-    d_cost, _ = _dp_backward(saved, grad_r, grad_r, N, M, gamma, False)
     X, Y = X.contiguous(), Y.contiguous()
     dX, dY = torch.empty_like(X), torch.empty_like(Y)
     if B:
+        dtype = X.dtype
+        grad_r = grad_r.to(dtype).contiguous()
+        s_cost = X.new_empty(B, N, M)
         with torch.cuda.device(X.device):
-            fn = getattr(nat.lib(), "tw_sqeuclid_grad_" + nat.suffix(X.dtype))
-            nat.check(nat.call("udtw_features_grad", fn, nat.ptr(X), nat.ptr(Y), nat.ptr(mask),
-                               nat.ptr(d_cost), B, N, M, D, nat.ptr(dX), nat.ptr(dY),
+            wb = _ws_bytes(B, N, M, dtype, False)
+            ws = torch.empty(wb, dtype=torch.uint8, device=X.device)
+            fn = getattr(nat.lib(), "tw_sdtw_backward_masked_" + nat.suffix(dtype))
+            nat.check(nat.call("sdtw_backward", fn, nat.ptr(grad_r), B, N, M, float(gamma),
+                               nat.ptr(saved), saved.numel(), nat.ptr(mask), nat.ptr(s_cost),
+                               nat.ptr(ws), wb, nat.stream_of(X)), "tw_sdtw_backward_masked")
+            fn = getattr(nat.lib(), "tw_sqeuclid_grad_" + nat.suffix(dtype))
+            nat.check(nat.call("udtw_features_grad", fn, nat.ptr(X), nat.ptr(Y), None,
+                               nat.ptr(s_cost), B, N, M, D, nat.ptr(dX), nat.ptr(dY),
                                nat.stream_of(X)), "tw_sqeuclid_grad")
     return dX, dY
 
