@@ -129,7 +129,7 @@ __device__ __forceinline__ void cost_epilogue_tile(
       mbar_arrive(acce);
     }
 #pragma unroll
-    for (int q = 0; q < 32; ++q) v[q] += w[q];  // (hi.hi + lo.hi) + (hi.lo + lo.lo)
+    for (int q = 0; q < 32; ++q) v[q] += w[q];  // (hi.hi + lo.hi) + hi.lo
     const int j0 = c.jb * BN + 32 * cc;
     float qv[32];
     uint32_t pos = 0;  // bit q: sq_raw > 0 at column j0 + q
@@ -291,6 +291,9 @@ __global__ void __launch_bounds__(COST_THREADS, 1)
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t IDESC = idesc_tf32(BM, 2 * BN, 0, 0);
+      // X_lo x Y_hi over the first BN columns only (X_lo x Y_lo is below fp32
+      // resolution)
+      constexpr uint32_t IDESC_LO = idesc_tf32(BM, BN, 0, 0);
       int it = 0, ti = 0;
       for (int t = blockIdx.x; t < total; t += gridDim.x, ++ti) {
         const int a = ti & 1;
@@ -315,7 +318,7 @@ __global__ void __launch_bounds__(COST_THREADS, 1)
             const uint64_t dal = smem_desc_sw128(al + kk * 32, 16, 1024);
             const uint64_t db = smem_desc_sw128(bh + kk * 32, 16, 1024);
             mma_tf32(d_tmem, dah, db, IDESC, (kc | kk) != 0);
-            mma_tf32(d_tmem, dal, db, IDESC, 1);
+            mma_tf32(d_tmem, dal, db, IDESC_LO, 1);
           }
           mma_commit(&sh.empty[s]);
         }
@@ -525,6 +528,9 @@ __global__ void __launch_bounds__(COST_THREADS, 1)
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t IDESC = idesc_tf32(BM, 2 * BN, 0, 0);
+      // X_lo x Y_hi over the first BN columns only (X_lo x Y_lo is below fp32
+      // resolution)
+      constexpr uint32_t IDESC_LO = idesc_tf32(BM, BN, 0, 0);
       int it = 0, ti = 0, ui = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++ui) {
@@ -561,7 +567,7 @@ __global__ void __launch_bounds__(COST_THREADS, 1)
               const uint64_t dal = smem_desc_sw128(al + kk * 32, 16, 1024);
               const uint64_t db = smem_desc_sw128(bh + kk * 32, 16, 1024);
               mma_tf32(d_tmem, dah, db, IDESC, (kc | kk) != 0);
-              mma_tf32(d_tmem, dal, db, IDESC, 1);
+              mma_tf32(d_tmem, dal, db, IDESC_LO, 1);
             }
             mma_commit(&sh.empty[s]);
           }
@@ -1150,9 +1156,12 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
   } else if (!dead && warp == GRAD_MMA_WARP) {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
-      // WIDE: B = [F_hi | F_lo] along N (2 BD columns), two MMAs per K step
+      // WIDE: B = [F_hi | F_lo] along N (2 BD columns), two MMAs per K step:
+      // S_hi x [F_hi | F_lo] over 2 BD columns and S_lo x F_hi over the first
+      // BD (the S_lo x F_lo term is below fp32 resolution and is skipped)
       const int ACC = WIDE ? 2 * BD : BD;
       const uint32_t idesc = idesc_tf32(128, ACC, (SIDE == 1 && !TA) ? 1 : 0, 1);
+      const uint32_t idesc_lo = idesc_tf32(128, BD, (SIDE == 1 && !TA) ? 1 : 0, 1);
       int it = 0, ti = 0;
       for (int u = blockIdx.x; u < total; u += gridDim.x, ++ti) {
         const int a = ti & 1;
@@ -1180,7 +1189,7 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
               const uint64_t dbh = smem_desc(fh + kk * 1024, 4096, 512, kLayoutSW128Base32);
               if (WIDE) {
                 mma_tf32_ts(d_tmem, ta + 8 * kk, dbh, idesc, (kc | kk) != 0);
-                mma_tf32_ts(d_tmem, ta + 32 + 8 * kk, dbh, idesc, 1);
+                mma_tf32_ts(d_tmem, ta + 32 + 8 * kk, dbh, idesc_lo, 1);
               } else {
                 const uint64_t dbl = smem_desc(fl + kk * 1024, 4096, 512, kLayoutSW128Base32);
                 mma_tf32_ts(d_tmem, ta + 32 + 8 * kk, dbh, idesc, (kc | kk) != 0);
@@ -1203,7 +1212,7 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
             const uint64_t dbh = smem_desc(fh + kk * 1024, 4096, 512, kLayoutSW128Base32);
             if (WIDE) {
               mma_tf32(d_tmem, dah, dbh, idesc, (kc | kk) != 0);
-              mma_tf32(d_tmem, dal, dbh, idesc, 1);
+              mma_tf32(d_tmem, dal, dbh, idesc_lo, 1);
             } else {
               const uint64_t dbl = smem_desc(fl + kk * 1024, 4096, 512, kLayoutSW128Base32);
               mma_tf32(d_tmem, dal, dbh, idesc, (kc | kk) != 0);
@@ -1246,7 +1255,7 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
           float w[32];
           tmem_ld32(tcol + BD, w);
 #pragma unroll
-          for (int q = 0; q < 32; ++q) v[q] += w[q];  // (hi.hi + lo.hi) + (hi.lo + lo.lo)
+          for (int q = 0; q < 32; ++q) v[q] += w[q];  // (hi.hi + lo.hi) + hi.lo
         }
         if (cc == g.nF - 1) {
           tc_fence_before();
