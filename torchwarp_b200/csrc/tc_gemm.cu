@@ -848,6 +848,16 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
           const int idx = kc * 32 + lane;
           vbl = idx < S ? __ldg(vb_b + idx) : 1.f;
         }
+        // the other side's features of this chunk (at most 3 float4 per
+        // thread: TA runs for D <= 96), read first so that their latency
+        // overlaps the split of S
+        float4 fv[3];
+        {
+          const float4* fr = reinterpret_cast<const float4*>(ld + g.l_f);
+#pragma unroll
+          for (int q = 0; q < 3; ++q)
+            if (q < g.nF) fv[q] = fr[ct + GRAD_CONV * q];
+        }
         float sv[16];
         if (SIDE == 0) {
           const uint32_t mword =
@@ -921,16 +931,15 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
         }
         // the other side's features: elementwise split into shared memory
         {
-          const float4* fr = reinterpret_cast<const float4*>(ld + g.l_f);
           float4* fh = reinterpret_cast<float4*>(cv + g.c_fh);
           float4* fl = reinterpret_cast<float4*>(cv + g.c_fl);
-          const int n4 = g.nF * 256;
-#pragma unroll 2
-          for (int k = ct; k < n4; k += GRAD_CONV) {
-            float4 lo;
-            fh[k] = split4(fr[k], lo);
-            fl[k] = lo;
-          }
+#pragma unroll
+          for (int q = 0; q < 3; ++q)
+            if (q < g.nF) {
+              float4 lo;
+              fh[ct + GRAD_CONV * q] = split4(fv[q], lo);
+              fl[ct + GRAD_CONV * q] = lo;
+            }
         }
         tmem_st_wait();
         mbar_arrive(&sh.lempty[s]);
