@@ -38,7 +38,10 @@ constexpr int TILE_A = BM * KC * 4;                       // 16 KB
 constexpr int TILE_B = BN * KC * 4;                       // 16 KB
 constexpr int STAGE_BYTES = 2 * TILE_A + 2 * TILE_B;      // hi and lo of A and B
 constexpr int STG_BYTES = BM * 32 * 4;                    // one 128 x 32 output chunk
-constexpr int COST_THREADS = 320;
+// Warps 0-3 and 10-13 epilogue (warp w reads TMEM lanes 32 (w % 4) ..; warps
+// 0-3 take the tile's columns [0, BN/2), warps 10-13 [BN/2, BN)), 4-7 split,
+// 8 TMA producer, 9 MMA issuer.
+constexpr int COST_THREADS = 448;
 // Per tile a 128 x 2BN accumulator: columns [0, BN) take A * B_hi products,
 // [BN, 2BN) A * B_lo (B_hi and B_lo are contiguous in shared memory, so one
 // N = 256 MMA covers both); two tiles in flight fill all 512 columns.
@@ -101,12 +104,13 @@ __device__ __forceinline__ float split_line(uint8_t* hi_base, uint8_t* lo_base, 
   return ss;
 }
 
-// Epilogue of one 128 x BN cost tile (accumulator a): TMEM -> registers ->
-// cost (and penalty, positivity mask) -> swizzled staging -> TMA store.
-// Called by the four epilogue warps; `si` counts staging-buffer uses.
+// Epilogue of one half (h) of a 128 x BN cost tile (accumulator a): TMEM ->
+// registers -> cost (and penalty, positivity mask) -> swizzled staging -> TMA
+// store.  Called by the four epilogue warps of half h, each half with its
+// own staging buffer and named barrier; `si` counts staging-buffer uses.
 template <bool VAR>
 __device__ __forceinline__ void cost_epilogue_tile(
-    const TileCoord& c, int a, uint32_t tmem, int warp, int row, const float* x2s,
+    const TileCoord& c, int a, uint32_t tmem, int warp, int row, int h, const float* x2s,
     const float* y2s, const float* vys, uint64_t* acce, uint64_t* nempty, uint8_t* stg_base,
     const CUtensorMap* mapC, const CUtensorMap* mapQ, const float* __restrict__ vx,
     const float* __restrict__ vy, int N, int M, float beta, float eps, int write_q,
@@ -117,14 +121,15 @@ __device__ __forceinline__ void cost_epilogue_tile(
   float vxi = 0.f;
   if (VAR) vxi = i < N ? vx[(long long)c.b * N + i] : 1.f;
   const float beta_ln2 = beta * 0.693147180559945309f;
+  constexpr int CPH = BN / 64;  // 32-column chunks per half
 #pragma unroll 1
-  for (int cc = 0; cc < BN / 32; ++cc) {
+  for (int cc = CPH * h; cc < CPH * (h + 1); ++cc) {
     float v[32], w[32];
     const uint32_t tcol =
-        tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(a * COST_ACC_COLS + 32 * cc);
+        tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(a * COST_ACC_COLS + 32 * cc);
     tmem_ld32(tcol, v);
     tmem_ld32(tcol + BN, w);
-    if (cc == BN / 32 - 1) {
+    if (cc == CPH * (h + 1) - 1) {
       tc_fence_before();
       mbar_arrive(acce);
     }
@@ -149,7 +154,7 @@ __device__ __forceinline__ void cost_epilogue_tile(
         v[q] = sq;
       }
     }
-    if (cc == BN / 32 - 1) mbar_arrive(nempty);
+    if (cc == CPH * (h + 1) - 1) mbar_arrive(nempty);
     if (mask != nullptr && j0 < M) {
       // words [b][j >> 5][i] with the row count padded to NP = 4 ceil(N/4)
       const int NP = (N + 3) & ~3;
@@ -164,16 +169,16 @@ __device__ __forceinline__ void cost_epilogue_tile(
 #pragma unroll
     for (int which = 0; which < (VAR ? 2 : 1); ++which) {
       if (which == 1 && !write_q) break;
-      uint8_t* buf = stg_base + (size_t)(si & 1) * STG_BYTES;
-      if (row == 0) bulk_wait_read<1>();
-      named_bar(1, 128);
+      uint8_t* buf = stg_base + (size_t)h * STG_BYTES;
+      if (row == 0) bulk_wait_read<0>();  // this half's previous store has read the buffer
+      named_bar(1 + h, 128);
       const float* src = which == 0 ? v : qv;
 #pragma unroll
       for (int q4 = 0; q4 < 8; ++q4)
         *reinterpret_cast<float4*>(buf + sw128_chunk(row, q4)) =
             make_float4(src[4 * q4], src[4 * q4 + 1], src[4 * q4 + 2], src[4 * q4 + 3]);
       fence_async_smem();
-      named_bar(1, 128);
+      named_bar(1 + h, 128);
       if (row == 0) {
         tma_store_3d(which == 0 ? mapC : mapQ, buf, j0, c.ib * BM, c.b);
         bulk_commit();
@@ -214,9 +219,9 @@ __global__ void __launch_bounds__(COST_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&sh.accf[a], 1);
-      mbar_init(&sh.acce[a], 128);
+      mbar_init(&sh.acce[a], 256);
       mbar_init(&sh.nfull[a], 128);
-      mbar_init(&sh.nempty[a], 128);
+      mbar_init(&sh.nempty[a], 256);
     }
     mbar_init(&sh.mma_done, 1);
     fence_barrier_init();
@@ -331,9 +336,10 @@ __global__ void __launch_bounds__(COST_THREADS, 1)
         if (mbar_try_wait(&sh.mma_done, 0)) break;
     }
     __syncwarp();
-  } else if (!dead && warp < 4) {
+  } else if (!dead && (warp < 4 || warp >= 10)) {
     // ------------------------------------------------ epilogue
-    const int row = tid;  // TMEM lane == tile row
+    const int row = 32 * (warp & 3) + lane;  // TMEM lane == tile row
+    const int h = warp >= 10 ? 1 : 0;       // column half of the tile
     int ti = 0, si = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++ti) {
       const TileCoord c = tile_of(t, nI, nJ);
@@ -341,8 +347,8 @@ __global__ void __launch_bounds__(COST_THREADS, 1)
       const unsigned ph = (unsigned)(ti >> 1) & 1u;
       const bool ok = mbar_wait(&sh.accf[a], ph, abort) && mbar_wait(&sh.nfull[a], ph, abort);
       if (!ok) record_timeout(abort);
-      if (named_bar_or(1, 128, !ok)) break;  // the four warps stop together
-      cost_epilogue_tile<VAR>(c, a, tmem, warp, row, sh.x2[a], sh.y2[a], sh.vyt[a],
+      if (named_bar_or(3, 256, !ok)) break;  // the eight warps stop together
+      cost_epilogue_tile<VAR>(c, a, tmem, warp, row, h, sh.x2[a], sh.y2[a], sh.vyt[a],
                               &sh.acce[a], &sh.nempty[a], stg_base, &mapC, &mapQ, vx, vy, N, M,
                               beta, eps, write_q, mask, si);
     }
@@ -421,9 +427,9 @@ __global__ void __launch_bounds__(COST_THREADS, 1)
       mbar_init(&sh.xempty[a], 1);
       mbar_init(&sh.xconv[a], 128);
       mbar_init(&sh.accf[a], 1);
-      mbar_init(&sh.acce[a], 128);
+      mbar_init(&sh.acce[a], 256);
       mbar_init(&sh.nfull[a], 128);
-      mbar_init(&sh.nempty[a], 128);
+      mbar_init(&sh.nempty[a], 256);
     }
     mbar_init(&sh.mma_done, 1);
     fence_barrier_init();
@@ -583,9 +589,10 @@ __global__ void __launch_bounds__(COST_THREADS, 1)
         if (mbar_try_wait(&sh.mma_done, 0)) break;
     }
     __syncwarp();
-  } else if (!dead && warp < 4) {
+  } else if (!dead && (warp < 4 || warp >= 10)) {
     // ------------------------------------------------ epilogue
-    const int row = tid;  // TMEM lane == tile row
+    const int row = 32 * (warp & 3) + lane;  // TMEM lane == tile row
+    const int h = warp >= 10 ? 1 : 0;       // column half of the tile
     int ti = 0, si = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
@@ -599,11 +606,11 @@ __global__ void __launch_bounds__(COST_THREADS, 1)
         const unsigned ph = (unsigned)(ti >> 1) & 1u;
         const bool good = mbar_wait(&sh.accf[a], ph, abort) && mbar_wait(&sh.nfull[a], ph, abort);
         if (!good) record_timeout(abort);
-        if (named_bar_or(1, 128, !good)) {  // the four warps stop together
+        if (named_bar_or(3, 256, !good)) {  // the eight warps stop together
           ok = false;
           break;
         }
-        cost_epilogue_tile<VAR>(c, a, tmem, warp, row, sh.x2[a], sh.y2[a], sh.vyt[a],
+        cost_epilogue_tile<VAR>(c, a, tmem, warp, row, h, sh.x2[a], sh.y2[a], sh.vyt[a],
                                 &sh.acce[a], &sh.nempty[a], stg_base, &mapC, &mapQ, vx, vy, N,
                                 M, beta, eps, write_q, mask, si);
       }
