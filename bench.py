@@ -48,16 +48,16 @@ ALGO_BYTES_PER_CELL = 8      # soft-DTW fwd+bwd: cost read + cost-gradient write
 # launch, DRAM bytes per cell of one launch measured by ncu).  Algorithmic:
 # the DP forward's cost read and the backward's cost-gradient write (the
 # 8 B/cell of the step split between them), the cost builder's cost write,
-# each chain-rule launch's cost-gradient read.  Measured: DRAM read +
-# write per cell from the `ncu --set full` capture of the same kernels at
-# B=4096, N=M=256 (profiles/soft_dtw_b4096_n256_kernels_ncu.md), applied per
-# cell to the launch being timed; feature bytes (X, Y, dX, dY) are added at
-# the timed shape.
+# each chain-rule launch's cost-gradient read.  Measured: DRAM read + write
+# of the full-size cfg5 launch (B=4096, N=M=1024, D=64) from a one-pass ncu
+# capture (profiles/soft_dtw_cfg5_launch_list.md), per cell, without the
+# feature bytes (X, Y read by the cost builder, dX or dY written by each
+# chain-rule side), which are added at the timed shape.
 CALLS = {
-    "udtw_cost": (1, 4, 4.0),            # C write (+ mask), + X, Y read
-    "sdtw_forward": (1, 4, 8.19),        # C read + saved R' write
-    "sdtw_backward": (1, 4, 9.72),       # saved R' read + dC write (+1.6 B/cell to find)
-    "udtw_features_grad": (2, 4, 4.1),   # dC (+ positivity mask) read per side
+    "udtw_cost": (1, 4, 4.12),           # C write + mask
+    "sdtw_forward": (1, 4, 8.16),        # C read + saved R' write
+    "sdtw_backward": (1, 4, 10.17),      # saved R' + mask read + masked dC write (+1.9 B/cell)
+    "udtw_features_grad": (2, 4, 4.57),  # masked dC read + the other side's features per unit
 }
 
 
@@ -281,8 +281,8 @@ def run_ours(a):
     roofline = {"bound": "hbm", "kernel": name, "achieved": achieved, "peak": peak,
                 "unit": "GB/s", "frac": achieved / peak, "peak_source": src,
                 "traffic": traffic,
-                "traffic_source": "ncu dram__bytes_read+write per cell of the B=4096 N=M=256 "
-                                  "capture, scaled to this launch's cells",
+                "traffic_source": "ncu dram__bytes_read+write per cell of the full-size cfg5 "
+                                  "launch (one-pass capture), scaled to this launch's cells",
                 "algorithmic_bytes_per_launch": algo, "avg_launch_ms": per_launch_ms,
                 "launches_per_call": launches_per_call,
                 "step_frac": (cells_local * ALGO_BYTES_PER_CELL / (ms_step / 1e3) / 1e9) / peak,
