@@ -248,14 +248,20 @@ def run_ours(a):
                 out_h[s].copy_(d.detach(), non_blocking=True)
                 free[s].record()
 
+        # The first step's copy has nothing to overlap with (pipeline fill);
+        # it stays inside the timed region, spread over at least 20 steps as
+        # in a long training loop.
+        e2e_steps = max(a.steps, 20)
         e2e_run(2)
-        ms_e = timed(lambda: e2e_run(a.steps), 1)
+        ms_e = timed(lambda: e2e_run(e2e_steps), 1)
         del bufs
-        e2e = {"value": cells_total / (ms_e / a.steps / 1e3), "unit": UNIT,
+        e2e = {"value": cells_total / (ms_e / e2e_steps / 1e3), "unit": UNIT,
                "h2d_bytes_per_step": int((Xh.numel() + Yh.numel()) * 4 * world),
-               "d2h_bytes_per_step": int(Bl * 4 * world), "ms_per_step": ms_e / a.steps,
+               "d2h_bytes_per_step": int(Bl * 4 * world), "ms_per_step": ms_e / e2e_steps,
+               "steps": e2e_steps,
                "copies": "pinned host -> device every step, overlapped with the previous "
-                         "step on a copy stream; distances read back every step"}
+                         "step on a copy stream; distances read back every step; the first "
+                         "copy (pipeline fill) is inside the timed region"}
 
     # dominant native kernel of the timed region (one C-ABI call may launch
     # several kernels of equal work: the chain rule runs its dX and dY sides)
