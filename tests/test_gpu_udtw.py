@@ -140,6 +140,7 @@ def test_scaled_reference_backend(tw, name):
     (1, 1, 1, 0), (3, 1, 9, 0), (3, 9, 1, 0), (5, 33, 7, 0), (4, 31, 32, 0), (2, 64, 65, 0),
     (7, 65, 64, 0), (2, 129, 140, 0), (3, 200, 260, 0), (300, 17, 23, 0), (611, 40, 41, 0),
     (2, 150, 160, 12), (3, 96, 100, 5.5), (700, 70, 60, 0), (650, 100, 95, 9),
+    (3000, 64, 20, 0), (2600, 128, 12, 0), (2700, 96, 10, 0),
 ])
 def test_dp_vs_oracle(tw, orc, B, N, M, band):
     """Shapes that cross the sub-band, band-pass and pairs-per-warp boundaries."""

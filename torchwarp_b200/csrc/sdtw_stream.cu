@@ -114,33 +114,50 @@ __device__ __forceinline__ void cursor_prev(Cursor& c, const StreamPlan& p) {
 
 // ---------------------------------------------------------------- forward
 
-// Copy the 8 stream columns of tile c of this lane's row of sub-band k into
-// its ring row (cp.async, zero-filled outside the data).
-template <typename T, int KS>
-__device__ __forceinline__ void load_row_tile(const T* __restrict__ src_base, T* ring_row,
-                                              const Cursor& c, int k, const StreamPlan& p,
-                                              const WarpInfo& wi, int vec) {
-  if (c.q < 0 || c.q >= wi.Q || c.j0 >= p.M) return;  // nothing, or all padding
-  const int j0 = c.j0;
+// What a lane does for the tiles of cursor c's pass in sub-band k: 0 nothing
+// (no pass), 1 zero-fill (a row past N), 2 copy its row, whose element offset
+// in the cost / penalty is `off`.  Recomputed only when a pass begins.
+template <int KS>
+__device__ __forceinline__ int row_mode(const Cursor& c, int k, const StreamPlan& p,
+                                        const WarpInfo& wi, long long& off) {
+  off = 0;
+  if (c.q < 0 || c.q >= wi.Q) return 0;
   const int row = c.band * 32 * KS + 32 * k + wi.lane;
-  const bool rv = row < p.N;
+  if (row >= p.N) return 1;
+  off = ((long long)(wi.p0 + c.pq) * p.N + row) * p.M;
+  return 2;
+}
+
+// Copy the 8 stream columns of tile c of this lane's row into its ring row
+// (cp.async, zero-filled outside the data); `mode` and `off` from row_mode.
+template <typename T>
+__device__ __forceinline__ void load_row_tile(const T* __restrict__ src_base, T* ring_row,
+                                              const Cursor& c, int mode, long long off,
+                                              const StreamPlan& p, int vec) {
+  if (mode == 0 || c.j0 >= p.M) return;  // nothing, or all padding
+  const int j0 = c.j0;
   T* dst = ring_row + ((c.u * TILE) & (RING - 1));
-  const T* src = src_base + ((long long)(wi.p0 + c.pq) * p.N + (rv ? row : 0)) * p.M;
+  const T* src = src_base + off;
   if (vec) {
     constexpr int PER = 16 / (int)sizeof(T);
+    if (mode == 2 && j0 + TILE <= p.M) {  // a whole tile of data
 #pragma unroll
-    for (int h = 0; h < TILE / PER; ++h) {
-      const int j = j0 + h * PER;
-      int cnt = rv ? min(PER, p.M - j) : 0;
-      cnt = cnt < 0 ? 0 : cnt;
-      cp_async16(dst + h * PER, cnt > 0 ? (const void*)(src + j) : (const void*)src_base,
-                 cnt * (int)sizeof(T));
+      for (int h = 0; h < TILE / PER; ++h) cp_async16(dst + h * PER, src + j0 + h * PER, 16);
+    } else {
+#pragma unroll
+      for (int h = 0; h < TILE / PER; ++h) {
+        const int j = j0 + h * PER;
+        int cnt = mode == 2 ? min(PER, p.M - j) : 0;
+        cnt = cnt < 0 ? 0 : cnt;
+        cp_async16(dst + h * PER, cnt > 0 ? (const void*)(src + j) : (const void*)src_base,
+                   cnt * (int)sizeof(T));
+      }
     }
   } else {
 #pragma unroll
     for (int h = 0; h < TILE; ++h) {
       const int j = j0 + h;
-      const bool v = rv && j < p.M;
+      const bool v = mode == 2 && j < p.M;
       cp_async_elem<sizeof(T)>(dst + h, v ? (const void*)(src + j) : (const void*)src_base,
                                v ? (int)sizeof(T) : 0);
     }
@@ -222,18 +239,22 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
   T* myQ = ringQ + lane * S;
 
   Cursor ld[KS], pt[KS];  // next tile to load / to patch, per sub-band (lane-dependent)
+  int lmode[KS];           // row_mode of ld's pass
+  long long loff[KS];
 #pragma unroll
   for (int k = 0; k < KS; ++k) {
     ld[k] = cursor_at(-4 * k - (lane >> 3), p);
     pt[k] = ld[k];
+    lmode[k] = row_mode<KS>(ld[k], k, p, wi, loff[k]);
   }
 #pragma unroll 1
   for (int pb = -LEAD; pb < 0; ++pb) {
 #pragma unroll
     for (int k = 0; k < KS; ++k) {
-      load_row_tile<T, KS>(a.C, myC + k * 32 * S, ld[k], k, p, wi, a.vec);
-      if (HAS_P) load_row_tile<T, KS>(a.Q, myQ + k * 32 * S, ld[k], k, p, wi, a.vec);
+      load_row_tile<T>(a.C, myC + k * 32 * S, ld[k], lmode[k], loff[k], p, a.vec);
+      if (HAS_P) load_row_tile<T>(a.Q, myQ + k * 32 * S, ld[k], lmode[k], loff[k], p, a.vec);
       cursor_next(ld[k], p);
+      if (ld[k].j0 == 0) lmode[k] = row_mode<KS>(ld[k], k, p, wi, loff[k]);
     }
     cp_async_commit();
   }
@@ -287,9 +308,10 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
     }
 #pragma unroll
     for (int k = 0; k < KS; ++k) {
-      load_row_tile<T, KS>(a.C, myC + k * 32 * S, ld[k], k, p, wi, a.vec);
-      if (HAS_P) load_row_tile<T, KS>(a.Q, myQ + k * 32 * S, ld[k], k, p, wi, a.vec);
+      load_row_tile<T>(a.C, myC + k * 32 * S, ld[k], lmode[k], loff[k], p, a.vec);
+      if (HAS_P) load_row_tile<T>(a.Q, myQ + k * 32 * S, ld[k], lmode[k], loff[k], p, a.vec);
       cursor_next(ld[k], p);
+      if (ld[k].j0 == 0) lmode[k] = row_mode<KS>(ld[k], k, p, wi, loff[k]);  // a new pass
     }
     cp_async_commit();
 
@@ -422,13 +444,16 @@ __device__ __forceinline__ T row_above_saved(const T* s_warp, int sc, const Stre
 // and zero on padding columns (j >= M), which carry no adjoint.  (The top row
 // of a pair's first band hands the adjoint of its virtual corner R(-1,-1) one
 // column back, into the previous pass's last padding column; it must stop there.)
-template <typename T>
+// SEEDB (N a multiple of the band height): the bottom row of a pair's last
+// band is row N-1, so the pair's seed dL/dR enters here, at column M-1.
+template <typename T, bool SEEDB>
 __device__ __forceinline__ T push_from_below(const T* dl, int sc, const StreamPlan& p,
-                                             const WarpInfo& wi) {
+                                             const WarpInfo& wi, const T* grad) {
   if (sc < 0) return T(0);
   const int q = sc / p.L;
   const int j = sc - q * p.L;
-  if (j >= p.M || q + 1 >= wi.Q || (q + 1) % p.NB == 0) return T(0);
+  if (j >= p.M || q >= wi.Q) return T(0);
+  if ((q + 1) % p.NB == 0) return (SEEDB && j == p.M - 1) ? grad[wi.p0 + q / p.NB] : T(0);
   return dl[j];
 }
 
@@ -494,19 +519,18 @@ __device__ __forceinline__ const uint32_t* mask_row(const uint32_t* mask, int np
 }
 
 // Write this lane's row of flush tile c (8 stream columns) from the staging
-// ring to dC (natural layout), data columns only; with `masked`, columns
-// whose bit in `word` is clear are written as 0.
-template <typename T, int KS>
+// ring to dC (natural layout), data columns only; `mode` and `off` come from
+// row_mode for the tile's pass.  With `masked`, columns whose bit in `word` is
+// clear are written as 0.
+template <typename T>
 __device__ __forceinline__ void flush_row_tile(T* __restrict__ dst_base, const T* ring_row,
-                                               const Cursor& c, int k, const StreamPlan& p,
-                                               const WarpInfo& wi, int vec, bool masked,
+                                               const Cursor& c, int mode, long long off,
+                                               const StreamPlan& p, int vec, bool masked,
                                                uint32_t word) {
-  if (c.q < 0 || c.q >= wi.Q || c.j0 >= p.M) return;
+  if (mode != 2 || c.j0 >= p.M) return;
   const int j0 = c.j0;
-  const int row = c.band * 32 * KS + 32 * k + wi.lane;
-  if (row >= p.N) return;
   const T* src = ring_row + ((c.u * TILE) & (RING - 1));
-  T* dst = dst_base + ((long long)(wi.p0 + c.pq) * p.N + row) * p.M + j0;
+  T* dst = dst_base + off + j0;
   const uint32_t bits = masked ? word >> (j0 & 31) : 0xffu;
   if (vec && j0 + TILE <= p.M) {
     constexpr int PER = 16 / (int)sizeof(T);
@@ -530,7 +554,7 @@ __device__ __forceinline__ void flush_row_tile(T* __restrict__ dst_base, const T
   }
 }
 
-template <typename T, int KS, bool HAS_P>
+template <typename T, int KS, bool HAS_P, bool SEEDB>
 __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
   constexpr int S = RingStride<T>::value;
   constexpr int RW = KS * 32 * S;
@@ -603,8 +627,8 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     const int c = 32 * (dw - h) + lane;
-    sd[c & 63] = push_from_below(dlR, c, p, wi);
-    if (HAS_P) sdp[c & 63] = push_from_below(dlP, c, p, wi);
+    sd[c & 63] = push_from_below<T, SEEDB>(dlR, c, p, wi, a.grad_r);
+    if (HAS_P) sdp[c & 63] = push_from_below<T, SEEDB>(dlP, c, p, wi, a.grad_p);
   }
   __syncwarp();
 
@@ -646,6 +670,8 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
   // tile completed by this lane in block b: u = b - 4k - lane/8; with a
   // positivity mask, its word is loaded a block before the flush
   Cursor fl[KS];
+  int fmode[KS];     // row_mode of fl's pass
+  long long foff[KS];
   uint32_t mwd[KS];
   const uint32_t* mrow[KS];
   const bool masked = a.mask != nullptr;
@@ -653,6 +679,7 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
 #pragma unroll
   for (int k = 0; k < KS; ++k) {
     fl[k] = cursor_at(btop - 4 * k - (lane >> 3), p);
+    fmode[k] = row_mode<KS>(fl[k], k, p, wi, foff[k]);
     mrow[k] = masked ? mask_row<KS>(a.mask, a.mask_np, fl[k], k, p, wi) : nullptr;
     mwd[k] = masked ? mrow[k][min(fl[k].j0 >> 5, mwl) * a.mask_np] : 0u;
   }
@@ -666,7 +693,7 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
       load_saved_row<T, KS>(sRl, t0 - TILE - 2 + s, Fn[s]);
       if (HAS_P) load_saved_row<T, KS>(sPl, t0 - TILE - 2 + s, FPn[s]);
     }
-    const int s_inj = (cap_t >= t0 && cap_t < t0 + TILE) ? cap_t - t0 : -1;
+    const int s_inj = (!SEEDB && cap_t >= t0 && cap_t < t0 + TILE) ? cap_t - t0 : -1;
     T* coll8 = coll + (t0 & 24);  // slot of step t0 + s is coll8[s]
     // The block's row -1 values (column t-1) and adjoints from below (column
     // t - 32 KS), read into registers before the block's first shared-memory
@@ -692,7 +719,7 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
     for (int s = TILE - 1; s >= 0; --s) {
       const int t = t0 + s;
       // the end cell of a pair receives dL/dR (and dL/dP) as its adjoint
-      if (s == s_inj) {
+      if (!SEEDB && s == s_inj) {
 #pragma unroll
         for (int k = 0; k < KS; ++k) {
           accL[k] += sdR[k];
@@ -766,20 +793,22 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
   T pbv = T(0), pbpv = T(0), pdv = T(0), pdpv = T(0);
   // Work between block t0 and block t0 - 8.
   auto between = [&](const int t0) {
-    const bool seedhere = cap_t >= t0 && cap_t < t0 + TILE;
+    const bool seedhere = !SEEDB && cap_t >= t0 && cap_t < t0 + TILE;
 
     // ---- between blocks
 #pragma unroll
     for (int k = 0; k < KS; ++k) {
-      flush_row_tile<T, KS>(a.dC, myC + k * 32 * S, fl[k], k, p, wi, a.vec, masked, mwd[k]);
+      flush_row_tile<T>(a.dC, myC + k * 32 * S, fl[k], fmode[k], foff[k], p, a.vec, masked,
+                        mwd[k]);
       if (HAS_P)
-        flush_row_tile<T, KS>(a.dQ, myQ + k * 32 * S, fl[k], k, p, wi, a.vec, false, 0u);
+        flush_row_tile<T>(a.dQ, myQ + k * 32 * S, fl[k], fmode[k], foff[k], p, a.vec, false, 0u);
       const int oq = fl[k].q;
       cursor_prev(fl[k], p);
-      if (masked) {
-        if (fl[k].q != oq) mrow[k] = mask_row<KS>(a.mask, a.mask_np, fl[k], k, p, wi);
-        mwd[k] = mrow[k][min(fl[k].j0 >> 5, mwl) * a.mask_np];
+      if (fl[k].q != oq) {  // a new pass
+        fmode[k] = row_mode<KS>(fl[k], k, p, wi, foff[k]);
+        if (masked) mrow[k] = mask_row<KS>(a.mask, a.mask_np, fl[k], k, p, wi);
       }
+      if (masked) mwd[k] = mrow[k][min(fl[k].j0 >> 5, mwl) * a.mask_np];
     }
     if (seedhere) {
       --cap_i;
@@ -832,8 +861,8 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
     if (dwn != dw) {
       dw = dwn;
       pdc = 32 * (dw - 1) + lane;
-      pdv = push_from_below(dlR, pdc, p, wi);
-      if (HAS_P) pdpv = push_from_below(dlP, pdc, p, wi);
+      pdv = push_from_below<T, SEEDB>(dlR, pdc, p, wi, a.grad_r);
+      if (HAS_P) pdpv = push_from_below<T, SEEDB>(dlP, pdc, p, wi, a.grad_p);
       pend_d = true;
     }
   };
@@ -863,7 +892,10 @@ int launch_fwd(const SdtwArgs<T>& a, cudaStream_t st) {
 
 template <typename T, int KS, bool HAS_P>
 int launch_bwd(const SdtwArgs<T>& a, cudaStream_t st) {
-  auto kern = sdtw_bwd_kernel<T, KS, HAS_P>;
+  // a pair's end cell is the last lane of the last sub-band when N is a
+  // multiple of the band height: its seed then needs no per-step test
+  auto kern = (a.p.N % (32 * KS)) == 0 ? sdtw_bwd_kernel<T, KS, HAS_P, true>
+                                       : sdtw_bwd_kernel<T, KS, HAS_P, false>;
   const size_t smem = a.p.smem_bwd;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return set_error(kLaunch, "sdtw backward: cannot reserve %zu bytes of shared memory", smem);
@@ -890,9 +922,10 @@ int bwd_ks(const SdtwArgs<T>& a, bool has_p, cudaStream_t st) {
 // device cannot be asked (no GPU: the shared-memory bound alone is used).
 template <typename T, int KS, bool HAS_P>
 int resident_blocks(int wpc, size_t smem) {
-  const void* kerns[3] = {(const void*)sdtw_fwd_kernel<T, KS, HAS_P, false>,
+  const void* kerns[4] = {(const void*)sdtw_fwd_kernel<T, KS, HAS_P, false>,
                           (const void*)sdtw_fwd_kernel<T, KS, HAS_P, true>,
-                          (const void*)sdtw_bwd_kernel<T, KS, HAS_P>};
+                          (const void*)sdtw_bwd_kernel<T, KS, HAS_P, false>,
+                          (const void*)sdtw_bwd_kernel<T, KS, HAS_P, true>};
   int best = INT_MAX;
   for (const void* k : kerns) {
     int n = 0;
