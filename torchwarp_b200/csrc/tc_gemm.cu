@@ -144,11 +144,12 @@ __device__ __forceinline__ void cost_epilogue_tile(
       pos |= (sq > 0.f ? 1u : 0u) << q;
       sq = sq > 0.f ? sq : 0.f;
       if (VAR) {
-        // var = max((vx_i + vy_j) / 2, eps); cost = sq / var through a
-        // correctly rounded reciprocal; penalty = beta ln(var) from log2
+        // var = max((vx_i + vy_j) / 2, eps); cost = sq / var through the
+        // hardware reciprocal (relative error ~2^-22, like the division's
+        // fp32 rounding); penalty = beta ln(var) from log2
         float var = 0.5f * (vxi + vys[32 * cc + q]);
         var = var > eps ? var : eps;
-        v[q] = sq * __frcp_rn(var);
+        v[q] = sq * rcp(var);
         qv[q] = beta_ln2 * lg2(var);
       } else {
         v[q] = sq;
@@ -891,7 +892,7 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
               float inv = 1.f, var_raw = 1.f;
               if (VAR) {
                 var_raw = 0.5f * (va_r + __shfl_sync(0xffffffffu, vbl, jj));
-                inv = __frcp_rn(var_raw > eps ? var_raw : eps);
+                inv = rcp(var_raw > eps ? var_raw : eps);
               }
               const float v = PRE ? ge[e] : (ce[e] > 0.f ? (VAR ? ge[e] * inv : ge[e]) : 0.f);
               rsum += v;
@@ -920,7 +921,7 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
             float inv = 1.f, var_raw = 1.f;
             if (VAR) {
               var_raw = 0.5f * (__shfl_sync(0xffffffffu, vbl, rr) + va_r);
-              inv = __frcp_rn(var_raw > eps ? var_raw : eps);
+              inv = rcp(var_raw > eps ? var_raw : eps);
             }
             const float v = PRE ? gv : (cvv > 0.f ? (VAR ? gv * inv : gv) : 0.f);
             rsum += v;
@@ -1048,9 +1049,10 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
                 var_raw = 0.5f * (va_r[0] + (j < S ? __ldg(vb_b + j) : 1.f));
                 var = var_raw > eps ? var_raw : eps;
               }
-              sv[e] = PRE ? ge[e] : (ce[e] > 0.f ? (VAR ? ge[e] / var : ge[e]) : 0.f);
+              const float rv = VAR ? rcp(var) : 1.f;
+              sv[e] = PRE ? ge[e] : (ce[e] > 0.f ? (VAR ? ge[e] * rv : ge[e]) : 0.f);
               rsum[0] += sv[e];
-              if (VAR && var_raw > eps) vsum[0] += (beta * qe[e] - ge[e] * ce[e]) / var;
+              if (VAR && var_raw > eps) vsum[0] += (beta * qe[e] - ge[e] * ce[e]) * rv;
             }
             float4 lo;
             const float4 hi = split4(make_float4(sv[0], sv[1], sv[2], sv[3]), lo);
@@ -1104,9 +1106,10 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
                 var_raw = 0.5f * (vbi + va_r[e]);
                 var = var_raw > eps ? var_raw : eps;
               }
-              sv[e] = PRE ? ge[e] : (ce[e] > 0.f ? (VAR ? ge[e] / var : ge[e]) : 0.f);
+              const float rv = VAR ? rcp(var) : 1.f;
+              sv[e] = PRE ? ge[e] : (ce[e] > 0.f ? (VAR ? ge[e] * rv : ge[e]) : 0.f);
               rsum[e] += sv[e];
-              if (VAR && var_raw > eps) vsum[e] += (beta * qe[e] - ge[e] * ce[e]) / var;
+              if (VAR && var_raw > eps) vsum[e] += (beta * qe[e] - ge[e] * ce[e]) * rv;
             }
             float4 lo;
             const float4 hi = split4(make_float4(sv[0], sv[1], sv[2], sv[3]), lo);
