@@ -989,8 +989,10 @@ StreamPlan make_stream_plan(int B, int N, int M, int eb, bool has_p, int sms) {
   p.M = M;
   // Sub-bands per warp: ILP inside a warp.  Thread-level parallelism (warps
   // per SM) is what hides the soft-min's latency, and every sub-band costs a
-  // ring of shared memory, so two sub-bands by default.
-  int ks = env_int("TW_STREAM_KS", N <= 32 ? 1 : 2);
+  // ring of shared memory, so two sub-bands by default; one with the uDTW
+  // penalty, whose second stream doubles the registers and shared memory of
+  // a sub-band (cfg5 uDTW: 68.2 ms per step at one, 71.8 at two).
+  int ks = env_int("TW_STREAM_KS", (N <= 32 || has_p) ? 1 : 2);
   p.KS = ks >= 4 ? 4 : (ks < 1 ? 1 : ks);
   const int rows = 32 * p.KS;
   p.NB = (N + rows - 1) / rows;
