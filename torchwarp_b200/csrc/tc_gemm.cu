@@ -10,11 +10,13 @@
 //
 // Each CTA is persistent (one per SM) and walks output tiles of 128 x 128
 // cells.  Warp roles:
-//   warps 0-3  epilogue: TMEM -> registers -> cost -> swizzled smem -> TMA store
+//   warps 0-3, 10-13  epilogue: TMEM -> registers -> cost -> swizzled smem ->
+//              TMA store (two warps per TMEM lane quadrant, each half of the
+//              tile's columns)
 //   warps 4-7  split:    fp32 tile -> (hi, lo) TF32 pair in place, row norms
 //   warp  8    TMA producer of the X / Y feature chunks (32 features each)
-//   warp  9    MMA issuer: per 8-feature step two N = 256 MMAs, A_hi [B_hi; B_lo]
-//              and A_lo [B_hi; B_lo] (all four TF32 products)
+//   warp  9    MMA issuer: per 8-feature step an N = 256 MMA A_hi [B_hi; B_lo]
+//              and an N = 128 MMA A_lo B_hi (the three 3xTF32 products)
 // Two TMEM accumulators (2 x 256 columns) let the epilogue of one tile
 // overlap the MMAs of the next.  No atomics: results are reproducible.
 #include <cstdlib>
@@ -319,7 +321,7 @@ __global__ void __launch_bounds__(COST_THREADS, 1)
           const uint32_t al = ah + TILE_A, bh = ah + 2 * TILE_A;
 #pragma unroll
           for (int kk = 0; kk < KC / 8; ++kk) {
-            // B = [B_hi; B_lo] (256 rows): A_hi B -> hi.hi | hi.lo, A_lo B -> lo.hi | lo.lo
+            // B = [B_hi; B_lo] (256 rows): A_hi B -> hi.hi | hi.lo; A_lo B_hi -> lo.hi
             const uint64_t dah = smem_desc_sw128(ah + kk * 32, 16, 1024);
             const uint64_t dal = smem_desc_sw128(al + kk * 32, 16, 1024);
             const uint64_t db = smem_desc_sw128(bh + kk * 32, 16, 1024);
@@ -569,7 +571,7 @@ __global__ void __launch_bounds__(COST_THREADS, 1)
             const uint32_t bh = smem_u32(y_base + (size_t)s * XR_CHUNK);
 #pragma unroll
             for (int kk = 0; kk < KC / 8; ++kk) {
-              // B = [B_hi; B_lo] (256 rows): A_hi B -> hi.hi | hi.lo, A_lo B -> lo.hi | lo.lo
+              // B = [B_hi; B_lo] (256 rows): A_hi B -> hi.hi | hi.lo; A_lo B_hi -> lo.hi
               const uint64_t dah = smem_desc_sw128(ah + kk * 32, 16, 1024);
               const uint64_t dal = smem_desc_sw128(al + kk * 32, 16, 1024);
               const uint64_t db = smem_desc_sw128(bh + kk * 32, 16, 1024);
@@ -637,11 +639,12 @@ __global__ void __launch_bounds__(COST_THREADS, 1)
 //   dvx = 0.5 rowsum(dvar), dvy = 0.5 colsum(dvar),
 //   dvar = (beta dQ - dC C) / var where var_raw > eps.
 // Two rings of shared memory: a deep landing ring that TMA fills with raw
-// chunks (dC [, C] [, dQ], the other side's 32 feature rows, the mask words)
-// so that enough bytes are in flight to cover HBM latency, and a two-deep
-// ring of converted operands: the split warps read a landing chunk, write S
-// and the features as TF32 (hi, lo) pairs into a converted slot (same
-// swizzled positions) and release the landing slot at once.  The MMA
+// chunks (dC [, C] [, dQ], the other side's 32 feature rows, the mask words;
+// with PRE only dC and the features) so that enough bytes are in flight to
+// cover HBM latency, and a ring of converted operands: the split warps read a
+// landing chunk, write S (to TMEM, or to shared memory for wide D) and the
+// features as TF32 (hi, lo) pairs into a converted slot (same swizzled
+// positions) and release the landing slot at once.  The MMA
 // contracts S (K-major for SIDE 0, MN-major for SIDE 1) with the features
 // (MN-major) into a 128 x BD TMEM accumulator; the epilogue adds 2 A rowsum
 // and stores through TMA.  MN-major TF32 operands are only valid in the
