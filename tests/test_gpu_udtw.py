@@ -172,6 +172,85 @@ def test_soft_dtw_cost_vs_oracle(tw, orc, B, N, M):
     _close(c.grad, dC)
 
 
+@pytest.mark.parametrize("ks", [1, 2, 3, 4])
+@pytest.mark.parametrize("B,N,M,pen", [
+    (3, 200, 260, False), (2, 129, 300, True), (2, 256, 520, False), (70, 100, 95, True),
+    (5, 384, 130, False),
+])
+def test_sub_band_counts_vs_oracle(tw, orc, monkeypatch, ks, B, N, M, pen):
+    """Every sub-band count the plan can choose (forced through TW_STREAM_KS),
+    float64, with and without the uDTW penalty stream."""
+    monkeypatch.setenv("TW_STREAM_KS", str(ks))
+    g = torch.Generator().manual_seed(ks * 7919 + B * 31 + N + M)
+    C = torch.rand(B, N, M, generator=g, dtype=torch.float64)
+    gr = torch.rand(B, generator=g, dtype=torch.float64)
+    c = C.to(DEV).requires_grad_(True)
+    if pen:
+        Q = torch.randn(B, N, M, generator=g, dtype=torch.float64)
+        gp = torch.randn(B, generator=g, dtype=torch.float64)
+        q = Q.to(DEV).requires_grad_(True)
+        d, p = tw.functional.udtw_from_cost(c, q, gamma=0.3)
+        (d * gr.to(DEV) + p * gp.to(DEV)).sum().backward()
+        od, op, dC, dQ = orc.udtw_from_cost(C.numpy(), Q.numpy(), gamma=0.3, g_d=gr.numpy(),
+                                            g_p=gp.numpy())
+        _close(p, op)
+        _close(q.grad, dQ)
+    else:
+        d = tw.functional.soft_dtw_from_cost(c, gamma=0.3)
+        (d * gr.to(DEV)).sum().backward()
+        od, dC = orc.soft_dtw_from_cost(C.numpy(), gamma=0.3)
+        dC = dC * gr.numpy()[:, None, None]
+    _close(d, od)
+    _close(c.grad, dC)
+
+
+def _saved_bytes(tw, B, N, M, eb, pen):
+    return tw._native.lib().tw_sdtw_saved_bytes(B, N, M, eb, int(pen))
+
+
+@pytest.mark.parametrize("B,N,M,eb,pen,want", [
+    (512, 1024, 1024, 4, False, 4),   # 3.5 pairs per SM: wide bands
+    (1184, 1024, 1024, 4, False, 4),  # 8 pairs per SM
+    (1185, 1024, 1024, 4, False, 2),
+    (4096, 1024, 1024, 4, False, 2),
+    (512, 1024, 1024, 8, False, 2),   # fp64 keeps two sub-bands
+    (512, 200, 200, 4, False, 2),     # short sequences keep two
+    (512, 1000, 1024, 4, False, 4),   # 1000 rows pad to 1024 with either count
+    (512, 576, 1024, 4, False, 2),    # 576 rows: 9 bands of 64, but 640 rows in bands of 128
+    (512, 1024, 1024, 4, True, 2),    # uDTW: one sub-band -> two
+    (2048, 1024, 1024, 4, True, 1),
+])
+def test_sub_band_choice(tw, monkeypatch, B, N, M, eb, pen, want):
+    """The plan's default sub-band count, read through the saved-stream size
+    (which depends on it) against the size with the count forced."""
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    if sms != 148:
+        pytest.skip("thresholds are written for 148 SMs")
+    monkeypatch.delenv("TW_STREAM_KS", raising=False)
+    auto = _saved_bytes(tw, B, N, M, eb, pen)
+    monkeypatch.setenv("TW_STREAM_KS", str(want))
+    assert auto == _saved_bytes(tw, B, N, M, eb, pen)
+    other = {4: 2, 2: 1 if pen else 4, 1: 2}[want]
+    monkeypatch.setenv("TW_STREAM_KS", str(other))
+    assert auto != _saved_bytes(tw, B, N, M, eb, pen)  # the size tells the counts apart
+
+
+def test_sub_band_counts_agree_fp32(tw, monkeypatch):
+    """The soft-min recursion per cell does not depend on how rows are split
+    into bands, so 2 and 4 sub-bands give bit-identical values and gradients."""
+    g = torch.Generator().manual_seed(11)
+    C = torch.rand(6, 640, 700, generator=g).to(DEV)
+    out = []
+    for ks in (2, 4):
+        monkeypatch.setenv("TW_STREAM_KS", str(ks))
+        c = C.clone().requires_grad_(True)
+        d = tw.functional.soft_dtw_from_cost(c, gamma=0.1)
+        d.sum().backward()
+        out.append((d.detach(), c.grad))
+    assert torch.equal(out[0][0], out[1][0])
+    torch.testing.assert_close(out[0][1], out[1][1], rtol=1e-6, atol=1e-9)
+
+
 def test_soft_dtw_features_fp32_vs_fp64(tw, orc):
     """cfg5-shaped soft-DTW (N=M=1024, D=64, gamma=0.01) in float32 against
     the float64 oracle: the forward value within 1e-5 relative."""
@@ -229,9 +308,13 @@ def _unpack_mask(mask, N, M):
 @pytest.mark.parametrize("shape", [(3, 70, 45), (2, 200, 130), (5, 33, 64), (4, 1, 1),
                                    (2, 129, 300), (1, 257, 9), (2, 70, 40), (1, 100, 296)])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float64])
-def test_sdtw_backward_masked(tw, shape, dtype):
+@pytest.mark.parametrize("ks", [None, 3, 4])
+def test_sdtw_backward_masked(tw, monkeypatch, shape, dtype, ks):
     """tw_sdtw_backward_masked writes the plain backward's d_cost with the
-    cells whose mask bit is clear set to zero, bit for bit."""
+    cells whose mask bit is clear set to zero, bit for bit (with the plan's
+    own sub-band count and with 3 and 4 forced)."""
+    if ks is not None:
+        monkeypatch.setenv("TW_STREAM_KS", str(ks))
     from torchwarp_b200 import _native as nat
     from torchwarp_b200.udtw import _ops
     B, N, M = shape

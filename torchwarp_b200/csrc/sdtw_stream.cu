@@ -992,7 +992,23 @@ StreamPlan make_stream_plan(int B, int N, int M, int eb, bool has_p, int sms) {
   // ring of shared memory, so two sub-bands by default; one with the uDTW
   // penalty, whose second stream doubles the registers and shared memory of
   // a sub-band (cfg5 uDTW: 68.2 ms per step at one, 71.8 at two).
-  int ks = env_int("TW_STREAM_KS", (N <= 32 || has_p) ? 1 : 2);
+  //
+  // With at most 8 pairs per SM (a batch sharded over 4 or 8 GPUs) there are
+  // too few warps to hide the latency, and twice the sub-bands per warp win
+  // in fp32 when both sequences are long enough that the wider band's delay
+  // line (32*KS + 128 columns) and skew stay small against M.  N=M=1024 fwd+bwd:
+  // B=512 6.42 -> 5.48 ms, B=1184 8.56 -> 8.00 ms (soft-DTW, 2 -> 4 sub-bands);
+  // B=1480 9.91 -> 12.44 ms; uDTW B=512 13.0 -> 10.0 ms (1 -> 2 sub-bands),
+  // B=2048 26.5 -> 28.5 ms.  fp64 lost at every batch tried (B=512: 27.0 ->
+  // 38.8 ms), and so did N=M=200 (0.36 -> 0.44 ms).
+  int ks_def = (N <= 32 || has_p) ? 1 : 2;
+  if (eb == 4 && N >= 512 && M >= 512 && B <= 8 * sms) {
+    const int wide = 2 * ks_def;
+    const int rows_now = (N + 32 * ks_def - 1) / (32 * ks_def) * (32 * ks_def);
+    const int rows_wide = (N + 32 * wide - 1) / (32 * wide) * (32 * wide);
+    if (rows_wide == rows_now) ks_def = wide;
+  }
+  int ks = env_int("TW_STREAM_KS", ks_def);
   p.KS = ks >= 4 ? 4 : (ks < 1 ? 1 : ks);
   const int rows = 32 * p.KS;
   p.NB = (N + rows - 1) / rows;
