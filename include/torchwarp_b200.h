@@ -50,10 +50,11 @@ extern "C" {
 int tw_version(void);
 /* Message of the last error on this host thread ("" if none). */
 const char* tw_last_error(void);
-/* Reads and clears the device-side error word of the tensor-core kernels
- * (0: none; TW_ERR_TIMEOUT: a bounded pipeline wait ran out; TW_ERR_LAUNCH:
- * unaligned shared memory).  Synchronises with the device.  No counterpart
- * in the reference, whose kernels have no device-side waits. */
+/* Reads and clears the device-side error words of the tensor-core kernels
+ * and of the DP sweeps (0: none; TW_ERR_TIMEOUT: a bounded pipeline wait, or
+ * a band group's window wait, ran out; TW_ERR_LAUNCH: unaligned shared
+ * memory).  Synchronises with the device.  No counterpart in the reference,
+ * whose kernels have no device-side waits. */
 int tw_device_error(void);
 
 /* ---------------------------------------------------------------------

@@ -204,35 +204,104 @@ def test_sub_band_counts_vs_oracle(tw, orc, monkeypatch, ks, B, N, M, pen):
     _close(c.grad, dC)
 
 
+@pytest.mark.parametrize("G,ks,B,N,M,pen,band", [
+    (2, 2, 3, 256, 300, False, 0),      # N a multiple of the band height: seed from below
+    (4, 2, 3, 256, 300, True, 0),
+    (4, 1, 5, 250, 310, True, 0),       # ragged last band
+    (2, 1, 5, 250, 310, False, 0),
+    (4, 4, 2, 1024, 40, False, 0),      # L padded to G (32 KS + 128)
+    (2, 2, 2, 200, 200, True, 15),      # Sakoe-Chiba band
+    (4, 1, 2999, 128, 20, True, 0),     # several pairs per group, ragged split
+    (2, 2, 1000, 256, 260, False, 4.5),
+    # g * D not a multiple of 32: the per-lane rings are indexed by step, not column
+    (2, 2, 3, 256, 1030, False, 0),     # L = 1040, D = 520
+    (4, 2, 2, 512, 1100, True, 0),      # L = 1120, D = 280
+    (4, 1, 3, 256, 700, True, 0),       # L = 704, D = 176
+    (4, 4, 2, 1024, 1030, False, 40),   # L = 1056, D = 264
+])
+def test_band_groups_vs_oracle(tw, orc, monkeypatch, G, ks, B, N, M, pen, band):
+    """Band groups (TW_STREAM_G): G warps per pair set, one band in G each,
+    float64 against the oracle, and no device-side wait ran out."""
+    monkeypatch.setenv("TW_STREAM_G", str(G))
+    monkeypatch.setenv("TW_STREAM_KS", str(ks))
+    g = torch.Generator().manual_seed(G * 101 + ks * 7 + B + N + M)
+    C = torch.rand(B, N, M, generator=g, dtype=torch.float64)
+    Q = torch.randn(B, N, M, generator=g, dtype=torch.float64) if pen else np.zeros((B, N, M))
+    gr = torch.rand(B, generator=g, dtype=torch.float64)
+    gp = torch.randn(B, generator=g, dtype=torch.float64)
+    c = C.to(DEV).requires_grad_(True)
+    bw = band or None
+    if pen:
+        q = Q.to(DEV).requires_grad_(True)
+        d, p = tw.functional.udtw_from_cost(c, q, gamma=0.3, bandwidth=bw)
+        (d * gr.to(DEV) + p * gp.to(DEV)).sum().backward()
+        od, op, dC, dQ = orc.udtw_from_cost(C.numpy(), Q.numpy(), gamma=0.3, bandwidth=bw,
+                                            g_d=gr.numpy(), g_p=gp.numpy())
+        _close(p, op)
+        _close(q.grad, dQ)
+    else:
+        d = tw.functional.soft_dtw_from_cost(c, gamma=0.3, bandwidth=bw)
+        (d * gr.to(DEV)).sum().backward()
+        od, _, dC, _ = orc.udtw_from_cost(C.numpy(), Q, gamma=0.3, bandwidth=bw, g_d=gr.numpy())
+    _close(d, od)
+    _close(c.grad, dC)
+    assert tw._native.lib().tw_device_error() == 0
+
+
+@pytest.mark.parametrize("ks", [2, 4])
+def test_band_groups_agree_fp32(tw, monkeypatch, ks):
+    """Splitting a pair's bands over 1, 2 or 4 warps does not change the
+    arithmetic of any cell: float32 values are bit-identical."""
+    g = torch.Generator().manual_seed(12)
+    C = torch.rand(6, 512, 1100, generator=g).to(DEV)  # 8 or 4 bands: G = 4 applies
+    monkeypatch.setenv("TW_STREAM_KS", str(ks))
+    out = []
+    for G in (1, 2, 4):
+        monkeypatch.setenv("TW_STREAM_G", str(G))
+        c = C.clone().requires_grad_(True)
+        d = tw.functional.soft_dtw_from_cost(c, gamma=0.1)
+        d.sum().backward()
+        out.append((d.detach(), c.grad))
+    for d, gC in out[1:]:
+        assert torch.equal(d, out[0][0])
+        torch.testing.assert_close(gC, out[0][1], rtol=1e-6, atol=1e-9)
+    assert tw._native.lib().tw_device_error() == 0
+
+
 def _saved_bytes(tw, B, N, M, eb, pen):
     return tw._native.lib().tw_sdtw_saved_bytes(B, N, M, eb, int(pen))
 
 
-@pytest.mark.parametrize("B,N,M,eb,pen,want", [
-    (512, 1024, 1024, 4, False, 4),   # 3.5 pairs per SM: wide bands
-    (1184, 1024, 1024, 4, False, 4),  # 8 pairs per SM
-    (1185, 1024, 1024, 4, False, 2),
-    (4096, 1024, 1024, 4, False, 2),
-    (512, 1024, 1024, 8, False, 2),   # fp64 keeps two sub-bands
-    (512, 200, 200, 4, False, 2),     # short sequences keep two
-    (512, 1000, 1024, 4, False, 4),   # 1000 rows pad to 1024 with either count
-    (512, 576, 1024, 4, False, 2),    # 576 rows: 9 bands of 64, but 640 rows in bands of 128
-    (512, 1024, 1024, 4, True, 2),    # uDTW: one sub-band -> two
-    (2048, 1024, 1024, 4, True, 1),
+@pytest.mark.parametrize("B,N,M,eb,pen,ks,G", [
+    (512, 1024, 1024, 4, False, 2, 4),    # 3.5 pairs per SM: 4 warps per pair
+    (1184, 1024, 1024, 4, False, 2, 2),
+    (1775, 1024, 1024, 4, False, 2, 2),   # just under 12 pairs per SM
+    (1776, 1024, 1024, 4, False, 2, 1),
+    (4096, 1024, 1024, 4, False, 2, 1),
+    (512, 1024, 1024, 8, False, 2, 4),    # fp64 too
+    (512, 200, 200, 4, False, 2, 1),      # M + 1 < 2 (64 + 128): no group
+    (512, 640, 1024, 4, False, 2, 2),     # 10 bands: G = 4 does not divide
+    (512, 576, 1024, 4, False, 2, 1),     # 9 bands: no group
+    (512, 1000, 300, 4, False, 2, 1),     # M + 1 < 384
+    (512, 1024, 1024, 4, True, 1, 4),     # uDTW: one sub-band, 4 warps per pair
+    (2048, 1024, 1024, 4, True, 1, 1),
 ])
-def test_sub_band_choice(tw, monkeypatch, B, N, M, eb, pen, want):
-    """The plan's default sub-band count, read through the saved-stream size
-    (which depends on it) against the size with the count forced."""
+def test_sub_band_choice(tw, monkeypatch, B, N, M, eb, pen, ks, G):
+    """The plan's default sub-band count and band-group size, read through the
+    saved-stream size (which depends on both) against the size with both
+    forced."""
     sms = torch.cuda.get_device_properties(0).multi_processor_count
     if sms != 148:
         pytest.skip("thresholds are written for 148 SMs")
     monkeypatch.delenv("TW_STREAM_KS", raising=False)
+    monkeypatch.delenv("TW_STREAM_G", raising=False)
     auto = _saved_bytes(tw, B, N, M, eb, pen)
-    monkeypatch.setenv("TW_STREAM_KS", str(want))
+    monkeypatch.setenv("TW_STREAM_KS", str(ks))
+    monkeypatch.setenv("TW_STREAM_G", str(G))
     assert auto == _saved_bytes(tw, B, N, M, eb, pen)
-    other = {4: 2, 2: 1 if pen else 4, 1: 2}[want]
-    monkeypatch.setenv("TW_STREAM_KS", str(other))
-    assert auto != _saved_bytes(tw, B, N, M, eb, pen)  # the size tells the counts apart
+    # the size tells the choices apart
+    monkeypatch.setenv("TW_STREAM_KS", str(1 if ks == 2 else 2))
+    assert auto != _saved_bytes(tw, B, N, M, eb, pen)
 
 
 def test_sub_band_counts_agree_fp32(tw, monkeypatch):
@@ -308,13 +377,15 @@ def _unpack_mask(mask, N, M):
 @pytest.mark.parametrize("shape", [(3, 70, 45), (2, 200, 130), (5, 33, 64), (4, 1, 1),
                                    (2, 129, 300), (1, 257, 9), (2, 70, 40), (1, 100, 296)])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float64])
-@pytest.mark.parametrize("ks", [None, 3, 4])
-def test_sdtw_backward_masked(tw, monkeypatch, shape, dtype, ks):
+@pytest.mark.parametrize("ks,G", [(None, None), (3, None), (4, None), (1, 4), (2, 2)])
+def test_sdtw_backward_masked(tw, monkeypatch, shape, dtype, ks, G):
     """tw_sdtw_backward_masked writes the plain backward's d_cost with the
     cells whose mask bit is clear set to zero, bit for bit (with the plan's
-    own sub-band count and with 3 and 4 forced)."""
+    own sub-band count, with 3 and 4 forced, and with band groups)."""
     if ks is not None:
         monkeypatch.setenv("TW_STREAM_KS", str(ks))
+    if G is not None:
+        monkeypatch.setenv("TW_STREAM_G", str(G))
     from torchwarp_b200 import _native as nat
     from torchwarp_b200.udtw import _ops
     B, N, M = shape

@@ -188,7 +188,9 @@ const char* tw_last_error(void) { return g_err; }
 
 int tw_device_error(void) {
   if (cudaDeviceSynchronize() != cudaSuccess) return set_error(kLaunch, "device synchronize failed");
-  return tc_take_device_error();
+  const int tc_err = tc_take_device_error();
+  const int dp_err = dp_take_device_error();
+  return tc_err != 0 ? tc_err : dp_err;
 }
 
 size_t tw_sdtw_saved_bytes(int B, int N, int M, int dtype_bytes, int has_penalty) {

@@ -16,8 +16,12 @@
 #include <tuple>
 
 #include "sdtw_stream.cuh"
+#include "tc_common.cuh"
 
 namespace tw {
+
+__device__ int g_dp_error;
+
 namespace {
 
 template <typename T> struct RingStride;
@@ -53,44 +57,103 @@ __device__ __forceinline__ int pos_mod(int a, int b) {
   return r < 0 ? r + b : r;
 }
 
+// g: warp within its band group; off = g * D, the shift of this warp's own
+// stream (local column = step - off); Q: local passes (npairs * NB / G); Tw:
+// steps every warp of the group runs (the group's stream length).
+// wprev / wnext: warps of the bands above / below this warp's bands.
 struct WarpInfo {
-  int w, wib, lane, npairs, p0, Q, Tw;
+  int w, wib, lane, npairs, p0, Q, Tw, g, off, wprev, wnext;
 };
 
-// Pair ranges are handed out in slot order s = (warp in CTA) * CTAs + CTA, so
-// the warps that get one extra pair are spread over all SMs.
+// Pair ranges are handed out per band group in slot order s = (group in
+// CTA) * CTAs + CTA, so the groups that get one extra pair are spread over
+// all SMs.  Every warp of a group gets the same answer.
 __device__ __forceinline__ bool warp_setup(const StreamPlan& p, int KS, WarpInfo& wi) {
   wi.lane = threadIdx.x & 31;
   wi.wib = threadIdx.x >> 5;
   wi.w = blockIdx.x * (blockDim.x >> 5) + wi.wib;
   if (wi.w >= p.warps) return false;
-  const int slot = wi.wib * gridDim.x + blockIdx.x;
+  const int gib = wi.wib / p.G;
+  wi.g = wi.wib - gib * p.G;
+  const int slot = gib * gridDim.x + blockIdx.x;
   wi.npairs = p.base + (slot < p.rem ? 1 : 0);
   if (wi.npairs == 0) return false;
   wi.p0 = slot * p.base + min(slot, p.rem);
-  wi.Q = wi.npairs * p.NB;
-  wi.Tw = wi.Q * p.L + 32 * KS - 1;
+  wi.Q = wi.npairs * (p.NB / p.G);
+  wi.Tw = wi.Q * p.L + 32 * KS - 1 + (p.G - 1) * p.D;
+  wi.off = wi.g * p.D;
+  wi.wprev = wi.g > 0 ? wi.w - 1 : wi.w + p.G - 1;
+  wi.wnext = wi.g < p.G - 1 ? wi.w + 1 : wi.w - (p.G - 1);
   return true;
+}
+
+// Band of this warp's local pass q (any q, also outside [0, Q)).
+__device__ __forceinline__ int band_of(int q, const StreamPlan& p, const WarpInfo& wi) {
+  return wi.g + p.G * pos_mod(q, p.NB / p.G);
+}
+__device__ __forceinline__ bool first_band(int q, const StreamPlan& p, const WarpInfo& wi) {
+  return wi.g == 0 && pos_mod(q, p.NB / p.G) == 0;
+}
+__device__ __forceinline__ bool last_band(int q, const StreamPlan& p, const WarpInfo& wi) {
+  return wi.g == p.G - 1 && pos_mod(q + 1, p.NB / p.G) == 0;
+}
+
+// One step of a band group's lockstep: every lane arrives on the group's
+// mbarrier (release) and waits for the phase to complete (acquire), so the
+// delay-line writes of every warp before it are visible to every warp after
+// it.  The wait is bounded; a warp whose wait runs out records kTimeout and
+// stops waiting (it keeps arriving, so the others are not held up), and the
+// sweep runs to its end with its results marked invalid by the error word.
+__device__ __forceinline__ void group_step(uint64_t* bar, unsigned& phase, bool& dead) {
+  tc::mbar_arrive(bar);
+  if (!dead) {
+    bool ok = false;
+    for (unsigned n = 0; n < tc::kSpinLimit; ++n)
+      if (tc::mbar_try_wait(bar, phase)) { ok = true; break; }
+    if (!ok) {
+      dead = true;
+      atomicExch(&g_dp_error, kTimeout);
+    }
+  }
+  phase ^= 1u;
+}
+
+// The groups' mbarriers (one per group of the CTA, 32 G arrivals), set up
+// before any warp leaves; a no-op without band groups.
+__device__ __forceinline__ uint64_t* group_barrier_init(const StreamPlan& p,
+                                                        unsigned char* smem_raw) {
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw);
+  if (p.G > 1) {
+    const int groups = (blockDim.x >> 5) / p.G;
+    if ((int)threadIdx.x < groups) tc::mbar_init(&bars[threadIdx.x], 32u * p.G);
+    __syncthreads();
+  }
+  return bars + (threadIdx.x >> 5) / p.G;
 }
 
 // Position of stream tile u (the 8 columns [8u, 8u+8)) in (pass, column)
 // space.  Kernels step cursors by one tile per 8-step block, so the hot loop
 // never divides by the runtime L or NB.
 struct Cursor {
-  int u;     // tile index
+  int u;     // tile index in step time (local tile + off / 8): its ring slot
   int q;     // pass (nothing to do when < 0 or >= Q)
   int j0;    // first column of the tile within the pass (L is a multiple of 8)
   int band;  // q mod NB
   int pq;    // q div NB: pair index within the warp
 };
 
-__device__ __forceinline__ Cursor cursor_at(int u, const StreamPlan& p) {
+// u is a tile of the warp's local stream.  Local pass q is band
+// g + G (q mod NB/G) of the pair q div (NB/G), so stepping a pass moves the
+// band by G.  The ring slot of a tile follows the step at which it is used,
+// so c.u counts in steps (shifted by off), not in local columns.
+__device__ __forceinline__ Cursor cursor_at(int u, const StreamPlan& p, const WarpInfo& wi) {
   Cursor c;
-  c.u = u;
+  c.u = u + wi.off / TILE;
   c.q = floor_div(u * TILE, p.L);
   c.j0 = u * TILE - c.q * p.L;
-  c.pq = floor_div(c.q, p.NB);
-  c.band = c.q - c.pq * p.NB;
+  const int nbg = p.NB / p.G;
+  c.pq = floor_div(c.q, nbg);
+  c.band = wi.g + p.G * (c.q - c.pq * nbg);
   return c;
 }
 __device__ __forceinline__ void cursor_next(Cursor& c, const StreamPlan& p) {
@@ -99,7 +162,8 @@ __device__ __forceinline__ void cursor_next(Cursor& c, const StreamPlan& p) {
   if (c.j0 >= p.L) {
     c.j0 = 0;
     ++c.q;
-    if (++c.band == p.NB) { c.band = 0; ++c.pq; }
+    c.band += p.G;
+    if (c.band >= p.NB) { c.band -= p.NB; ++c.pq; }
   }
 }
 __device__ __forceinline__ void cursor_prev(Cursor& c, const StreamPlan& p) {
@@ -108,7 +172,8 @@ __device__ __forceinline__ void cursor_prev(Cursor& c, const StreamPlan& p) {
   if (c.j0 < 0) {
     c.j0 = p.L - TILE;
     --c.q;
-    if (--c.band < 0) { c.band = p.NB - 1; --c.pq; }
+    c.band -= p.G;
+    if (c.band < 0) { c.band += p.NB; --c.pq; }
   }
 }
 
@@ -173,18 +238,19 @@ __device__ __forceinline__ void patch_row_tile(T* ring_row, const Cursor& c, con
   for (int h = max(0, p.M - c.j0); h < TILE; ++h) dst[h] = padv;
 }
 
-// Value of "row -1" that lane 0 of sub-band 0 sees at stream column sc:
-// the previous band's bottom row (delay line), +Big above a pair's first
-// band, and 0 at the last column of a pass that precedes a first band (it is
-// the diagonal predecessor of cell (0,0), R(-1,-1) = 0).  For P: 0 / delay line.
+// Value of "row -1" that lane 0 of sub-band 0 sees at local stream column
+// sc: the previous band's bottom row (the delay line `dl` of the warp that
+// computed it), +Big above a pair's first band, and 0 at the last column of a
+// pass that precedes a first band in this warp's stream (it is the diagonal
+// predecessor of cell (0,0), R(-1,-1) = 0).  For P: 0 / delay line.
 template <typename T>
 __device__ __forceinline__ T row_above(const T* dl, int sc, const StreamPlan& p,
                                        const WarpInfo& wi, T first_value) {
   const int q = floor_div(sc, p.L);
   const int j = sc - q * p.L;
-  const bool first = q < 0 || q >= wi.Q || pos_mod(q, p.NB) == 0;
+  const bool first = q < 0 || q >= wi.Q || first_band(q, p, wi);
   T v = first ? first_value : dl[j];
-  if (j == p.L - 1 && pos_mod(q + 1, p.NB) == 0) v = T(0);
+  if (j == p.L - 1 && first_band(q + 1, p, wi)) v = T(0);
   return v;
 }
 
@@ -217,12 +283,14 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
   constexpr int S = RingStride<T>::value;
   constexpr int RW = KS * 32 * S;  // ring elements per operand per warp
   const StreamPlan& p = a.p;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  uint64_t* gbar = group_barrier_init(p, smem_raw);
   WarpInfo wi;
   if (!warp_setup(p, KS, wi)) return;
   const int lane = wi.lane;
   const T big = Big<T>::value;
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  T* ringC = reinterpret_cast<T*>(smem_raw) + (size_t)wi.wib * warp_smem_elems(KS, S, HAS_P);
+  T* ringC = reinterpret_cast<T*>(smem_raw + StreamPlan::kSmemHeader) +
+             (size_t)wi.wib * warp_smem_elems(KS, S, HAS_P);
   T* ringQ = ringC + RW;
   // bottom-row values of the current 32-step window: R at [0, 32), P at [32, 64)
   T* coll = ringC + RW * (HAS_P ? 2 : 1);
@@ -243,7 +311,7 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
   long long loff[KS];
 #pragma unroll
   for (int k = 0; k < KS; ++k) {
-    ld[k] = cursor_at(-4 * k - (lane >> 3), p);
+    ld[k] = cursor_at(-4 * k - (lane >> 3) - wi.off / TILE, p, wi);
     pt[k] = ld[k];
     lmode[k] = row_mode<KS>(ld[k], k, p, wi, loff[k]);
   }
@@ -267,23 +335,29 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
     left[k] = up[k] = dg[k] = big;
     Pl[k] = Pu[k] = Pd[k] = T(0);
     if (HAS_BAND) {
-      const int sc = -32 * k - lane;
+      const int sc = -32 * k - lane - wi.off;
       const int q = floor_div(sc, p.L);
       jk[k] = sc - q * p.L;
-      rowk[k] = pos_mod(q, p.NB) * rows + 32 * k + lane;
+      rowk[k] = band_of(q, p, wi) * rows + 32 * k + lane;
     }
   }
   if (lane == 0) dg[0] = T(0);
 
+  // own delay line (written) and that of the warp of the band above (read)
   T* dlR = a.dlR + (long long)wi.w * p.L;
   T* dlP = HAS_P ? a.dlP + (long long)wi.w * p.L : nullptr;
-  fb[lane] = row_above(dlR, lane, p, wi, big);
-  fb[32 + lane] = row_above(dlR, 32 + lane, p, wi, big);
+  const T* dlRa = a.dlR + (long long)wi.wprev * p.L;
+  const T* dlPa = HAS_P ? a.dlP + (long long)wi.wprev * p.L : nullptr;
+  fb[lane] = row_above(dlRa, lane - wi.off, p, wi, big);
+  fb[32 + lane] = row_above(dlRa, 32 + lane - wi.off, p, wi, big);
   if (HAS_P) {
-    fbp[lane] = row_above(dlP, lane, p, wi, T(0));
-    fbp[32 + lane] = row_above(dlP, 32 + lane, p, wi, T(0));
+    fbp[lane] = row_above(dlPa, lane - wi.off, p, wi, T(0));
+    fbp[32 + lane] = row_above(dlPa, 32 + lane - wi.off, p, wi, T(0));
   }
   __syncwarp();
+  unsigned gphase = 0;
+  bool gdead = false;
+  const int ql = wi.Q * p.L;  // local columns of the warp's passes
 
   const long long woff = p.saved_offset(wi.w);
   const T kap = a.kappa;
@@ -348,7 +422,7 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
           Pn[k] = ok ? Pn[k] : T(0);
           const int jn = jk[k] + 1;
           const bool wrap = jn == p.L;
-          int rn = rowk[k] + rows;
+          int rn = rowk[k] + p.G * rows;
           rn = rn >= p.NB * rows ? rn - p.NB * rows : rn;
           jk[k] = wrap ? 0 : jn;
           rowk[k] = wrap ? rn : rowk[k];
@@ -385,29 +459,34 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
       __syncwarp();
       const T wbR = coll[lane];
       const T wbP = HAS_P ? coll[32 + lane] : T(0);
-      const int scx = t0 - 23 - 32 * KS + lane;
-      if (scx >= 0) {
+      const int scx = t0 - 23 - 32 * KS + lane - wi.off;
+      if (scx >= 0 && scx < ql) {
         const int j = scx - (scx / p.L) * p.L;
         dlR[j] = wbR;
         if (HAS_P) dlP[j] = wbP;
       }
-      __syncwarp();
+      if (p.G > 1) group_step(gbar, gphase, gdead);
+      else __syncwarp();
       // the window that just ended makes room for the one after next (the
-      // delay line was written a pass ago, so these loads hit L2)
+      // delay line was written D >= 32 KS + 128 steps earlier, so these loads
+      // hit L2)
       const int cn = t0 + TILE + 32 + lane;
-      fb[cn & 63] = row_above(dlR, cn, p, wi, big);
-      if (HAS_P) fbp[cn & 63] = row_above(dlP, cn, p, wi, T(0));
+      fb[cn & 63] = row_above(dlRa, cn - wi.off, p, wi, big);
+      if (HAS_P) fbp[cn & 63] = row_above(dlPa, cn - wi.off, p, wi, T(0));
       __syncwarp();
     }
   }
   cp_async_wait<0>();
 
-  // R[N-1, M-1] of each pair, read back from this lane's own saved stream
+  // R[N-1, M-1] of each pair, read back from the saved stream of the lane
+  // (and warp of the group) that computed it
   const int kstar = ((p.N - 1) % rows) / 32, lstar = (p.N - 1) % 32;
-  if (lane == lstar) {
+  const int bstar = (p.N - 1) / rows;
+  if (lane == lstar && bstar % p.G == wi.g) {
+    const int nbg = p.NB / p.G;
     for (int i = 0; i < wi.npairs; ++i) {
-      const long long ct = (long long)(i * p.NB + (p.N - 1) / rows) * p.L + (p.M - 1) +
-                           32 * kstar + lstar;
+      const long long ct = (long long)(i * nbg + bstar / p.G) * p.L + (p.M - 1) + 32 * kstar +
+                           lstar + wi.off;
       const T v = a.sR[woff + (ct * KS + kstar) * 32 + lane];
       a.out_r[wi.p0 + i] = v >= big * T(0.5) ? T(INFINITY) : v * a.inv_kappa;
       if (HAS_P) a.out_p[wi.p0 + i] = a.sP[woff + (ct * KS + kstar) * 32 + lane];
@@ -425,17 +504,19 @@ __device__ __forceinline__ void load_saved_row(const T* __restrict__ s_lane, int
   for (int k = 0; k < KS; ++k) out[k] = s_lane[((long long)r * KS + k) * 32];
 }
 
-// Row -1 value lane 0 of sub-band 0 used at stream column sc in the forward
-// sweep, re-read from the saved stream (bottom row of the previous band).
+// Row -1 value lane 0 of sub-band 0 used at step sc in the forward sweep,
+// re-read from the saved stream `s_above` of the warp of the band above (its
+// bottom row, which that warp computed D - 32 KS + 1 steps earlier).
 template <typename T, int KS>
-__device__ __forceinline__ T row_above_saved(const T* s_warp, int sc, const StreamPlan& p,
+__device__ __forceinline__ T row_above_saved(const T* s_above, int sc, const StreamPlan& p,
                                              const WarpInfo& wi, T first_value) {
-  const int q = floor_div(sc, p.L);
-  const int j = sc - q * p.L;
-  const bool first = q < 0 || q >= wi.Q || pos_mod(q, p.NB) == 0;
+  const int sl = sc - wi.off;
+  const int q = floor_div(sl, p.L);
+  const int j = sl - q * p.L;
+  const bool first = q < 0 || q >= wi.Q || first_band(q, p, wi);
   T v = first_value;
-  if (!first) v = s_warp[((long long)(sc - p.L + 32 * KS - 1) * KS + (KS - 1)) * 32 + 31];
-  if (j == p.L - 1 && pos_mod(q + 1, p.NB) == 0) v = T(0);
+  if (!first) v = s_above[((long long)(sc - p.D + 32 * KS - 1) * KS + (KS - 1)) * 32 + 31];
+  if (j == p.L - 1 && first_band(q + 1, p, wi)) v = T(0);
   return v;
 }
 
@@ -446,14 +527,17 @@ __device__ __forceinline__ T row_above_saved(const T* s_warp, int sc, const Stre
 // column back, into the previous pass's last padding column; it must stop there.)
 // SEEDB (N a multiple of the band height): the bottom row of a pair's last
 // band is row N-1, so the pair's seed dL/dR enters here, at column M-1.
+// sc is a step; `dl` is the delay line of the warp of the band below.
 template <typename T, bool SEEDB>
 __device__ __forceinline__ T push_from_below(const T* dl, int sc, const StreamPlan& p,
                                              const WarpInfo& wi, const T* grad) {
-  if (sc < 0) return T(0);
-  const int q = sc / p.L;
-  const int j = sc - q * p.L;
+  const int sl = sc - wi.off;
+  if (sl < 0) return T(0);
+  const int q = sl / p.L;
+  const int j = sl - q * p.L;
   if (j >= p.M || q >= wi.Q) return T(0);
-  if ((q + 1) % p.NB == 0) return (SEEDB && j == p.M - 1) ? grad[wi.p0 + q / p.NB] : T(0);
+  if (last_band(q, p, wi))
+    return (SEEDB && j == p.M - 1) ? grad[wi.p0 + q / (p.NB / p.G)] : T(0);
   return dl[j];
 }
 
@@ -559,12 +643,14 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
   constexpr int S = RingStride<T>::value;
   constexpr int RW = KS * 32 * S;
   const StreamPlan& p = a.p;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  uint64_t* gbar = group_barrier_init(p, smem_raw);
   WarpInfo wi;
   if (!warp_setup(p, KS, wi)) return;
   const int lane = wi.lane;
   const T big = Big<T>::value;
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  T* base = reinterpret_cast<T*>(smem_raw) + (size_t)wi.wib * warp_smem_elems(KS, S, HAS_P);
+  T* base = reinterpret_cast<T*>(smem_raw + StreamPlan::kSmemHeader) +
+            (size_t)wi.wib * warp_smem_elems(KS, S, HAS_P);
   T* outC = base;
   T* outQ = base + RW;
   // top-row sends of the current 32-step window: R at [0, 32), P at [32, 64)
@@ -582,6 +668,9 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
   const long long woff = p.saved_offset(wi.w);
   const T* sRw = a.sR + woff;
   const T* sPw = HAS_P ? a.sP + woff : nullptr;
+  // saved stream of the warp of the band above (row -1 values)
+  const T* sRa = a.sR + p.saved_offset(wi.wprev);
+  const T* sPa = HAS_P ? a.sP + p.saved_offset(wi.wprev) : nullptr;
   const int Tend = (wi.Tw + TILE - 1) / TILE * TILE;
   const int btop = Tend / TILE - 1;
   const T* sRl = sRw + lane;
@@ -599,8 +688,12 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
     if (HAS_P) load_saved_row<T, KS>(sPl, TILE * btop - 2 + s, FP[s]);
   }
 
+  // own delay line (top-row sends, written) and that of the warp of the band
+  // below (read)
   T* dlR = a.dlR + (long long)wi.w * p.L;
   T* dlP = HAS_P ? a.dlP + (long long)wi.w * p.L : nullptr;
+  const T* dlRb = a.dlR + (long long)wi.wnext * p.L;
+  const T* dlPb = HAS_P ? a.dlP + (long long)wi.wnext * p.L : nullptr;
 
   T accL[KS], accB[KS], dgp[KS], Qacc[KS], QaccB[KS], dgq[KS];
   T cur[KS], Xc[KS], Pcur[KS], PXc[KS];
@@ -617,8 +710,8 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int c = 32 * (bw - h) + lane;
-      sb[c & 63] = row_above_saved<T, KS>(sRw, c, p, wi, big);
-      if (HAS_P) sbp[c & 63] = row_above_saved<T, KS>(sPw, c, p, wi, T(0));
+      sb[c & 63] = row_above_saved<T, KS>(sRa, c, p, wi, big);
+      if (HAS_P) sbp[c & 63] = row_above_saved<T, KS>(sPa, c, p, wi, T(0));
     }
   }
   // Adjoint from the band below, by the bottom row's column t - 32 KS at
@@ -627,14 +720,14 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     const int c = 32 * (dw - h) + lane;
-    sd[c & 63] = push_from_below<T, SEEDB>(dlR, c, p, wi, a.grad_r);
-    if (HAS_P) sdp[c & 63] = push_from_below<T, SEEDB>(dlP, c, p, wi, a.grad_p);
+    sd[c & 63] = push_from_below<T, SEEDB>(dlRb, c, p, wi, a.grad_r);
+    if (HAS_P) sdp[c & 63] = push_from_below<T, SEEDB>(dlPb, c, p, wi, a.grad_p);
   }
   __syncwarp();
 
   {  // cur = saved row t_first - 1, Xc = X(t_first)
-    const T b0 = row_above_saved<T, KS>(sRw, t_first, p, wi, big);
-    const T b0p = HAS_P ? row_above_saved<T, KS>(sPw, t_first, p, wi, T(0)) : T(0);
+    const T b0 = row_above_saved<T, KS>(sRa, t_first, p, wi, big);
+    const T b0p = HAS_P ? row_above_saved<T, KS>(sPa, t_first, p, wi, T(0)) : T(0);
     load_saved_row<T, KS>(sRl, t_first - 1, cur);
 #pragma unroll
     for (int k = 0; k < KS; ++k) Pcur[k] = T(0);
@@ -650,16 +743,22 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
 
   const int rows = 32 * KS;
   const int kstar = ((p.N - 1) % rows) / 32, lstar = (p.N - 1) % 32;
-  const int NBL = p.NB * p.L;
-  int cap_i = wi.npairs - 1;
-  int cap_t = cap_i * NBL + ((p.N - 1) / rows) * p.L + (p.M - 1) + 32 * kstar + lstar;
+  const int bstar = (p.N - 1) / rows;
+  const int NBL = (p.NB / p.G) * p.L;  // local steps per pair
+  // the end cell of each pair lies in band bstar, in the stream of warp
+  // bstar mod G of the group; the other warps have no seed
+  const bool has_end = bstar % p.G == wi.g;
+  int cap_i = has_end ? wi.npairs - 1 : -1;
+  int cap_t = has_end ? cap_i * NBL + (bstar / p.G) * p.L + (p.M - 1) + 32 * kstar + lstar +
+                            wi.off
+                      : -1;
   // adjoint seeds dL/dR (dL/dP) of the current pair's end cell, held by the
   // lane and sub-band that own it
   const bool seed_lane = lane == lstar;
   T sdR[KS], sdP[KS];
   {
-    const T sr = a.grad_r[wi.p0 + cap_i];
-    const T sp = HAS_P ? a.grad_p[wi.p0 + cap_i] : T(0);
+    const T sr = cap_i >= 0 ? a.grad_r[wi.p0 + cap_i] : T(0);
+    const T sp = HAS_P && cap_i >= 0 ? a.grad_p[wi.p0 + cap_i] : T(0);
 #pragma unroll
     for (int k = 0; k < KS; ++k) {
       sdR[k] = (seed_lane && k == kstar) ? sr : T(0);
@@ -678,7 +777,7 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
   const int mwl = ((p.M + 31) >> 5) - 1;  // last word of a mask row
 #pragma unroll
   for (int k = 0; k < KS; ++k) {
-    fl[k] = cursor_at(btop - 4 * k - (lane >> 3), p);
+    fl[k] = cursor_at(btop - 4 * k - (lane >> 3) - wi.off / TILE, p, wi);
     fmode[k] = row_mode<KS>(fl[k], k, p, wi, foff[k]);
     mrow[k] = masked ? mask_row<KS>(a.mask, a.mask_np, fl[k], k, p, wi) : nullptr;
     mwd[k] = masked ? mrow[k][min(fl[k].j0 >> 5, mwl) * a.mask_np] : 0u;
@@ -788,6 +887,9 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
     }
   };
 
+  unsigned gphase = 0;
+  bool gdead = false;
+  const int ql = wi.Q * p.L;  // local columns of the warp's passes
   bool pend_b = false, pend_d = false;  // refills waiting for their shared-memory store
   int pbc = 0, pdc = 0;
   T pbv = T(0), pbpv = T(0), pdv = T(0), pdpv = T(0);
@@ -846,14 +948,18 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
       __syncwarp();
       const T wdR = coll[lane];
       const T wdP = HAS_P ? coll[32 + lane] : T(0);
-      const int j = (t0 + lane) - ((t0 + lane) / p.L) * p.L;
-      dlR[j] = wdR;
-      if (HAS_P) dlP[j] = wdP;
-      __syncwarp();
+      const int sl = t0 + lane - wi.off;
+      if (sl >= 0 && sl < ql) {
+        const int j = sl - (sl / p.L) * p.L;
+        dlR[j] = wdR;
+        if (HAS_P) dlP[j] = wdP;
+      }
+      if (p.G > 1) group_step(gbar, gphase, gdead);
+      else __syncwarp();
       // row -1 values two windows down replace the window just finished
       pbc = t0 - 64 + lane;
-      pbv = row_above_saved<T, KS>(sRw, pbc, p, wi, big);
-      if (HAS_P) pbpv = row_above_saved<T, KS>(sPw, pbc, p, wi, T(0));
+      pbv = row_above_saved<T, KS>(sRa, pbc, p, wi, big);
+      if (HAS_P) pbpv = row_above_saved<T, KS>(sPa, pbc, p, wi, T(0));
       pend_b = true;
     }
     // the next block (t0 - 8) may open a new window of bottom-row columns
@@ -861,8 +967,8 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
     if (dwn != dw) {
       dw = dwn;
       pdc = 32 * (dw - 1) + lane;
-      pdv = push_from_below<T, SEEDB>(dlR, pdc, p, wi, a.grad_r);
-      if (HAS_P) pdpv = push_from_below<T, SEEDB>(dlP, pdc, p, wi, a.grad_p);
+      pdv = push_from_below<T, SEEDB>(dlRb, pdc, p, wi, a.grad_r);
+      if (HAS_P) pdpv = push_from_below<T, SEEDB>(dlPb, pdc, p, wi, a.grad_p);
       pend_d = true;
     }
   };
@@ -993,82 +1099,121 @@ StreamPlan make_stream_plan(int B, int N, int M, int eb, bool has_p, int sms) {
   // penalty, whose second stream doubles the registers and shared memory of
   // a sub-band (cfg5 uDTW: 68.2 ms per step at one, 71.8 at two).
   //
-  // With at most 8 pairs per SM (a batch sharded over 4 or 8 GPUs) there are
-  // too few warps to hide the latency, and twice the sub-bands per warp win
-  // in fp32 when both sequences are long enough that the wider band's delay
-  // line (32*KS + 128 columns) and skew stay small against M.  N=M=1024 fwd+bwd:
-  // B=512 6.42 -> 5.48 ms, B=1184 8.56 -> 8.00 ms (soft-DTW, 2 -> 4 sub-bands);
-  // B=1480 9.91 -> 12.44 ms; uDTW B=512 13.0 -> 10.0 ms (1 -> 2 sub-bands),
-  // B=2048 26.5 -> 28.5 ms.  fp64 lost at every batch tried (B=512: 27.0 ->
-  // 38.8 ms), and so did N=M=200 (0.36 -> 0.44 ms).
-  int ks_def = (N <= 32 || has_p) ? 1 : 2;
-  if (eb == 4 && N >= 512 && M >= 512 && B <= 8 * sms) {
-    const int wide = 2 * ks_def;
-    const int rows_now = (N + 32 * ks_def - 1) / (32 * ks_def) * (32 * ks_def);
-    const int rows_wide = (N + 32 * wide - 1) / (32 * wide) * (32 * wide);
-    if (rows_wide == rows_now) ks_def = wide;
+  // Small batches (a batch sharded over 4 or 8 GPUs, or fewer than 12 pairs
+  // per SM on one) give too few warps to hide the latency.  Band groups put
+  // G warps on each pair: G is the smallest of 2 and 4 that brings B * G to
+  // 12 warps per SM (or the largest that applies), with G dividing NB and the
+  // lag L / G >= 32 KS + 128 met without widening L.  N=M=1024, fp32 soft-DTW
+  // fwd+bwd on the cost: B=32 4.56 ms (best sub-band count, one warp per
+  // pair) -> 1.71 ms (G = 4), B=512 5.77 -> 3.80 ms (G = 4), B=1024 7.58 ->
+  // 6.81 ms (G = 2), B=2048 13.1 ms at G = 1 vs 13.3 at G = 2; uDTW B=512
+  // 10.4 -> 7.7 ms, fp64 B=512 28.0 -> 17.4 (G = 2) / 18.7 ms (G = 4).  With
+  // groups, more sub-bands per warp lose: B=512 4 sub-bands and G = 2
+  // 4.23 ms, B=1024 4 and G = 2 8.13 ms.  TW_STREAM_KS and TW_STREAM_G force
+  // either choice.
+  const int ks_def = (N <= 32 || has_p) ? 1 : 2;
+  const int ks_env = env_int("TW_STREAM_KS", 0);
+  int ks = ks_env > 0 ? ks_env : ks_def;
+  ks = ks >= 4 ? 4 : (ks < 1 ? 1 : ks);
+  auto group_fits = [&](int g, int k) {
+    const int r = 32 * k;
+    const int nb = (N + r - 1) / r;
+    return nb % g == 0 && M + 1 >= g * (r + 128);
+  };
+  int G = env_int("TW_STREAM_G", 0);
+  if (G <= 0) {
+    G = 1;
+    const long long want = 12LL * sms;
+    if ((long long)B < want) {
+      for (int g : {2, 4}) {
+        if (!group_fits(g, ks)) continue;
+        G = g;
+        if ((long long)B * g >= want) break;
+      }
+    }
   }
-  int ks = env_int("TW_STREAM_KS", ks_def);
-  p.KS = ks >= 4 ? 4 : (ks < 1 ? 1 : ks);
+  p.KS = ks;
   const int rows = 32 * p.KS;
   p.NB = (N + rows - 1) / rows;
-  // The band-to-band delay line needs L >= 32*KS + 128 (see row_above); a
-  // single-band pair has no delay line and only needs the padding column.
+  // G warps share a group's pairs, one band in G each; G divides NB.
+  G = G >= 4 ? 4 : (G >= 2 ? 2 : 1);
+  while (G > 1 && p.NB % G != 0) G /= 2;
+  p.G = G;
+  // The band-to-band delay line needs a lag D >= 32*KS + 128 between the
+  // starts of consecutive passes (see row_above); D = L / G, so L >= G (32 KS
+  // + 128), a multiple of 8 G.  A single-band pair has no delay line and only
+  // needs the padding column.
   int L = M + 1;
-  if (p.NB > 1 && L < rows + 128) L = rows + 128;
-  p.L = (L + TILE - 1) / TILE * TILE;
+  if (p.NB > 1 && L < G * (rows + 128)) L = G * (rows + 128);
+  p.L = (L + TILE * G - 1) / (TILE * G) * (TILE * G);
+  p.D = p.L / G;
   const int S = eb == 4 ? RingStride<float>::value : RingStride<double>::value;
   const size_t per_w = (size_t)warp_smem_elems(p.KS, S, has_p) * eb;
+  const size_t hdr = StreamPlan::kSmemHeader;
   // Warps per SM: bounded by shared memory (the per-lane rings), by the
   // registers of the heavier of the two sweeps, and by 32.
   int wps = (int)((size_t)(216 * 1024) / per_w);
   wps = wps < 1 ? 1 : (wps > 32 ? 32 : wps);
   const int cap = env_int("TW_STREAM_WPS", 0);
   if (cap > 0 && cap < wps) wps = cap;
-  // Warps per CTA (4, 2 or 1) and pairs per warp.  Every warp carries whole
-  // pairs and every CTA is resident from the start, so a sweep lasts about
-  // (pairs per warp) x (warps on the fullest SM) warp-steps of issue.  Take
-  // the CTA size that minimises that product (ties: the larger CTA).  Small
-  // CTAs spread the warps evenly: 2048 warps in 4-warp CTAs put 16 warps on
-  // some SMs, in 2-warp CTAs at most 14.
-  int wpc = 1;
-  long long per_warp = 1, warps_needed = 1, best_cost = LLONG_MAX;
+  // Warps per CTA (4, 2 or 1; a multiple of G) and pairs per group.  Every
+  // group carries whole pairs and every CTA is resident from the start, so a
+  // sweep lasts about (pairs per group) x (warps on the fullest SM)
+  // warp-steps of issue.  Take the CTA size that minimises that product
+  // (ties: the larger CTA).  Small CTAs spread the warps evenly: 2048 warps
+  // in 4-warp CTAs put 16 warps on some SMs, in 2-warp CTAs at most 14.
+  int wpc = G;
+  long long per_group = 1, groups_needed = 1, best_cost = LLONG_MAX;
   for (int c : {4, 2, 1}) {
-    if (c > wps) continue;
+    if (c > wps || c % G != 0) continue;
     int n = wps / c;
-    const int resident = resident_blocks_any(eb, p.KS, has_p, c, per_w * c);
+    const int resident = resident_blocks_any(eb, p.KS, has_p, c, per_w * c + hdr);
     if (resident >= 0 && resident < n) n = resident;
     if (n < 1) continue;
-    const long long cap = (long long)sms * n * c;
-    const long long pw = B > 0 ? (B + cap - 1) / cap : 1;
-    const long long wn = B > 0 ? (B + pw - 1) / pw : 1;
-    const long long ctas_c = (wn + c - 1) / c;
+    const int gpc = c / G;
+    const long long capg = (long long)sms * n * gpc;
+    const long long pg = B > 0 ? (B + capg - 1) / capg : 1;
+    const long long gn = B > 0 ? (B + pg - 1) / pg : 1;
+    const long long ctas_c = (gn + gpc - 1) / gpc;
     const long long fullest = c * ((ctas_c + sms - 1) / sms);
-    const long long cost = pw * fullest;
+    const long long cost = pg * fullest;
     if (cost < best_cost) {
       best_cost = cost;
       wpc = c;
-      per_warp = pw;
-      warps_needed = wn;
+      per_group = pg;
+      groups_needed = gn;
     }
   }
-  if (best_cost == LLONG_MAX) {  // nothing fits the residency estimate: one warp per CTA
-    per_warp = B > 0 ? (B + sms - 1) / sms : 1;
-    warps_needed = B > 0 ? (B + per_warp - 1) / per_warp : 1;
+  if (best_cost == LLONG_MAX) {  // nothing fits the residency estimate: one group per CTA
+    wpc = G;
+    per_group = B > 0 ? (B + sms - 1) / sms : 1;
+    groups_needed = B > 0 ? (B + per_group - 1) / per_group : 1;
   }
-  int ctas = (int)((warps_needed + wpc - 1) / wpc);
+  const int gpc = wpc / G;
+  int ctas = (int)((groups_needed + gpc - 1) / gpc);
   if (ctas < 1) ctas = 1;
   p.wpc = wpc;
   p.warps = ctas * wpc;
-  p.base = B / p.warps;
-  p.rem = B % p.warps;
+  const int groups = p.warps / G;
+  p.base = B / groups;
+  p.rem = B % groups;
   const long long maxpairs = p.base + (p.rem ? 1 : 0);
-  const long long Tw = maxpairs * p.NB * p.L + 32 * p.KS - 1;
+  const long long Tw = maxpairs * (p.NB / G) * p.L + 32 * p.KS - 1 + (long long)(G - 1) * p.D;
   p.tmax = (Tw + TILE - 1) / TILE * TILE;
   p.tstride = SLICE_ALIGN(p.tmax + StreamPlan::kPreRows);
-  p.smem_fwd = per_w * p.wpc;
-  p.smem_bwd = per_w * p.wpc;
+  p.smem_fwd = per_w * p.wpc + hdr;
+  p.smem_bwd = per_w * p.wpc + hdr;
   return p;
+}
+
+int dp_take_device_error() {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_dp_error, sizeof(int)) != cudaSuccess) return kLaunch;
+  if (v != 0) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_dp_error, &zero, sizeof(int));
+  }
+  return v;
 }
 
 template <typename T>

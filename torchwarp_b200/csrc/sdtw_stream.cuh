@@ -14,6 +14,13 @@
 //   * Row i-1 -> row i hand-off is one rotating __shfl per sub-band (lane 31 of
 //     sub-band k-1 feeds lane 0 of sub-band k); band b -> band b+1 goes through
 //     a per-warp delay line of L values in global scratch.
+//   * Band groups (G > 1, for batches too small to fill the SMs): G warps of
+//     one CTA share a group's pairs, warp g taking bands g, g+G, g+2G, ...
+//     Pass q of the group starts D = L/G steps after pass q-1, so warp g runs
+//     its own stream shifted by g*D steps, reads band b-1's bottom row from
+//     the delay line of the warp that computed it, and the G warps stay in
+//     step through one bounded mbarrier wait per 32-step window.  G = 1 is
+//     the single-warp stream above.
 //
 // Saved state: R (and P for uDTW) of every cell, in stream order
 // [warp][t][k][lane] (one coalesced 128-byte row per sub-band and step), in
@@ -31,10 +38,12 @@ struct StreamPlan {
   int B = 0, N = 0, M = 0;
   int KS = 1;        // sub-bands per warp
   int NB = 1;        // bands per pair
-  int L = 0;         // stream columns per band pass (multiple of 8)
-  int warps = 0;     // warps launched
+  int L = 0;         // stream columns per band pass (multiple of 8 G)
+  int G = 1;         // warps per band group (divides NB and wpc)
+  int D = 0;         // L / G: steps between the starts of consecutive passes
+  int warps = 0;     // warps launched (a multiple of G)
   int wpc = 4;       // warps per CTA
-  int base = 0, rem = 0;   // warp w: base + (w < rem) pairs from w*base + min(w, rem)
+  int base = 0, rem = 0;   // group s: base + (s < rem) pairs from s*base + min(s, rem)
   long long tmax = 0;      // saved rows per warp (multiple of 8)
   size_t smem_fwd = 0, smem_bwd = 0;   // dynamic shared memory per CTA
 
@@ -49,6 +58,8 @@ struct StreamPlan {
     return ((long long)w * tstride + kPreRows) * KS * 32;
   }
   long long delay_elems() const { return (long long)warps * L; }
+  // dynamic shared memory in front of the warps' regions: the groups' mbarriers
+  static constexpr int kSmemHeader = 64;
 };
 
 // elem_bytes: 4 or 8.  has_p: uDTW penalty accumulator.  sms: SM count.
@@ -85,6 +96,10 @@ struct SdtwArgs {
   int vec = 0;      // 16-byte global accesses allowed for C/Q/dC/dQ
   StreamPlan p;
 };
+
+// Reads and clears the device-side error word of the stream kernels (a band
+// group's window wait that ran out: kTimeout).
+int dp_take_device_error();
 
 template <typename T>
 int sdtw_stream_forward(const SdtwArgs<T>& a, bool has_p, bool has_band, cudaStream_t st);
