@@ -57,6 +57,13 @@ __device__ __forceinline__ int pos_mod(int a, int b) {
   return r < 0 ? r + b : r;
 }
 
+// Group size and bands per warp stream: compile-time 1 and NB in the kernels
+// without band groups, so their code is the single-warp stream's.
+template <bool GRP>
+__device__ __forceinline__ int grp_G(const StreamPlan& p) { return GRP ? p.G : 1; }
+template <bool GRP>
+__device__ __forceinline__ int grp_NBg(const StreamPlan& p) { return GRP ? p.NBg : p.NB; }
+
 // g: warp within its band group; off = g * D, the shift of this warp's own
 // stream (local column = step - off); Q: local passes (npairs * NB / G); Tw:
 // steps every warp of the group runs (the group's stream length).
@@ -68,34 +75,38 @@ struct WarpInfo {
 // Pair ranges are handed out per band group in slot order s = (group in
 // CTA) * CTAs + CTA, so the groups that get one extra pair are spread over
 // all SMs.  Every warp of a group gets the same answer.
+template <bool GRP>
 __device__ __forceinline__ bool warp_setup(const StreamPlan& p, int KS, WarpInfo& wi) {
   wi.lane = threadIdx.x & 31;
   wi.wib = threadIdx.x >> 5;
   wi.w = blockIdx.x * (blockDim.x >> 5) + wi.wib;
   if (wi.w >= p.warps) return false;
-  const int gib = wi.wib / p.G;
-  wi.g = wi.wib - gib * p.G;
+  const int gib = wi.wib / grp_G<GRP>(p);
+  wi.g = wi.wib - gib * grp_G<GRP>(p);
   const int slot = gib * gridDim.x + blockIdx.x;
   wi.npairs = p.base + (slot < p.rem ? 1 : 0);
   if (wi.npairs == 0) return false;
   wi.p0 = slot * p.base + min(slot, p.rem);
-  wi.Q = wi.npairs * (p.NB / p.G);
-  wi.Tw = wi.Q * p.L + 32 * KS - 1 + (p.G - 1) * p.D;
+  wi.Q = wi.npairs * grp_NBg<GRP>(p);
+  wi.Tw = wi.Q * p.L + 32 * KS - 1 + (grp_G<GRP>(p) - 1) * p.D;
   wi.off = wi.g * p.D;
-  wi.wprev = wi.g > 0 ? wi.w - 1 : wi.w + p.G - 1;
-  wi.wnext = wi.g < p.G - 1 ? wi.w + 1 : wi.w - (p.G - 1);
+  wi.wprev = wi.g > 0 ? wi.w - 1 : wi.w + grp_G<GRP>(p) - 1;
+  wi.wnext = wi.g < grp_G<GRP>(p) - 1 ? wi.w + 1 : wi.w - (grp_G<GRP>(p) - 1);
   return true;
 }
 
 // Band of this warp's local pass q (any q, also outside [0, Q)).
+template <bool GRP>
 __device__ __forceinline__ int band_of(int q, const StreamPlan& p, const WarpInfo& wi) {
-  return wi.g + p.G * pos_mod(q, p.NB / p.G);
+  return wi.g + grp_G<GRP>(p) * pos_mod(q, grp_NBg<GRP>(p));
 }
+template <bool GRP>
 __device__ __forceinline__ bool first_band(int q, const StreamPlan& p, const WarpInfo& wi) {
-  return wi.g == 0 && pos_mod(q, p.NB / p.G) == 0;
+  return wi.g == 0 && pos_mod(q, grp_NBg<GRP>(p)) == 0;
 }
+template <bool GRP>
 __device__ __forceinline__ bool last_band(int q, const StreamPlan& p, const WarpInfo& wi) {
-  return wi.g == p.G - 1 && pos_mod(q + 1, p.NB / p.G) == 0;
+  return wi.g == grp_G<GRP>(p) - 1 && pos_mod(q + 1, grp_NBg<GRP>(p)) == 0;
 }
 
 // One step of a band group's lockstep: every lane arrives on the group's
@@ -118,17 +129,19 @@ __device__ __forceinline__ void group_step(uint64_t* bar, unsigned& phase, bool&
   phase ^= 1u;
 }
 
-// The groups' mbarriers (one per group of the CTA, 32 G arrivals), set up
-// before any warp leaves; a no-op without band groups.
+// The groups' mbarriers (one per group of the CTA, 32 G arrivals), at `area`
+// after the warps' regions, set up before any warp leaves; a no-op without
+// band groups.
+template <bool GRP>
 __device__ __forceinline__ uint64_t* group_barrier_init(const StreamPlan& p,
-                                                        unsigned char* smem_raw) {
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw);
-  if (p.G > 1) {
-    const int groups = (blockDim.x >> 5) / p.G;
-    if ((int)threadIdx.x < groups) tc::mbar_init(&bars[threadIdx.x], 32u * p.G);
+                                                        unsigned char* area) {
+  uint64_t* bars = reinterpret_cast<uint64_t*>(area);
+  if (grp_G<GRP>(p) > 1) {
+    const int groups = (blockDim.x >> 5) / grp_G<GRP>(p);
+    if ((int)threadIdx.x < groups) tc::mbar_init(&bars[threadIdx.x], 32u * grp_G<GRP>(p));
     __syncthreads();
   }
-  return bars + (threadIdx.x >> 5) / p.G;
+  return bars + (threadIdx.x >> 5) / grp_G<GRP>(p);
 }
 
 // Position of stream tile u (the 8 columns [8u, 8u+8)) in (pass, column)
@@ -146,33 +159,35 @@ struct Cursor {
 // g + G (q mod NB/G) of the pair q div (NB/G), so stepping a pass moves the
 // band by G.  The ring slot of a tile follows the step at which it is used,
 // so c.u counts in steps (shifted by off), not in local columns.
+template <bool GRP>
 __device__ __forceinline__ Cursor cursor_at(int u, const StreamPlan& p, const WarpInfo& wi) {
   Cursor c;
   c.u = u + wi.off / TILE;
   c.q = floor_div(u * TILE, p.L);
   c.j0 = u * TILE - c.q * p.L;
-  const int nbg = p.NB / p.G;
-  c.pq = floor_div(c.q, nbg);
-  c.band = wi.g + p.G * (c.q - c.pq * nbg);
+  c.pq = floor_div(c.q, grp_NBg<GRP>(p));
+  c.band = wi.g + grp_G<GRP>(p) * (c.q - c.pq * grp_NBg<GRP>(p));
   return c;
 }
+template <bool GRP>
 __device__ __forceinline__ void cursor_next(Cursor& c, const StreamPlan& p) {
   ++c.u;
   c.j0 += TILE;
   if (c.j0 >= p.L) {
     c.j0 = 0;
     ++c.q;
-    c.band += p.G;
+    c.band += grp_G<GRP>(p);
     if (c.band >= p.NB) { c.band -= p.NB; ++c.pq; }
   }
 }
+template <bool GRP>
 __device__ __forceinline__ void cursor_prev(Cursor& c, const StreamPlan& p) {
   --c.u;
   c.j0 -= TILE;
   if (c.j0 < 0) {
     c.j0 = p.L - TILE;
     --c.q;
-    c.band -= p.G;
+    c.band -= grp_G<GRP>(p);
     if (c.band < 0) { c.band += p.NB; --c.pq; }
   }
 }
@@ -243,14 +258,14 @@ __device__ __forceinline__ void patch_row_tile(T* ring_row, const Cursor& c, con
 // computed it), +Big above a pair's first band, and 0 at the last column of a
 // pass that precedes a first band in this warp's stream (it is the diagonal
 // predecessor of cell (0,0), R(-1,-1) = 0).  For P: 0 / delay line.
-template <typename T>
+template <bool GRP, typename T>
 __device__ __forceinline__ T row_above(const T* dl, int sc, const StreamPlan& p,
                                        const WarpInfo& wi, T first_value) {
   const int q = floor_div(sc, p.L);
   const int j = sc - q * p.L;
-  const bool first = q < 0 || q >= wi.Q || first_band(q, p, wi);
+  const bool first = q < 0 || q >= wi.Q || first_band<GRP>(q, p, wi);
   T v = first ? first_value : dl[j];
-  if (j == p.L - 1 && first_band(q + 1, p, wi)) v = T(0);
+  if (j == p.L - 1 && first_band<GRP>(q + 1, p, wi)) v = T(0);
   return v;
 }
 
@@ -278,19 +293,20 @@ __device__ __forceinline__ void cell_forward(T c, T kap, T qv, T left, T up, T d
   }
 }
 
-template <typename T, int KS, bool HAS_P, bool HAS_BAND>
+template <typename T, int KS, bool HAS_P, bool HAS_BAND, bool GRP>
 __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
   constexpr int S = RingStride<T>::value;
   constexpr int RW = KS * 32 * S;  // ring elements per operand per warp
   const StreamPlan& p = a.p;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  uint64_t* gbar = group_barrier_init(p, smem_raw);
+  constexpr int WE = warp_smem_elems(KS, S, HAS_P);
+  uint64_t* gbar =
+      group_barrier_init<GRP>(p, smem_raw + (blockDim.x >> 5) * WE * sizeof(T));
   WarpInfo wi;
-  if (!warp_setup(p, KS, wi)) return;
+  if (!warp_setup<GRP>(p, KS, wi)) return;
   const int lane = wi.lane;
   const T big = Big<T>::value;
-  T* ringC = reinterpret_cast<T*>(smem_raw + StreamPlan::kSmemHeader) +
-             (size_t)wi.wib * warp_smem_elems(KS, S, HAS_P);
+  T* ringC = reinterpret_cast<T*>(smem_raw) + (size_t)wi.wib * WE;
   T* ringQ = ringC + RW;
   // bottom-row values of the current 32-step window: R at [0, 32), P at [32, 64)
   T* coll = ringC + RW * (HAS_P ? 2 : 1);
@@ -311,7 +327,7 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
   long long loff[KS];
 #pragma unroll
   for (int k = 0; k < KS; ++k) {
-    ld[k] = cursor_at(-4 * k - (lane >> 3) - wi.off / TILE, p, wi);
+    ld[k] = cursor_at<GRP>(-4 * k - (lane >> 3) - wi.off / TILE, p, wi);
     pt[k] = ld[k];
     lmode[k] = row_mode<KS>(ld[k], k, p, wi, loff[k]);
   }
@@ -321,7 +337,7 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
     for (int k = 0; k < KS; ++k) {
       load_row_tile<T>(a.C, myC + k * 32 * S, ld[k], lmode[k], loff[k], p, a.vec);
       if (HAS_P) load_row_tile<T>(a.Q, myQ + k * 32 * S, ld[k], lmode[k], loff[k], p, a.vec);
-      cursor_next(ld[k], p);
+      cursor_next<GRP>(ld[k], p);
       if (ld[k].j0 == 0) lmode[k] = row_mode<KS>(ld[k], k, p, wi, loff[k]);
     }
     cp_async_commit();
@@ -338,7 +354,7 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
       const int sc = -32 * k - lane - wi.off;
       const int q = floor_div(sc, p.L);
       jk[k] = sc - q * p.L;
-      rowk[k] = band_of(q, p, wi) * rows + 32 * k + lane;
+      rowk[k] = band_of<GRP>(q, p, wi) * rows + 32 * k + lane;
     }
   }
   if (lane == 0) dg[0] = T(0);
@@ -348,11 +364,11 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
   T* dlP = HAS_P ? a.dlP + (long long)wi.w * p.L : nullptr;
   const T* dlRa = a.dlR + (long long)wi.wprev * p.L;
   const T* dlPa = HAS_P ? a.dlP + (long long)wi.wprev * p.L : nullptr;
-  fb[lane] = row_above(dlRa, lane - wi.off, p, wi, big);
-  fb[32 + lane] = row_above(dlRa, 32 + lane - wi.off, p, wi, big);
+  fb[lane] = row_above<GRP>(dlRa, lane - wi.off, p, wi, big);
+  fb[32 + lane] = row_above<GRP>(dlRa, 32 + lane - wi.off, p, wi, big);
   if (HAS_P) {
-    fbp[lane] = row_above(dlPa, lane - wi.off, p, wi, T(0));
-    fbp[32 + lane] = row_above(dlPa, 32 + lane - wi.off, p, wi, T(0));
+    fbp[lane] = row_above<GRP>(dlPa, lane - wi.off, p, wi, T(0));
+    fbp[32 + lane] = row_above<GRP>(dlPa, 32 + lane - wi.off, p, wi, T(0));
   }
   __syncwarp();
   unsigned gphase = 0;
@@ -378,13 +394,13 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
 #pragma unroll
     for (int k = 0; k < KS; ++k) {
       patch_row_tile(myC + k * 32 * S, pt[k], p, wi, a.pad_raw);
-      cursor_next(pt[k], p);
+      cursor_next<GRP>(pt[k], p);
     }
 #pragma unroll
     for (int k = 0; k < KS; ++k) {
       load_row_tile<T>(a.C, myC + k * 32 * S, ld[k], lmode[k], loff[k], p, a.vec);
       if (HAS_P) load_row_tile<T>(a.Q, myQ + k * 32 * S, ld[k], lmode[k], loff[k], p, a.vec);
-      cursor_next(ld[k], p);
+      cursor_next<GRP>(ld[k], p);
       if (ld[k].j0 == 0) lmode[k] = row_mode<KS>(ld[k], k, p, wi, loff[k]);  // a new pass
     }
     cp_async_commit();
@@ -422,7 +438,7 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
           Pn[k] = ok ? Pn[k] : T(0);
           const int jn = jk[k] + 1;
           const bool wrap = jn == p.L;
-          int rn = rowk[k] + p.G * rows;
+          int rn = rowk[k] + grp_G<GRP>(p) * rows;
           rn = rn >= p.NB * rows ? rn - p.NB * rows : rn;
           jk[k] = wrap ? 0 : jn;
           rowk[k] = wrap ? rn : rowk[k];
@@ -460,19 +476,19 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
       const T wbR = coll[lane];
       const T wbP = HAS_P ? coll[32 + lane] : T(0);
       const int scx = t0 - 23 - 32 * KS + lane - wi.off;
-      if (scx >= 0 && scx < ql) {
+      if (scx >= 0 && (!GRP || scx < ql)) {
         const int j = scx - (scx / p.L) * p.L;
         dlR[j] = wbR;
         if (HAS_P) dlP[j] = wbP;
       }
-      if (p.G > 1) group_step(gbar, gphase, gdead);
+      if constexpr (GRP) group_step(gbar, gphase, gdead);
       else __syncwarp();
       // the window that just ended makes room for the one after next (the
       // delay line was written D >= 32 KS + 128 steps earlier, so these loads
       // hit L2)
       const int cn = t0 + TILE + 32 + lane;
-      fb[cn & 63] = row_above(dlRa, cn - wi.off, p, wi, big);
-      if (HAS_P) fbp[cn & 63] = row_above(dlPa, cn - wi.off, p, wi, T(0));
+      fb[cn & 63] = row_above<GRP>(dlRa, cn - wi.off, p, wi, big);
+      if (HAS_P) fbp[cn & 63] = row_above<GRP>(dlPa, cn - wi.off, p, wi, T(0));
       __syncwarp();
     }
   }
@@ -482,11 +498,10 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
   // (and warp of the group) that computed it
   const int kstar = ((p.N - 1) % rows) / 32, lstar = (p.N - 1) % 32;
   const int bstar = (p.N - 1) / rows;
-  if (lane == lstar && bstar % p.G == wi.g) {
-    const int nbg = p.NB / p.G;
+  if (lane == lstar && bstar % grp_G<GRP>(p) == wi.g) {
     for (int i = 0; i < wi.npairs; ++i) {
-      const long long ct = (long long)(i * nbg + bstar / p.G) * p.L + (p.M - 1) + 32 * kstar +
-                           lstar + wi.off;
+      const long long ct = (long long)(i * grp_NBg<GRP>(p) + bstar / grp_G<GRP>(p)) * p.L +
+                           (p.M - 1) + 32 * kstar + lstar + wi.off;
       const T v = a.sR[woff + (ct * KS + kstar) * 32 + lane];
       a.out_r[wi.p0 + i] = v >= big * T(0.5) ? T(INFINITY) : v * a.inv_kappa;
       if (HAS_P) a.out_p[wi.p0 + i] = a.sP[woff + (ct * KS + kstar) * 32 + lane];
@@ -507,16 +522,25 @@ __device__ __forceinline__ void load_saved_row(const T* __restrict__ s_lane, int
 // Row -1 value lane 0 of sub-band 0 used at step sc in the forward sweep,
 // re-read from the saved stream `s_above` of the warp of the band above (its
 // bottom row, which that warp computed D - 32 KS + 1 steps earlier).
-template <typename T, int KS>
+template <typename T, int KS, bool GRP>
 __device__ __forceinline__ T row_above_saved(const T* s_above, int sc, const StreamPlan& p,
                                              const WarpInfo& wi, T first_value) {
+  if constexpr (!GRP) {  // one warp per pair: the band above is this warp's previous pass
+    const int q = floor_div(sc, p.L);
+    const int j = sc - q * p.L;
+    const bool first = q < 0 || q >= wi.Q || pos_mod(q, p.NB) == 0;
+    T v = first_value;
+    if (!first) v = s_above[((long long)(sc - p.L + 32 * KS - 1) * KS + (KS - 1)) * 32 + 31];
+    if (j == p.L - 1 && pos_mod(q + 1, p.NB) == 0) v = T(0);
+    return v;
+  }
   const int sl = sc - wi.off;
   const int q = floor_div(sl, p.L);
   const int j = sl - q * p.L;
-  const bool first = q < 0 || q >= wi.Q || first_band(q, p, wi);
+  const bool first = q < 0 || q >= wi.Q || first_band<GRP>(q, p, wi);
   T v = first_value;
   if (!first) v = s_above[((long long)(sc - p.D + 32 * KS - 1) * KS + (KS - 1)) * 32 + 31];
-  if (j == p.L - 1 && first_band(q + 1, p, wi)) v = T(0);
+  if (j == p.L - 1 && first_band<GRP>(q + 1, p, wi)) v = T(0);
   return v;
 }
 
@@ -528,16 +552,24 @@ __device__ __forceinline__ T row_above_saved(const T* s_above, int sc, const Str
 // SEEDB (N a multiple of the band height): the bottom row of a pair's last
 // band is row N-1, so the pair's seed dL/dR enters here, at column M-1.
 // sc is a step; `dl` is the delay line of the warp of the band below.
-template <typename T, bool SEEDB>
+template <typename T, bool SEEDB, bool GRP>
 __device__ __forceinline__ T push_from_below(const T* dl, int sc, const StreamPlan& p,
                                              const WarpInfo& wi, const T* grad) {
+  if constexpr (!GRP) {  // one warp per pair: the band below is this warp's next pass
+    if (sc < 0) return T(0);
+    const int q = sc / p.L;
+    const int j = sc - q * p.L;
+    if (j >= p.M || q >= wi.Q) return T(0);
+    if ((q + 1) % p.NB == 0) return (SEEDB && j == p.M - 1) ? grad[wi.p0 + q / p.NB] : T(0);
+    return dl[j];
+  }
   const int sl = sc - wi.off;
   if (sl < 0) return T(0);
   const int q = sl / p.L;
   const int j = sl - q * p.L;
   if (j >= p.M || q >= wi.Q) return T(0);
-  if (last_band(q, p, wi))
-    return (SEEDB && j == p.M - 1) ? grad[wi.p0 + q / (p.NB / p.G)] : T(0);
+  if (last_band<GRP>(q, p, wi))
+    return (SEEDB && j == p.M - 1) ? grad[wi.p0 + q / grp_NBg<GRP>(p)] : T(0);
   return dl[j];
 }
 
@@ -638,19 +670,20 @@ __device__ __forceinline__ void flush_row_tile(T* __restrict__ dst_base, const T
   }
 }
 
-template <typename T, int KS, bool HAS_P, bool SEEDB>
+template <typename T, int KS, bool HAS_P, bool SEEDB, bool GRP>
 __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
   constexpr int S = RingStride<T>::value;
   constexpr int RW = KS * 32 * S;
   const StreamPlan& p = a.p;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  uint64_t* gbar = group_barrier_init(p, smem_raw);
+  constexpr int WE = warp_smem_elems(KS, S, HAS_P);
+  uint64_t* gbar =
+      group_barrier_init<GRP>(p, smem_raw + (blockDim.x >> 5) * WE * sizeof(T));
   WarpInfo wi;
-  if (!warp_setup(p, KS, wi)) return;
+  if (!warp_setup<GRP>(p, KS, wi)) return;
   const int lane = wi.lane;
   const T big = Big<T>::value;
-  T* base = reinterpret_cast<T*>(smem_raw + StreamPlan::kSmemHeader) +
-            (size_t)wi.wib * warp_smem_elems(KS, S, HAS_P);
+  T* base = reinterpret_cast<T*>(smem_raw) + (size_t)wi.wib * WE;
   T* outC = base;
   T* outQ = base + RW;
   // top-row sends of the current 32-step window: R at [0, 32), P at [32, 64)
@@ -710,8 +743,8 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int c = 32 * (bw - h) + lane;
-      sb[c & 63] = row_above_saved<T, KS>(sRa, c, p, wi, big);
-      if (HAS_P) sbp[c & 63] = row_above_saved<T, KS>(sPa, c, p, wi, T(0));
+      sb[c & 63] = row_above_saved<T, KS, GRP>(sRa, c, p, wi, big);
+      if (HAS_P) sbp[c & 63] = row_above_saved<T, KS, GRP>(sPa, c, p, wi, T(0));
     }
   }
   // Adjoint from the band below, by the bottom row's column t - 32 KS at
@@ -720,14 +753,14 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     const int c = 32 * (dw - h) + lane;
-    sd[c & 63] = push_from_below<T, SEEDB>(dlRb, c, p, wi, a.grad_r);
-    if (HAS_P) sdp[c & 63] = push_from_below<T, SEEDB>(dlPb, c, p, wi, a.grad_p);
+    sd[c & 63] = push_from_below<T, SEEDB, GRP>(dlRb, c, p, wi, a.grad_r);
+    if (HAS_P) sdp[c & 63] = push_from_below<T, SEEDB, GRP>(dlPb, c, p, wi, a.grad_p);
   }
   __syncwarp();
 
   {  // cur = saved row t_first - 1, Xc = X(t_first)
-    const T b0 = row_above_saved<T, KS>(sRa, t_first, p, wi, big);
-    const T b0p = HAS_P ? row_above_saved<T, KS>(sPa, t_first, p, wi, T(0)) : T(0);
+    const T b0 = row_above_saved<T, KS, GRP>(sRa, t_first, p, wi, big);
+    const T b0p = HAS_P ? row_above_saved<T, KS, GRP>(sPa, t_first, p, wi, T(0)) : T(0);
     load_saved_row<T, KS>(sRl, t_first - 1, cur);
 #pragma unroll
     for (int k = 0; k < KS; ++k) Pcur[k] = T(0);
@@ -744,13 +777,13 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
   const int rows = 32 * KS;
   const int kstar = ((p.N - 1) % rows) / 32, lstar = (p.N - 1) % 32;
   const int bstar = (p.N - 1) / rows;
-  const int NBL = (p.NB / p.G) * p.L;  // local steps per pair
+  const int NBL = grp_NBg<GRP>(p) * p.L;  // local steps per pair
   // the end cell of each pair lies in band bstar, in the stream of warp
   // bstar mod G of the group; the other warps have no seed
-  const bool has_end = bstar % p.G == wi.g;
+  const bool has_end = bstar % grp_G<GRP>(p) == wi.g;
   int cap_i = has_end ? wi.npairs - 1 : -1;
-  int cap_t = has_end ? cap_i * NBL + (bstar / p.G) * p.L + (p.M - 1) + 32 * kstar + lstar +
-                            wi.off
+  int cap_t = has_end ? cap_i * NBL + (bstar / grp_G<GRP>(p)) * p.L + (p.M - 1) + 32 * kstar +
+                            lstar + wi.off
                       : -1;
   // adjoint seeds dL/dR (dL/dP) of the current pair's end cell, held by the
   // lane and sub-band that own it
@@ -777,7 +810,7 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
   const int mwl = ((p.M + 31) >> 5) - 1;  // last word of a mask row
 #pragma unroll
   for (int k = 0; k < KS; ++k) {
-    fl[k] = cursor_at(btop - 4 * k - (lane >> 3) - wi.off / TILE, p, wi);
+    fl[k] = cursor_at<GRP>(btop - 4 * k - (lane >> 3) - wi.off / TILE, p, wi);
     fmode[k] = row_mode<KS>(fl[k], k, p, wi, foff[k]);
     mrow[k] = masked ? mask_row<KS>(a.mask, a.mask_np, fl[k], k, p, wi) : nullptr;
     mwd[k] = masked ? mrow[k][min(fl[k].j0 >> 5, mwl) * a.mask_np] : 0u;
@@ -905,7 +938,7 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
       if (HAS_P)
         flush_row_tile<T>(a.dQ, myQ + k * 32 * S, fl[k], fmode[k], foff[k], p, a.vec, false, 0u);
       const int oq = fl[k].q;
-      cursor_prev(fl[k], p);
+      cursor_prev<GRP>(fl[k], p);
       if (fl[k].q != oq) {  // a new pass
         fmode[k] = row_mode<KS>(fl[k], k, p, wi, foff[k]);
         if (masked) mrow[k] = mask_row<KS>(a.mask, a.mask_np, fl[k], k, p, wi);
@@ -948,18 +981,24 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
       __syncwarp();
       const T wdR = coll[lane];
       const T wdP = HAS_P ? coll[32 + lane] : T(0);
-      const int sl = t0 + lane - wi.off;
-      if (sl >= 0 && sl < ql) {
-        const int j = sl - (sl / p.L) * p.L;
+      if constexpr (!GRP) {
+        const int j = (t0 + lane) - ((t0 + lane) / p.L) * p.L;
         dlR[j] = wdR;
         if (HAS_P) dlP[j] = wdP;
+      } else {
+        const int sl = t0 + lane - wi.off;
+        if (sl >= 0 && sl < ql) {
+          const int j = sl - (sl / p.L) * p.L;
+          dlR[j] = wdR;
+          if (HAS_P) dlP[j] = wdP;
+        }
       }
-      if (p.G > 1) group_step(gbar, gphase, gdead);
+      if constexpr (GRP) group_step(gbar, gphase, gdead);
       else __syncwarp();
       // row -1 values two windows down replace the window just finished
       pbc = t0 - 64 + lane;
-      pbv = row_above_saved<T, KS>(sRa, pbc, p, wi, big);
-      if (HAS_P) pbpv = row_above_saved<T, KS>(sPa, pbc, p, wi, T(0));
+      pbv = row_above_saved<T, KS, GRP>(sRa, pbc, p, wi, big);
+      if (HAS_P) pbpv = row_above_saved<T, KS, GRP>(sPa, pbc, p, wi, T(0));
       pend_b = true;
     }
     // the next block (t0 - 8) may open a new window of bottom-row columns
@@ -967,8 +1006,8 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
     if (dwn != dw) {
       dw = dwn;
       pdc = 32 * (dw - 1) + lane;
-      pdv = push_from_below<T, SEEDB>(dlRb, pdc, p, wi, a.grad_r);
-      if (HAS_P) pdpv = push_from_below<T, SEEDB>(dlPb, pdc, p, wi, a.grad_p);
+      pdv = push_from_below<T, SEEDB, GRP>(dlRb, pdc, p, wi, a.grad_r);
+      if (HAS_P) pdpv = push_from_below<T, SEEDB, GRP>(dlPb, pdc, p, wi, a.grad_p);
       pend_d = true;
     }
   };
@@ -985,7 +1024,8 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
 
 template <typename T, int KS, bool HAS_P, bool HAS_BAND>
 int launch_fwd(const SdtwArgs<T>& a, cudaStream_t st) {
-  auto kern = sdtw_fwd_kernel<T, KS, HAS_P, HAS_BAND>;
+  auto kern = a.p.G > 1 ? sdtw_fwd_kernel<T, KS, HAS_P, HAS_BAND, true>
+                        : sdtw_fwd_kernel<T, KS, HAS_P, HAS_BAND, false>;
   const size_t smem = a.p.smem_fwd;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return set_error(kLaunch, "sdtw forward: cannot reserve %zu bytes of shared memory", smem);
@@ -1000,8 +1040,11 @@ template <typename T, int KS, bool HAS_P>
 int launch_bwd(const SdtwArgs<T>& a, cudaStream_t st) {
   // a pair's end cell is the last lane of the last sub-band when N is a
   // multiple of the band height: its seed then needs no per-step test
-  auto kern = (a.p.N % (32 * KS)) == 0 ? sdtw_bwd_kernel<T, KS, HAS_P, true>
-                                       : sdtw_bwd_kernel<T, KS, HAS_P, false>;
+  const bool seedb = (a.p.N % (32 * KS)) == 0;
+  auto kern = a.p.G > 1 ? (seedb ? sdtw_bwd_kernel<T, KS, HAS_P, true, true>
+                                 : sdtw_bwd_kernel<T, KS, HAS_P, false, true>)
+                        : (seedb ? sdtw_bwd_kernel<T, KS, HAS_P, true, false>
+                                 : sdtw_bwd_kernel<T, KS, HAS_P, false, false>);
   const size_t smem = a.p.smem_bwd;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return set_error(kLaunch, "sdtw backward: cannot reserve %zu bytes of shared memory", smem);
@@ -1026,12 +1069,13 @@ int bwd_ks(const SdtwArgs<T>& a, bool has_p, cudaStream_t st) {
 // Blocks of `wpc` warps per SM that both sweeps of a plan can keep resident
 // with `smem` bytes each (registers and shared memory), or -1 when the
 // device cannot be asked (no GPU: the shared-memory bound alone is used).
-template <typename T, int KS, bool HAS_P>
+// GRP: the kernels with band groups.
+template <typename T, int KS, bool HAS_P, bool GRP>
 int resident_blocks(int wpc, size_t smem) {
-  const void* kerns[4] = {(const void*)sdtw_fwd_kernel<T, KS, HAS_P, false>,
-                          (const void*)sdtw_fwd_kernel<T, KS, HAS_P, true>,
-                          (const void*)sdtw_bwd_kernel<T, KS, HAS_P, false>,
-                          (const void*)sdtw_bwd_kernel<T, KS, HAS_P, true>};
+  const void* kerns[4] = {(const void*)sdtw_fwd_kernel<T, KS, HAS_P, false, GRP>,
+                          (const void*)sdtw_fwd_kernel<T, KS, HAS_P, true, GRP>,
+                          (const void*)sdtw_bwd_kernel<T, KS, HAS_P, false, GRP>,
+                          (const void*)sdtw_bwd_kernel<T, KS, HAS_P, true, GRP>};
   int best = INT_MAX;
   for (const void* k : kerns) {
     int n = 0;
@@ -1046,10 +1090,10 @@ int resident_blocks(int wpc, size_t smem) {
   return best;
 }
 
-int resident_blocks_any(int eb, int KS, bool has_p, int wpc, size_t smem) {
+int resident_blocks_any(int eb, int KS, bool has_p, bool grp, int wpc, size_t smem) {
   static std::mutex mu;
-  static std::map<std::tuple<int, int, bool, int, size_t>, int> cache;
-  const auto key = std::make_tuple(eb, KS, has_p, wpc, smem);
+  static std::map<std::tuple<int, int, bool, bool, int, size_t>, int> cache;
+  const auto key = std::make_tuple(eb, KS, has_p, grp, wpc, smem);
   {
     std::lock_guard<std::mutex> g(mu);
     auto it = cache.find(key);
@@ -1057,7 +1101,10 @@ int resident_blocks_any(int eb, int KS, bool has_p, int wpc, size_t smem) {
   }
   int n = -1;
 #define TW_RB(TT, K)                                                                          \
-  n = has_p ? resident_blocks<TT, K, true>(wpc, smem) : resident_blocks<TT, K, false>(wpc, smem)
+  n = has_p ? (grp ? resident_blocks<TT, K, true, true>(wpc, smem)                             \
+                   : resident_blocks<TT, K, true, false>(wpc, smem))                           \
+            : (grp ? resident_blocks<TT, K, false, true>(wpc, smem)                            \
+                   : resident_blocks<TT, K, false, false>(wpc, smem))
   if (eb == 4) {
     if (KS == 1) TW_RB(float, 1);
     else if (KS == 2) TW_RB(float, 2);
@@ -1139,6 +1186,7 @@ StreamPlan make_stream_plan(int B, int N, int M, int eb, bool has_p, int sms) {
   G = G >= 4 ? 4 : (G >= 2 ? 2 : 1);
   while (G > 1 && p.NB % G != 0) G /= 2;
   p.G = G;
+  p.NBg = p.NB / G;
   // The band-to-band delay line needs a lag D >= 32*KS + 128 between the
   // starts of consecutive passes (see row_above); D = L / G, so L >= G (32 KS
   // + 128), a multiple of 8 G.  A single-band pair has no delay line and only
@@ -1149,7 +1197,10 @@ StreamPlan make_stream_plan(int B, int N, int M, int eb, bool has_p, int sms) {
   p.D = p.L / G;
   const int S = eb == 4 ? RingStride<float>::value : RingStride<double>::value;
   const size_t per_w = (size_t)warp_smem_elems(p.KS, S, has_p) * eb;
-  const size_t hdr = StreamPlan::kSmemHeader;
+  // the groups' mbarriers; none without groups, where 64 bytes more per CTA
+  // would push cfg5's backward (8 CTAs of 19968 + 1024 bytes = 164 KB exactly)
+  // to the next shared-memory carveout and cost it 32 KB of L1
+  const size_t hdr = G > 1 ? StreamPlan::kSmemHeader : 0;
   // Warps per SM: bounded by shared memory (the per-lane rings), by the
   // registers of the heavier of the two sweeps, and by 32.
   int wps = (int)((size_t)(216 * 1024) / per_w);
@@ -1167,7 +1218,7 @@ StreamPlan make_stream_plan(int B, int N, int M, int eb, bool has_p, int sms) {
   for (int c : {4, 2, 1}) {
     if (c > wps || c % G != 0) continue;
     int n = wps / c;
-    const int resident = resident_blocks_any(eb, p.KS, has_p, c, per_w * c + hdr);
+    const int resident = resident_blocks_any(eb, p.KS, has_p, G > 1, c, per_w * c + hdr);
     if (resident >= 0 && resident < n) n = resident;
     if (n < 1) continue;
     const int gpc = c / G;
@@ -1198,7 +1249,7 @@ StreamPlan make_stream_plan(int B, int N, int M, int eb, bool has_p, int sms) {
   p.base = B / groups;
   p.rem = B % groups;
   const long long maxpairs = p.base + (p.rem ? 1 : 0);
-  const long long Tw = maxpairs * (p.NB / G) * p.L + 32 * p.KS - 1 + (long long)(G - 1) * p.D;
+  const long long Tw = maxpairs * p.NBg * p.L + 32 * p.KS - 1 + (long long)(G - 1) * p.D;
   p.tmax = (Tw + TILE - 1) / TILE * TILE;
   p.tstride = SLICE_ALIGN(p.tmax + StreamPlan::kPreRows);
   p.smem_fwd = per_w * p.wpc + hdr;

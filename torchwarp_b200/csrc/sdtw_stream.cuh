@@ -40,6 +40,7 @@ struct StreamPlan {
   int NB = 1;        // bands per pair
   int L = 0;         // stream columns per band pass (multiple of 8 G)
   int G = 1;         // warps per band group (divides NB and wpc)
+  int NBg = 1;       // NB / G: bands of a pair in one warp's stream
   int D = 0;         // L / G: steps between the starts of consecutive passes
   int warps = 0;     // warps launched (a multiple of G)
   int wpc = 4;       // warps per CTA
@@ -58,7 +59,8 @@ struct StreamPlan {
     return ((long long)w * tstride + kPreRows) * KS * 32;
   }
   long long delay_elems() const { return (long long)warps * L; }
-  // dynamic shared memory in front of the warps' regions: the groups' mbarriers
+  // dynamic shared memory after the warps' regions: the groups' mbarriers
+  // (reserved only when G > 1)
   static constexpr int kSmemHeader = 64;
 };
 
