@@ -376,6 +376,7 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
   const int ql = wi.Q * p.L;  // local columns of the warp's passes
 
   const long long woff = p.saved_offset(wi.w);
+  const long long eoff = p.edge_offset(wi.w);
   const T kap = a.kappa;
   // rows below the stream start read as +Big (R) / 0 (P) in the backward
 #pragma unroll 1
@@ -475,6 +476,9 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
       __syncwarp();
       const T wbR = coll[lane];
       const T wbP = HAS_P ? coll[32 + lane] : T(0);
+      // the window's bottom-row values (steps t0 - 24 .. t0 + 7) to the edge stream
+      a.sR[eoff + t0 - 24 + lane] = wbR;
+      if (HAS_P) a.sP[eoff + t0 - 24 + lane] = wbP;
       const int scx = t0 - 23 - 32 * KS + lane - wi.off;
       if (scx >= 0 && (!GRP || scx < ql)) {
         const int j = scx - (scx / p.L) * p.L;
@@ -520,17 +524,18 @@ __device__ __forceinline__ void load_saved_row(const T* __restrict__ s_lane, int
 }
 
 // Row -1 value lane 0 of sub-band 0 used at step sc in the forward sweep,
-// re-read from the saved stream `s_above` of the warp of the band above (its
-// bottom row, which that warp computed D - 32 KS + 1 steps earlier).
+// re-read from the edge stream `e_above` of the warp of the band above (its
+// bottom row, which that warp computed D - 32 KS + 1 steps earlier).  Lanes
+// read consecutive steps: one coalesced load per window.
 template <typename T, int KS, bool GRP>
-__device__ __forceinline__ T row_above_saved(const T* s_above, int sc, const StreamPlan& p,
+__device__ __forceinline__ T row_above_saved(const T* e_above, int sc, const StreamPlan& p,
                                              const WarpInfo& wi, T first_value) {
   if constexpr (!GRP) {  // one warp per pair: the band above is this warp's previous pass
     const int q = floor_div(sc, p.L);
     const int j = sc - q * p.L;
     const bool first = q < 0 || q >= wi.Q || pos_mod(q, p.NB) == 0;
     T v = first_value;
-    if (!first) v = s_above[((long long)(sc - p.L + 32 * KS - 1) * KS + (KS - 1)) * 32 + 31];
+    if (!first) v = e_above[sc - p.L + 32 * KS - 1];
     if (j == p.L - 1 && pos_mod(q + 1, p.NB) == 0) v = T(0);
     return v;
   }
@@ -539,7 +544,7 @@ __device__ __forceinline__ T row_above_saved(const T* s_above, int sc, const Str
   const int j = sl - q * p.L;
   const bool first = q < 0 || q >= wi.Q || first_band<GRP>(q, p, wi);
   T v = first_value;
-  if (!first) v = s_above[((long long)(sc - p.D + 32 * KS - 1) * KS + (KS - 1)) * 32 + 31];
+  if (!first) v = e_above[sc - p.D + 32 * KS - 1];
   if (j == p.L - 1 && first_band<GRP>(q + 1, p, wi)) v = T(0);
   return v;
 }
@@ -701,9 +706,9 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
   const long long woff = p.saved_offset(wi.w);
   const T* sRw = a.sR + woff;
   const T* sPw = HAS_P ? a.sP + woff : nullptr;
-  // saved stream of the warp of the band above (row -1 values)
-  const T* sRa = a.sR + p.saved_offset(wi.wprev);
-  const T* sPa = HAS_P ? a.sP + p.saved_offset(wi.wprev) : nullptr;
+  // edge stream of the warp of the band above (row -1 values)
+  const T* eRa = a.sR + p.edge_offset(wi.wprev);
+  const T* ePa = HAS_P ? a.sP + p.edge_offset(wi.wprev) : nullptr;
   const int Tend = (wi.Tw + TILE - 1) / TILE * TILE;
   const int btop = Tend / TILE - 1;
   const T* sRl = sRw + lane;
@@ -743,8 +748,8 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int c = 32 * (bw - h) + lane;
-      sb[c & 63] = row_above_saved<T, KS, GRP>(sRa, c, p, wi, big);
-      if (HAS_P) sbp[c & 63] = row_above_saved<T, KS, GRP>(sPa, c, p, wi, T(0));
+      sb[c & 63] = row_above_saved<T, KS, GRP>(eRa, c, p, wi, big);
+      if (HAS_P) sbp[c & 63] = row_above_saved<T, KS, GRP>(ePa, c, p, wi, T(0));
     }
   }
   // Adjoint from the band below, by the bottom row's column t - 32 KS at
@@ -759,8 +764,8 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
   __syncwarp();
 
   {  // cur = saved row t_first - 1, Xc = X(t_first)
-    const T b0 = row_above_saved<T, KS, GRP>(sRa, t_first, p, wi, big);
-    const T b0p = HAS_P ? row_above_saved<T, KS, GRP>(sPa, t_first, p, wi, T(0)) : T(0);
+    const T b0 = row_above_saved<T, KS, GRP>(eRa, t_first, p, wi, big);
+    const T b0p = HAS_P ? row_above_saved<T, KS, GRP>(ePa, t_first, p, wi, T(0)) : T(0);
     load_saved_row<T, KS>(sRl, t_first - 1, cur);
 #pragma unroll
     for (int k = 0; k < KS; ++k) Pcur[k] = T(0);
@@ -997,8 +1002,8 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
       else __syncwarp();
       // row -1 values two windows down replace the window just finished
       pbc = t0 - 64 + lane;
-      pbv = row_above_saved<T, KS, GRP>(sRa, pbc, p, wi, big);
-      if (HAS_P) pbpv = row_above_saved<T, KS, GRP>(sPa, pbc, p, wi, T(0));
+      pbv = row_above_saved<T, KS, GRP>(eRa, pbc, p, wi, big);
+      if (HAS_P) pbpv = row_above_saved<T, KS, GRP>(ePa, pbc, p, wi, T(0));
       pend_b = true;
     }
     // the next block (t0 - 8) may open a new window of bottom-row columns

@@ -24,7 +24,8 @@
 //
 // Saved state: R (and P for uDTW) of every cell, in stream order
 // [warp][t][k][lane] (one coalesced 128-byte row per sub-band and step), in
-// the log2 domain R' = R * log2(e) / gamma.  The backward sweep replays the
+// the log2 domain R' = R * log2(e) / gamma, and each warp's band-bottom row
+// again as a compact edge stream [warp][t].  The backward sweep replays the
 // stream in reverse and needs nothing else: the soft-min weights of a cell's
 // three predecessors are recomputed from their saved R', so neither the cost
 // nor the penalty is read again.
@@ -53,10 +54,20 @@ struct StreamPlan {
   // Warp slices are `tstride` rows apart (>= tmax + kPreRows).
   static constexpr int kPreRows = 16;
   long long tstride = 0;
-  long long saved_elems() const { return (long long)warps * tstride * KS * 32; }
+  // Each of the R and P blocks of the saved buffer is the stream of every
+  // warp followed by its edge stream: the value of lane 31 of sub-band KS-1
+  // (the band's bottom row) at every step, tstride values per warp, which
+  // the backward reads as the row above the next band.
+  long long saved_elems() const {
+    return (long long)warps * tstride * KS * 32 + (long long)warps * tstride;
+  }
   // offset of warp w's stream row 0
   __host__ __device__ long long saved_offset(int w) const {
     return ((long long)w * tstride + kPreRows) * KS * 32;
+  }
+  // offset of warp w's edge value of step 0
+  __host__ __device__ long long edge_offset(int w) const {
+    return (long long)warps * tstride * KS * 32 + (long long)w * tstride + kPreRows;
   }
   long long delay_elems() const { return (long long)warps * L; }
   // dynamic shared memory after the warps' regions: the groups' mbarriers
