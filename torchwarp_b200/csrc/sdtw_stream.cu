@@ -48,6 +48,17 @@ __host__ __device__ constexpr int warp_smem_elems(int KS, int S, bool has_p) {
   return KS * 32 * S * (has_p ? 2 : 1) + 64 + (has_p ? 256 : 128);
 }
 
+// n / v.d for 0 <= n < 2^31 (see Divisor).
+__device__ __forceinline__ int udiv(int n, const Divisor& v) {
+  return (int)((__umulhi((unsigned)n, v.m) + (unsigned)n) >> v.l);
+}
+// floor(n / v.d) and the non-negative remainder, for any sign of n.
+__device__ __forceinline__ int fl_div(int n, const Divisor& v) {
+  const int q = udiv(n >= 0 ? n : -n - 1, v);
+  return n >= 0 ? q : -q - 1;
+}
+__device__ __forceinline__ int p_mod(int n, const Divisor& v) { return n - fl_div(n, v) * v.d; }
+
 __device__ __forceinline__ int floor_div(int a, int b) {
   const int q = a / b;
   return (a % b != 0 && a < 0) ? q - 1 : q;
@@ -63,6 +74,10 @@ template <bool GRP>
 __device__ __forceinline__ int grp_G(const StreamPlan& p) { return GRP ? p.G : 1; }
 template <bool GRP>
 __device__ __forceinline__ int grp_NBg(const StreamPlan& p) { return GRP ? p.NBg : p.NB; }
+template <bool GRP>
+__device__ __forceinline__ const Divisor& grp_dNBg(const StreamPlan& p) {
+  return GRP ? p.dNBg : p.dNB;
+}
 
 // g: warp within its band group; off = g * D, the shift of this warp's own
 // stream (local column = step - off); Q: local passes (npairs * NB / G); Tw:
@@ -102,11 +117,11 @@ __device__ __forceinline__ int band_of(int q, const StreamPlan& p, const WarpInf
 }
 template <bool GRP>
 __device__ __forceinline__ bool first_band(int q, const StreamPlan& p, const WarpInfo& wi) {
-  return wi.g == 0 && pos_mod(q, grp_NBg<GRP>(p)) == 0;
+  return wi.g == 0 && p_mod(q, grp_dNBg<GRP>(p)) == 0;
 }
 template <bool GRP>
 __device__ __forceinline__ bool last_band(int q, const StreamPlan& p, const WarpInfo& wi) {
-  return wi.g == grp_G<GRP>(p) - 1 && pos_mod(q + 1, grp_NBg<GRP>(p)) == 0;
+  return wi.g == grp_G<GRP>(p) - 1 && p_mod(q + 1, grp_dNBg<GRP>(p)) == 0;
 }
 
 // One step of a band group's lockstep: every lane arrives on the group's
@@ -261,7 +276,7 @@ __device__ __forceinline__ void patch_row_tile(T* ring_row, const Cursor& c, con
 template <bool GRP, typename T>
 __device__ __forceinline__ T row_above(const T* dl, int sc, const StreamPlan& p,
                                        const WarpInfo& wi, T first_value) {
-  const int q = floor_div(sc, p.L);
+  const int q = fl_div(sc, p.dL);
   const int j = sc - q * p.L;
   const bool first = q < 0 || q >= wi.Q || first_band<GRP>(q, p, wi);
   T v = first ? first_value : dl[j];
@@ -481,7 +496,7 @@ __global__ void __launch_bounds__(128) sdtw_fwd_kernel(const SdtwArgs<T> a) {
       if (HAS_P) a.sP[eoff + t0 - 24 + lane] = wbP;
       const int scx = t0 - 23 - 32 * KS + lane - wi.off;
       if (scx >= 0 && (!GRP || scx < ql)) {
-        const int j = scx - (scx / p.L) * p.L;
+        const int j = scx - udiv(scx, p.dL) * p.L;
         dlR[j] = wbR;
         if (HAS_P) dlP[j] = wbP;
       }
@@ -531,16 +546,16 @@ template <typename T, int KS, bool GRP>
 __device__ __forceinline__ T row_above_saved(const T* e_above, int sc, const StreamPlan& p,
                                              const WarpInfo& wi, T first_value) {
   if constexpr (!GRP) {  // one warp per pair: the band above is this warp's previous pass
-    const int q = floor_div(sc, p.L);
+    const int q = fl_div(sc, p.dL);
     const int j = sc - q * p.L;
-    const bool first = q < 0 || q >= wi.Q || pos_mod(q, p.NB) == 0;
+    const bool first = q < 0 || q >= wi.Q || p_mod(q, p.dNB) == 0;
     T v = first_value;
     if (!first) v = e_above[sc - p.L + 32 * KS - 1];
-    if (j == p.L - 1 && pos_mod(q + 1, p.NB) == 0) v = T(0);
+    if (j == p.L - 1 && p_mod(q + 1, p.dNB) == 0) v = T(0);
     return v;
   }
   const int sl = sc - wi.off;
-  const int q = floor_div(sl, p.L);
+  const int q = fl_div(sl, p.dL);
   const int j = sl - q * p.L;
   const bool first = q < 0 || q >= wi.Q || first_band<GRP>(q, p, wi);
   T v = first_value;
@@ -562,19 +577,20 @@ __device__ __forceinline__ T push_from_below(const T* dl, int sc, const StreamPl
                                              const WarpInfo& wi, const T* grad) {
   if constexpr (!GRP) {  // one warp per pair: the band below is this warp's next pass
     if (sc < 0) return T(0);
-    const int q = sc / p.L;
+    const int q = udiv(sc, p.dL);
     const int j = sc - q * p.L;
     if (j >= p.M || q >= wi.Q) return T(0);
-    if ((q + 1) % p.NB == 0) return (SEEDB && j == p.M - 1) ? grad[wi.p0 + q / p.NB] : T(0);
+    const int pq = udiv(q + 1, p.dNB);
+    if (pq * p.NB == q + 1) return (SEEDB && j == p.M - 1) ? grad[wi.p0 + pq - 1] : T(0);
     return dl[j];
   }
   const int sl = sc - wi.off;
   if (sl < 0) return T(0);
-  const int q = sl / p.L;
+  const int q = udiv(sl, p.dL);
   const int j = sl - q * p.L;
   if (j >= p.M || q >= wi.Q) return T(0);
   if (last_band<GRP>(q, p, wi))
-    return (SEEDB && j == p.M - 1) ? grad[wi.p0 + q / grp_NBg<GRP>(p)] : T(0);
+    return (SEEDB && j == p.M - 1) ? grad[wi.p0 + udiv(q, grp_dNBg<GRP>(p))] : T(0);
   return dl[j];
 }
 
@@ -987,13 +1003,13 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
       const T wdR = coll[lane];
       const T wdP = HAS_P ? coll[32 + lane] : T(0);
       if constexpr (!GRP) {
-        const int j = (t0 + lane) - ((t0 + lane) / p.L) * p.L;
+        const int j = (t0 + lane) - udiv(t0 + lane, p.dL) * p.L;
         dlR[j] = wdR;
         if (HAS_P) dlP[j] = wdP;
       } else {
         const int sl = t0 + lane - wi.off;
         if (sl >= 0 && sl < ql) {
-          const int j = sl - (sl / p.L) * p.L;
+          const int j = sl - udiv(sl, p.dL) * p.L;
           dlR[j] = wdR;
           if (HAS_P) dlP[j] = wdP;
         }
@@ -1192,6 +1208,8 @@ StreamPlan make_stream_plan(int B, int N, int M, int eb, bool has_p, int sms) {
   while (G > 1 && p.NB % G != 0) G /= 2;
   p.G = G;
   p.NBg = p.NB / G;
+  p.dNB = make_divisor(p.NB);
+  p.dNBg = make_divisor(p.NBg);
   // The band-to-band delay line needs a lag D >= 32*KS + 128 between the
   // starts of consecutive passes (see row_above); D = L / G, so L >= G (32 KS
   // + 128), a multiple of 8 G.  A single-band pair has no delay line and only
@@ -1200,6 +1218,7 @@ StreamPlan make_stream_plan(int B, int N, int M, int eb, bool has_p, int sms) {
   if (p.NB > 1 && L < G * (rows + 128)) L = G * (rows + 128);
   p.L = (L + TILE * G - 1) / (TILE * G) * (TILE * G);
   p.D = p.L / G;
+  p.dL = make_divisor(p.L);
   const int S = eb == 4 ? RingStride<float>::value : RingStride<double>::value;
   const size_t per_w = (size_t)warp_smem_elems(p.KS, S, has_p) * eb;
   // the groups' mbarriers; none without groups, where 64 bytes more per CTA
@@ -1260,6 +1279,16 @@ StreamPlan make_stream_plan(int B, int N, int M, int eb, bool has_p, int sms) {
   p.smem_fwd = per_w * p.wpc + hdr;
   p.smem_bwd = per_w * p.wpc + hdr;
   return p;
+}
+
+Divisor make_divisor(int d) {
+  Divisor v;
+  v.d = d < 1 ? 1 : d;
+  int l = 0;
+  while ((1ll << l) < v.d) ++l;
+  v.l = l;
+  v.m = (uint32_t)((((unsigned __int128)1 << 32) * (((unsigned __int128)1 << l) - v.d)) / v.d + 1);
+  return v;
 }
 
 int dp_take_device_error() {

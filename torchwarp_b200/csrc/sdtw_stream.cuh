@@ -35,6 +35,18 @@
 
 namespace tw {
 
+// Division by a divisor fixed for a launch (Granlund & Montgomery, "Division
+// by invariant integers using multiplication", PLDI 1994: the round-up
+// multiplier with the add-back step).  With l = ceil(log2 d) and
+// m = floor(2^32 (2^l - d) / d) + 1, n / d = (umulhi(m, n) + n) >> l exactly
+// for 0 <= n < 2^31.
+struct Divisor {
+  uint32_t m = 1;
+  int l = 0;
+  int d = 1;
+};
+Divisor make_divisor(int d);
+
 struct StreamPlan {
   int B = 0, N = 0, M = 0;
   int KS = 1;        // sub-bands per warp
@@ -42,6 +54,7 @@ struct StreamPlan {
   int L = 0;         // stream columns per band pass (multiple of 8 G)
   int G = 1;         // warps per band group (divides NB and wpc)
   int NBg = 1;       // NB / G: bands of a pair in one warp's stream
+  Divisor dL, dNB, dNBg;   // L, NB and NBg as invariant divisors
   int D = 0;         // L / G: steps between the starts of consecutive passes
   int warps = 0;     // warps launched (a multiple of G)
   int wpc = 4;       // warps per CTA
