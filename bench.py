@@ -55,9 +55,9 @@ ALGO_BYTES_PER_CELL = 8      # soft-DTW fwd+bwd: cost read + cost-gradient write
 # chain-rule side), which are added at the timed shape.
 CALLS = {
     "udtw_cost": (1, 4, 4.12),           # C write + mask
-    "sdtw_forward": (1, 4, 8.16),        # C read + saved R' write
-    "sdtw_backward": (1, 4, 10.17),      # saved R' + mask read + masked dC write (+1.9 B/cell)
-    "udtw_features_grad": (2, 4, 4.57),  # masked dC read + the other side's features per unit
+    "sdtw_forward": (1, 4, 8.22),        # C read + saved R' write + edge stream
+    "sdtw_backward": (1, 4, 8.34),       # saved R' + edge + mask read + masked dC write
+    "udtw_features_grad": (2, 4, 4.55),  # masked dC read + the other side's features per unit
 }
 
 
