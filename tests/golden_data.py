@@ -90,3 +90,18 @@ def scaled(name):
 
 
 SCALED_CASES = list(_inputs.SCALED_CASES)
+
+
+_HIGHER = None
+HIGHER_COST_CASES = ["c7x9", "c33x40", "c70x65", "c64x130", "c40x44_band6", "c20x20_g005"]
+HIGHER_FEAT_CASES = ["f20x24d5", "f70x66d8"]
+
+
+def higher(name):
+    """{field: array} of a higher-order case (tests/golden/make_higher_order.py)."""
+    global _HIGHER
+    if _HIGHER is None:
+        with np.load(HERE / "golden" / "higher_order.npz") as z:
+            _HIGHER = dict(z.items())
+    head = name + "/"
+    return {k[len(head):]: v for k, v in _HIGHER.items() if k.startswith(head)}

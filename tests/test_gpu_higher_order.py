@@ -1,0 +1,153 @@
+"""Second-order and forward-mode derivatives of soft-DTW through the native
+kernels (B200), against the reference's own autograd DP.
+
+The fixtures (tests/golden/make_higher_order.py) are float64 outputs of the
+reference's pure-PyTorch DP (``torchwarp/udtw/_autograd.py`` of
+hibana2077/torchwarp), which is how the reference differentiates through its
+first-order backward.  Here the same quantities come from native kernels:
+the double backward is a Hessian-vector product run as the uDTW forward and
+backward with the direction as the penalty, and jvp is the uDTW forward with
+the tangent as the penalty.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import golden_data as G
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+ATOL, RTOL = 1e-9, 1e-8   # float64; second derivatives take more arithmetic than values
+
+
+@pytest.fixture(scope="module")
+def tw():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    import torchwarp_b200
+    return torchwarp_b200
+
+
+def _t(a, dtype=torch.float64):
+    return torch.as_tensor(np.asarray(a), dtype=dtype, device=DEV)
+
+
+def _close(got, want, atol=ATOL, rtol=RTOL):
+    np.testing.assert_allclose(got.detach().double().cpu().numpy(), np.asarray(want), atol=atol,
+                               rtol=rtol)
+
+
+def _cost_second_order(tw, h, dtype=torch.float64):
+    gamma, band = h["args"]
+    c = _t(h["C"], dtype).requires_grad_(True)
+    g = _t(h["g"], dtype).requires_grad_(True)
+    d = tw.functional.soft_dtw_from_cost(c, gamma=float(gamma), bandwidth=float(band) or None)
+    (dC,) = torch.autograd.grad((d * g).sum(), c, create_graph=True)
+    hC, hg = torch.autograd.grad((dC * _t(h["V"], dtype)).sum(), (c, g))
+    return d, dC, hC, hg
+
+
+@pytest.mark.parametrize("name", G.HIGHER_COST_CASES)
+def test_cost_double_backward(tw, name):
+    h = G.higher(name)
+    d, dC, hC, hg = _cost_second_order(tw, h)
+    _close(d, h["d"], 1e-10, 1e-9)
+    _close(dC, h["dC"], 1e-10, 1e-9)
+    _close(hC, h["hvp_C"])
+    _close(hg, h["hvp_g"])
+    assert tw._native.lib().tw_device_error() == 0
+
+
+@pytest.mark.parametrize("name", G.HIGHER_COST_CASES)
+def test_cost_jvp(tw, name):
+    h = G.higher(name)
+    gamma, band = h["args"]
+    f = lambda c: tw.functional.soft_dtw_from_cost(c, gamma=float(gamma),  # noqa: E731
+                                                   bandwidth=float(band) or None)
+    d, jvp = torch.func.jvp(f, (_t(h["C"]),), (_t(h["T"]),))
+    _close(d, h["d"], 1e-10, 1e-9)
+    _close(jvp, h["jvp"])
+
+
+@pytest.mark.parametrize("name", G.HIGHER_FEAT_CASES)
+def test_features_double_backward(tw, name):
+    h = G.higher(name)
+    (gamma,) = h["args"]
+    x = _t(h["X"]).requires_grad_(True)
+    y = _t(h["Y"]).requires_grad_(True)
+    g = _t(h["g"]).requires_grad_(True)
+    d = tw.functional.soft_dtw(x, y, gamma=float(gamma))
+    dX, dY = torch.autograd.grad((d * g).sum(), (x, y), create_graph=True)
+    hX, hY, hg = torch.autograd.grad((dX * _t(h["VX"])).sum() + (dY * _t(h["VY"])).sum(),
+                                     (x, y, g))
+    _close(d, h["d"], 1e-10, 1e-9)
+    _close(dX, h["dX"], 1e-9, 1e-8)
+    _close(dY, h["dY"], 1e-9, 1e-8)
+    _close(hX, h["hvp_X"], 1e-8, 1e-7)
+    _close(hY, h["hvp_Y"], 1e-8, 1e-7)
+    _close(hg, h["hvp_g"], 1e-8, 1e-7)
+
+
+def test_features_jvp_matches_cost_path(tw):
+    """jvp on features equals the jvp of the cost path along the cost's tangent."""
+    h = G.higher("f20x24d5")
+    (gamma,) = h["args"]
+    X, Y, VX, VY = (_t(h[k]) for k in ("X", "Y", "VX", "VY"))
+    f = lambda a, b: tw.functional.soft_dtw(a, b, gamma=float(gamma))  # noqa: E731
+    d, jvp = torch.func.jvp(f, (X, Y), (VX, VY))
+    eps = 1e-6
+    fd = (f(X + eps * VX, Y + eps * VY) - f(X - eps * VX, Y - eps * VY)) / (2 * eps)
+    _close(d, h["d"], 1e-10, 1e-9)
+    _close(jvp, fd.cpu().numpy(), 1e-6, 1e-6)
+
+
+def test_udtw_jvp_against_central_difference(tw):
+    """jvp of uDTW on matrices (distance and penalty sum) along tangents of
+    both, against a float64 central difference."""
+    g = torch.Generator().manual_seed(3)
+    B, N, M = 3, 45, 52
+    C = torch.rand(B, N, M, generator=g, dtype=torch.float64).to(DEV)
+    Q = torch.randn(B, N, M, generator=g, dtype=torch.float64).to(DEV)
+    Ct = torch.randn(B, N, M, generator=g, dtype=torch.float64).to(DEV)
+    Qt = torch.randn(B, N, M, generator=g, dtype=torch.float64).to(DEV)
+    f = lambda c, q: tw.functional.udtw_from_cost(c, q, gamma=0.3)  # noqa: E731
+    (d, p), (d_t, p_t) = torch.func.jvp(f, (C, Q), (Ct, Qt))
+    eps = 1e-6
+    dp_, pp_ = f(C + eps * Ct, Q + eps * Qt)
+    dm_, pm_ = f(C - eps * Ct, Q - eps * Qt)
+    _close(d_t, ((dp_ - dm_) / (2 * eps)).cpu().numpy(), 1e-6, 1e-6)
+    _close(p_t, ((pp_ - pm_) / (2 * eps)).cpu().numpy(), 1e-6, 1e-6)
+
+
+def test_cost_double_backward_fp32(tw):
+    """float32 double backward against the float64 fixture: max-normalised
+    error within the reference's float32 bar (1e-3)."""
+    h = G.higher("c70x65")
+    _, _, hC, hg = _cost_second_order(tw, h, torch.float32)
+    for got, want in ((hC, h["hvp_C"]), (hg, h["hvp_g"])):
+        err = np.abs(got.detach().double().cpu().numpy() - want).max() / np.abs(want).max()
+        assert err < 1e-3, err
+
+
+def test_third_order_raises(tw):
+    h = G.higher("c7x9")
+    c = _t(h["C"]).requires_grad_(True)
+    d = tw.functional.soft_dtw_from_cost(c, gamma=0.3)
+    (dC,) = torch.autograd.grad(d.sum(), c, create_graph=True)
+    (hC,) = torch.autograd.grad((dC * _t(h["V"])).sum(), c, create_graph=True)
+    with pytest.raises(RuntimeError):
+        torch.autograd.grad(hC.sum(), c)
+
+
+def test_udtw_second_order_raises(tw):
+    """Second derivatives of uDTW with a penalty are not native: asking for
+    them raises instead of returning a silently incomplete gradient."""
+    g = torch.Generator().manual_seed(4)
+    C = torch.rand(2, 9, 11, generator=g, dtype=torch.float64).to(DEV).requires_grad_(True)
+    Q = torch.randn(2, 9, 11, generator=g, dtype=torch.float64).to(DEV).requires_grad_(True)
+    d, p = tw.functional.udtw_from_cost(C, Q, gamma=0.3)
+    (dC,) = torch.autograd.grad((d + p).sum(), C, create_graph=True)
+    with pytest.raises(RuntimeError):
+        torch.autograd.grad(dC.sum(), C)

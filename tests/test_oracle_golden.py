@@ -245,3 +245,23 @@ def test_optimal_path_known_answers(orc):
             R[t, u] = cost[t - 1, u - 1] + min(R[t - 1, u], R[t, u - 1], R[t - 1, u - 1])
     assert path[0][:2] == (0, 0) and path[-1][:2] == (T - 1, U - 1)
     assert abs(sum(cost[t, u] for t, u, _ in path) - R[T, U]) < 1e-12
+
+
+@pytest.mark.parametrize("name", G.HIGHER_COST_CASES)
+def test_oracle_second_order_identity(orc, name):
+    """soft-DTW's Hessian-vector product and jvp through the uDTW penalty
+    recursion, against the reference's own autograd DP
+    (tests/golden/make_higher_order.py).  With penalty Q = V, the uDTW end
+    value is <E, V> (E = dd/dC), and its gradient for seeds (0, g) is
+    g * (d^2 d/dC^2) V: the identity the native double backward uses."""
+    h = G.higher(name)
+    gamma, band = h["args"]
+    bw = band or None
+    d, p, dC, dQ = orc.udtw_from_cost(h["C"], h["V"], gamma=gamma, bandwidth=bw, g_d=0.0,
+                                      g_p=h["g"])
+    close(d, h["d"])
+    close(p, h["hvp_g"], atol=1e-9, rtol=1e-8)
+    close(dC, h["hvp_C"], atol=1e-9, rtol=1e-8)
+    close(dQ, h["dC"])
+    _, jp, _, _ = orc.udtw_from_cost(h["C"], h["T"], gamma=gamma, bandwidth=bw, g_d=1.0, g_p=0.0)
+    close(jp, h["jvp"], atol=1e-9, rtol=1e-8)

@@ -25,8 +25,17 @@ implementation:
 
 Each op has a fake (meta) implementation for torch.compile, a vmap rule that
 folds the vmapped dimension into the batch, and runs in float32 under
-autocast.  First-order reverse mode calls the native backward; the backward
-itself is not differentiable (create_graph=True through it raises).
+autocast.  First-order reverse mode calls the native backward.
+
+Higher-order derivatives of soft-DTW (no penalty), on a cost or on features,
+are native too.  Differentiating through the backward (create_graph=True) is
+a Hessian-vector product: with the incoming direction V as a uDTW penalty,
+the penalty recursion ends at <E, V> (E = dd/dcost), and the native uDTW
+backward of that value is H V.  Forward mode (jvp) is the same uDTW forward
+with the tangent as the penalty, and for uDTW one native backward.  The
+reference routes all of these through its pure-PyTorch autograd DP
+(udtw/_ops.py:226-258, udtw/_autograd.py:32-79).  Second derivatives of uDTW
+with a penalty, and third derivatives, raise.
 """
 
 from typing import Optional, Tuple
@@ -302,6 +311,55 @@ def _zeros_if_none(g, like, B):
     return like.new_zeros(B) if g is None else g
 
 
+def _pairwise_dot(a, b):
+    """[B] sums of a * b over each pair's cells."""
+    return (a * b).flatten(1).sum(1)
+
+
+class SdtwCostGrad(torch.autograd.Function):
+    """(cost, saved, g) -> g * dd/dcost for soft-DTW on a cost, differentiable
+    once more with the native kernels.
+
+    The backward is a Hessian-vector product.  Taking the direction V (the
+    gradient that arrives for d_cost) as a uDTW penalty, the penalty recursion
+    P_s = V_s + sum_p w_p P_p ends at <E, V> with E = dd/dcost.  The native
+    uDTW forward returns that value, which is the gradient for g.  The native
+    uDTW backward seeded with (0, g) returns g * (d^2 d / dcost^2) V, which is
+    the gradient for the cost.  A third derivative raises."""
+
+    @staticmethod
+    def forward(cost, saved, g, gamma, bandwidth):
+        B, N, M = cost.shape
+        return sdtw_dp_backward(saved, g, g, N, M, gamma, False)[0]
+
+    @staticmethod
+    def setup_context(ctx, inputs, output):
+        cost, saved, g, gamma, bandwidth = inputs
+        ctx.save_for_backward(cost, g)
+        ctx.args = (gamma, bandwidth)
+
+    @staticmethod
+    @torch.autograd.function.once_differentiable
+    def backward(ctx, V):
+        cost, g = ctx.saved_tensors
+        gamma, bandwidth = ctx.args
+        B, N, M = cost.shape
+        _, v_e, saved_v = sdtw_dp(cost, V.to(cost.dtype), gamma, bandwidth)
+        hv, _ = sdtw_dp_backward(saved_v, torch.zeros_like(g), g, N, M, gamma, True)
+        return hv, None, v_e, None, None
+
+
+@torch.autograd.function.once_differentiable
+def _dp_backward_once(ctx, saved, g_r, g_p):
+    gamma, has_p, _ = ctx.args
+    B, N, M = ctx.shape
+    like = saved.new_empty(0, dtype=ctx.dtype)
+    g_r = _zeros_if_none(g_r, like, B).to(ctx.dtype)
+    g_p = _zeros_if_none(g_p, like, B).to(ctx.dtype)
+    d_cost, d_pen = sdtw_dp_backward(saved, g_r, g_p, N, M, gamma, has_p)
+    return d_cost, (d_pen if has_p else None), None, None
+
+
 class DP(torch.autograd.Function):
     """(cost, penalty?) -> (distance, penalty_sum, saved)."""
 
@@ -314,22 +372,49 @@ class DP(torch.autograd.Function):
         cost, penalty, gamma, bandwidth = inputs
         ctx.mark_non_differentiable(output[2])
         ctx.set_materialize_grads(False)
-        ctx.save_for_backward(output[2])
+        # the cost is kept for a backward that is differentiated again (soft-DTW)
+        ctx.save_for_backward(output[2], cost if penalty is None else None)
+        if penalty is None:
+            ctx.save_for_forward(cost, output[2])
+        else:
+            ctx.save_for_forward(cost, penalty, output[2])
         ctx.shape = tuple(cost.shape)
         ctx.dtype = cost.dtype
-        ctx.args = (gamma, penalty is not None)
+        ctx.args = (gamma, penalty is not None, bandwidth)
 
     @staticmethod
-    @torch.autograd.function.once_differentiable
     def backward(ctx, g_r, g_p, _g_saved):
-        (saved,) = ctx.saved_tensors
-        gamma, has_p = ctx.args
+        saved, cost = ctx.saved_tensors
+        gamma, has_p, bandwidth = ctx.args
+        if torch.is_grad_enabled() and not has_p:
+            # create_graph: a backward that is itself differentiable (natively)
+            g = _zeros_if_none(g_r, cost, ctx.shape[0]).to(ctx.dtype)
+            return SdtwCostGrad.apply(cost, saved, g, gamma, bandwidth), None, None, None
+        return _dp_backward_once(ctx, saved, g_r, g_p)
+
+    @staticmethod
+    def jvp(ctx, cost_t, penalty_t, _gamma_t, _bandwidth_t):
+        gamma, has_p, bandwidth = ctx.args
         B, N, M = ctx.shape
-        like = saved.new_empty(0, dtype=ctx.dtype)
-        g_r = _zeros_if_none(g_r, like, B).to(ctx.dtype)
-        g_p = _zeros_if_none(g_p, like, B).to(ctx.dtype)
-        d_cost, d_pen = sdtw_dp_backward(saved, g_r, g_p, N, M, gamma, has_p)
-        return d_cost, (d_pen if has_p else None), None, None
+        if not has_p:
+            cost, _ = ctx.saved_tensors
+            if cost_t is None:
+                return cost.new_zeros(B), None, None
+            # d/de d(cost + e T) = <E, T>: the uDTW forward with T as the penalty
+            _, r_t, _ = sdtw_dp(cost, cost_t.to(cost.dtype), gamma, bandwidth)
+            return r_t, None, None
+        cost, penalty, saved = ctx.saved_tensors
+        # one native backward of the penalty sum: dp/dcost, and dp/dpenalty = E
+        d_cost, e = sdtw_dp_backward(saved, cost.new_zeros(B), cost.new_ones(B), N, M, gamma,
+                                     True)
+        r_t = cost.new_zeros(B)
+        p_t = cost.new_zeros(B)
+        if cost_t is not None:
+            r_t = r_t + _pairwise_dot(e, cost_t)
+            p_t = p_t + _pairwise_dot(d_cost, cost_t)
+        if penalty_t is not None:
+            p_t = p_t + _pairwise_dot(e, penalty_t)
+        return r_t, p_t, None
 
 
 class Fused(torch.autograd.Function):
@@ -361,6 +446,21 @@ class Fused(torch.autograd.Function):
         return dX, dY, (dvx if has_p else None), (dvy if has_p else None), None, None, None, None
 
 
+def _sqeuclid(X, Y):
+    """||x_i - y_j||^2 clamped at 0, the native cost's formula, as a
+    differentiable expression (its GEMM runs in cuBLAS)."""
+    x2 = (X * X).sum(-1)
+    y2 = (Y * Y).sum(-1)
+    return (x2[:, :, None] + y2[:, None, :] - 2.0 * torch.bmm(X, Y.transpose(1, 2))).clamp_min(0)
+
+
+@torch.autograd.function.once_differentiable
+def _sdtw_fused_backward_once(ctx, X, Y, mask, saved, g_r):
+    g_r = _zeros_if_none(g_r, X, X.shape[0])
+    dX, dY = sdtw_fused_backward(X, Y, mask, saved, g_r, ctx.gamma)
+    return dX, dY, None, None
+
+
 class SdtwFused(torch.autograd.Function):
     """(X, Y) -> (distance, saved, mask): soft-DTW with squared-Euclidean cost."""
 
@@ -374,15 +474,42 @@ class SdtwFused(torch.autograd.Function):
         ctx.mark_non_differentiable(output[1], output[2])
         ctx.set_materialize_grads(False)
         ctx.save_for_backward(X, Y, output[2], output[1])
+        ctx.save_for_forward(X, Y)
         ctx.gamma = gamma
+        ctx.bandwidth = bandwidth
 
     @staticmethod
-    @torch.autograd.function.once_differentiable
     def backward(ctx, g_r, _g_saved, _g_mask):
         X, Y, mask, saved = ctx.saved_tensors
-        g_r = _zeros_if_none(g_r, X, X.shape[0])
-        dX, dY = sdtw_fused_backward(X, Y, mask, saved, g_r, ctx.gamma)
+        if not torch.is_grad_enabled():
+            return _sdtw_fused_backward_once(ctx, X, Y, mask, saved, g_r)
+        # create_graph: the cost is rebuilt as a differentiable expression and
+        # the DP part goes through SdtwCostGrad, whose own backward is native;
+        # autograd supplies the cost's second derivatives
+        g = _zeros_if_none(g_r, X, X.shape[0]).to(X.dtype)
+        cost = _sqeuclid(X, Y)
+        s = SdtwCostGrad.apply(cost, saved, g, ctx.gamma, ctx.bandwidth)
+        wrt = [t for t in (X, Y) if t.requires_grad]
+        grads = iter(torch.autograd.grad(cost, wrt, s, create_graph=True) if wrt else ())
+        dX = next(grads) if X.requires_grad else None
+        dY = next(grads) if Y.requires_grad else None
         return dX, dY, None, None
+
+    @staticmethod
+    def jvp(ctx, X_t, Y_t, _gamma_t, _bandwidth_t):
+        X, Y = ctx.saved_tensors
+        B = X.shape[0]
+        if X_t is None and Y_t is None:
+            return X.new_zeros(B), None, None
+        X_t = torch.zeros_like(X) if X_t is None else X_t.to(X.dtype)
+        Y_t = torch.zeros_like(Y) if Y_t is None else Y_t.to(Y.dtype)
+        cost = _sqeuclid(X, Y)
+        # the cost's tangent, zero where the clamp holds it at 0
+        cost_t = (2.0 * (X * X_t).sum(-1)[:, :, None] + 2.0 * (Y * Y_t).sum(-1)[:, None, :]
+                  - 2.0 * (torch.bmm(X_t, Y.transpose(1, 2)) + torch.bmm(X, Y_t.transpose(1, 2))))
+        cost_t = torch.where(cost > 0, cost_t, torch.zeros_like(cost_t))
+        _, r_t, _ = sdtw_dp(cost, cost_t, ctx.gamma, ctx.bandwidth)
+        return r_t, None, None
 
 
 def sdtw_fused_apply(X, Y, gamma, bandwidth):
