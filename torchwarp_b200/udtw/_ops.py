@@ -316,6 +316,17 @@ def _pairwise_dot(a, b):
     return (a * b).flatten(1).sum(1)
 
 
+# The saved stream (uint8) and the positivity mask (int32) leave the autograd
+# Functions as float32 views of the same bytes: forward-mode transforms give
+# every output a tangent, and a tangent needs a floating-point dtype.
+def _as_f32(t):
+    return t.view(torch.float32)
+
+
+def _as_bytes(t):
+    return t.view(torch.uint8)
+
+
 class SdtwCostGrad(torch.autograd.Function):
     """(cost, saved, g) -> g * dd/dcost for soft-DTW on a cost, differentiable
     once more with the native kernels.
@@ -365,7 +376,8 @@ class DP(torch.autograd.Function):
 
     @staticmethod
     def forward(cost, penalty, gamma, bandwidth):
-        return sdtw_dp(cost, penalty, gamma, bandwidth)
+        out_r, out_p, saved = sdtw_dp(cost, penalty, gamma, bandwidth)
+        return out_r, out_p, _as_f32(saved)
 
     @staticmethod
     def setup_context(ctx, inputs, output):
@@ -385,6 +397,7 @@ class DP(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g_r, g_p, _g_saved):
         saved, cost = ctx.saved_tensors
+        saved = _as_bytes(saved)
         gamma, has_p, bandwidth = ctx.args
         if torch.is_grad_enabled() and not has_p:
             # create_graph: a backward that is itself differentiable (natively)
@@ -405,7 +418,7 @@ class DP(torch.autograd.Function):
             return r_t, None, None
         cost, penalty, saved = ctx.saved_tensors
         # one native backward of the penalty sum: dp/dcost, and dp/dpenalty = E
-        d_cost, e = sdtw_dp_backward(saved, cost.new_zeros(B), cost.new_ones(B), N, M, gamma,
+        d_cost, e = sdtw_dp_backward(_as_bytes(saved), cost.new_zeros(B), cost.new_ones(B), N, M, gamma,
                                      True)
         r_t = cost.new_zeros(B)
         p_t = cost.new_zeros(B)
@@ -466,7 +479,8 @@ class SdtwFused(torch.autograd.Function):
 
     @staticmethod
     def forward(X, Y, gamma, bandwidth):
-        return sdtw_fused(X, Y, gamma, bandwidth)
+        out_r, saved, mask = sdtw_fused(X, Y, gamma, bandwidth)
+        return out_r, _as_f32(saved), _as_f32(mask)
 
     @staticmethod
     def setup_context(ctx, inputs, output):
@@ -481,6 +495,7 @@ class SdtwFused(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g_r, _g_saved, _g_mask):
         X, Y, mask, saved = ctx.saved_tensors
+        mask, saved = mask.view(torch.int32), _as_bytes(saved)
         if not torch.is_grad_enabled():
             return _sdtw_fused_backward_once(ctx, X, Y, mask, saved, g_r)
         # create_graph: the cost is rebuilt as a differentiable expression and
