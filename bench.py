@@ -74,7 +74,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--workload", default="cfg5",
-                    choices=["cfg5", "cfg5-udtw", "cfg1", "cfg2", "cfg3", "cfg4", "cfg4-cost"],
+                    choices=["cfg5", "cfg5-udtw", "cfg1", "cfg2", "cfg3", "cfg4", "cfg4-cost",
+                             "train-ecg"],
                     help="cfg5 (default) is the headline line; the others time the remaining "
                          "configurations on one GPU (secondary lines, same JSON shape)")
     return ap.parse_args()
@@ -416,6 +417,8 @@ def _secondary(a):
     def rn(*shape):
         return torch.randn(*shape, device=dev, generator=g)
 
+    extra = {}
+
     if w == "cfg5-udtw":
         B, N, D = a.batch, a.length, a.dim
         X, Y = rn(B, N, D), rn(B, N, D)
@@ -468,6 +471,90 @@ def _secondary(a):
         def step():
             q, s_ = Q.detach().requires_grad_(True), S_.detach().requires_grad_(True)
             twb.functional.fvm(q, s_, gamma=0.1).sum().backward()
+    elif w == "train-ecg":
+        # One training step of a forecaster with the uDTW loss, in the shape
+        # and settings of the reference's ECG5000 speed experiment
+        # (experiments/ecg5000_speed.py:36-76, ecg5000_forecast.py config
+        # "default"/"udtw"): 84 observed and 56 predicted samples, batch 50,
+        # an MLP forecaster (84 -> 256 -> 56, ReLU), a sigma network
+        # (56 -> 64 -> 56, sigma = 2 sigmoid + 0.1), uDTW gamma 0.1, beta 0.01,
+        # Adam lr 1e-3.  ECG5000 is not available: the series are seeded
+        # synthetic heartbeats (Gaussian waves plus noise, z-normalised).
+        n_in, n_out, batch = 84, 56, 50
+        t = torch.linspace(0.0, 1.0, n_in + n_out, device=dev)
+        amp = torch.rand(500, 3, 1, device=dev, generator=g) + 0.5
+        ctr = torch.rand(500, 3, 1, device=dev, generator=g)
+        wid = 0.02 + 0.05 * torch.rand(500, 3, 1, device=dev, generator=g)
+        beats = (amp * torch.exp(-0.5 * ((t - ctr) / wid) ** 2)).sum(1) + 0.05 * rn(500, 140)
+        beats = (beats - beats.mean(1, keepdim=True)) / beats.std(1, keepdim=True)
+        x_all, y_all = beats[:, :n_in], beats[:, n_in:]
+        torch.manual_seed(42)
+        f = torch.nn.Sequential(torch.nn.Linear(n_in, 256), torch.nn.ReLU(),
+                                torch.nn.Linear(256, n_out)).to(dev)
+        sig_net = torch.nn.Sequential(torch.nn.Linear(n_out, 64), torch.nn.ReLU(),
+                                      torch.nn.Linear(64, n_out)).to(dev)
+
+        def sigma(v):
+            return 2.0 * torch.sigmoid(sig_net(v)) + 0.1
+
+        crit = twb.UDTW(gamma=0.1, beta=0.01, normalize=False)
+        opt = torch.optim.Adam(list(f.parameters()) + list(sig_net.parameters()), lr=1e-3,
+                               capturable=True)
+        cells, algo = batch * n_out * n_out, 16 * batch * n_out * n_out
+        metric = "uDTW training steps (forecaster B=50, 84 -> 56 samples), DP cells/s"
+        sx, sy = x_all.new_empty(batch, n_in), y_all.new_empty(batch, n_out)
+        it = [0]
+
+        def train_step():
+            pred = f(sx)
+            d, p_ = crit(pred.unsqueeze(-1), sy.unsqueeze(-1), sigma(pred).unsqueeze(-1),
+                         sigma(sy).unsqueeze(-1))
+            opt.zero_grad(set_to_none=False)
+            (d + p_).mean().backward()
+            opt.step()
+
+        def next_batch():
+            k = it[0]
+            it[0] += 1
+            idx = torch.arange(k * batch, (k + 1) * batch, device=dev) % x_all.shape[0]
+            sx.copy_(x_all[idx])
+            sy.copy_(y_all[idx])
+
+        def eager_step():
+            next_batch()
+            train_step()
+
+        # The step is launch-bound (about 30 small kernels), so it is captured
+        # once as a CUDA graph: forecaster, sigma network, uDTW loss (native
+        # cost, DP forward, DP backward, chain rule), backward and Adam.  The
+        # graph is captured after warm-up steps on a side stream; every timed
+        # step copies its batch into the captured inputs and replays.
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                eager_step()
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            train_step()
+
+        def step():
+            next_batch()
+            graph.replay()
+
+        for _ in range(3):
+            eager_step()
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(a.steps):
+            eager_step()
+        t1.record()
+        torch.cuda.synchronize()
+        extra["eager_ms_per_step"] = t0.elapsed_time(t1) / a.steps
+        extra["step"] = ("one CUDA-graph replay of forward, uDTW loss, backward and Adam, "
+                         "after a copy of the batch into the captured inputs")
     else:  # cfg4-cost
         Cc = rn(1024, 7, 7, 10, 10).abs()
         cells, algo = 1024 * 49 * 10 * 10, 40140800
@@ -502,7 +589,7 @@ def _secondary(a):
                         "algorithmic_bytes_per_step": algo, "achieved": achieved,
                         "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                         "peak_source": src},
-           "native_calls_ms": calls})
+           "native_calls_ms": calls, **extra})
 
 
 _JSON_FD = None

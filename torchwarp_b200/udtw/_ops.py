@@ -316,17 +316,6 @@ def _pairwise_dot(a, b):
     return (a * b).flatten(1).sum(1)
 
 
-# The saved stream (uint8) and the positivity mask (int32) leave the autograd
-# Functions as float32 views of the same bytes: forward-mode transforms give
-# every output a tangent, and a tangent needs a floating-point dtype.
-def _as_f32(t):
-    return t.view(torch.float32)
-
-
-def _as_bytes(t):
-    return t.view(torch.uint8)
-
-
 class SdtwCostGrad(torch.autograd.Function):
     """(cost, saved, g) -> g * dd/dcost for soft-DTW on a cost, differentiable
     once more with the native kernels.
@@ -376,8 +365,7 @@ class DP(torch.autograd.Function):
 
     @staticmethod
     def forward(cost, penalty, gamma, bandwidth):
-        out_r, out_p, saved = sdtw_dp(cost, penalty, gamma, bandwidth)
-        return out_r, out_p, _as_f32(saved)
+        return sdtw_dp(cost, penalty, gamma, bandwidth)
 
     @staticmethod
     def setup_context(ctx, inputs, output):
@@ -397,7 +385,6 @@ class DP(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g_r, g_p, _g_saved):
         saved, cost = ctx.saved_tensors
-        saved = _as_bytes(saved)
         gamma, has_p, bandwidth = ctx.args
         if torch.is_grad_enabled() and not has_p:
             # create_graph: a backward that is itself differentiable (natively)
@@ -411,14 +398,16 @@ class DP(torch.autograd.Function):
         B, N, M = ctx.shape
         if not has_p:
             cost, _ = ctx.saved_tensors
+            # the penalty-sum output is a differentiable zero without a
+            # penalty; it gets a zero tangent (None there trips forward mode)
             if cost_t is None:
-                return cost.new_zeros(B), None, None
+                return cost.new_zeros(B), cost.new_zeros(B), None
             # d/de d(cost + e T) = <E, T>: the uDTW forward with T as the penalty
             _, r_t, _ = sdtw_dp(cost, cost_t.to(cost.dtype), gamma, bandwidth)
-            return r_t, None, None
+            return r_t, torch.zeros_like(r_t), None
         cost, penalty, saved = ctx.saved_tensors
         # one native backward of the penalty sum: dp/dcost, and dp/dpenalty = E
-        d_cost, e = sdtw_dp_backward(_as_bytes(saved), cost.new_zeros(B), cost.new_ones(B), N, M, gamma,
+        d_cost, e = sdtw_dp_backward(saved, cost.new_zeros(B), cost.new_ones(B), N, M, gamma,
                                      True)
         r_t = cost.new_zeros(B)
         p_t = cost.new_zeros(B)
@@ -479,8 +468,7 @@ class SdtwFused(torch.autograd.Function):
 
     @staticmethod
     def forward(X, Y, gamma, bandwidth):
-        out_r, saved, mask = sdtw_fused(X, Y, gamma, bandwidth)
-        return out_r, _as_f32(saved), _as_f32(mask)
+        return sdtw_fused(X, Y, gamma, bandwidth)
 
     @staticmethod
     def setup_context(ctx, inputs, output):
@@ -495,7 +483,6 @@ class SdtwFused(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g_r, _g_saved, _g_mask):
         X, Y, mask, saved = ctx.saved_tensors
-        mask, saved = mask.view(torch.int32), _as_bytes(saved)
         if not torch.is_grad_enabled():
             return _sdtw_fused_backward_once(ctx, X, Y, mask, saved, g_r)
         # create_graph: the cost is rebuilt as a differentiable expression and
