@@ -218,6 +218,24 @@ int tw_qs_cost_grad_f64(const double* query, const double* support, const double
                         const double* d_cost, int B, int R, int U, int D, int metric,
                         double* d_query, double* d_support, void* stream);
 
+/* RBF base cost: query [B, R, D], support [B, U, D] -> cost [B, R, U] with
+ * cost_ru = sum_d [2 - 2 exp(-sigma (q_rd - s_ud)^2)], sigma > 0.  Replaces
+ * the PyTorch rbf_cost of jeanie/distances.py:41-51, which materialises the
+ * [.., R, U, D] difference tensor. */
+int tw_qs_rbf_cost_f32(const float* query, const float* support, int B, int R, int U, int D,
+                       double sigma, float* cost, void* stream);
+int tw_qs_rbf_cost_f64(const double* query, const double* support, int B, int R, int U, int D,
+                       double sigma, double* cost, void* stream);
+/* Its gradient given d_cost [B, R, U]: d_query [B, R, D] and d_support
+ * [B, U, D], written (not accumulated); deterministic (no atomics).  Replaces
+ * autograd through the same expression. */
+int tw_qs_rbf_cost_grad_f32(const float* query, const float* support, const float* d_cost,
+                            int B, int R, int U, int D, double sigma, float* d_query,
+                            float* d_support, void* stream);
+int tw_qs_rbf_cost_grad_f64(const double* query, const double* support, const double* d_cost,
+                            int B, int R, int U, int D, double sigma, double* d_query,
+                            double* d_support, void* stream);
+
 /* FVM viewpoint soft-min: cost [B, Kf, TU] -> temporal [B, TU] =
  * -gamma logsumexp_n(-cost / gamma), and its backward d_cost = softmax_n *
  * d_temporal.  Replaces jeanie/fvm.py:36-37 (torch logsumexp). */

@@ -108,6 +108,51 @@ def test_distances_golden(tw, name):
     _close(getattr(tw, name)(_t(ref["qb"]), _t(ref["sb"])), ref["batch_value"])
 
 
+def _rbf_definition(q, s, sigma):
+    diff = q.unsqueeze(-2) - s.unsqueeze(-3)
+    return (2.0 - 2.0 * torch.exp(-sigma * diff.pow(2))).sum(-1)
+
+
+@pytest.mark.parametrize("qshape,sshape,sigma", [
+    ((2, 5, 3), (2, 7, 3), 0.5),             # two sequences
+    ((3, 4, 6, 8), (3, 37, 8), 0.3),         # JEANIE layout, U across support chunks
+    ((2, 3, 2, 5, 7), (2, 1, 4, 9, 7), 1.2),  # FVM with support-side viewpoints (broadcast)
+    ((2, 15, 10, 256), (2, 10, 256), 0.5),   # cfg3 feature size
+])
+def test_rbf_cost_native_vs_definition(tw, qshape, sshape, sigma):
+    """The native rbf cost and its gradient against the reference's PyTorch
+    definition (jeanie/distances.py:41-51), float64."""
+    g = torch.Generator().manual_seed(sum(qshape) + sum(sshape))
+    q = torch.randn(*qshape, generator=g, dtype=torch.float64).to(DEV).requires_grad_(True)
+    s = torch.randn(*sshape, generator=g, dtype=torch.float64).to(DEV).requires_grad_(True)
+    if len(sshape) == len(qshape):
+        want = _rbf_definition(q, s, sigma)
+    else:
+        want = _rbf_definition(q, s.unsqueeze(-3), sigma)
+    got = tw.rbf_cost(q, s, sigma=sigma)
+    assert got.shape == want.shape
+    w = torch.randn(want.shape, generator=g, dtype=torch.float64).to(DEV)
+    gq, gs = torch.autograd.grad((got * w).sum(), (q, s))
+    wq, ws = torch.autograd.grad((want * w).sum(), (q, s))
+    _close(got, want.detach().cpu().numpy())
+    _close(gq, wq.cpu().numpy())
+    _close(gs, ws.cpu().numpy())
+
+
+def test_rbf_cost_fp32_and_deterministic(tw):
+    g = torch.Generator().manual_seed(9)
+    q = torch.randn(8, 150, 64, generator=g).to(DEV).requires_grad_(True)
+    s = torch.randn(8, 10, 64, generator=g).to(DEV).requires_grad_(True)
+    got = tw.rbf_cost(q, s)
+    want = _rbf_definition(q.double(), s.double(), 0.5)
+    err = (got.double() - want).abs().max() / want.abs().max()
+    assert err < 1e-6, err
+    w = torch.randn(got.shape, generator=g).to(DEV)
+    g1 = torch.autograd.grad((got * w).sum(), (q, s), retain_graph=True)
+    g2 = torch.autograd.grad((got * w).sum(), (q, s))
+    assert all(torch.equal(a, b) for a, b in zip(g1, g2))
+
+
 def test_end_to_end_golden(tw):
     ref = G.official("jeanie.end_to_end")
     q, s = _t(ref["q"]).requires_grad_(), _t(ref["s"]).requires_grad_()

@@ -137,15 +137,6 @@ def test_softmin_is_torch_level():
     torch.testing.assert_close(TF.softmin(v, 0.5, dim=1), -0.5 * torch.logsumexp(-v / 0.5, dim=1))
 
 
-def test_rbf_cost_matches_definition():
-    g = torch.Generator().manual_seed(0)
-    X, Y = torch.rand(2, 5, 3, generator=g, dtype=torch.float64), \
-        torch.rand(2, 7, 3, generator=g, dtype=torch.float64)
-    diff = X.unsqueeze(2) - Y.unsqueeze(1)
-    torch.testing.assert_close(tw.rbf_cost(X, Y, sigma=0.5),
-                               (2 - 2 * torch.exp(-0.5 * diff.pow(2))).sum(-1))
-
-
 @pytest.mark.parametrize("call", [
     lambda: TF.soft_dtw_from_cost(torch.rand(1, 3, 4), gamma=0.1),
     lambda: TF.soft_dtw(torch.rand(1, 3, 2), torch.rand(1, 4, 2), gamma=0.1),

@@ -61,6 +61,10 @@ SIGNATURES = {
     "tw_qs_cost_f64": (_c_i, [_c_p, _c_p] + [_c_i] * 5 + [_c_p, _c_p]),
     "tw_qs_cost_grad_f32": (_c_i, [_c_p] * 4 + [_c_i] * 5 + [_c_p, _c_p, _c_p]),
     "tw_qs_cost_grad_f64": (_c_i, [_c_p] * 4 + [_c_i] * 5 + [_c_p, _c_p, _c_p]),
+    "tw_qs_rbf_cost_f32": (_c_i, [_c_p, _c_p] + [_c_i] * 4 + [_c_d, _c_p, _c_p]),
+    "tw_qs_rbf_cost_f64": (_c_i, [_c_p, _c_p] + [_c_i] * 4 + [_c_d, _c_p, _c_p]),
+    "tw_qs_rbf_cost_grad_f32": (_c_i, [_c_p] * 3 + [_c_i] * 4 + [_c_d] + [_c_p] * 3),
+    "tw_qs_rbf_cost_grad_f64": (_c_i, [_c_p] * 3 + [_c_i] * 4 + [_c_d] + [_c_p] * 3),
     "tw_fvm_softmin_f32": (_c_i, [_c_p, _c_i, _c_i, _c_i, _c_d, _c_p, _c_p]),
     "tw_fvm_softmin_f64": (_c_i, [_c_p, _c_i, _c_i, _c_i, _c_d, _c_p, _c_p]),
     "tw_fvm_softmin_backward_f32": (_c_i, [_c_p, _c_p, _c_i, _c_i, _c_i, _c_d, _c_p, _c_p]),

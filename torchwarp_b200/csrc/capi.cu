@@ -162,6 +162,10 @@ int qs_cost(const T*, const T*, int, int, int, int, int, T*, cudaStream_t);
 template <typename T>
 int qs_grad(const T*, const T*, const T*, const T*, int, int, int, int, int, T*, T*, cudaStream_t);
 template <typename T>
+int qs_rbf_cost(const T*, const T*, int, int, int, int, double, T*, cudaStream_t);
+template <typename T>
+int qs_rbf_grad(const T*, const T*, const T*, int, int, int, int, double, T*, T*, cudaStream_t);
+template <typename T>
 int fvm_softmin(const T*, int, int, int, double, T*, cudaStream_t);
 template <typename T>
 int fvm_softmin_bwd(const T*, const T*, int, int, int, double, T*, cudaStream_t);
@@ -347,6 +351,26 @@ int tw_udtw_features_grad_f64(const double* X, const double* Y, const double* vx
       return set_error(kInvalid, "tw_qs_cost_grad: null pointer");                             \
     return qs_grad<T>(query, support, cost, d_cost, B, R, U, D, metric, d_query, d_support,    \
                       (cudaStream_t)stream);                                                     \
+  }                                                                                             \
+  int tw_qs_rbf_cost_##SUF(const T* query, const T* support, int B, int R, int U, int D,       \
+                           double sigma, T* cost, void* stream) {                               \
+    g_err[0] = 0;                                                                               \
+    if (B < 0 || R <= 0 || U <= 0 || D <= 0 || !(sigma > 0))                                   \
+      return set_error(kInvalid, "tw_qs_rbf_cost: invalid arguments");                         \
+    if (B && (!query || !support || !cost))                                                     \
+      return set_error(kInvalid, "tw_qs_rbf_cost: null pointer");                              \
+    return qs_rbf_cost<T>(query, support, B, R, U, D, sigma, cost, (cudaStream_t)stream);      \
+  }                                                                                             \
+  int tw_qs_rbf_cost_grad_##SUF(const T* query, const T* support, const T* d_cost, int B,      \
+                                int R, int U, int D, double sigma, T* d_query, T* d_support,    \
+                                void* stream) {                                                 \
+    g_err[0] = 0;                                                                               \
+    if (B < 0 || R <= 0 || U <= 0 || D <= 0 || !(sigma > 0))                                   \
+      return set_error(kInvalid, "tw_qs_rbf_cost_grad: invalid arguments");                    \
+    if (B && (!query || !support || !d_cost || !d_query || !d_support))                        \
+      return set_error(kInvalid, "tw_qs_rbf_cost_grad: null pointer");                         \
+    return qs_rbf_grad<T>(query, support, d_cost, B, R, U, D, sigma, d_query, d_support,       \
+                          (cudaStream_t)stream);                                                 \
   }                                                                                             \
   int tw_fvm_softmin_##SUF(const T* cost, int B, int Kf, int TU, double gamma, T* temporal,    \
                            void* stream) {                                                      \

@@ -648,6 +648,133 @@ int qs_grad(const T* q, const T* s, const T* cost, const T* dcost, int B, int Rr
   return check_launch<T>("query/support gradient");
 }
 
+// ------------------------------------------------------------ rbf cost
+// cost_ru = sum_d [2 - 2 exp(-sigma (q_rd - s_ud)^2)] (jeanie/distances.py:41-51),
+// computed without the [R, U, D] difference tensor the PyTorch form builds.
+// Each dimension adds -2 expm1(-sigma delta^2), which is 2 - 2 e^(-sigma delta^2)
+// without cancellation for close frames.  Same chunking as qs_cost_kernel: CU
+// support frames in shared memory, one query row per thread.
+template <typename T>
+__global__ void __launch_bounds__(JT) qs_rbf_cost_kernel(const T* __restrict__ q,
+                                                         const T* __restrict__ s, int Rr, int U,
+                                                         int D, T sigma, T* __restrict__ cost) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  T* ss = reinterpret_cast<T*>(smem_raw);  // [CU][D]
+  const int b = blockIdx.y;
+  const T* qb = q + (long long)b * Rr * D;
+  const T* sb = s + (long long)b * U * D;
+  for (int u0 = 0; u0 < U; u0 += CU) {
+    const int nu = min(CU, U - u0);
+    __syncthreads();
+    for (int e = threadIdx.x; e < CU * D; e += JT)
+      ss[e] = e < nu * D ? sb[(long long)u0 * D + e] : T(0);
+    __syncthreads();
+    for (int r = blockIdx.x * JT + threadIdx.x; r < Rr; r += gridDim.x * JT) {
+      const T* qr = qb + (long long)r * D;
+      T acc[CU];
+#pragma unroll
+      for (int u = 0; u < CU; ++u) acc[u] = T(0);
+      for (int d = 0; d < D; ++d) {
+        const T v = qr[d];
+#pragma unroll
+        for (int u = 0; u < CU; ++u) {
+          const T dl = v - ss[u * D + d];
+          acc[u] -= expm1(-sigma * dl * dl);
+        }
+      }
+      T* cr = cost + ((long long)b * Rr + r) * U + u0;
+#pragma unroll
+      for (int u = 0; u < CU; ++u) {
+        if (u >= nu) break;
+        cr[u] = T(2) * acc[u];
+      }
+    }
+  }
+}
+
+// d_cost -> d_query: dq_rd = 4 sigma sum_u dcost_ru (q_rd - s_ud) e^(-sigma (q_rd - s_ud)^2).
+// One thread per (pair, row, feature), features fastest (coalesced q, s, dq;
+// the row's dcost values are shared by the warp).
+template <typename T>
+__global__ void __launch_bounds__(256) qs_rbf_dq_kernel(const T* __restrict__ q,
+                                                        const T* __restrict__ s,
+                                                        const T* __restrict__ dcost, int B,
+                                                        int Rr, int U, int D, T sigma,
+                                                        T* __restrict__ dq) {
+  const long long n = (long long)B * Rr * D;
+  for (long long i = blockIdx.x * 256ll + threadIdx.x; i < n; i += (long long)gridDim.x * 256) {
+    const int d = (int)(i % D);
+    const long long br = i / D;  // b * Rr + r
+    const int b = (int)(br / Rr);
+    const T v = q[i];
+    const T* g = dcost + br * U;
+    const T* sb = s + (long long)b * U * D + d;
+    T acc = T(0);
+    for (int u = 0; u < U; ++u) {
+      const T dl = v - sb[(long long)u * D];
+      acc += g[u] * dl * exp(-sigma * dl * dl);
+    }
+    dq[i] = T(4) * sigma * acc;
+  }
+}
+
+// d_cost -> d_support: ds_ud = -4 sigma sum_r dcost_ru (q_rd - s_ud) e^(-sigma (q_rd - s_ud)^2),
+// one thread per (pair, support frame, feature), rows summed in order.
+template <typename T>
+__global__ void __launch_bounds__(256) qs_rbf_ds_kernel(const T* __restrict__ q,
+                                                        const T* __restrict__ s,
+                                                        const T* __restrict__ dcost, int B,
+                                                        int Rr, int U, int D, T sigma,
+                                                        T* __restrict__ ds) {
+  const long long n = (long long)B * U * D;
+  for (long long i = blockIdx.x * 256ll + threadIdx.x; i < n; i += (long long)gridDim.x * 256) {
+    const int d = (int)(i % D);
+    const long long bu = i / D;  // b * U + u
+    const int b = (int)(bu / U);
+    const int u = (int)(bu - (long long)b * U);
+    const T sv = s[i];
+    const T* qb = q + (long long)b * Rr * D + d;
+    const T* g = dcost + (long long)b * Rr * U + u;
+    T acc = T(0);
+    for (int r = 0; r < Rr; ++r) {
+      const T dl = qb[(long long)r * D] - sv;
+      acc += g[(long long)r * U] * dl * exp(-sigma * dl * dl);
+    }
+    ds[i] = -T(4) * sigma * acc;
+  }
+}
+
+template <typename T>
+int qs_rbf_cost(const T* q, const T* s, int B, int Rr, int U, int D, double sigma, T* cost,
+                cudaStream_t st) {
+  if (B == 0 || Rr == 0 || U == 0) return kOk;
+  const size_t smem = (size_t)CU * D * sizeof(T);
+  if (smem > 200 * 1024) return set_error(kUnsupported, "feature dimension %d too large", D);
+  auto kern = qs_rbf_cost_kernel<T>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      cudaSuccess)
+    return set_error(kLaunch, "rbf cost: shared memory");
+  int gx = (Rr + JT - 1) / JT;
+  gx = gx > 64 ? 64 : gx;
+  dim3 grid(gx, B);
+  kern<<<grid, JT, smem, st>>>(q, s, Rr, U, D, (T)sigma, cost);
+  return check_launch<T>("rbf cost");
+}
+
+template <typename T>
+int qs_rbf_grad(const T* q, const T* s, const T* dcost, int B, int Rr, int U, int D,
+                double sigma, T* dq, T* ds, cudaStream_t st) {
+  if (B == 0) return kOk;
+  auto blocks = [](long long n) {
+    long long g = (n + 255) / 256;
+    return (int)(g < 1 ? 1 : (g > 148 * 32 ? 148 * 32 : g));
+  };
+  const long long nq = (long long)B * Rr * D, ns = (long long)B * U * D;
+  if (nq > 0) qs_rbf_dq_kernel<T><<<blocks(nq), 256, 0, st>>>(q, s, dcost, B, Rr, U, D, (T)sigma, dq);
+  if (ns > 0) qs_rbf_ds_kernel<T><<<blocks(ns), 256, 0, st>>>(q, s, dcost, B, Rr, U, D, (T)sigma, ds);
+  return check_launch<T>("rbf cost gradient");
+}
+
 template <typename T>
 int fvm_softmin(const T* cost, int B, int Kf, int TU, double gamma, T* temporal, cudaStream_t st) {
   if (B == 0 || TU == 0) return kOk;
@@ -675,6 +802,10 @@ int fvm_softmin_bwd(const T* cost, const T* dtemp, int B, int Kf, int TU, double
   template int qs_cost<T>(const T*, const T*, int, int, int, int, int, T*, cudaStream_t);      \
   template int qs_grad<T>(const T*, const T*, const T*, const T*, int, int, int, int, int, T*, \
                           T*, cudaStream_t);                                                     \
+  template int qs_rbf_cost<T>(const T*, const T*, int, int, int, int, double, T*,             \
+                              cudaStream_t);                                                     \
+  template int qs_rbf_grad<T>(const T*, const T*, const T*, int, int, int, int, double, T*, T*, \
+                              cudaStream_t);                                                     \
   template int fvm_softmin<T>(const T*, int, int, int, double, T*, cudaStream_t);              \
   template int fvm_softmin_bwd<T>(const T*, const T*, int, int, int, double, T*, cudaStream_t);
 TW_INST(float)

@@ -178,6 +178,81 @@ class QSCost(torch.autograd.Function):
         return dq, ds, None
 
 
+# ------------------------------------------------------------ rbf cost
+
+@torch.library.custom_op("torchwarp_b200::qs_rbf_cost", mutates_args=())
+def qs_rbf_cost(query: Tensor, support: Tensor, sigma: float) -> Tensor:
+    """cost [B,R,U] = sum_d [2 - 2 exp(-sigma (q - s)^2)], without the
+    [B,R,U,D] difference tensor (jeanie/distances.py:41-51)."""
+    nat.require_cuda(query, support)
+    B, Rr, D = query.shape
+    U = support.shape[1]
+    query, support = query.contiguous(), support.contiguous()
+    cost = query.new_empty(B, Rr, U)
+    if B and Rr and U:
+        with torch.cuda.device(query.device):
+            nat.check(nat.call("qs_rbf_cost", _fn("tw_qs_rbf_cost", query.dtype),
+                               nat.ptr(query), nat.ptr(support), B, Rr, U, D, float(sigma),
+                               nat.ptr(cost), nat.stream_of(query)), "tw_qs_rbf_cost")
+    return cost
+
+
+@qs_rbf_cost.register_fake
+def _(query, support, sigma):
+    return query.new_empty(query.shape[0], query.shape[1], support.shape[1])
+
+
+@torch.library.custom_op("torchwarp_b200::qs_rbf_cost_backward", mutates_args=())
+def qs_rbf_cost_backward(query: Tensor, support: Tensor, d_cost: Tensor,
+                         sigma: float) -> Tuple[Tensor, Tensor]:
+    nat.require_cuda(query, support)
+    B, Rr, D = query.shape
+    U = support.shape[1]
+    query, support = query.contiguous(), support.contiguous()
+    d_cost = d_cost.to(query.dtype).contiguous()
+    dq, ds = torch.empty_like(query), torch.empty_like(support)
+    if B and Rr and U:
+        with torch.cuda.device(query.device):
+            nat.check(nat.call("qs_rbf_cost_grad", _fn("tw_qs_rbf_cost_grad", query.dtype),
+                               nat.ptr(query), nat.ptr(support), nat.ptr(d_cost), B, Rr, U, D,
+                               float(sigma), nat.ptr(dq), nat.ptr(ds), nat.stream_of(query)),
+                      "tw_qs_rbf_cost_grad")
+    elif B:
+        dq.zero_()
+        ds.zero_()
+    return dq, ds
+
+
+@qs_rbf_cost_backward.register_fake
+def _(query, support, d_cost, sigma):
+    return torch.empty_like(query), torch.empty_like(support)
+
+
+_register_autocast(qs_rbf_cost)
+_register_autocast(qs_rbf_cost_backward)
+
+
+class QSRbfCost(torch.autograd.Function):
+    """(query [B,R,D], support [B,U,D]) -> rbf cost [B,R,U]."""
+
+    @staticmethod
+    def forward(query, support, sigma):
+        return qs_rbf_cost(query, support, sigma)
+
+    @staticmethod
+    def setup_context(ctx, inputs, output):
+        query, support, sigma = inputs
+        ctx.save_for_backward(query, support)
+        ctx.sigma = sigma
+
+    @staticmethod
+    @torch.autograd.function.once_differentiable
+    def backward(ctx, g):
+        query, support = ctx.saved_tensors
+        dq, ds = qs_rbf_cost_backward(query, support, g, ctx.sigma)
+        return dq, ds, None
+
+
 # ------------------------------------------------------------ FVM soft-min
 
 @torch.library.custom_op("torchwarp_b200::fvm_softmin", mutates_args=())

@@ -7,8 +7,10 @@ Two layouts:
   two sequences: x [..., N, D], y [..., M, D] (same rank) -> [..., N, M]
 The (squared) Euclidean distances run in the native query/support cost kernel
 (GEMM form |q|^2 + |s|^2 - 2 q.s, clamped at 0; the Euclidean root has zero
-gradient at 0).  ``rbf_cost`` has no GEMM form and stays a PyTorch
-expression, as in the reference.
+gradient at 0).  ``rbf_cost`` has no GEMM form; it runs in its own native
+kernel, which sums over the features per (frame, frame) pair instead of
+materialising the [..., T, U, D] difference tensor of the reference's
+PyTorch expression.
 """
 
 import torch
@@ -25,8 +27,9 @@ def _check(query, support):
     return support.unsqueeze(-3) if query.ndim > support.ndim else support
 
 
-def _native_cost(query, support, metric):
-    """Flatten to query rows [L, R, D] against supports [L, U, D], run the kernel."""
+def _native_cost(query, support, metric, sigma=None):
+    """Flatten to query rows [L, R, D] against supports [L, U, D], run the kernel
+    (the rbf kernel when sigma is given)."""
     dtype = torch.promote_types(query.dtype, support.dtype)
     if dtype not in (torch.float32, torch.float64):
         dtype = torch.float32
@@ -39,12 +42,18 @@ def _native_cost(query, support, metric):
         U = support.shape[-2]
         q = query.to(dtype).expand(*lead, K, T, D).reshape(-1, K * T, D)
         sp = support.to(dtype).expand(*lead, U, D).reshape(-1, U, D)
-        out = _ops.QSCost.apply(q, sp, metric)
+        out = _apply(q, sp, metric, sigma)
         return out.reshape(*lead, K, T, U)
     N, M = query.shape[-2], support.shape[-2]
     q = query.to(dtype).expand(*lead, N, D).reshape(-1, N, D)
     sp = support.to(dtype).expand(*lead, M, D).reshape(-1, M, D)
-    return _ops.QSCost.apply(q, sp, metric).reshape(*lead, N, M)
+    return _apply(q, sp, metric, sigma).reshape(*lead, N, M)
+
+
+def _apply(q, sp, metric, sigma):
+    if sigma is not None:
+        return _ops.QSRbfCost.apply(q, sp, float(sigma))
+    return _ops.QSCost.apply(q, sp, metric)
 
 
 def squared_euclidean_cost(query: torch.Tensor, support: torch.Tensor) -> torch.Tensor:
@@ -62,11 +71,10 @@ def euclidean_cost(query: torch.Tensor, support: torch.Tensor) -> torch.Tensor:
 def rbf_cost(query: torch.Tensor, support: torch.Tensor, sigma: float = 0.5) -> torch.Tensor:
     """RBF-style base cost d(x,y) = sum_d [2 - 2 exp(-sigma (x_d - y_d)^2)].
 
-    This per-dimension form cannot be written as a matmul, so it
-    materialises the [..., K, T, U, D] difference tensor.
+    The per-dimension form has no matmul; the native kernel sums it per
+    (frame, frame) pair without the [..., K, T, U, D] difference tensor.
     """
     if sigma <= 0:
         raise ValueError("sigma must be > 0")
-    s = _check(query, support)
-    diff = query.unsqueeze(-2) - s.unsqueeze(-3)
-    return (2.0 - 2.0 * torch.exp(-sigma * diff.pow(2))).sum(dim=-1)
+    _check(query, support)
+    return _native_cost(query, support, None, sigma)

@@ -3,9 +3,8 @@
 Semantics of hibana2077/torchwarp src/torchwarp/jeanie/functional.py:28-175
 (Wang et al., IJCV 2024, Algorithm 1 and its two-axis extension): every
 entry point takes a batch; shifts are clamped to K-1; a 4-D query/cost has one
-viewpoint axis.  The DP, the (squared) Euclidean cost and their backward
-passes run in the native library; ``metric="rbf"`` builds the cost in
-PyTorch (as the reference) and runs the native DP on it.
+viewpoint axis.  The DP, the (squared) Euclidean and rbf costs and their
+backward passes run in the native library.
 """
 
 import torch
