@@ -116,7 +116,7 @@ def _rbf_definition(q, s, sigma):
 @pytest.mark.parametrize("qshape,sshape,sigma", [
     ((2, 5, 3), (2, 7, 3), 0.5),             # two sequences
     ((3, 4, 6, 8), (3, 37, 8), 0.3),         # JEANIE layout, U across support chunks
-    ((2, 3, 2, 5, 7), (2, 1, 4, 9, 7), 1.2),  # FVM with support-side viewpoints (broadcast)
+    ((2, 3, 1, 5, 7), (2, 1, 4, 9, 7), 1.2),  # FVM with support-side viewpoints (broadcast)
     ((2, 15, 10, 256), (2, 10, 256), 0.5),   # cfg3 feature size
 ])
 def test_rbf_cost_native_vs_definition(tw, qshape, sshape, sigma):
