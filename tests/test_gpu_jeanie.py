@@ -261,14 +261,19 @@ def test_features_vs_oracle(tw, orc, metric):
     _close(ss.grad, ods, atol=1e-9, rtol=1e-8)
 
 
-def test_fvm_support_viewpoints(tw, orc):
+@pytest.mark.parametrize("metric", G.METRICS)
+@pytest.mark.parametrize("qshape,sshape", [((2, 4, 6, 5), (2, 3, 7, 5)),
+                                           ((2, 2, 3, 6, 5), (2, 3, 2, 7, 5))])
+def test_fvm_support_viewpoints(tw, orc, metric, qshape, sshape):
+    """Support-side viewpoints: the cost of every (query, support) viewpoint
+    pair comes from one query/support launch over all K' U support frames."""
     g = torch.Generator().manual_seed(7)
-    q = torch.randn(2, 4, 6, 5, generator=g, dtype=torch.float64)
-    s = torch.randn(2, 3, 7, 5, generator=g, dtype=torch.float64)
+    q = torch.randn(*qshape, generator=g, dtype=torch.float64)
+    s = torch.randn(*sshape, generator=g, dtype=torch.float64)
     qq, ss = _t(q).requires_grad_(), _t(s).requires_grad_()
-    d = tw.functional.fvm(qq, ss, gamma=0.1)
+    d = tw.functional.fvm(qq, ss, gamma=0.1, metric=metric)
     d.sum().backward()
-    od, odq, ods = orc.fvm(q.numpy(), s.numpy(), gamma=0.1)
+    od, odq, ods = orc.fvm(q.numpy(), s.numpy(), gamma=0.1, metric=metric)
     _close(d, od)
     _close(qq.grad, odq)
     _close(ss.grad, ods)

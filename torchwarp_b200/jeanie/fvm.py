@@ -45,6 +45,14 @@ def fvm(query, support, *, gamma=0.1, metric="euclidean", backend="auto"):
     if support.ndim == 3:
         cost = _METRICS[metric](q, support)                      # [B, K, T, U]
     else:
+        # Every (query viewpoint, support viewpoint) pair: all K' U support
+        # frames of a pair form one support set of the query/support kernel,
+        # [B, K T, K' U], instead of expanding the query K' times and the
+        # support K times; one permute of the (small) cost gives the
+        # reference's [B, K, K', T, U] (jeanie/fvm.py:62-66).
+        K = q.shape[1]
         s = support.reshape(B, -1, U, D)
-        cost = _METRICS[metric](q.unsqueeze(2), s.unsqueeze(1))  # [B, K, K', T, U]
+        Kp = s.shape[1]
+        full = _METRICS[metric](q.reshape(B, K * T, D), s.reshape(B, Kp * U, D))
+        cost = full.reshape(B, K, T, Kp, U).permute(0, 1, 3, 2, 4)
     return fvm_from_cost(cost, gamma=gamma, backend=backend)
