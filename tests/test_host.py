@@ -145,6 +145,10 @@ def test_softmin_is_torch_level():
     lambda: TF.jeanie(torch.rand(1, 2, 3, 4), torch.rand(1, 5, 4), gamma=0.1),
     lambda: TF.fvm_from_cost(torch.rand(1, 2, 3, 4), gamma=0.1),
     lambda: tw.euclidean_cost(torch.rand(2, 3, 4), torch.rand(2, 5, 4)),
+    lambda: tw.rbf_cost(torch.rand(2, 3, 4), torch.rand(2, 5, 4)),
+    lambda: TF.fvm(torch.rand(1, 2, 3, 4), torch.rand(1, 2, 5, 4), gamma=0.1, metric="rbf"),
+    lambda: torch.func.jvp(lambda c: TF.soft_dtw_from_cost(c, gamma=0.1),
+                           (torch.rand(1, 3, 4),), (torch.rand(1, 3, 4),)),
     lambda: tw.paths.optimal_path(torch.rand(1, 3, 4)),
 ])
 def test_no_cpu_fallback(call):
