@@ -151,3 +151,56 @@ def test_udtw_second_order_raises(tw):
     (dC,) = torch.autograd.grad((d + p).sum(), C, create_graph=True)
     with pytest.raises(RuntimeError):
         torch.autograd.grad(dC.sum(), C)
+
+
+def _fd_check(f, primals, tangents, eps=1e-6):
+    """torch.func.jvp against a float64 central difference."""
+    _, jvp = torch.func.jvp(f, primals, tangents)
+    plus = f(*[p + eps * t for p, t in zip(primals, tangents)])
+    minus = f(*[p - eps * t for p, t in zip(primals, tangents)])
+    _close(jvp, ((plus - minus) / (2 * eps)).cpu().numpy(), 1e-6, 1e-6)
+
+
+def _rn(g, *shape):
+    return torch.randn(*shape, generator=g, dtype=torch.float64).to(DEV)
+
+
+@pytest.mark.parametrize("case", ["jeanie_cost", "jeanie_euclidean", "jeanie_sqeuclidean",
+                                  "fvm_cost", "fvm_features", "fvm_support_viewpoints"])
+def test_jeanie_fvm_jvp(tw, case):
+    """Forward mode of JEANIE and FVM: native backward weights (JEANIE DP,
+    FVM soft-min), the cost's tangent and the soft-DTW jvp, against central
+    differences."""
+    g = torch.Generator().manual_seed(len(case))
+    TF = tw.functional
+    if case == "jeanie_cost":
+        c = torch.rand(2, 3, 2, 6, 7, generator=g, dtype=torch.float64).to(DEV)
+        _fd_check(lambda x: TF.jeanie_from_cost(x, gamma=0.1, max_shift=1), (c,), (_rn(g, *c.shape),))
+    elif case.startswith("jeanie_"):
+        metric = case.split("_")[1]
+        q, s = _rn(g, 2, 3, 2, 6, 5), _rn(g, 2, 7, 5)
+        _fd_check(lambda a, b: TF.jeanie(a, b, gamma=0.1, max_shift=1, metric=metric), (q, s),
+                  (_rn(g, *q.shape), _rn(g, *s.shape)))
+    elif case == "fvm_cost":
+        c = torch.rand(2, 3, 2, 6, 7, generator=g, dtype=torch.float64).to(DEV)
+        _fd_check(lambda x: TF.fvm_from_cost(x, gamma=0.1), (c,), (_rn(g, *c.shape),))
+    elif case == "fvm_features":
+        q, s = _rn(g, 2, 4, 6, 5), _rn(g, 2, 7, 5)
+        _fd_check(lambda a, b: TF.fvm(a, b, gamma=0.1), (q, s), (_rn(g, *q.shape), _rn(g, *s.shape)))
+    else:
+        q, s = _rn(g, 2, 4, 6, 5), _rn(g, 2, 3, 7, 5)
+        _fd_check(lambda a, b: TF.fvm(a, b, gamma=0.1, metric="sqeuclidean"), (q, s),
+                  (_rn(g, *q.shape), _rn(g, *s.shape)))
+
+
+def _jeanie_with_accumulator(tw, x):
+    d, R = tw.functional.jeanie_from_cost(x, gamma=0.1, max_shift=1, return_accumulator=True)
+    return d + R.sum((1, 2, 3, 4))
+
+
+def test_jeanie_accumulator_jvp_raises(tw):
+    """A tangent for the JEANIE accumulator is not native: forward mode with
+    return_accumulator=True raises instead of returning a wrong tangent."""
+    c = torch.rand(1, 2, 2, 4, 5, dtype=torch.float64).to(DEV)
+    with pytest.raises(NotImplementedError):
+        torch.func.jvp(lambda x: _jeanie_with_accumulator(tw, x), (c,), (torch.ones_like(c),))

@@ -85,27 +85,49 @@ _register_autocast(jeanie_dp_backward)
 
 
 class JeanieDP(torch.autograd.Function):
-    """cost5 -> (out, R); both differentiable."""
+    """cost5 -> (out, R).  R (the accumulator) is differentiable when the
+    caller asked for it (keep_R), and an internal, non-differentiable output
+    otherwise.
+
+    Forward mode: the tangent of the distance along T is <dout/dcost, T>, from
+    one native backward with unit seeds.  A tangent for the accumulator would
+    need a tangent DP that is not native, so forward mode with keep_R raises."""
 
     @staticmethod
-    def forward(cost, s1, s2, gamma):
+    def forward(cost, s1, s2, gamma, keep_R):
         return jeanie_dp(cost, s1, s2, gamma)
 
     @staticmethod
     def setup_context(ctx, inputs, output):
-        cost, s1, s2, gamma = inputs
+        cost, s1, s2, gamma, keep_R = inputs
         ctx.set_materialize_grads(False)
+        if not keep_R:
+            ctx.mark_non_differentiable(output[1])
         ctx.save_for_backward(cost, output[1])
-        ctx.args = (s1, s2, gamma)
+        ctx.save_for_forward(cost, output[1])
+        ctx.args = (s1, s2, gamma, keep_R)
 
     @staticmethod
     @torch.autograd.function.once_differentiable
     def backward(ctx, g_out, g_R):
         cost, R = ctx.saved_tensors
-        s1, s2, gamma = ctx.args
+        s1, s2, gamma, _ = ctx.args
         if g_out is None:
             g_out = cost.new_zeros(cost.shape[0])
-        return jeanie_dp_backward(cost, R, g_out, g_R, s1, s2, gamma), None, None, None
+        return jeanie_dp_backward(cost, R, g_out, g_R, s1, s2, gamma), None, None, None, None
+
+    @staticmethod
+    def jvp(ctx, cost_t, _s1_t, _s2_t, _gamma_t, _keep_t):
+        cost, R = ctx.saved_tensors
+        s1, s2, gamma, keep_R = ctx.args
+        if keep_R:
+            raise NotImplementedError("forward mode through the JEANIE accumulator "
+                                      "(return_accumulator=True) is not implemented")
+        B = cost.shape[0]
+        if cost_t is None:
+            return cost.new_zeros(B), None
+        w = jeanie_dp_backward(cost, R, cost.new_ones(B), None, s1, s2, gamma)
+        return (w * cost_t).flatten(1).sum(1), None
 
 
 # ------------------------------------------------------ query/support cost
@@ -168,6 +190,7 @@ class QSCost(torch.autograd.Function):
     def setup_context(ctx, inputs, output):
         query, support, metric = inputs
         ctx.save_for_backward(query, support, output)
+        ctx.save_for_forward(query, support, output)
         ctx.metric = metric
 
     @staticmethod
@@ -176,6 +199,20 @@ class QSCost(torch.autograd.Function):
         query, support, cost = ctx.saved_tensors
         dq, ds = qs_cost_backward(query, support, cost, g, ctx.metric)
         return dq, ds, None
+
+    @staticmethod
+    def jvp(ctx, q_t, s_t, _metric_t):
+        """Tangent of the cost: sq' = 2 q.q' + 2 s.s' - 2 (q' s^T + q s'^T), zero
+        where the clamp holds sq at 0; the Euclidean root divides by 2 cost."""
+        q, s, cost = ctx.saved_tensors
+        q_t = torch.zeros_like(q) if q_t is None else q_t.to(q.dtype)
+        s_t = torch.zeros_like(s) if s_t is None else s_t.to(s.dtype)
+        sq_t = (2.0 * (q * q_t).sum(-1)[:, :, None] + 2.0 * (s * s_t).sum(-1)[:, None, :]
+                - 2.0 * (torch.bmm(q_t, s.transpose(1, 2)) + torch.bmm(q, s_t.transpose(1, 2))))
+        pos = cost > 0
+        if ctx.metric == 1:
+            sq_t = sq_t / (2.0 * torch.where(pos, cost, torch.ones_like(cost)))
+        return torch.where(pos, sq_t, torch.zeros_like(sq_t))
 
 
 # ------------------------------------------------------------ rbf cost
@@ -309,6 +346,7 @@ class FvmSoftmin(torch.autograd.Function):
     def setup_context(ctx, inputs, output):
         cost, gamma = inputs
         ctx.save_for_backward(cost)
+        ctx.save_for_forward(cost)
         ctx.gamma = gamma
 
     @staticmethod
@@ -316,3 +354,14 @@ class FvmSoftmin(torch.autograd.Function):
     def backward(ctx, g):
         (cost,) = ctx.saved_tensors
         return fvm_softmin_backward(cost, g, ctx.gamma), None
+
+    @staticmethod
+    def jvp(ctx, cost_t, _gamma_t):
+        """temporal' = sum over viewpoints of softmax weights * cost'; the
+        weights come from the native backward with a unit seed."""
+        (cost,) = ctx.saved_tensors
+        B, Kf, T, U = cost.shape
+        if cost_t is None:
+            return cost.new_zeros(B, T, U)
+        w = fvm_softmin_backward(cost, cost.new_ones(B, T, U), ctx.gamma)
+        return (w * cost_t.to(cost.dtype)).sum(1)
