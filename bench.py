@@ -50,7 +50,7 @@ ALGO_BYTES_PER_CELL = 8      # soft-DTW fwd+bwd: cost read + cost-gradient write
 # 8 B/cell of the step split between them), the cost builder's cost write,
 # each chain-rule launch's cost-gradient read.  Measured: DRAM read + write
 # of the full-size cfg5 launch (B=4096, N=M=1024, D=64) from a one-pass ncu
-# capture (profiles/soft_dtw_cfg5_launch_list.md), per cell, without the
+# capture of dram__bytes_read.sum + dram__bytes_write.sum, per cell, without the
 # feature bytes (X, Y read by the cost builder, dX or dY written by each
 # chain-rule side), which are added at the timed shape.
 CALLS = {
@@ -405,9 +405,9 @@ def run_reference(a):
 
 def _secondary(a):
     """One GPU, inputs resident, fwd+bwd per step, CUDA-event timed; the
-    configurations of the other SURVEY configs (seeded synthetic inputs with
-    their shapes) and the uDTW variant of cfg5.  Algorithmic bytes follow the
-    byte accounting of each configuration."""
+    reference's other benchmark configurations (seeded synthetic inputs with
+    their shapes), the uDTW variant of cfg5 and a training step.  Algorithmic
+    bytes follow the byte accounting of each configuration."""
     import torchwarp_b200 as twb
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
