@@ -204,3 +204,25 @@ def test_jeanie_accumulator_jvp_raises(tw):
     c = torch.rand(1, 2, 2, 4, 5, dtype=torch.float64).to(DEV)
     with pytest.raises(NotImplementedError):
         torch.func.jvp(lambda x: _jeanie_with_accumulator(tw, x), (c,), (torch.ones_like(c),))
+
+
+def test_features_double_backward_normalized(tw):
+    """normalize=True evaluates d(X, X): the double backward must give each
+    argument slot its own partial derivative.  Checked against a central
+    difference of the (native, first-order) gradient along (VX, VY)."""
+    g = torch.Generator().manual_seed(21)
+    X, Y = _rn(g, 2, 12, 3), _rn(g, 2, 14, 3)
+    VX, VY = _rn(g, 2, 12, 3), _rn(g, 2, 14, 3)
+    f = lambda a, b: tw.functional.soft_dtw(a, b, gamma=0.3, normalize=True)  # noqa: E731
+
+    def grads(a, b):
+        a, b = a.detach().requires_grad_(True), b.detach().requires_grad_(True)
+        return torch.autograd.grad(f(a, b).sum(), (a, b))
+
+    x, y = X.clone().requires_grad_(True), Y.clone().requires_grad_(True)
+    dX, dY = torch.autograd.grad(f(x, y).sum(), (x, y), create_graph=True)
+    hX, hY = torch.autograd.grad((dX * VX).sum() + (dY * VY).sum(), (x, y))
+    eps = 1e-6
+    gp, gm = grads(X + eps * VX, Y + eps * VY), grads(X - eps * VX, Y - eps * VY)
+    _close(hX, ((gp[0] - gm[0]) / (2 * eps)).cpu().numpy(), 1e-6, 1e-5)
+    _close(hY, ((gp[1] - gm[1]) / (2 * eps)).cpu().numpy(), 1e-6, 1e-5)

@@ -489,9 +489,14 @@ class SdtwFused(torch.autograd.Function):
         # the DP part goes through SdtwCostGrad, whose own backward is native;
         # autograd supplies the cost's second derivatives
         g = _zeros_if_none(g_r, X, X.shape[0]).to(X.dtype)
-        cost = _sqeuclid(X, Y)
+        # one view per argument slot: with X passed as both arguments
+        # (normalize=True computes d(X, X)) each slot gets its own partial
+        # derivative, not the total one twice
+        Xs = X.view_as(X) if X.requires_grad else X
+        Ys = Y.view_as(Y) if Y.requires_grad else Y
+        cost = _sqeuclid(Xs, Ys)
         s = SdtwCostGrad.apply(cost, saved, g, ctx.gamma, ctx.bandwidth)
-        wrt = [t for t in (X, Y) if t.requires_grad]
+        wrt = [t for t in (Xs, Ys) if t.requires_grad]
         grads = iter(torch.autograd.grad(cost, wrt, s, create_graph=True) if wrt else ())
         dX = next(grads) if X.requires_grad else None
         dY = next(grads) if Y.requires_grad else None
