@@ -72,3 +72,80 @@ SCALED_CASES = {
 def make(name):
     """(list of (tensor, requires_grad), kwargs) for a scaled case."""
     return SCALED_CASES[name]()
+
+
+# ------------------------------------------------------ benchmark configurations
+#
+# The five configurations of the benchmark, built as the measurement protocol
+# states: a generator seeded with the configuration's index, float64 draws in
+# the listed order, cast later.  cfg5 keeps its sequence shape (N = M = 1024,
+# D = 64, gamma = 0.01) with two pairs instead of 4096, so that the CPU
+# reference finishes in seconds; the per-pair arithmetic is the same.
+
+def _cfg1():
+    g = _g(1)
+    X, Y = torch.randn(64, 30, 8, generator=g, **f64), torch.randn(64, 40, 8, generator=g, **f64)
+    sx = torch.rand(64, 30, 1, generator=g, **f64) + 0.5
+    sy = torch.rand(64, 40, 1, generator=g, **f64) + 0.5
+    return [X, Y, sx, sy], dict(gamma=1.0, beta=1.0)
+
+
+def _cfg2():
+    g = _g(2)
+    X, Y = _znorm_walk(g, 500, 140), _znorm_walk(g, 500, 140)
+    return [X, Y], dict(gamma=0.1)
+
+
+def _cfg3():
+    g = _g(3)
+    q = torch.randn(1024, 15, 10, 256, generator=g, **f64)
+    s = torch.randn(1024, 10, 256, generator=g, **f64)
+    return [q, s], dict(gamma=0.1, max_shift=1, metric="euclidean")
+
+
+def _cfg4():
+    g = _g(4)
+    q = torch.randn(1024, 7, 7, 10, 256, generator=g, **f64)
+    s = torch.randn(1024, 10, 256, generator=g, **f64)
+    c = torch.randn(1024, 7, 7, 10, 10, generator=g, **f64).abs()
+    return [q, s, c], dict(gamma=0.1)
+
+
+def _cfg5(B=2):
+    g = _g(5)
+    X, Y = torch.randn(B, 1024, 64, generator=g, **f64), torch.randn(B, 1024, 64, generator=g, **f64)
+    return [X, Y], dict(gamma=0.01)
+
+
+def _cfg5_udtw(B=2):
+    g = _g(5)
+    X, Y = torch.randn(B, 1024, 64, generator=g, **f64), torch.randn(B, 1024, 64, generator=g, **f64)
+    sx = torch.rand(B, 1024, 1, generator=g, **f64) + 0.5
+    sy = torch.rand(B, 1024, 1, generator=g, **f64) + 0.5
+    return [X, Y, sx, sy], dict(gamma=0.01, beta=1.0)
+
+
+# name -> (builder, function, indices of the inputs the loss is differentiated
+# against).  The function names are those of torchwarp.functional.
+CONFIG_CASES = {
+    "cfg1_udtw": (_cfg1, "udtw", (0, 1, 2, 3)),
+    "cfg2_soft_dtw": (_cfg2, "soft_dtw", (0,)),
+    "cfg3_jeanie": (_cfg3, "jeanie", (0, 1)),
+    "cfg4_fvm": (lambda: (_cfg4()[0][:2], _cfg4()[1]), "fvm", (0, 1)),
+    "cfg4_fvm_from_cost": (lambda: (_cfg4()[0][2:], _cfg4()[1]), "fvm_from_cost", (0,)),
+    "cfg5_soft_dtw": (_cfg5, "soft_dtw", (0, 1)),
+    "cfg5_udtw": (_cfg5_udtw, "udtw", (0, 1, 2, 3)),
+}
+
+
+def config_loss(F, name, tensors, kwargs, **extra):
+    """The benchmark loss of a configuration through the functional API F
+    (the reference's or this package's): uDTW sums distance and penalty."""
+    fn = getattr(F, CONFIG_CASES[name][1])
+    out = fn(*tensors, **kwargs, **extra)
+    if isinstance(out, tuple):
+        d, p = out
+        loss = d + p
+        # cfg1's loss is the batch mean; every other loss sums the pairs
+        return d, (loss.mean() if name == "cfg1_udtw" else loss.sum())
+    return out, out.sum()

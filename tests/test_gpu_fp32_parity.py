@@ -1,0 +1,94 @@
+"""float32 accuracy per benchmark configuration, against the reference's float32.
+
+The reference's own float32 misses a fixed gradient tolerance against its
+float64 at small gamma and long sequences (the soft-min weights
+exp(-delta/gamma) amplify the rounding of the accumulated DP value).  Its
+error per configuration, measured on the same seeded inputs by
+``tests/golden/make_fp32_bars.py`` with the reference's PyTorch backend, is
+the bar:
+
+* the float64 path of this package is first held to the reference's float64
+  on the configuration itself: forward values at rtol 1e-9 and a subsample
+  plus checksums of each gradient at rtol 1e-8;
+* that float64 result is then the truth for this package's float32 path,
+  whose errors (forward max relative error, gradient max-normalised error
+  max|g32 - g64| / max|g64|, fraction of elements outside 1e-4 rel + 1e-6 abs)
+  must not exceed the reference float32's on the same configuration, with
+  the north star's tolerances (1e-5 forward, 1e-4 max-normalised gradient)
+  as the floor of each bar; the fraction of elements outside 1e-4 / 1e-6
+  gets a floor of 0.1 % of the elements (a handful of elements at cfg1).
+
+``TW_FP32_REPORT=<path>`` appends one JSON line per configuration with both
+sets of figures.
+"""
+
+import json
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE / "golden"))
+
+import inputs as I  # noqa: E402
+from make_fp32_bars import error_metrics  # noqa: E402
+
+DEV = "cuda"
+BARS = np.load(HERE / "golden" / "fp32_bars.npz")
+
+
+@pytest.fixture(scope="module")
+def tw():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    import torchwarp_b200
+    return torchwarp_b200
+
+
+def _run(tw, name, dtype):
+    build, _, wrt = I.CONFIG_CASES[name]
+    tensors, kw = build()
+    xs = [t.to(dtype).to(DEV).requires_grad_(k in wrt) for k, t in enumerate(tensors)]
+    d, loss = I.config_loss(tw.functional, name, xs, kw)
+    grads = torch.autograd.grad(loss, [xs[k] for k in wrt])
+    return (d.detach().double().cpu().numpy(), [g.double().cpu().numpy() for g in grads])
+
+
+def _bar(name, key, i=None):
+    k = name + "::" + key + ("" if i is None else "::{}".format(i))
+    return float(BARS[k])
+
+
+@pytest.mark.parametrize("name", list(I.CONFIG_CASES))
+def test_fp32_error_within_reference_bar(tw, name):
+    v64, g64 = _run(tw, name, torch.float64)
+    # this package's float64 against the reference's float64
+    np.testing.assert_allclose(v64, BARS[name + "::value64"], rtol=1e-9, atol=1e-10)
+    for i, g in enumerate(g64):
+        stride = int(BARS["{}::gstride::{}".format(name, i)])
+        want = BARS["{}::gsub64::{}".format(name, i)]
+        scale = float(BARS["{}::gsum64::{}".format(name, i)][2])
+        np.testing.assert_allclose(g.reshape(-1)[::stride], want, rtol=1e-8, atol=1e-10 * scale)
+        s = BARS["{}::gsum64::{}".format(name, i)]
+        np.testing.assert_allclose([g.sum(), (g * g).sum()], s[:2], rtol=1e-8,
+                                   atol=1e-10 * scale * g.size)
+    v32, g32 = _run(tw, name, torch.float32)
+    fwd, mn, fail = error_metrics(v32, v64, g32, g64)
+    rec = {"case": name, "fwd_rel": fwd, "maxnorm": mn, "fail": fail,
+           "ref_fwd_rel": _bar(name, "fwd_rel"),
+           "ref_maxnorm": [_bar(name, "maxnorm", i) for i in range(len(g64))],
+           "ref_fail": [_bar(name, "fail", i) for i in range(len(g64))]}
+    path = os.environ.get("TW_FP32_REPORT")
+    if path:
+        with open(path, "a") as f:
+            f.write(json.dumps(rec) + "\n")
+    assert fwd <= max(rec["ref_fwd_rel"], 1e-5), rec
+    for i in range(len(g64)):
+        assert mn[i] <= max(rec["ref_maxnorm"][i], 1e-4), rec
+        assert fail[i] <= max(rec["ref_fail"][i], 1e-3), rec
