@@ -14,8 +14,10 @@ autograd Functions :299-447) with native sm_100a kernels only:
 * ``torchwarp_b200::fvm_softmin(cost, gamma)`` -> temporal [B, T, U] and its
   backward (FVM's viewpoint soft-min).
 
-Each op has a fake implementation (torch.compile) and runs in float32 under
-autocast; the backward ops are first-order only.
+Each op has a fake implementation (torch.compile), a vmap rule that merges
+the vmapped dimension with the pairs (``torchwarp_b200._vmap``), and runs in
+float32 under autocast; the autograd Functions let torch.func generate their
+vmap rules from these.  The backward ops are first-order only.
 """
 
 from typing import Optional, Tuple
@@ -24,6 +26,7 @@ import torch
 from torch import Tensor
 
 from .. import _native as nat
+from .._vmap import register_fold_rule
 
 
 def _register_autocast(op):
@@ -82,6 +85,8 @@ def _(cost, R, grad_out, grad_R, s1, s2, gamma):
 
 _register_autocast(jeanie_dp)
 _register_autocast(jeanie_dp_backward)
+register_fold_rule(jeanie_dp)
+register_fold_rule(jeanie_dp_backward)
 
 
 class JeanieDP(torch.autograd.Function):
@@ -92,6 +97,8 @@ class JeanieDP(torch.autograd.Function):
     Forward mode: the tangent of the distance along T is <dout/dcost, T>, from
     one native backward with unit seeds.  A tangent for the accumulator would
     need a tangent DP that is not native, so forward mode with keep_R raises."""
+
+    generate_vmap_rule = True
 
     @staticmethod
     def forward(cost, s1, s2, gamma, keep_R):
@@ -177,10 +184,14 @@ def _(query, support, cost, d_cost, metric):
 
 _register_autocast(qs_cost)
 _register_autocast(qs_cost_backward)
+register_fold_rule(qs_cost)
+register_fold_rule(qs_cost_backward)
 
 
 class QSCost(torch.autograd.Function):
     """(query [B,R,D], support [B,U,D]) -> cost [B,R,U]."""
+
+    generate_vmap_rule = True
 
     @staticmethod
     def forward(query, support, metric):
@@ -267,10 +278,14 @@ def _(query, support, d_cost, sigma):
 
 _register_autocast(qs_rbf_cost)
 _register_autocast(qs_rbf_cost_backward)
+register_fold_rule(qs_rbf_cost)
+register_fold_rule(qs_rbf_cost_backward)
 
 
 class QSRbfCost(torch.autograd.Function):
     """(query [B,R,D], support [B,U,D]) -> rbf cost [B,R,U]."""
+
+    generate_vmap_rule = True
 
     @staticmethod
     def forward(query, support, sigma):
@@ -333,10 +348,14 @@ def _(cost, d_temporal, gamma):
 
 _register_autocast(fvm_softmin)
 _register_autocast(fvm_softmin_backward)
+register_fold_rule(fvm_softmin)
+register_fold_rule(fvm_softmin_backward)
 
 
 class FvmSoftmin(torch.autograd.Function):
     """cost [B,Kf,T,U] -> temporal [B,T,U]."""
+
+    generate_vmap_rule = True
 
     @staticmethod
     def forward(cost, gamma):

@@ -24,8 +24,11 @@ implementation:
   forward.
 
 Each op has a fake (meta) implementation for torch.compile, a vmap rule that
-folds the vmapped dimension into the batch, and runs in float32 under
-autocast.  First-order reverse mode calls the native backward.
+merges the vmapped dimension with the pairs (``torchwarp_b200._vmap``; the
+saved stream's size is a multiple of the pair count so that it splits per
+slice), and runs in float32 under autocast.  The autograd Functions let
+torch.func generate their vmap rules from these.  First-order reverse mode
+calls the native backward.
 
 Higher-order derivatives of soft-DTW (no penalty), on a cost or on features,
 are native too.  Differentiating through the backward (create_graph=True) is
@@ -44,6 +47,7 @@ import torch
 from torch import Tensor
 
 from .. import _native as nat
+from .._vmap import register_fold_rule, round_to_pairs
 
 # ------------------------------------------------------------------ helpers
 
@@ -57,22 +61,6 @@ def _ws_bytes(B, N, M, dtype, has_p):
     return int(nat.lib().tw_sdtw_workspace_bytes(B, N, M,
                                                  torch.empty((), dtype=dtype).element_size(),
                                                  int(has_p)))
-
-
-def _register_vmap(op, n_tensors):
-    """vmap rule: fold the vmapped dimension into the leading batch dim."""
-    def rule(info, in_dims, *args):
-        V = info.batch_size
-        folded = []
-        for k, (a, d) in enumerate(zip(args, in_dims)):
-            if k < n_tensors and isinstance(a, Tensor):
-                a = a.unsqueeze(0).expand(V, *a.shape) if d is None else a.movedim(d, 0)
-                a = a.reshape(V * a.shape[1], *a.shape[2:]).contiguous()
-            folded.append(a)
-        outs = op(*folded)
-        outs = tuple(o.reshape(V, o.shape[0] // V, *o.shape[1:]) for o in outs)
-        return outs, tuple(0 for _ in outs)
-    op.register_vmap(rule)
 
 
 def _register_autocast(op):
@@ -91,7 +79,7 @@ def _dp_forward(cost, penalty, gamma, bandwidth):
     if B == 0:
         return out_r, out_p, torch.empty(0, dtype=torch.uint8, device=cost.device)
     with torch.cuda.device(cost.device):
-        sb = _saved_bytes(B, N, M, cost.dtype, has_p)
+        sb = round_to_pairs(_saved_bytes(B, N, M, cost.dtype, has_p), B)
         wb = _ws_bytes(B, N, M, cost.dtype, has_p)
         saved = torch.empty(sb, dtype=torch.uint8, device=cost.device)
         ws = torch.empty(wb, dtype=torch.uint8, device=cost.device)
@@ -138,7 +126,7 @@ def sdtw_dp(cost: Tensor, penalty: Optional[Tensor], gamma: float,
 @sdtw_dp.register_fake
 def _(cost, penalty, gamma, bandwidth):
     B, N, M = cost.shape
-    nbytes = _saved_bytes(B, N, M, cost.dtype, penalty is not None) if B else 0
+    nbytes = round_to_pairs(_saved_bytes(B, N, M, cost.dtype, penalty is not None), B) if B else 0
     return (cost.new_empty(B), cost.new_empty(B),
             cost.new_empty(nbytes, dtype=torch.uint8))
 
@@ -158,6 +146,8 @@ def _(saved, grad_r, grad_p, N, M, gamma, has_penalty):
 
 _register_autocast(sdtw_dp)
 _register_autocast(sdtw_dp_backward)
+register_fold_rule(sdtw_dp, flat_out=(2,))
+register_fold_rule(sdtw_dp_backward, flat_in=(0,), placeholder_out=(1,))
 
 
 # ------------------------------------- cost built from the features, then DP
@@ -186,7 +176,7 @@ def udtw_fused(X: Tensor, Y: Tensor, vx: Optional[Tensor], vy: Optional[Tensor],
 @udtw_fused.register_fake
 def _(X, Y, vx, vy, gamma, beta, eps, bandwidth):
     B, N, M = X.shape[0], X.shape[1], Y.shape[1]
-    nbytes = _saved_bytes(B, N, M, X.dtype, vx is not None) if B else 0
+    nbytes = round_to_pairs(_saved_bytes(B, N, M, X.dtype, vx is not None), B) if B else 0
     return (X.new_empty(B), X.new_empty(B), X.new_empty(nbytes, dtype=torch.uint8),
             X.new_empty(B, N, M))
 
@@ -224,6 +214,8 @@ def _(X, Y, vx, vy, cost, saved, grad_r, grad_p, gamma, beta, eps):
 
 _register_autocast(udtw_fused)
 _register_autocast(udtw_fused_backward)
+register_fold_rule(udtw_fused, flat_out=(2,))
+register_fold_rule(udtw_fused_backward, flat_in=(5,))
 
 
 # ----------- soft-DTW from features: positivity mask instead of the saved cost
@@ -262,7 +254,7 @@ def sdtw_fused(X: Tensor, Y: Tensor, gamma: float, bandwidth: float) -> Tuple[Te
 @sdtw_fused.register_fake
 def _(X, Y, gamma, bandwidth):
     B, N, M = X.shape[0], X.shape[1], Y.shape[1]
-    nbytes = _saved_bytes(B, N, M, X.dtype, False) if B else 0
+    nbytes = round_to_pairs(_saved_bytes(B, N, M, X.dtype, False), B) if B else 0
     return (X.new_empty(B), X.new_empty(nbytes, dtype=torch.uint8),
             X.new_empty(B, _mask_words(M), _mask_rows(N), dtype=torch.int32))
 
@@ -303,6 +295,8 @@ def _(X, Y, mask, saved, grad_r, gamma):
 
 _register_autocast(sdtw_fused)
 _register_autocast(sdtw_fused_backward)
+register_fold_rule(sdtw_fused, flat_out=(1,))
+register_fold_rule(sdtw_fused_backward, flat_in=(3,))
 
 
 # ------------------------------------------------------- autograd Functions
@@ -326,6 +320,8 @@ class SdtwCostGrad(torch.autograd.Function):
     uDTW forward returns that value, which is the gradient for g.  The native
     uDTW backward seeded with (0, g) returns g * (d^2 d / dcost^2) V, which is
     the gradient for the cost.  A third derivative raises."""
+
+    generate_vmap_rule = True
 
     @staticmethod
     def forward(cost, saved, g, gamma, bandwidth):
@@ -362,6 +358,8 @@ def _dp_backward_once(ctx, saved, g_r, g_p):
 
 class DP(torch.autograd.Function):
     """(cost, penalty?) -> (distance, penalty_sum, saved)."""
+
+    generate_vmap_rule = True
 
     @staticmethod
     def forward(cost, penalty, gamma, bandwidth):
@@ -422,6 +420,8 @@ class DP(torch.autograd.Function):
 class Fused(torch.autograd.Function):
     """(X, Y, vx?, vy?) -> (distance, penalty_sum, saved, cost)."""
 
+    generate_vmap_rule = True
+
     @staticmethod
     def forward(X, Y, vx, vy, gamma, beta, eps, bandwidth):
         return udtw_fused(X, Y, vx, vy, gamma, beta, eps, bandwidth)
@@ -448,12 +448,27 @@ class Fused(torch.autograd.Function):
         return dX, dY, (dvx if has_p else None), (dvy if has_p else None), None, None, None, None
 
 
+class _full_fp32_matmul:
+    """Context in which float32 matmuls run in full float32 (no TF32), so the
+    cost rebuilt for a differentiable backward agrees with the native cost
+    kernel (3xTF32, float32 accuracy) whatever the caller's TF32 setting."""
+
+    def __enter__(self):
+        self.prev = torch.backends.cuda.matmul.allow_tf32
+        torch.backends.cuda.matmul.allow_tf32 = False
+
+    def __exit__(self, *exc):
+        torch.backends.cuda.matmul.allow_tf32 = self.prev
+
+
 def _sqeuclid(X, Y):
     """||x_i - y_j||^2 clamped at 0, the native cost's formula, as a
-    differentiable expression (its GEMM runs in cuBLAS)."""
+    differentiable expression (its GEMM runs in cuBLAS, in full float32)."""
     x2 = (X * X).sum(-1)
     y2 = (Y * Y).sum(-1)
-    return (x2[:, :, None] + y2[:, None, :] - 2.0 * torch.bmm(X, Y.transpose(1, 2))).clamp_min(0)
+    with _full_fp32_matmul():
+        G = torch.bmm(X, Y.transpose(1, 2))
+    return (x2[:, :, None] + y2[:, None, :] - 2.0 * G).clamp_min(0)
 
 
 @torch.autograd.function.once_differentiable
@@ -465,6 +480,8 @@ def _sdtw_fused_backward_once(ctx, X, Y, mask, saved, g_r):
 
 class SdtwFused(torch.autograd.Function):
     """(X, Y) -> (distance, saved, mask): soft-DTW with squared-Euclidean cost."""
+
+    generate_vmap_rule = True
 
     @staticmethod
     def forward(X, Y, gamma, bandwidth):
@@ -497,7 +514,10 @@ class SdtwFused(torch.autograd.Function):
         cost = _sqeuclid(Xs, Ys)
         s = SdtwCostGrad.apply(cost, saved, g, ctx.gamma, ctx.bandwidth)
         wrt = [t for t in (Xs, Ys) if t.requires_grad]
-        grads = iter(torch.autograd.grad(cost, wrt, s, create_graph=True) if wrt else ())
+        # the first-order values go through the cost's bmm backward: full
+        # float32 there too (second-order terms follow the caller's setting)
+        with _full_fp32_matmul():
+            grads = iter(torch.autograd.grad(cost, wrt, s, create_graph=True) if wrt else ())
         dX = next(grads) if X.requires_grad else None
         dY = next(grads) if Y.requires_grad else None
         return dX, dY, None, None
