@@ -86,9 +86,11 @@ int tw_sdtw_forward_f64(const double* cost, const double* penalty, int B, int N,
  * `saved` is still the caller's (it is an output consumed by the backward).
  * Limits: shapes whose scratch (tw_sdtw_workspace_bytes) exceeds 4 MiB are
  * rejected with TW_ERR_WORKSPACE; every call shares the one buffer, so calls
- * that overlap on the GPU race and must be serialised by the caller; the
- * first call on a device looks up the buffer's device address and should
- * come before any stream capture. */
+ * that overlap on the GPU race and must be serialised by the caller.  Each
+ * call looks up the buffer's device address on the current device (so a
+ * device reset between calls is harmless); the first call on a device also
+ * loads the library's device code there and should come before any stream
+ * capture. */
 int tw_sdtw_forward_noalloc_f32(const float* cost, const float* penalty, int B, int N, int M,
                                 double gamma, double bandwidth, float* out_r, float* out_p,
                                 void* saved, size_t saved_bytes, void* stream);

@@ -226,3 +226,27 @@ def test_features_double_backward_normalized(tw):
     gp, gm = grads(X + eps * VX, Y + eps * VY), grads(X - eps * VX, Y - eps * VY)
     _close(hX, ((gp[0] - gm[0]) / (2 * eps)).cpu().numpy(), 1e-6, 1e-5)
     _close(hY, ((gp[1] - gm[1]) / (2 * eps)).cpu().numpy(), 1e-6, 1e-5)
+
+
+@pytest.mark.parametrize("allow_tf32", [False, True])
+def test_features_create_graph_first_order_matches_plain_fp32(tw, allow_tf32):
+    """Under create_graph the features backward rebuilds the cost with a cuBLAS
+    bmm; it runs in full float32 whatever the caller's TF32 setting, so the
+    first-order gradients match the plain native path (tensor-core cost and
+    chain rule, 3xTF32) to float32 rounding."""
+    g = torch.Generator().manual_seed(21)
+    X = torch.randn(3, 96, 64, generator=g).to(DEV)
+    Y = torch.randn(3, 80, 64, generator=g).to(DEV)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = allow_tf32
+    try:
+        x1, y1 = X.clone().requires_grad_(True), Y.clone().requires_grad_(True)
+        gx1, gy1 = torch.autograd.grad(tw.functional.soft_dtw(x1, y1, gamma=0.5).sum(), (x1, y1))
+        x2, y2 = X.clone().requires_grad_(True), Y.clone().requires_grad_(True)
+        gx2, gy2 = torch.autograd.grad(tw.functional.soft_dtw(x2, y2, gamma=0.5).sum(),
+                                       (x2, y2), create_graph=True)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    for a, b in ((gx1, gx2), (gy1, gy2)):
+        err = (a - b.detach()).abs().max() / a.abs().max()
+        assert err < 1e-5, err

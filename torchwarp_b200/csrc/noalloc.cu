@@ -16,8 +16,6 @@
 // and nothing is cleared.
 #include <cuda_runtime.h>
 
-#include <mutex>
-
 #include "../../include/torchwarp_b200.h"
 #include "common.cuh"
 
@@ -35,24 +33,24 @@ constexpr size_t kStaticScratchBytes = size_t(4) << 20;
 static __device__ __align__(256) unsigned char g_sdtw_scratch[kStaticScratchBytes];
 
 // Device address of g_sdtw_scratch on the current device.  In host code the
-// symbol's name is only a host-side handle, so the address is looked up once
-// per device (with that device current) and cached.
+// symbol's name is only a host-side handle, so the address is looked up with
+// the caller's device current.  The lookup runs on every call and is not
+// cached: it is not a stream operation and costs little, and a cached address
+// would go stale if the caller reset the device (cudaDeviceReset) or its
+// primary context was torn down and created again, which can place the
+// module's globals elsewhere.  The first lookup on a device loads the module
+// there (lazy loading), which is why the first call should come before any
+// stream capture.
 int scratch_address(void** out) {
-  static std::mutex mu;
-  static void* cache[64] = {nullptr};
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+  if (cudaGetDevice(&dev) != cudaSuccess)
     return set_error(kLaunch, "tw_sdtw_forward_noalloc_f32: no current CUDA device");
-  std::lock_guard<std::mutex> lock(mu);
-  if (cache[dev] == nullptr) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_sdtw_scratch);
-    if (e != cudaSuccess || p == nullptr)
-      return set_error(kLaunch, "tw_sdtw_forward_noalloc_f32: cudaGetSymbolAddress failed: %s",
-                       cudaGetErrorString(e));
-    cache[dev] = p;
-  }
-  *out = cache[dev];
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_sdtw_scratch);
+  if (e != cudaSuccess || p == nullptr)
+    return set_error(kLaunch, "tw_sdtw_forward_noalloc_f32: cudaGetSymbolAddress failed: %s",
+                     cudaGetErrorString(e));
+  *out = p;
   return kOk;
 }
 
