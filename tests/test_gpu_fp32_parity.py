@@ -9,7 +9,10 @@ the bar:
 
 * the float64 path of this package is first held to the reference's float64
   on the configuration itself: forward values at rtol 1e-9 and a subsample
-  plus checksums of each gradient at rtol 1e-8;
+  plus checksums of each gradient at rtol 1e-7 (at cfg5, gamma = 0.01 and
+  N = M = 1024, two float64 implementations already differ by about 2e-8
+  per gradient element: the accumulated value R ~ 1e5 has a float64 ulp of
+  ~1.5e-11, which the soft-min weights amplify by 1/gamma);
 * that float64 result is then the truth for this package's float32 path,
   whose errors (forward max relative error, gradient max-normalised error
   max|g32 - g64| / max|g64|, fraction of elements outside 1e-4 rel + 1e-6 abs)
@@ -74,9 +77,9 @@ def test_fp32_error_within_reference_bar(tw, name):
         stride = int(BARS["{}::gstride::{}".format(name, i)])
         want = BARS["{}::gsub64::{}".format(name, i)]
         scale = float(BARS["{}::gsum64::{}".format(name, i)][2])
-        np.testing.assert_allclose(g.reshape(-1)[::stride], want, rtol=1e-8, atol=1e-10 * scale)
+        np.testing.assert_allclose(g.reshape(-1)[::stride], want, rtol=1e-7, atol=1e-10 * scale)
         s = BARS["{}::gsum64::{}".format(name, i)]
-        np.testing.assert_allclose([g.sum(), (g * g).sum()], s[:2], rtol=1e-8,
+        np.testing.assert_allclose([g.sum(), (g * g).sum()], s[:2], rtol=1e-7,
                                    atol=1e-10 * scale * g.size)
     v32, g32 = _run(tw, name, torch.float32)
     fwd, mn, fail = error_metrics(v32, v64, g32, g64)

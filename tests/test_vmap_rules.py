@@ -74,6 +74,36 @@ def f(x):
     return PairSq.apply(x)[0]
 
 
+@torch.library.custom_op("twtest::pair_dist", mutates_args=())
+def pair_dist(q: Tensor, s: Tensor) -> Tensor:
+    """A single-result op: (q [B, R, D], s [B, U, D]) -> [B, R, U]."""
+    return torch.cdist(q, s)
+
+
+@pair_dist.register_fake
+def _(q, s):
+    return q.new_empty(q.shape[0], q.shape[1], s.shape[1])
+
+
+register_fold_rule(pair_dist)
+
+
+class PairDist(torch.autograd.Function):
+    generate_vmap_rule = True
+
+    @staticmethod
+    def forward(q, s):
+        return pair_dist(q, s)
+
+    @staticmethod
+    def setup_context(ctx, inputs, output):
+        pass
+
+    @staticmethod
+    def backward(ctx, g):
+        return None, None
+
+
 def test_round_to_pairs():
     assert round_to_pairs(0, 5) == 0
     assert round_to_pairs(10, 5) == 10
@@ -133,3 +163,18 @@ def test_any_slice_count(V):
     x = torch.randn(V, 3, 5, dtype=f64)
     g = torch.func.vmap(torch.func.grad(lambda a: f(a).sum()))(x)
     assert torch.allclose(g, 2.0 * x)
+
+
+def test_single_result_op_through_reshapes():
+    # the query/support layout of JEANIE: views and expands before the op
+    q = torch.randn(3, 2, 4, 5, 3, dtype=f64)
+    s = torch.randn(3, 2, 6, 3, dtype=f64)
+
+    def cost(a, b):
+        B, K, T, D = a.shape
+        sp = b.unsqueeze(-3).expand(B, 1, 6, D).reshape(-1, 6, D)
+        return PairDist.apply(a.reshape(B, K * T, D), sp).reshape(B, K, T, 6)
+
+    got = torch.func.vmap(cost)(q, s)
+    want = torch.cdist(q.reshape(3, 2, 20, 3), s).reshape(3, 2, 4, 5, 6)
+    assert torch.allclose(got, want)

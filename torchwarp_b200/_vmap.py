@@ -37,7 +37,8 @@ def round_to_pairs(nbytes: int, pairs: int) -> int:
 
 
 def _as_tuple(out):
-    return (out, False) if isinstance(out, Tensor) else (tuple(out), True)
+    """(results as a tuple, whether the op returns a tuple)."""
+    return ((out,), False) if isinstance(out, Tensor) else (tuple(out), True)
 
 
 def register_fold_rule(op, flat_in: Iterable[int] = (), flat_out: Iterable[int] = (),

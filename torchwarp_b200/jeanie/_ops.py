@@ -26,6 +26,7 @@ import torch
 from torch import Tensor
 
 from .. import _native as nat
+from .. import _transforms
 from .._vmap import register_fold_rule
 
 
@@ -115,7 +116,7 @@ class JeanieDP(torch.autograd.Function):
         ctx.args = (s1, s2, gamma, keep_R)
 
     @staticmethod
-    @torch.autograd.function.once_differentiable
+    @_transforms.once_differentiable
     def backward(ctx, g_out, g_R):
         cost, R = ctx.saved_tensors
         s1, s2, gamma, _ = ctx.args
@@ -205,7 +206,7 @@ class QSCost(torch.autograd.Function):
         ctx.metric = metric
 
     @staticmethod
-    @torch.autograd.function.once_differentiable
+    @_transforms.once_differentiable
     def backward(ctx, g):
         query, support, cost = ctx.saved_tensors
         dq, ds = qs_cost_backward(query, support, cost, g, ctx.metric)
@@ -298,7 +299,7 @@ class QSRbfCost(torch.autograd.Function):
         ctx.sigma = sigma
 
     @staticmethod
-    @torch.autograd.function.once_differentiable
+    @_transforms.once_differentiable
     def backward(ctx, g):
         query, support = ctx.saved_tensors
         dq, ds = qs_rbf_cost_backward(query, support, g, ctx.sigma)
@@ -369,7 +370,7 @@ class FvmSoftmin(torch.autograd.Function):
         ctx.gamma = gamma
 
     @staticmethod
-    @torch.autograd.function.once_differentiable
+    @_transforms.once_differentiable
     def backward(ctx, g):
         (cost,) = ctx.saved_tensors
         return fvm_softmin_backward(cost, g, ctx.gamma), None
@@ -384,3 +385,8 @@ class FvmSoftmin(torch.autograd.Function):
             return cost.new_zeros(B, T, U)
         w = fvm_softmin_backward(cost, cost.new_ones(B, T, U), ctx.gamma)
         return (w * cost_t.to(cost.dtype)).sum(1)
+
+
+JeanieDPTraced = _transforms.traceable(JeanieDP)
+QSCostTraced = _transforms.traceable(QSCost)
+FvmSoftminTraced = _transforms.traceable(FvmSoftmin)

@@ -15,6 +15,7 @@ PyTorch expression.
 
 import torch
 
+from .. import _transforms
 from . import _ops
 
 
@@ -53,7 +54,7 @@ def _native_cost(query, support, metric, sigma=None):
 def _apply(q, sp, metric, sigma):
     if sigma is not None:
         return _ops.QSRbfCost.apply(q, sp, float(sigma))
-    return _ops.QSCost.apply(q, sp, metric)
+    return _transforms.pick(_ops.QSCost, _ops.QSCostTraced).apply(q, sp, metric)
 
 
 def squared_euclidean_cost(query: torch.Tensor, support: torch.Tensor) -> torch.Tensor:

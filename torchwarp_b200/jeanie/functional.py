@@ -9,6 +9,7 @@ backward passes run in the native library.
 
 import torch
 
+from .. import _transforms
 from . import _ops
 from .distances import _native_cost, rbf_cost
 
@@ -48,7 +49,8 @@ def _jeanie_dp(cost, gamma=0.1, max_shift_1=1, max_shift_2=1, backend="auto",
         cost = cost.float()
     s1 = min(int(max_shift_1), K1 - 1)
     s2 = min(int(max_shift_2), K2 - 1)
-    out, R = _ops.JeanieDP.apply(cost, s1, s2, float(gamma), bool(return_accumulator))
+    out, R = _transforms.pick(_ops.JeanieDP, _ops.JeanieDPTraced).apply(
+        cost, s1, s2, float(gamma), bool(return_accumulator))
     return out, (R if return_accumulator else None)
 
 

@@ -8,6 +8,7 @@ the result (native DP).
 import torch
 
 from .. import sdtw
+from .. import _transforms
 from . import _ops
 from .distances import euclidean_cost, rbf_cost, squared_euclidean_cost
 
@@ -28,7 +29,7 @@ def fvm_from_cost(cost, *, gamma=0.1, backend="auto"):
     flat = cost.reshape(B, -1, T, U)
     if flat.dtype not in (torch.float32, torch.float64):
         flat = flat.float()
-    temporal = _ops.FvmSoftmin.apply(flat, float(gamma))
+    temporal = _transforms.pick(_ops.FvmSoftmin, _ops.FvmSoftminTraced).apply(flat, float(gamma))
     return sdtw.soft_dtw_from_cost(temporal, gamma=gamma, backend=backend)
 
 

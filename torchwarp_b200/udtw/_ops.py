@@ -47,6 +47,7 @@ import torch
 from torch import Tensor
 
 from .. import _native as nat
+from .. import _transforms
 from .._vmap import register_fold_rule, round_to_pairs
 
 # ------------------------------------------------------------------ helpers
@@ -335,7 +336,7 @@ class SdtwCostGrad(torch.autograd.Function):
         ctx.args = (gamma, bandwidth)
 
     @staticmethod
-    @torch.autograd.function.once_differentiable
+    @_transforms.once_differentiable
     def backward(ctx, V):
         cost, g = ctx.saved_tensors
         gamma, bandwidth = ctx.args
@@ -345,7 +346,7 @@ class SdtwCostGrad(torch.autograd.Function):
         return hv, None, v_e, None, None
 
 
-@torch.autograd.function.once_differentiable
+@_transforms.once_differentiable
 def _dp_backward_once(ctx, saved, g_r, g_p):
     gamma, has_p, _ = ctx.args
     B, N, M = ctx.shape
@@ -435,7 +436,7 @@ class Fused(torch.autograd.Function):
         ctx.args = (gamma, beta, eps)
 
     @staticmethod
-    @torch.autograd.function.once_differentiable
+    @_transforms.once_differentiable
     def backward(ctx, g_r, g_p, _g_saved, _g_cost):
         X, Y, vx, vy, saved, cost = ctx.saved_tensors
         gamma, beta, eps = ctx.args
@@ -471,7 +472,7 @@ def _sqeuclid(X, Y):
     return (x2[:, :, None] + y2[:, None, :] - 2.0 * G).clamp_min(0)
 
 
-@torch.autograd.function.once_differentiable
+@_transforms.once_differentiable
 def _sdtw_fused_backward_once(ctx, X, Y, mask, saved, g_r):
     g_r = _zeros_if_none(g_r, X, X.shape[0])
     dX, dY = sdtw_fused_backward(X, Y, mask, saved, g_r, ctx.gamma)
@@ -511,15 +512,19 @@ class SdtwFused(torch.autograd.Function):
         # derivative, not the total one twice
         Xs = X.view_as(X) if X.requires_grad else X
         Ys = Y.view_as(Y) if Y.requires_grad else Y
+        if not (Xs.requires_grad or Ys.requires_grad):
+            # grad mode is on but nothing at this level is differentiable
+            # (vmapped cotangents of torch.func.jacrev / vjp): first order
+            return _sdtw_fused_backward_once(ctx, X, Y, mask, saved, g_r)
         cost = _sqeuclid(Xs, Ys)
         s = SdtwCostGrad.apply(cost, saved, g, ctx.gamma, ctx.bandwidth)
         wrt = [t for t in (Xs, Ys) if t.requires_grad]
         # the first-order values go through the cost's bmm backward: full
         # float32 there too (second-order terms follow the caller's setting)
         with _full_fp32_matmul():
-            grads = iter(torch.autograd.grad(cost, wrt, s, create_graph=True) if wrt else ())
-        dX = next(grads) if X.requires_grad else None
-        dY = next(grads) if Y.requires_grad else None
+            grads = iter(torch.autograd.grad(cost, wrt, s, create_graph=True))
+        dX = next(grads) if Xs.requires_grad else None
+        dY = next(grads) if Ys.requires_grad else None
         return dX, dY, None, None
 
     @staticmethod
@@ -539,12 +544,16 @@ class SdtwFused(torch.autograd.Function):
         return r_t, None, None
 
 
+DPTraced = _transforms.traceable(DP)
+SdtwFusedTraced = _transforms.traceable(SdtwFused)
+
+
 def sdtw_fused_apply(X, Y, gamma, bandwidth):
-    return SdtwFused.apply(X, Y, gamma, bandwidth)
+    return _transforms.pick(SdtwFused, SdtwFusedTraced).apply(X, Y, gamma, bandwidth)
 
 
 def dp_apply(cost, penalty, gamma, bandwidth):
-    return DP.apply(cost, penalty, gamma, bandwidth)
+    return _transforms.pick(DP, DPTraced).apply(cost, penalty, gamma, bandwidth)
 
 
 def fused_apply(X, Y, vx, vy, gamma, beta, eps, bandwidth):
