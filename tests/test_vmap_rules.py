@@ -178,3 +178,48 @@ def test_single_result_op_through_reshapes():
     got = torch.func.vmap(cost)(q, s)
     want = torch.cdist(q.reshape(3, 2, 20, 3), s).reshape(3, 2, 4, 5, 6)
     assert torch.allclose(got, want)
+
+
+# ---------------------------------------------- first-order-only backwards
+
+from torchwarp_b200 import _transforms  # noqa: E402
+
+
+class OnceSq(torch.autograd.Function):
+    generate_vmap_rule = True
+
+    @staticmethod
+    def forward(x):
+        return x * x
+
+    @staticmethod
+    def setup_context(ctx, inputs, output):
+        ctx.save_for_backward(inputs[0])
+
+    @staticmethod
+    @_transforms.once_differentiable
+    def backward(ctx, g):
+        (x,) = ctx.saved_tensors
+        return 2 * x * g
+
+
+def test_once_differentiable_first_order_under_torch_func():
+    x = torch.randn(3, 4, dtype=f64)
+    f = lambda a: OnceSq.apply(a).sum()  # noqa: E731
+    assert torch.allclose(torch.func.grad(f)(x), 2 * x)
+    assert torch.allclose(torch.func.vmap(torch.func.grad(f))(x), 2 * x)
+    J = torch.func.jacrev(OnceSq.apply)(x[0])
+    assert torch.allclose(J, torch.diag(2 * x[0]))
+
+
+def test_once_differentiable_second_order_raises():
+    x = torch.randn(4, dtype=f64)
+    f = lambda a: OnceSq.apply(a).sum()  # noqa: E731
+    with pytest.raises(RuntimeError, match="differentiate twice"):
+        torch.func.jacrev(torch.func.jacrev(f))(x)
+    with pytest.raises(RuntimeError, match="differentiate twice"):
+        torch.func.grad(lambda a: torch.func.grad(f)(a).sum())(x)
+    y = x.clone().requires_grad_(True)
+    (gy,) = torch.autograd.grad(f(y), y, create_graph=True)
+    with pytest.raises(RuntimeError):
+        gy.sum().backward()

@@ -63,7 +63,10 @@ def build(force=False, verbose=False):
         raise RuntimeError("nvcc failed:\n" + "\n".join(errors))
     objs = [o for o, _ in results]
     if force or not LIB.exists() or any(o.stat().st_mtime > LIB.stat().st_mtime for o in objs):
-        cmd = [nvcc(), *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lcudart"]
+        # --no-undefined: a symbol missing from every object fails the build
+        # here, not the first dlopen on a GPU box
+        cmd = [nvcc(), *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lcudart",
+               "-Xlinker", "--no-undefined"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError("link failed:\n{}{}".format(r.stdout, r.stderr))

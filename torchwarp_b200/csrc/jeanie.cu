@@ -19,6 +19,16 @@
 #include "common.cuh"
 
 namespace tw {
+
+// tensor-core cost and chain rule (tc_gemm.cu)
+bool tc_cost_eligible(const float* X, const float* Y, const float* vx, const float* vy, int N,
+                      int M, int D, const float* C, const float* Q);
+int tc_cost_f32(const float* X, const float* Y, const float* vx, const float* vy, int B, int N,
+                int M, int D, double beta, double eps, float* C, float* Q, uint32_t* mask,
+                cudaStream_t st);
+int tc_qs_grad_f32(const float* Q, const float* Sp, const float* C, const float* dC, int B,
+                   int R, int U, int D, int sqrt_cost, float* dQ, float* dSp, cudaStream_t st);
+
 namespace {
 
 struct JGrid {
@@ -606,11 +616,44 @@ int jeanie_backward(const T* C, const T* R, const T* g_out, const T* g_R, int B,
   return check_launch<T>("jeanie backward");
 }
 
+// The Euclidean cost from the clamped squared one, in place (n a multiple of 4,
+// 16-byte aligned).
+__global__ void sqrt_inplace_kernel(float4* __restrict__ c, long long n4) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4;
+       i += (long long)gridDim.x * blockDim.x) {
+    float4 v = c[i];
+    v.x = sqrtf(v.x);
+    v.y = sqrtf(v.y);
+    v.z = sqrtf(v.z);
+    v.w = sqrtf(v.w);
+    c[i] = v;
+  }
+}
+
+// The tensor-core route of the query/support cost and its chain rule (fp32):
+// a real contraction (64 <= D <= 256) over enough rows and support frames to
+// fill the 128 x 128 tiles, with the uDTW cost kernel's alignment rules.
+inline bool al16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+bool qs_tc_eligible(const float* q, const float* s, const float* c, int Rr, int U, int D) {
+  return Rr >= 64 && U >= 32 && D <= 256 &&
+         tc_cost_eligible(q, s, nullptr, nullptr, Rr, U, D, c, nullptr);
+}
+
 template <typename T>
 int qs_cost(const T* q, const T* s, int B, int Rr, int U, int D, int metric, T* cost,
             cudaStream_t st) {
   if (B == 0 || Rr == 0) return kOk;
   if constexpr (sizeof(T) == 4) {
+    if (qs_tc_eligible(q, s, cost, Rr, U, D)) {
+      int rc = tc_cost_f32(q, s, nullptr, nullptr, B, Rr, U, D, 0.0, 1e-8, cost, nullptr,
+                           nullptr, st);
+      if (rc != kOk || metric != 1) return rc;
+      const long long n4 = (long long)B * Rr * U / 4;
+      const int grid = (int)(n4 / 256 + 1 < 4 * 148 ? n4 / 256 + 1 : 4 * 148);
+      sqrt_inplace_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<float4*>(cost), n4);
+      return check_launch<T>("euclidean cost");
+    }
     if (qs_fast(q, s, nullptr, nullptr, B, Rr, U, D, metric, cost, nullptr, nullptr, st) == kOk)
       return check_launch<T>("query/support cost");
   }
@@ -632,6 +675,8 @@ int qs_grad(const T* q, const T* s, const T* cost, const T* dcost, int B, int Rr
             int metric, T* dq, T* ds, cudaStream_t st) {
   if (B == 0 || Rr == 0) return kOk;
   if constexpr (sizeof(T) == 4) {
+    if (qs_tc_eligible(q, s, cost, Rr, U, D) && al16(dcost) && al16(dq) && al16(ds))
+      return tc_qs_grad_f32(q, s, cost, dcost, B, Rr, U, D, metric == 1 ? 1 : 0, dq, ds, st);
     if (qs_fast(q, s, cost, dcost, B, Rr, U, D, metric, nullptr, dq, ds, st) == kOk)
       return check_launch<T>("query/support gradient");
   }

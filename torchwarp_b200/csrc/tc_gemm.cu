@@ -694,6 +694,14 @@ __device__ __forceinline__ float4 split4(float4 v, float4& lo) {
   return hi;
 }
 
+// S of a cell whose cost c the chain rule reads (no variance, no mask): the
+// clamp's derivative passes dC where c > 0; with sqrt_cost, c is a Euclidean
+// cost sqrt(sq) and dsq = dC / (2 c) (zero gradient at c = 0, as
+// jeanie/distances.py:34-38).
+__device__ __forceinline__ float s_of_cost(float g, float c, int sqrt_cost) {
+  return c > 0.f ? (sqrt_cost ? g * (0.5f * rcp(c)) : g) : 0.f;
+}
+
 // PRE: dC already carries the positivity mask (S = dC), so neither the cost
 // nor mask words are loaded and the split warps skip the mask test.
 template <int SIDE, bool VAR, bool MASKED, bool TA, bool WIDE, bool PRE = false>
@@ -703,7 +711,7 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
                    const __grid_constant__ CUtensorMap mapOut, const float* __restrict__ A,
                    const float* __restrict__ va, const float* __restrict__ vb,
                    float* __restrict__ dva, int B, int N, int M, int D, float beta, float eps,
-                   int has_dq, GradGeom g, const uint32_t* __restrict__ mask) {
+                   int has_dq, GradGeom g, const uint32_t* __restrict__ mask, int sqrt_cost) {
   static_assert(!(PRE && (VAR || MASKED)), "PRE is the plain soft-DTW chain rule");
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* land_base = smem;
@@ -897,7 +905,9 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
                 var_raw = 0.5f * (va_r + __shfl_sync(0xffffffffu, vbl, jj));
                 inv = rcp(var_raw > eps ? var_raw : eps);
               }
-              const float v = PRE ? ge[e] : (ce[e] > 0.f ? (VAR ? ge[e] * inv : ge[e]) : 0.f);
+              const float v = PRE ? ge[e]
+                            : (VAR ? (ce[e] > 0.f ? ge[e] * inv : 0.f)
+                                   : s_of_cost(ge[e], ce[e], sqrt_cost));
               rsum += v;
               if (VAR && var_raw > eps) vsum += (beta * qe[e] - ge[e] * ce[e]) * inv;
               sv[4 * k + e] = v;
@@ -926,7 +936,8 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
               var_raw = 0.5f * (__shfl_sync(0xffffffffu, vbl, rr) + va_r);
               inv = rcp(var_raw > eps ? var_raw : eps);
             }
-            const float v = PRE ? gv : (cvv > 0.f ? (VAR ? gv * inv : gv) : 0.f);
+            const float v = PRE ? gv
+                            : (VAR ? (cvv > 0.f ? gv * inv : 0.f) : s_of_cost(gv, cvv, sqrt_cost));
             rsum += v;
             if (VAR && var_raw > eps) vsum += (beta * qv - gv * cvv) * inv;
             sv[k] = v;
@@ -1053,7 +1064,8 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
                 var = var_raw > eps ? var_raw : eps;
               }
               const float rv = VAR ? rcp(var) : 1.f;
-              sv[e] = PRE ? ge[e] : (ce[e] > 0.f ? (VAR ? ge[e] * rv : ge[e]) : 0.f);
+              sv[e] = PRE ? ge[e]
+                      : (VAR ? (ce[e] > 0.f ? ge[e] * rv : 0.f) : s_of_cost(ge[e], ce[e], sqrt_cost));
               rsum[0] += sv[e];
               if (VAR && var_raw > eps) vsum[0] += (beta * qe[e] - ge[e] * ce[e]) * rv;
             }
@@ -1110,7 +1122,8 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
                 var = var_raw > eps ? var_raw : eps;
               }
               const float rv = VAR ? rcp(var) : 1.f;
-              sv[e] = PRE ? ge[e] : (ce[e] > 0.f ? (VAR ? ge[e] * rv : ge[e]) : 0.f);
+              sv[e] = PRE ? ge[e]
+                      : (VAR ? (ce[e] > 0.f ? ge[e] * rv : 0.f) : s_of_cost(ge[e], ce[e], sqrt_cost));
               rsum[e] += sv[e];
               if (VAR && var_raw > eps) vsum[e] += (beta * qe[e] - ge[e] * ce[e]) * rv;
             }
@@ -1441,7 +1454,7 @@ template <int SIDE, bool VAR, bool MASKED, bool TA, bool WIDE, bool PRE>
 int grad_side_impl(const float* A, const float* F, const float* va, const float* vb,
                    const float* C, const float* dC, const float* dQ, int B, int N, int M, int D,
                    double beta, double eps, float* dA, float* dva, cudaStream_t st,
-                   const uint32_t* mask) {
+                   const uint32_t* mask, int sqrt_cost) {
   const int R = SIDE == 0 ? N : M, S = SIDE == 0 ? M : N;
   CUtensorMap mDC, mC, mDQ, mF, mOut;
   int rc;
@@ -1513,7 +1526,8 @@ int grad_side_impl(const float* A, const float* F, const float* va, const float*
   auto kern = tc_grad_kernel<SIDE, VAR, MASKED, TA, WIDE, PRE>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   kern<<<grid, GRAD_THREADS, smem, st>>>(mDC, mC, mDQ, mF, mOut, A, va, vb, dva, B, N, M, D,
-                                         (float)beta, (float)eps, has_dq ? 1 : 0, g, mask);
+                                         (float)beta, (float)eps, has_dq ? 1 : 0, g, mask,
+                                         sqrt_cost);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(kLaunch, "tc grad launch: %s", cudaGetErrorString(e));
   return kOk;
@@ -1526,7 +1540,7 @@ template <int SIDE, bool VAR, bool MASKED = false, bool PRE = false>
 int grad_side(const float* A, const float* F, const float* va, const float* vb, const float* C,
               const float* dC, const float* dQ, int B, int N, int M, int D, double beta,
               double eps, float* dA, float* dva, cudaStream_t st,
-              const uint32_t* mask = nullptr) {
+              const uint32_t* mask = nullptr, int sqrt_cost = 0) {
   const char* env = std::getenv("TW_GRAD_SMEM_S");
   const bool smem_s = env != nullptr && env[0] != '\0' && env[0] != '0';
   const int BD = 32 * ((D + 31) / 32);
@@ -1534,12 +1548,12 @@ int grad_side(const float* A, const float* F, const float* va, const float* vb, 
   // fit in 512 (D <= 96); wide MMAs with S in shared memory up to D = 128.
   if (!smem_s && 4 * BD + 64 <= 512)
     return grad_side_impl<SIDE, VAR, MASKED, true, true, PRE>(A, F, va, vb, C, dC, dQ, B, N, M, D,
-                                                              beta, eps, dA, dva, st, mask);
+                                                              beta, eps, dA, dva, st, mask, sqrt_cost);
   if (2 * BD <= 256)
     return grad_side_impl<SIDE, VAR, MASKED, false, true, PRE>(A, F, va, vb, C, dC, dQ, B, N, M,
-                                                               D, beta, eps, dA, dva, st, mask);
+                                                               D, beta, eps, dA, dva, st, mask, sqrt_cost);
   return grad_side_impl<SIDE, VAR, MASKED, false, false, PRE>(A, F, va, vb, C, dC, dQ, B, N, M, D,
-                                                              beta, eps, dA, dva, st, mask);
+                                                              beta, eps, dA, dva, st, mask, sqrt_cost);
 }
 
 }  // namespace
@@ -1567,6 +1581,19 @@ int tc_grad_f32(const float* X, const float* Y, const float* vx, const float* vy
     return rc;
   return grad_side<1, false>(Y, X, nullptr, nullptr, C, dC, nullptr, B, N, M, D, beta, eps, dY,
                              nullptr, st);
+}
+
+// Chain rule of a query/support cost built by tc_cost_f32 (no variance):
+// S = dC where cost > 0, or dC / (2 cost) for the Euclidean cost (sqrt_cost).
+int tc_qs_grad_f32(const float* Q, const float* Sp, const float* C, const float* dC, int B,
+                   int R, int U, int D, int sqrt_cost, float* dQ, float* dSp, cudaStream_t st) {
+  if (B == 0 || R == 0 || U == 0) return kOk;
+  int rc;
+  if ((rc = grad_side<0, false>(Q, Sp, nullptr, nullptr, C, dC, nullptr, B, R, U, D, 0.0, 1e-8,
+                                dQ, nullptr, st, nullptr, sqrt_cost)))
+    return rc;
+  return grad_side<1, false>(Sp, Q, nullptr, nullptr, C, dC, nullptr, B, R, U, D, 0.0, 1e-8, dSp,
+                             nullptr, st, nullptr, sqrt_cost);
 }
 
 // Squared-Euclidean chain rule with the positivity mask of the cost kernel in
