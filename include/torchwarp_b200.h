@@ -250,6 +250,45 @@ int tw_fvm_softmin_backward_f32(const float* cost, const float* d_temporal, int 
 int tw_fvm_softmin_backward_f64(const double* cost, const double* d_temporal, int B, int Kf,
                                 int TU, double gamma, double* d_cost, void* stream);
 
+/* ---------------------------------------------------------------------
+ * Fused JEANIE and FVM, float32: one call per direction builds each pair's
+ * query/support cost from the features (or takes a cost), runs FVM's
+ * viewpoint soft-min and the temporal soft-min DP on chip, and in the
+ * backward the DP adjoint and the chain rule back to the features.
+ *   features: query [B, K1*K2*T, D] (rows in (viewpoint, t) order), support
+ *             [B, U, D], cost = NULL; metric 0 squared Euclidean (clamped at
+ *             0), 1 Euclidean (no gradient at distance 0).
+ *   cost:     query = support = NULL, cost [B, K1, K2, T, U].
+ *   fvm = 0:  JEANIE with viewpoint shifts s1, s2 (clamped to K-1 by the
+ *             caller); out [B] = soft-min over the viewpoints of the end
+ *             cells; R [B, K1, K2, T, U] (may be NULL) = the accumulator.
+ *   fvm = 1:  FVM (K2 = 1, K1 = all viewpoints): soft-min over the
+ *             viewpoints at every (t, u), then soft-DTW; R must be NULL.
+ *   saved:    tw_jeanie_fused_saved_bytes() bytes, 16-byte aligned, written
+ *             by the forward and read by the backward (with the same cost
+ *             pointer for a cost input).
+ *   Backward for L = sum_b grad_out[b] out[b] + <grad_R, R> (grad_R NULL for
+ *   none; always NULL for FVM): d_query [B, K T, D], d_support [B, U, D]
+ *   with features, d_cost [B, K1, K2, T, U] with a cost; written, not
+ *   accumulated.
+ * tw_jeanie_fused_supported says whether a shape runs here (even D <= 256,
+ * U <= 15 with features, a pair's state within 96 KB of shared memory);
+ * other shapes use tw_qs_cost_* + tw_jeanie_* / tw_fvm_softmin_*.
+ * Replaces jeanie_fused_forward / jeanie_fused_backward
+ * (src/torchwarp/csrc/jeanie_cuda.cu:621-683, with jeanie/_ops.py:155-230)
+ * and FVM's logsumexp + soft-DTW (src/torchwarp/jeanie/fvm.py:15-67). */
+int tw_jeanie_fused_supported(int K, int T, int U, int D, int fvm, int features);
+size_t tw_jeanie_fused_saved_bytes(int B, int K, int T, int U, int fvm, int features);
+int tw_jeanie_fused_forward_f32(const float* query, const float* support, const float* cost,
+                                int B, int K1, int K2, int T, int U, int D, int s1, int s2,
+                                int metric, int fvm, double gamma, float* out, float* R,
+                                void* saved, size_t saved_bytes, void* stream);
+int tw_jeanie_fused_backward_f32(const float* query, const float* support, const float* cost,
+                                 const float* grad_out, const float* grad_R, int B, int K1, int K2,
+                                 int T, int U, int D, int s1, int s2, int metric, int fvm,
+                                 double gamma, const void* saved, size_t saved_bytes,
+                                 float* d_query, float* d_support, float* d_cost, void* stream);
+
 /* Hard alignment path (gamma -> 0) of cost [B, K, T, U] (float64), with the
  * tie-break of src/torchwarp/paths.py:85-117 (viewpoint ascending, then
  * (t-1,u-1), (t-1,u), (t,u-1), strict <; end viewpoint = first argmin);

@@ -1,0 +1,173 @@
+"""Fused float32 JEANIE / FVM kernels (tw_jeanie_fused_*) on a B200.
+
+float32 results of the fused path (cost from the features, viewpoint
+soft-min, DP and chain rule in one native call per direction) against the
+float64 CPU oracle, which follows the reference's recurrences
+(hibana2077/torchwarp src/torchwarp/jeanie/_torch_dp.py, jeanie/fvm.py), at
+float32 tolerances: forward values within 1e-5 relative, gradients within
+1e-4 max-normalised (max |g32 - g64| / max |g64|).  Also: agreement with the
+separate-kernel float32 path (TW_JEANIE_UNFUSED=1), bitwise determinism, the
+differentiable accumulator, and shapes that fall back.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def tw():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    import torchwarp_b200
+    return torchwarp_b200
+
+
+def _rel(a, b):
+    a = a.detach().double().cpu().numpy() if torch.is_tensor(a) else np.asarray(a)
+    return np.abs(a - b).max() / max(np.abs(b).max(), 1e-300)
+
+
+def _fvalues(got, want, fwd=1e-5, grad=1e-4):
+    assert _rel(got[0], want[0]) < fwd, _rel(got[0], want[0])
+    for a, b in zip(got[1:], want[1:]):
+        assert _rel(a, b) < grad, _rel(a, b)
+
+
+JEANIE_CASES = [
+    # (query shape, support shape, max_shift, metric)
+    ((3, 15, 10, 256), (3, 10, 256), 1, "euclidean"),      # cfg3's shape (few pairs)
+    ((4, 5, 7, 64), (4, 9, 64), 2, "sqeuclidean"),
+    ((2, 1, 12, 6), (2, 5, 6), 0, "euclidean"),             # one viewpoint
+    ((2, 3, 4, 6, 100), (2, 11, 100), (1, 2), "euclidean"),  # two viewpoint axes, D = 100
+    ((5, 8, 1, 2), (5, 15, 2), 3, "sqeuclidean"),           # T = 1, U = 15, D = 2
+]
+
+
+@pytest.mark.parametrize("qshape,sshape,shift,metric", JEANIE_CASES)
+def test_jeanie_features_fp32_vs_oracle(tw, orc, qshape, sshape, shift, metric):
+    g = torch.Generator().manual_seed(sum(qshape))
+    q = torch.randn(*qshape, generator=g, dtype=torch.float64)
+    s = torch.randn(*sshape, generator=g, dtype=torch.float64)
+    q32, s32 = q.float(), s.float()
+    qq = q32.to(DEV).requires_grad_(True)
+    ss = s32.to(DEV).requires_grad_(True)
+    d = tw.functional.jeanie(qq, ss, gamma=0.1, max_shift=shift, metric=metric)
+    d.sum().backward()
+    od, _, odq, ods = orc.jeanie(q32.double().numpy(), s32.double().numpy(), gamma=0.1,
+                                 max_shift=shift, metric=metric)
+    _fvalues((d, qq.grad, ss.grad), (od, odq, ods))
+
+
+@pytest.mark.parametrize("metric", ["euclidean", "sqeuclidean"])
+def test_jeanie_accumulator_fp32_vs_oracle(tw, orc, metric):
+    g = torch.Generator().manual_seed(17)
+    q = torch.randn(3, 6, 8, 32, generator=g, dtype=torch.float64).float()
+    s = torch.randn(3, 9, 32, generator=g, dtype=torch.float64).float()
+    gR = torch.randn(3, 6, 8, 9, generator=g, dtype=torch.float64)
+    qq = q.to(DEV).requires_grad_(True)
+    ss = s.to(DEV).requires_grad_(True)
+    d, R = tw.functional.jeanie(qq, ss, gamma=0.2, max_shift=1, metric=metric,
+                                return_accumulator=True)
+    (d.sum() + (R * gR.float().to(DEV)).sum()).backward()
+    od, oR, odq, ods = orc.jeanie(q.double().numpy(), s.double().numpy(), gamma=0.2,
+                                  max_shift=1, metric=metric, g_R=gR.numpy())
+    assert _rel(R, oR) < 1e-5
+    _fvalues((d, qq.grad, ss.grad), (od, odq, ods))
+
+
+@pytest.mark.parametrize("shape,shift", [((4, 15, 10, 10), 1), ((3, 2, 3, 9, 13), (1, 1)),
+                                         ((2, 1, 30, 40), 0)])
+def test_jeanie_cost_fp32_vs_oracle(tw, orc, shape, shift):
+    g = torch.Generator().manual_seed(len(shape) * 7 + shape[-1])
+    c = torch.rand(*shape, generator=g, dtype=torch.float64).float()
+    gR = torch.randn(*shape, generator=g, dtype=torch.float64)
+    cc = c.to(DEV).requires_grad_(True)
+    d, R = tw.functional.jeanie_from_cost(cc, gamma=0.1, max_shift=shift,
+                                          return_accumulator=True)
+    (d.sum() + (R * gR.float().to(DEV)).sum()).backward()
+    od, oR, odc = orc.jeanie_from_cost(c.double().numpy(), gamma=0.1, max_shift=shift,
+                                       g_R=gR.numpy())
+    assert _rel(R, oR) < 1e-5
+    _fvalues((d, cc.grad), (od, odc))
+
+
+@pytest.mark.parametrize("qshape,sshape,metric", [
+    ((3, 7, 7, 10, 256), (3, 10, 256), "euclidean"),        # cfg4's shape (few pairs)
+    ((4, 5, 6, 64), (4, 8, 64), "sqeuclidean"),
+    ((2, 3, 1, 14), (2, 15, 14), "euclidean"),
+])
+def test_fvm_features_fp32_vs_oracle(tw, orc, qshape, sshape, metric):
+    g = torch.Generator().manual_seed(sum(qshape) + 1)
+    q = torch.randn(*qshape, generator=g, dtype=torch.float64).float()
+    s = torch.randn(*sshape, generator=g, dtype=torch.float64).float()
+    qq = q.to(DEV).requires_grad_(True)
+    ss = s.to(DEV).requires_grad_(True)
+    d = tw.functional.fvm(qq, ss, gamma=0.1, metric=metric)
+    d.sum().backward()
+    od, odq, ods = orc.fvm(q.double().numpy(), s.double().numpy(), gamma=0.1, metric=metric)
+    _fvalues((d, qq.grad, ss.grad), (od, odq, ods))
+
+
+@pytest.mark.parametrize("shape", [(5, 7, 7, 10, 10), (3, 4, 12, 9)])
+def test_fvm_cost_fp32_vs_oracle(tw, orc, shape):
+    g = torch.Generator().manual_seed(shape[-1])
+    c = torch.randn(*shape, generator=g, dtype=torch.float64).abs().float()
+    cc = c.to(DEV).requires_grad_(True)
+    d = tw.functional.fvm_from_cost(cc, gamma=0.1)
+    d.sum().backward()
+    od, odc = orc.fvm_from_cost(c.double().numpy(), gamma=0.1)
+    _fvalues((d, cc.grad), (od, odc))
+
+
+def test_fused_matches_separate_kernels(tw, monkeypatch):
+    g = torch.Generator().manual_seed(5)
+    q = torch.randn(6, 15, 10, 256, generator=g).to(DEV)
+    s = torch.randn(6, 10, 256, generator=g).to(DEV)
+    out = []
+    for unfused in ("0", "1"):
+        monkeypatch.setenv("TW_JEANIE_UNFUSED", unfused)
+        qq, ss = q.clone().requires_grad_(True), s.clone().requires_grad_(True)
+        d = tw.functional.jeanie(qq, ss, gamma=0.1, max_shift=1)
+        f = tw.functional.fvm(qq, ss, gamma=0.1)
+        (d.sum() + f.sum()).backward()
+        out.append((d.detach(), f.detach(), qq.grad, ss.grad))
+    # the separate-kernel path keeps R in absolute float32 and is itself
+    # about 4e-4 (max-normalised) from the float64 truth at this shape; the
+    # fused path is within 3e-5 of it
+    for a, b in zip(*out):
+        assert _rel(a, b.double().cpu().numpy()) < 1e-3
+
+
+def test_fused_deterministic(tw):
+    g = torch.Generator().manual_seed(6)
+    q = torch.randn(16, 7, 7, 10, 128, generator=g).to(DEV)
+    s = torch.randn(16, 10, 128, generator=g).to(DEV)
+
+    def run():
+        qq, ss = q.clone().requires_grad_(True), s.clone().requires_grad_(True)
+        d = tw.functional.jeanie(qq, ss, gamma=0.1, max_shift=(1, 1))
+        f = tw.functional.fvm(qq, ss, gamma=0.1)
+        (d.sum() + f.sum()).backward()
+        return d, f, qq.grad, ss.grad
+
+    for a, b in zip(run(), run()):
+        assert torch.equal(a, b)
+
+
+def test_unsupported_shape_falls_back(tw, orc):
+    # 20 support frames exceed the fused kernel's 15; the separate kernels run
+    from torchwarp_b200.jeanie import _ops
+    assert not _ops.fused_supported(4, 6, 20, 32, False, True)
+    g = torch.Generator().manual_seed(8)
+    q = torch.randn(2, 4, 6, 32, generator=g, dtype=torch.float64).float()
+    s = torch.randn(2, 20, 32, generator=g, dtype=torch.float64).float()
+    qq = q.to(DEV).requires_grad_(True)
+    d = tw.functional.jeanie(qq, s.to(DEV), gamma=0.1, max_shift=1)
+    d.sum().backward()
+    od, _, odq, _ = orc.jeanie(q.double().numpy(), s.double().numpy(), gamma=0.1, max_shift=1)
+    _fvalues((d, qq.grad), (od, odq))

@@ -42,6 +42,39 @@ def test_library_exports_every_declared_symbol():
         assert name in _native.SIGNATURES, name
 
 
+def _header_param_types():
+    """{function: [parameter type per parameter]} of the header's declarations."""
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    out = {}
+    for m in re.finditer(r"\b(tw_[a-z0-9_]+)\s*\(([^)]*)\)\s*;", text):
+        params = [p.strip() for p in m.group(2).split(",") if p.strip() not in ("", "void")]
+        out[m.group(1)] = [re.sub(r"\s*\b[A-Za-z_][A-Za-z0-9_]*$", "", p) for p in params]
+    return out
+
+
+def _ctype_of(decl):
+    if "*" in decl:
+        return ctypes.c_void_p
+    if "size_t" in decl:
+        return ctypes.c_size_t
+    if "double" in decl:
+        return ctypes.c_double
+    return ctypes.c_int
+
+
+def test_ctypes_signatures_match_header():
+    """Every ctypes binding has the header's parameter count and kinds
+    (pointer, size_t, double, int): a mismatch would pass garbage through the
+    C ABI on the GPU box."""
+    decls = _header_param_types()
+    assert len(decls) == len(_header_functions())
+    for name, params in decls.items():
+        _, argtypes = _native.SIGNATURES[name]
+        assert len(argtypes) == len(params), (name, len(argtypes), len(params))
+        for k, (decl, got) in enumerate(zip(params, argtypes)):
+            assert got is _ctype_of(decl), (name, k, decl, got)
+
+
 def test_library_host_calls_without_gpu():
     lib = _native.lib()
     assert lib.tw_version() >= 100

@@ -69,6 +69,12 @@ SIGNATURES = {
     "tw_fvm_softmin_f64": (_c_i, [_c_p, _c_i, _c_i, _c_i, _c_d, _c_p, _c_p]),
     "tw_fvm_softmin_backward_f32": (_c_i, [_c_p, _c_p, _c_i, _c_i, _c_i, _c_d, _c_p, _c_p]),
     "tw_fvm_softmin_backward_f64": (_c_i, [_c_p, _c_p, _c_i, _c_i, _c_i, _c_d, _c_p, _c_p]),
+    "tw_jeanie_fused_supported": (_c_i, [_c_i] * 6),
+    "tw_jeanie_fused_saved_bytes": (_c_sz, [_c_i] * 6),
+    "tw_jeanie_fused_forward_f32": (_c_i, [_c_p] * 3 + [_c_i] * 10 + [_c_d, _c_p, _c_p, _c_p, _c_sz,
+                                                                  _c_p]),
+    "tw_jeanie_fused_backward_f32": (_c_i, [_c_p] * 5 + [_c_i] * 10 + [_c_d, _c_p, _c_sz, _c_p,
+                                                                   _c_p, _c_p, _c_p]),
     "tw_optimal_path_f64": (_c_i, [_c_p] + [_c_i] * 6 + [_c_p] * 5),
 }
 

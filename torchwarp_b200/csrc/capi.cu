@@ -171,6 +171,12 @@ template <typename T>
 int fvm_softmin_bwd(const T*, const T*, int, int, int, double, T*, cudaStream_t);
 int optimal_path(const double*, int, int, int, int, int, int, double*, int*, int*, int*,
                  cudaStream_t);
+bool jf_supported(int K, int T, int U, int D, bool fvm, bool feat);
+size_t jf_saved_bytes(int B, int K, int T, int U, bool fvm, bool feat);
+int jf_run(const float* q, const float* s, const float* cost, int B, int K1, int K2, int T, int U,
+           int D, int s1, int s2, int metric, bool fvm, double gamma, bool fwd, float* out,
+           float* Rnat, void* saved, size_t saved_bytes, const float* g_out, const float* g_R,
+           float* dq, float* ds, float* dC, cudaStream_t st);
 
 static int check_jeanie(const char* who, int B, int K1, int K2, int T, int U, int s1, int s2,
                         double gamma) {
@@ -390,6 +396,61 @@ int tw_udtw_features_grad_f64(const double* X, const double* Y, const double* vx
 TW_JEANIE_ENTRIES(f32, float)
 TW_JEANIE_ENTRIES(f64, double)
 #undef TW_JEANIE_ENTRIES
+
+int tw_jeanie_fused_supported(int K, int T, int U, int D, int fvm, int features) {
+  return jf_supported(K, T, U, D, fvm != 0, features != 0) ? 1 : 0;
+}
+
+size_t tw_jeanie_fused_saved_bytes(int B, int K, int T, int U, int fvm, int features) {
+  if (B < 0 || K <= 0 || T <= 0 || U <= 0) return 0;
+  return jf_saved_bytes(B, K, T, U, fvm != 0, features != 0);
+}
+
+static int check_fused(const char* who, const float* query, const float* support,
+                       const float* cost, int B, int K1, int K2, int T, int U, int D, int s1,
+                       int s2, int metric, int fvm, double gamma) {
+  if (B < 0 || K1 <= 0 || K2 <= 0 || T <= 0 || U <= 0 || s1 < 0 || s2 < 0 || !(gamma > 0) ||
+      (metric != 0 && metric != 1) || (fvm && K2 != 1))
+    return set_error(kInvalid, "%s: invalid arguments (B=%d K1=%d K2=%d T=%d U=%d D=%d)", who, B,
+                     K1, K2, T, U, D);
+  const bool feat = query != nullptr;
+  if (B && (feat ? (support == nullptr || cost != nullptr || D <= 0) : cost == nullptr))
+    return set_error(kInvalid, "%s: pass query and support (and no cost), or a cost", who);
+  return kOk;
+}
+
+int tw_jeanie_fused_forward_f32(const float* query, const float* support, const float* cost,
+                                int B, int K1, int K2, int T, int U, int D, int s1, int s2,
+                                int metric, int fvm, double gamma, float* out, float* R,
+                                void* saved, size_t saved_bytes, void* stream) {
+  g_err[0] = 0;
+  if (int e = check_fused("tw_jeanie_fused_forward", query, support, cost, B, K1, K2, T, U, D, s1,
+                          s2, metric, fvm, gamma))
+    return e;
+  if (B && (!out || !saved)) return set_error(kInvalid, "tw_jeanie_fused_forward: null pointer");
+  return jf_run(query, support, cost, B, K1, K2, T, U, D, s1, s2, metric, fvm != 0, gamma, true,
+                out, fvm ? nullptr : R, saved, saved_bytes, nullptr, nullptr, nullptr, nullptr,
+                nullptr, (cudaStream_t)stream);
+}
+
+int tw_jeanie_fused_backward_f32(const float* query, const float* support, const float* cost,
+                                 const float* grad_out, const float* grad_R, int B, int K1, int K2,
+                                 int T, int U, int D, int s1, int s2, int metric, int fvm,
+                                 double gamma, const void* saved, size_t saved_bytes,
+                                 float* d_query, float* d_support, float* d_cost, void* stream) {
+  g_err[0] = 0;
+  if (int e = check_fused("tw_jeanie_fused_backward", query, support, cost, B, K1, K2, T, U, D,
+                          s1, s2, metric, fvm, gamma))
+    return e;
+  const bool feat = query != nullptr;
+  if (B && (!grad_out || !saved || (feat ? (!d_query || !d_support) : !d_cost)))
+    return set_error(kInvalid, "tw_jeanie_fused_backward: null pointer");
+  if (fvm && grad_R != nullptr)
+    return set_error(kInvalid, "tw_jeanie_fused_backward: FVM has no accumulator gradient");
+  return jf_run(query, support, cost, B, K1, K2, T, U, D, s1, s2, metric, fvm != 0, gamma, false,
+                nullptr, nullptr, const_cast<void*>(saved), saved_bytes, grad_out, grad_R,
+                d_query, d_support, d_cost, (cudaStream_t)stream);
+}
 
 int tw_optimal_path_f64(const double* cost, int B, int K, int T, int U, int max_shift,
                         int start_view, double* r_ws, int* back_ws, int* path, int* length,

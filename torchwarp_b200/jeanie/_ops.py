@@ -20,6 +20,7 @@ float32 under autocast; the autograd Functions let torch.func generate their
 vmap rules from these.  The backward ops are first-order only.
 """
 
+import os
 from typing import Optional, Tuple
 
 import torch
@@ -27,7 +28,7 @@ from torch import Tensor
 
 from .. import _native as nat
 from .. import _transforms
-from .._vmap import register_fold_rule
+from .._vmap import register_fold_rule, round_to_pairs
 
 
 def _register_autocast(op):
@@ -390,3 +391,182 @@ class FvmSoftmin(torch.autograd.Function):
 JeanieDPTraced = _transforms.traceable(JeanieDP)
 QSCostTraced = _transforms.traceable(QSCost)
 FvmSoftminTraced = _transforms.traceable(FvmSoftmin)
+
+
+# ------------------------------------------- fused JEANIE / FVM (float32)
+
+def fused_supported(K, T, U, D, fvm, features):
+    """Whether tw_jeanie_fused_* take this shape (features: even D <= 256,
+    U <= 15; a pair's state within the kernel's shared memory).  The
+    environment variable TW_JEANIE_UNFUSED (any value but "0") turns the
+    fused path off, for A/B comparisons with the separate cost / soft-min /
+    DP kernels."""
+    env = os.environ.get("TW_JEANIE_UNFUSED", "")
+    if env not in ("", "0"):
+        return False
+    return bool(nat.lib().tw_jeanie_fused_supported(int(K), int(T), int(U), int(D), int(fvm),
+                                                    int(features)))
+
+
+def _fused_saved_bytes(B, K, T, U, fvm, features):
+    return int(nat.lib().tw_jeanie_fused_saved_bytes(B, K, T, U, int(fvm), int(features)))
+
+
+@torch.library.custom_op("torchwarp_b200::jeanie_fused", mutates_args=())
+def jeanie_fused(query: Optional[Tensor], support: Optional[Tensor], cost: Optional[Tensor],
+                 K1: int, K2: int, T: int, U: int, s1: int, s2: int, gamma: float, metric: int,
+                 fvm: bool, keep_R: bool) -> Tuple[Tensor, Tensor, Tensor]:
+    """JEANIE (fvm False) or FVM (fvm True) on features (query [B, K1 K2 T, D],
+    support [B, U, D]) or on a cost [B, K1, K2, T, U] ([B, K, T, U] for FVM).
+    Returns (out [B], accumulator [B, K1, K2, T, U] or an empty tensor, saved
+    state bytes)."""
+    feat = query is not None
+    ref = query if feat else cost
+    nat.require_cuda(ref, support)
+    B = ref.shape[0]
+    D = query.shape[-1] if feat else 0
+    q = query.contiguous() if feat else None
+    s = support.contiguous() if feat else None
+    c = None if feat else cost.contiguous()
+    out = ref.new_empty(B)
+    R = ref.new_empty(B, K1, K2, T, U) if (keep_R and not fvm) else ref.new_empty(0)
+    sb = round_to_pairs(_fused_saved_bytes(B, K1 * K2, T, U, fvm, feat), B)
+    saved = torch.empty(sb, dtype=torch.uint8, device=ref.device)
+    if B:
+        with torch.cuda.device(ref.device):
+            nat.check(nat.call("jeanie_fused_forward", nat.lib().tw_jeanie_fused_forward_f32,
+                               nat.ptr(q), nat.ptr(s), nat.ptr(c), B, K1, K2, T, U, D, s1, s2,
+                               metric, int(fvm), float(gamma), nat.ptr(out),
+                               nat.ptr(R) if R.numel() else None, nat.ptr(saved), sb,
+                               nat.stream_of(ref)), "tw_jeanie_fused_forward")
+    return out, R, saved
+
+
+@jeanie_fused.register_fake
+def _(query, support, cost, K1, K2, T, U, s1, s2, gamma, metric, fvm, keep_R):
+    feat = query is not None
+    ref = query if feat else cost
+    B = ref.shape[0]
+    sb = round_to_pairs(_fused_saved_bytes(B, K1 * K2, T, U, fvm, feat), B) if B else 0
+    R = ref.new_empty(B, K1, K2, T, U) if (keep_R and not fvm) else ref.new_empty(0)
+    return ref.new_empty(B), R, ref.new_empty(sb, dtype=torch.uint8)
+
+
+@torch.library.custom_op("torchwarp_b200::jeanie_fused_backward", mutates_args=())
+def jeanie_fused_backward(query: Optional[Tensor], support: Optional[Tensor],
+                          cost: Optional[Tensor], saved: Tensor, grad_out: Tensor,
+                          grad_R: Optional[Tensor], K1: int, K2: int, T: int, U: int, s1: int,
+                          s2: int, gamma: float, metric: int,
+                          fvm: bool) -> Tuple[Tensor, Tensor, Tensor]:
+    """(d_query, d_support, d_cost) for L = sum grad_out * out + <grad_R, R>;
+    the inputs that were not given come back as empty tensors."""
+    feat = query is not None
+    ref = query if feat else cost
+    nat.require_cuda(ref, grad_out)
+    B = ref.shape[0]
+    D = query.shape[-1] if feat else 0
+    q = query.contiguous() if feat else None
+    s = support.contiguous() if feat else None
+    c = None if feat else cost.contiguous()
+    dq = torch.empty_like(q) if feat else ref.new_empty(0)
+    ds = torch.empty_like(s) if feat else ref.new_empty(0)
+    dC = ref.new_empty(0) if feat else torch.empty_like(c)
+    if B:
+        g_out = grad_out.to(ref.dtype).contiguous()
+        gR = None if grad_R is None else grad_R.to(ref.dtype).contiguous()
+        with torch.cuda.device(ref.device):
+            nat.check(nat.call("jeanie_fused_backward", nat.lib().tw_jeanie_fused_backward_f32,
+                               nat.ptr(q), nat.ptr(s), nat.ptr(c), nat.ptr(g_out), nat.ptr(gR), B,
+                               K1, K2, T, U, D, s1, s2, metric, int(fvm), float(gamma),
+                               nat.ptr(saved), saved.numel(), nat.ptr(dq) if feat else None,
+                               nat.ptr(ds) if feat else None, None if feat else nat.ptr(dC),
+                               nat.stream_of(ref)), "tw_jeanie_fused_backward")
+    return dq, ds, dC
+
+
+@jeanie_fused_backward.register_fake
+def _(query, support, cost, saved, grad_out, grad_R, K1, K2, T, U, s1, s2, gamma, metric, fvm):
+    feat = query is not None
+    ref = query if feat else cost
+    return ((torch.empty_like(query) if feat else ref.new_empty(0)),
+            (torch.empty_like(support) if feat else ref.new_empty(0)),
+            (ref.new_empty(0) if feat else torch.empty_like(cost)))
+
+
+_register_autocast(jeanie_fused)
+_register_autocast(jeanie_fused_backward)
+register_fold_rule(jeanie_fused, flat_out=(2,), placeholder_out=(1,))
+register_fold_rule(jeanie_fused_backward, flat_in=(3,), placeholder_out=(0, 1, 2))
+
+
+class JeanieFused(torch.autograd.Function):
+    """(query?, support?, cost?) -> (out, accumulator, saved): JEANIE or FVM in
+    one native call per direction (float32).  The accumulator is
+    differentiable when requested (keep_R).
+
+    Forward mode: the tangent of the distance is the inner product of its
+    gradient (one native backward with unit seeds) with the input tangents;
+    with keep_R it raises, as for JeanieDP."""
+
+    generate_vmap_rule = True
+
+    @staticmethod
+    def forward(query, support, cost, K1, K2, T, U, s1, s2, gamma, metric, fvm, keep_R):
+        return jeanie_fused(query, support, cost, K1, K2, T, U, s1, s2, gamma, metric, fvm,
+                            keep_R)
+
+    @staticmethod
+    def setup_context(ctx, inputs, output):
+        query, support, cost, K1, K2, T, U, s1, s2, gamma, metric, fvm, keep_R = inputs
+        ctx.set_materialize_grads(False)
+        ctx.mark_non_differentiable(output[2])
+        if not keep_R or fvm:
+            ctx.mark_non_differentiable(output[1])
+        ctx.save_for_backward(query, support, cost, output[2])
+        ctx.save_for_forward(query, support, cost, output[2])
+        ctx.args = (K1, K2, T, U, s1, s2, gamma, metric, fvm, keep_R)
+
+    @staticmethod
+    @_transforms.once_differentiable
+    def backward(ctx, g_out, g_R, _g_saved):
+        query, support, cost, saved = ctx.saved_tensors
+        K1, K2, T, U, s1, s2, gamma, metric, fvm, _ = ctx.args
+        ref = query if query is not None else cost
+        if g_out is None:
+            g_out = ref.new_zeros(ref.shape[0])
+        dq, ds, dC = jeanie_fused_backward(query, support, cost, saved, g_out, g_R, K1, K2, T, U,
+                                           s1, s2, gamma, metric, fvm)
+        if query is not None:
+            return (dq, ds, None) + (None,) * 10
+        return (None, None, dC) + (None,) * 10
+
+    @staticmethod
+    def jvp(ctx, q_t, s_t, c_t, *_):
+        query, support, cost, saved = ctx.saved_tensors
+        K1, K2, T, U, s1, s2, gamma, metric, fvm, keep_R = ctx.args
+        if keep_R and not fvm:
+            raise NotImplementedError("forward mode through the JEANIE accumulator "
+                                      "(return_accumulator=True) is not implemented")
+        ref = query if query is not None else cost
+        B = ref.shape[0]
+        dq, ds, dC = jeanie_fused_backward(query, support, cost, saved, ref.new_ones(B), None, K1,
+                                           K2, T, U, s1, s2, gamma, metric, fvm)
+        t = ref.new_zeros(B)
+        if query is not None:
+            if q_t is not None:
+                t = t + (dq * q_t).flatten(1).sum(1)
+            if s_t is not None:
+                t = t + (ds * s_t).flatten(1).sum(1)
+        elif c_t is not None:
+            t = t + (dC * c_t).flatten(1).sum(1)
+        return t, None, None
+
+
+JeanieFusedTraced = _transforms.traceable(JeanieFused)
+
+
+def fused_apply(query, support, cost, K1, K2, T, U, s1, s2, gamma, metric, fvm, keep_R):
+    """JeanieFused.apply (its traceable twin under torch.compile)."""
+    return _transforms.pick(JeanieFused, JeanieFusedTraced).apply(
+        query, support, cost, int(K1), int(K2), int(T), int(U), int(s1), int(s2), float(gamma),
+        int(metric), bool(fvm), bool(keep_R))

@@ -17,6 +17,12 @@ _BACKENDS = ("auto", "cuda", "torch")
 _METRICS = {"sqeuclidean": 0, "euclidean": 1}
 
 
+def _feature_dtype(query, support):
+    """The dtype the native kernels compute in for these features."""
+    dtype = torch.promote_types(query.dtype, support.dtype)
+    return dtype if dtype in (torch.float32, torch.float64) else torch.float32
+
+
 def _check_common(gamma, max_shift_1, max_shift_2, backend):
     if gamma <= 0:
         raise ValueError("gamma must be > 0")
@@ -49,6 +55,10 @@ def _jeanie_dp(cost, gamma=0.1, max_shift_1=1, max_shift_2=1, backend="auto",
         cost = cost.float()
     s1 = min(int(max_shift_1), K1 - 1)
     s2 = min(int(max_shift_2), K2 - 1)
+    if cost.dtype == torch.float32 and _ops.fused_supported(K1 * K2, T, U, 0, False, False):
+        out, R, _ = _ops.fused_apply(None, None, cost, K1, K2, T, U, s1, s2, gamma, 0, False,
+                                     return_accumulator)
+        return out, (R if return_accumulator else None)
     out, R = _transforms.pick(_ops.JeanieDP, _ops.JeanieDPTraced).apply(
         cost, s1, s2, float(gamma), bool(return_accumulator))
     return out, (R if return_accumulator else None)
@@ -68,6 +78,14 @@ def _jeanie_dp_features(query, support, gamma=0.1, max_shift_1=1, max_shift_2=1,
     U = support.shape[1]
     if min(K1, K2, T, U) == 0:
         raise ValueError("query/support dimensions must be non-empty")
+    if metric != "rbf" and _feature_dtype(query, support) == torch.float32 and \
+            _ops.fused_supported(K1 * K2, T, U, D, False, True):
+        # one native call per direction: cost, DP and chain rule on chip
+        out, R, _ = _ops.fused_apply(
+            query.to(torch.float32).reshape(B, K1 * K2 * T, D), support.to(torch.float32), None,
+            K1, K2, T, U, min(int(max_shift_1), K1 - 1), min(int(max_shift_2), K2 - 1), gamma,
+            _METRICS[metric], False, return_accumulator)
+        return out, (R if return_accumulator else None)
     if metric == "rbf":
         cost = rbf_cost(query.reshape(B, K1 * K2, T, D), support).reshape(B, K1, K2, T, U)
     else:

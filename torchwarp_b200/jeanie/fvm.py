@@ -8,12 +8,21 @@ the result (native DP).
 import torch
 
 from .. import sdtw
+from ..udtw.functional import _BACKENDS, _check_backend
 from .. import _transforms
 from . import _ops
 from .distances import euclidean_cost, rbf_cost, squared_euclidean_cost
 
 _METRICS = {"euclidean": euclidean_cost, "sqeuclidean": squared_euclidean_cost,
             "rbf": rbf_cost}
+
+
+def _check_backend_name(backend):
+    """The backend check of soft_dtw_from_cost (sdtw.py), for the fused path
+    that does not go through it."""
+    if backend not in _BACKENDS:
+        raise ValueError("backend must be one of {}".format(_BACKENDS))
+    _check_backend(backend)
 
 
 def fvm_from_cost(cost, *, gamma=0.1, backend="auto"):
@@ -29,6 +38,12 @@ def fvm_from_cost(cost, *, gamma=0.1, backend="auto"):
     flat = cost.reshape(B, -1, T, U)
     if flat.dtype not in (torch.float32, torch.float64):
         flat = flat.float()
+    _check_backend_name(backend)
+    K = flat.shape[1]
+    if flat.dtype == torch.float32 and min(K, T, U) > 0 and \
+            _ops.fused_supported(K, T, U, 0, True, False):
+        # viewpoint soft-min and soft-DTW in one native call per direction
+        return _ops.fused_apply(None, None, flat, K, 1, T, U, 0, 0, gamma, 0, True, False)[0]
     temporal = _transforms.pick(_ops.FvmSoftmin, _ops.FvmSoftminTraced).apply(flat, float(gamma))
     return sdtw.soft_dtw_from_cost(temporal, gamma=gamma, backend=backend)
 
@@ -44,6 +59,18 @@ def fvm(query, support, *, gamma=0.1, metric="euclidean", backend="auto"):
     U = support.shape[-2]
     q = query.reshape(B, -1, T, D)
     if support.ndim == 3:
+        K = q.shape[1]
+        dtype = torch.promote_types(query.dtype, support.dtype)
+        dtype = dtype if dtype in (torch.float32, torch.float64) else torch.float32
+        if metric != "rbf" and dtype == torch.float32 and gamma > 0 and \
+                support.shape[0] == B and support.shape[-1] == D and min(K, T, U) > 0 and \
+                _ops.fused_supported(K, T, U, D, True, True):
+            _check_backend_name(backend)
+            # cost, viewpoint soft-min, soft-DTW and their backward on chip:
+            # the [B, K, T, U] cost never reaches HBM as a separate tensor
+            return _ops.fused_apply(q.to(torch.float32).reshape(B, K * T, D),
+                                    support.to(torch.float32), None, K, 1, T, U, 0, 0, gamma,
+                                    1 if metric == "euclidean" else 0, True, False)[0]
         cost = _METRICS[metric](q, support)                      # [B, K, T, U]
     else:
         # Every (query viewpoint, support viewpoint) pair: all K' U support
