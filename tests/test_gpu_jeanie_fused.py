@@ -42,9 +42,10 @@ JEANIE_CASES = [
     # (query shape, support shape, max_shift, metric)
     ((3, 15, 10, 256), (3, 10, 256), 1, "euclidean"),      # cfg3's shape (few pairs)
     ((4, 5, 7, 64), (4, 9, 64), 2, "sqeuclidean"),
-    ((2, 1, 12, 6), (2, 5, 6), 0, "euclidean"),             # one viewpoint
+    ((2, 1, 12, 8), (2, 5, 8), 0, "euclidean"),             # one viewpoint
     ((2, 3, 4, 6, 100), (2, 11, 100), (1, 2), "euclidean"),  # two viewpoint axes, D = 100
-    ((5, 8, 1, 2), (5, 15, 2), 3, "sqeuclidean"),           # T = 1, U = 15, D = 2
+    ((5, 8, 1, 4), (5, 15, 4), 3, "sqeuclidean"),           # T = 1, U = 15, D = 4
+    ((3, 6, 5, 6), (3, 7, 6), 1, "euclidean"),              # D = 6: separate kernels
 ]
 
 
@@ -99,7 +100,8 @@ def test_jeanie_cost_fp32_vs_oracle(tw, orc, shape, shift):
 @pytest.mark.parametrize("qshape,sshape,metric", [
     ((3, 7, 7, 10, 256), (3, 10, 256), "euclidean"),        # cfg4's shape (few pairs)
     ((4, 5, 6, 64), (4, 8, 64), "sqeuclidean"),
-    ((2, 3, 1, 14), (2, 15, 14), "euclidean"),
+    ((2, 3, 1, 12), (2, 15, 12), "euclidean"),
+    ((2, 3, 5, 10), (2, 6, 10), "euclidean"),                # D = 10: separate kernels
 ])
 def test_fvm_features_fp32_vs_oracle(tw, orc, qshape, sshape, metric):
     g = torch.Generator().manual_seed(sum(qshape) + 1)

@@ -9,10 +9,10 @@
 // (viewpoint soft-min, then soft-DTW).  Recurrences as jeanie.cu.
 //
 // Layout and roles.
-//   * The CTA has W = ceil(D / 64) warps; warp w owns features
-//     [64 w, 64 w + 64) of every query row and support frame (two per lane).
-//     Each warp streams all K*T query rows of the pair (its feature slice,
-//     256 contiguous bytes per row, JF_PF rows in flight), keeps its slice
+//   * The CTA has W = ceil(D / 128) warps; warp w owns features
+//     [128 w, 128 w + 128) of every query row and support frame (four per
+//     lane).  Each warp streams all K*T query rows of the pair (its feature
+//     slice, 512 contiguous bytes per row, JF_PF rows in flight), keeps its slice
 //     of the U support frames in registers, and reduces the U dot products
 //     and |q|^2 of a row across its lanes by recursive halving (16 values in
 //     16 shuffles).  The W partial sums of a row meet in shared memory in a
@@ -84,8 +84,17 @@ __device__ __forceinline__ int jf_slot(int lane) {
   return ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
 }
 
-__device__ __forceinline__ float2 ld_row2(const float* p, bool ok) {
-  return ok ? __ldg(reinterpret_cast<const float2*>(p)) : make_float2(0.f, 0.f);
+__device__ __forceinline__ float4 ld_row4(const float* p, bool ok) {
+  return ok ? __ldg(reinterpret_cast<const float4*>(p)) : make_float4(0.f, 0.f, 0.f, 0.f);
+}
+__device__ __forceinline__ float dot4(float4 a, float4 b) {
+  return fmaf(a.x, b.x, fmaf(a.y, b.y, fmaf(a.z, b.z, a.w * b.w)));
+}
+__device__ __forceinline__ void fma4(float4& acc, float w, float4 v) {
+  acc.x = fmaf(w, v.x, acc.x);
+  acc.y = fmaf(w, v.y, acc.y);
+  acc.z = fmaf(w, v.z, acc.z);
+  acc.w = fmaf(w, v.w, acc.w);
 }
 
 // ------------------------------------------------------------ the DP
@@ -211,8 +220,11 @@ struct JFSmem {
   float* C;     // [K T U] cost (FVM backward: dC, then dsq, in place)
   float* tmp;   // FVM: [T U] viewpoint soft-min
   float* r;     // [dpn] relative DP values
-  float* G;     // [dpn] adjoint (JEANIE backward: then dsq, in place)
+  float* G;     // [dpn] adjoint
   float* part;  // [W][JF_ROWS][16] partial row sums (forward, features)
+  float* Sp;    // [K T][16] dL/dsq per query row, zero past U (backward, features)
+  float* rs;    // [K T] row sums of Sp
+  float* cs;    // [16] column sums of Sp
 };
 
 __host__ __device__ inline size_t jf_align16(size_t n) { return (n + 15) & ~size_t(15); }
@@ -220,6 +232,8 @@ __host__ __device__ inline size_t jf_align16(size_t n) { return (n + 15) & ~size
 // Byte offsets of the shared-memory regions (same on host and device).
 __host__ __device__ inline size_t jf_smem_layout(int K, int T, int U, int W, bool fvm, bool fwd,
                                                  bool feat, size_t* off) {
+  const int R = K * T;
+  const bool chain = !fwd && feat;
   const int KTU = K * T * U, TU = T * U, ND = T + U - 1, dpn = fvm ? TU : KTU;
   size_t o = 0;
   off[0] = o; o = jf_align16(o + sizeof(double) * ND);   // base
@@ -230,12 +244,15 @@ __host__ __device__ inline size_t jf_smem_layout(int K, int T, int U, int W, boo
   off[5] = o; o = jf_align16(o + sizeof(float) * dpn);   // r
   off[6] = o; o = jf_align16(o + sizeof(float) * (fwd ? 0 : dpn));  // G
   off[7] = o; o = jf_align16(o + sizeof(float) * ((fwd && feat) ? W * JF_ROWS * JF_SLOT : 0));
+  off[8] = o; o = jf_align16(o + sizeof(float) * (chain ? R * JF_SLOT : 0));
+  off[9] = o; o = jf_align16(o + sizeof(float) * (chain ? R : 0));
+  off[10] = o; o = jf_align16(o + sizeof(float) * (chain ? JF_SLOT : 0));
   return o;
 }
 
 __device__ inline JFSmem jf_carve(unsigned char* smem, int K, int T, int U, int W, bool fvm,
                                   bool fwd, bool feat) {
-  size_t off[8];
+  size_t off[11];
   jf_smem_layout(K, T, U, W, fvm, fwd, feat, off);
   JFSmem s;
   s.base = reinterpret_cast<double*>(smem + off[0]);
@@ -246,6 +263,9 @@ __device__ inline JFSmem jf_carve(unsigned char* smem, int K, int T, int U, int 
   s.r = reinterpret_cast<float*>(smem + off[5]);
   s.G = reinterpret_cast<float*>(smem + off[6]);
   s.part = reinterpret_cast<float*>(smem + off[7]);
+  s.Sp = reinterpret_cast<float*>(smem + off[8]);
+  s.rs = reinterpret_cast<float*>(smem + off[9]);
+  s.cs = reinterpret_cast<float*>(smem + off[10]);
   return s;
 }
 
@@ -289,7 +309,7 @@ struct JFArgs {
 // (all warps' partials, fixed order) to s2[0..U).
 template <int CU>
 __device__ __forceinline__ void load_support(const JFArgs& a, int b, int warp, int lane, int d0,
-                                             bool dv, float2 (&sv)[CU], float* part,
+                                             bool dv, float4 (&sv)[CU], float* part,
                                              float* s2) {
   const JFGeom& g = a.g;
   const float* sb = a.s + (long long)b * g.U * g.D + d0;
@@ -298,8 +318,8 @@ __device__ __forceinline__ void load_support(const JFArgs& a, int b, int warp, i
   for (int u = 0; u < JF_SLOT; ++u) v[u] = 0.f;
 #pragma unroll
   for (int u = 0; u < CU; ++u) {
-    sv[u] = ld_row2(sb + (long long)u * g.D, dv && u < g.U);
-    v[u] = fmaf(sv[u].x, sv[u].x, sv[u].y * sv[u].y);
+    sv[u] = ld_row4(sb + (long long)u * g.D, dv && u < g.U);
+    v[u] = dot4(sv[u], sv[u]);
   }
   const float red = reduce16(v, lane);
   if (!(lane & 1)) part[warp * JF_SLOT + jf_slot(lane)] = red;
@@ -314,32 +334,32 @@ __device__ __forceinline__ void load_support(const JFArgs& a, int b, int warp, i
 
 // The pair's cost [K T, U] into C (shared memory) from the features.
 template <int CU>
-__device__ void build_cost(const JFArgs& a, int b, const JFSmem& sm, float2 (&sv)[CU]) {
+__device__ void build_cost(const JFArgs& a, int b, const JFSmem& sm, float4 (&sv)[CU]) {
   const JFGeom& g = a.g;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int d0 = 64 * warp + 2 * lane;
+  const int d0 = 128 * warp + 4 * lane;
   const bool dv = d0 < g.D;
   load_support<CU>(a, b, warp, lane, d0, dv, sv, sm.part, sm.s2);
   const float* qb = a.q + (long long)b * g.R * g.D + d0;
-  float2 pf[JF_PF];
+  float4 pf[JF_PF];
 #pragma unroll
-  for (int p = 0; p < JF_PF; ++p) pf[p] = ld_row2(qb + (long long)p * g.D, dv && p < g.R);
+  for (int p = 0; p < JF_PF; ++p) pf[p] = ld_row4(qb + (long long)p * g.D, dv && p < g.R);
   for (int r0 = 0; r0 < g.R; r0 += JF_ROWS) {
 #pragma unroll 1
     for (int k = 0; k < JF_ROWS; k += JF_PF) {
 #pragma unroll
       for (int p = 0; p < JF_PF; ++p) {
         const int r = r0 + k + p;
-        const float2 qv = pf[p];
+        const float4 qv = pf[p];
         const int rn = r + JF_PF;
-        pf[p] = ld_row2(qb + (long long)rn * g.D, dv && rn < g.R);
+        pf[p] = ld_row4(qb + (long long)rn * g.D, dv && rn < g.R);
         if (r < g.R) {
           float v[JF_SLOT];
 #pragma unroll
           for (int u = 0; u < JF_SLOT; ++u) v[u] = 0.f;
 #pragma unroll
-          for (int u = 0; u < CU; ++u) v[u] = fmaf(qv.x, sv[u].x, qv.y * sv[u].y);
-          v[JF_SLOT - 1] = fmaf(qv.x, qv.x, qv.y * qv.y);
+          for (int u = 0; u < CU; ++u) v[u] = dot4(qv, sv[u]);
+          v[JF_SLOT - 1] = dot4(qv, qv);
           const float red = reduce16(v, lane);
           if (!(lane & 1)) sm.part[(warp * JF_ROWS + k + p) * JF_SLOT + jf_slot(lane)] = red;
         }
@@ -374,7 +394,7 @@ __global__ void __launch_bounds__(128) jf_forward_kernel(const JFArgs a) {
   const int KTU = g.K * g.T * g.U, TU = g.T * g.U, ND = g.T + g.U - 1;
   const int dpn = FVM ? TU : KTU;
   if constexpr (FEAT) {
-    float2 sv[CU];
+    float4 sv[CU];
     build_cost<CU>(a, b, sm, sv);
     float* Cs = reinterpret_cast<float*>(a.saved + a.sv.c) + (long long)b * KTU;
     for (int i = threadIdx.x; i < KTU; i += blockDim.x) Cs[i] = sm.C[i];
@@ -454,67 +474,90 @@ __global__ void __launch_bounds__(128) jf_backward_kernel(const JFArgs a) {
                        g.U, g.s1, g.s2, g.kap, g.ikap, lane);
   }
   __syncthreads();
-  // dL/dC per cell; with features, turned into dL/dsq in place (S below):
-  // the clamp passes it where the cost is > 0, the Euclidean root divides by
-  // 2 cost (no gradient at cost 0, jeanie/distances.py:34-38)
-  float* S = FVM ? sm.C : sm.G;
-  for (int i = threadIdx.x; i < KTU; i += blockDim.x) {
-    const float c = sm.C[i];
-    float dc;
+  // dL/dC per cell; with features, dL/dsq per query row (Sp, padded to 16
+  // columns with zeros) and its row and column sums: the clamp passes dL/dC
+  // where the cost is > 0, the Euclidean root divides by 2 cost (no gradient
+  // at cost 0, jeanie/distances.py:34-38)
+  auto dcost = [&](int i) {
     if constexpr (FVM) {
       const int tu = i % TU;
-      dc = ex2((sm.tmp[tu] - c) * g.kap) * sm.G[tu];  // viewpoint soft-min weight x dtemporal
+      return ex2((sm.tmp[tu] - sm.C[i]) * g.kap) * sm.G[tu];  // viewpoint weight x dtemporal
     } else {
-      dc = sm.G[i];
+      return sm.G[i];
     }
-    if constexpr (!FEAT) {
-      a.dC[(long long)b * KTU + i] = dc;
-    } else {
-      S[i] = c > 0.f ? (g.metric == 1 ? dc * (0.5f / c) : dc) : 0.f;
+  };
+  if constexpr (!FEAT) {
+    for (int i = threadIdx.x; i < KTU; i += blockDim.x) a.dC[(long long)b * KTU + i] = dcost(i);
+  } else {
+    for (int i = threadIdx.x; i < g.R * JF_SLOT; i += blockDim.x) {
+      const int r = i >> 4, u = i & 15;
+      float v = 0.f;
+      if (u < g.U) {
+        const int o = r * g.U + u;
+        const float c = sm.C[o], dc = dcost(o);
+        v = c > 0.f ? (g.metric == 1 ? dc * (0.5f / c) : dc) : 0.f;
+      }
+      sm.Sp[i] = v;
     }
-  }
-  if constexpr (FEAT) {
     __syncthreads();
-    const int d0 = 64 * warp + 2 * lane;
+    for (int r = threadIdx.x; r < g.R; r += blockDim.x) {
+      float t = 0.f;
+      for (int u = 0; u < g.U; ++u) t += sm.Sp[r * JF_SLOT + u];
+      sm.rs[r] = t;
+    }
+    if ((int)threadIdx.x < JF_SLOT) {
+      float t = 0.f;
+      for (int r = 0; r < g.R; ++r) t += sm.Sp[r * JF_SLOT + threadIdx.x];
+      sm.cs[threadIdx.x] = t;
+    }
+    __syncthreads();
+    // dq_r = 2 (q_r rowsum_r - sum_u S_ru s_u); ds_u = 2 (s_u colsum_u - sum_r S_ru q_r)
+    const int d0 = 128 * warp + 4 * lane;
     const bool dv = d0 < g.D;
     const float* sb = a.s + (long long)b * g.U * g.D + d0;
-    float2 sv[CU], acc[CU];
-    float cs[CU];
+    float4 sv[CU], acc[CU];
 #pragma unroll
     for (int u = 0; u < CU; ++u) {
-      sv[u] = ld_row2(sb + (long long)u * g.D, dv && u < g.U);
-      acc[u] = make_float2(0.f, 0.f);
-      cs[u] = 0.f;
+      sv[u] = ld_row4(sb + (long long)u * g.D, dv && u < g.U);
+      acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     const float* qb = a.q + (long long)b * g.R * g.D + d0;
     float* dqb = a.dq + (long long)b * g.R * g.D + d0;
-    float2 pf[JF_PF];
+    float4 pf[JF_PF];
 #pragma unroll
-    for (int p = 0; p < JF_PF; ++p) pf[p] = ld_row2(qb + (long long)p * g.D, dv && p < g.R);
+    for (int p = 0; p < JF_PF; ++p) pf[p] = ld_row4(qb + (long long)p * g.D, dv && p < g.R);
     for (int r0 = 0; r0 < g.R; r0 += JF_PF) {
 #pragma unroll
       for (int p = 0; p < JF_PF; ++p) {
         const int r = r0 + p;
-        const float2 qv = pf[p];
+        const float4 qv = pf[p];
         const int rn = r + JF_PF;
-        pf[p] = ld_row2(qb + (long long)rn * g.D, dv && rn < g.R);
+        pf[p] = ld_row4(qb + (long long)rn * g.D, dv && rn < g.R);
         if (r < g.R) {
-          float rsum = 0.f, tx = 0.f, ty = 0.f;
+          float w[16];
+          const float4* srow = reinterpret_cast<const float4*>(sm.Sp + r * JF_SLOT);
+#pragma unroll
+          for (int k = 0; k < (CU + 3) / 4; ++k) {
+            const float4 t4 = srow[k];
+            w[4 * k] = t4.x;
+            w[4 * k + 1] = t4.y;
+            w[4 * k + 2] = t4.z;
+            w[4 * k + 3] = t4.w;
+          }
+          float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
           for (int u = 0; u < CU; ++u) {
-            const float w = u < g.U ? S[r * g.U + u] : 0.f;
-            rsum += w;
-            cs[u] += w;
-            tx = fmaf(w, sv[u].x, tx);
-            ty = fmaf(w, sv[u].y, ty);
-            acc[u].x = fmaf(w, qv.x, acc[u].x);
-            acc[u].y = fmaf(w, qv.y, acc[u].y);
+            fma4(t, w[u], sv[u]);
+            fma4(acc[u], w[u], qv);
           }
           if (dv) {
-            float2 o;
-            o.x = 2.f * (qv.x * rsum - tx);
-            o.y = 2.f * (qv.y * rsum - ty);
-            *reinterpret_cast<float2*>(dqb + (long long)r * g.D) = o;
+            const float rsum = sm.rs[r];
+            float4 o;
+            o.x = 2.f * fmaf(qv.x, rsum, -t.x);
+            o.y = 2.f * fmaf(qv.y, rsum, -t.y);
+            o.z = 2.f * fmaf(qv.z, rsum, -t.z);
+            o.w = 2.f * fmaf(qv.w, rsum, -t.w);
+            *reinterpret_cast<float4*>(dqb + (long long)r * g.D) = o;
           }
         }
       }
@@ -524,10 +567,13 @@ __global__ void __launch_bounds__(128) jf_backward_kernel(const JFArgs a) {
 #pragma unroll
       for (int u = 0; u < CU; ++u) {
         if (u < g.U) {
-          float2 o;
-          o.x = 2.f * (sv[u].x * cs[u] - acc[u].x);
-          o.y = 2.f * (sv[u].y * cs[u] - acc[u].y);
-          *reinterpret_cast<float2*>(dsb + (long long)u * g.D) = o;
+          const float cu = sm.cs[u];
+          float4 o;
+          o.x = 2.f * fmaf(sv[u].x, cu, -acc[u].x);
+          o.y = 2.f * fmaf(sv[u].y, cu, -acc[u].y);
+          o.z = 2.f * fmaf(sv[u].z, cu, -acc[u].z);
+          o.w = 2.f * fmaf(sv[u].w, cu, -acc[u].w);
+          *reinterpret_cast<float4*>(dsb + (long long)u * g.D) = o;
         }
       }
     }
@@ -536,7 +582,7 @@ __global__ void __launch_bounds__(128) jf_backward_kernel(const JFArgs a) {
 
 template <int CU, bool FVM, bool FEAT>
 int jf_launch(const JFArgs& a, bool fwd, cudaStream_t st) {
-  size_t off[8];
+  size_t off[11];
   const size_t smem = jf_smem_layout(a.g.K, a.g.T, a.g.U, a.W, FVM, fwd, FEAT, off);
   auto kern = fwd ? jf_forward_kernel<CU, FVM, FEAT> : jf_backward_kernel<CU, FVM, FEAT>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
@@ -548,9 +594,12 @@ int jf_launch(const JFArgs& a, bool fwd, cudaStream_t st) {
   return kOk;
 }
 
+// CU: support frames held in registers (the smallest instance >= U)
 template <bool FVM, bool FEAT>
 int jf_dispatch(const JFArgs& a, bool fwd, cudaStream_t st) {
-  if (!FEAT || a.g.U <= 8) return jf_launch<8, FVM, FEAT>(a, fwd, st);
+  if (!FEAT || a.g.U <= 4) return jf_launch<4, FVM, FEAT>(a, fwd, st);
+  if (a.g.U <= 8) return jf_launch<8, FVM, FEAT>(a, fwd, st);
+  if (a.g.U <= 12) return jf_launch<12, FVM, FEAT>(a, fwd, st);
   return jf_launch<15, FVM, FEAT>(a, fwd, st);
 }
 
@@ -558,15 +607,15 @@ constexpr size_t JF_SMEM_MAX = 96 * 1024;
 
 }  // namespace
 
-// Whether the fused kernels take this shape: float32, features with an even
-// D <= 256 and at most 15 support frames (or a cost input), and a pair's
-// shared-memory state within JF_SMEM_MAX.
+// Whether the fused kernels take this shape: float32, features with D <= 256
+// a multiple of 4 and at most 15 support frames (or a cost input), and a
+// pair's shared-memory state within JF_SMEM_MAX.
 bool jf_supported(int K, int T, int U, int D, bool fvm, bool feat) {
   if (K <= 0 || T <= 0 || U <= 0) return false;
-  if (feat && (D <= 0 || D > 256 || (D & 1) || U > 15)) return false;
+  if (feat && (D <= 0 || D > 256 || (D & 3) || U > 15)) return false;
   if ((long long)K * T * U > (1 << 15)) return false;
-  const int W = feat ? (D + 63) / 64 : 1;
-  size_t off[8];
+  const int W = feat ? (D + 127) / 128 : 1;
+  size_t off[11];
   const size_t fw = jf_smem_layout(K, T, U, W, fvm, true, feat, off);
   const size_t bw = jf_smem_layout(K, T, U, W, fvm, false, feat, off);
   return fw <= JF_SMEM_MAX && bw <= JF_SMEM_MAX;
@@ -588,9 +637,9 @@ int jf_run(const float* q, const float* s, const float* cost, int B, int K1, int
   const JFSaved sv = jf_saved_layout(B, K, T, U, fvm, feat);
   if (saved_bytes < sv.total)
     return set_error(kWorkspace, "fused JEANIE: saved needs %zu bytes", sv.total);
-  if (feat && ((((uintptr_t)q | (uintptr_t)s) & 7u) ||
-               (!fwd && (((uintptr_t)dq | (uintptr_t)ds) & 7u))))
-    return set_error(kUnsupported, "fused JEANIE: features must be 8-byte aligned");
+  if (feat && ((((uintptr_t)q | (uintptr_t)s) & 15u) ||
+               (!fwd && (((uintptr_t)dq | (uintptr_t)ds) & 15u))))
+    return set_error(kUnsupported, "fused JEANIE: features must be 16-byte aligned");
   if ((uintptr_t)saved & 15u) return set_error(kInvalid, "fused JEANIE: saved not 16-byte aligned");
   if (B == 0) return kOk;
   JFArgs a{};
@@ -606,7 +655,7 @@ int jf_run(const float* q, const float* s, const float* cost, int B, int K1, int
   a.ds = ds;
   a.dC = dC;
   a.B = B;
-  a.W = feat ? (D + 63) / 64 : 1;
+  a.W = feat ? (D + 127) / 128 : 1;
   const double kap = 1.4426950408889634 / gamma;
   a.g = JFGeom{K1, K2, K, T, U, D, s1, s2, metric, K * T, (float)kap, (float)(1.0 / kap)};
   a.sv = sv;
