@@ -131,26 +131,54 @@ def test_cost_double_backward_fp32(tw):
         assert err < 1e-3, err
 
 
-def test_third_order_raises(tw):
+def _third_fd(tw, f, c, V, eps=1e-6):
+    """d/de of <H(c + e V) V, V> by a central difference of the second
+    derivative, and the third derivative from autograd."""
+    def second(x):
+        x = x.detach().requires_grad_(True)
+        (g,) = torch.autograd.grad(f(x), x, create_graph=True)
+        (h,) = torch.autograd.grad((g * V).sum(), x, create_graph=True)
+        return h, x
+    h, x = second(c)
+    (t3,) = torch.autograd.grad((h * V).sum(), x)
+    hp, _ = second(c + eps * V)
+    hm, _ = second(c - eps * V)
+    fd = (((hp - hm) * V).sum() / (2 * eps)).item()
+    return (t3 * V).sum().item(), fd
+
+
+def test_soft_dtw_third_order(tw):
+    """Third derivatives of soft-DTW (through the restatement) against a
+    central difference of the native second derivative."""
     h = G.higher("c7x9")
-    c = _t(h["C"]).requires_grad_(True)
-    d = tw.functional.soft_dtw_from_cost(c, gamma=0.3)
-    (dC,) = torch.autograd.grad(d.sum(), c, create_graph=True)
-    (hC,) = torch.autograd.grad((dC * _t(h["V"])).sum(), c, create_graph=True)
-    with pytest.raises(RuntimeError):
-        torch.autograd.grad(hC.sum(), c)
+    c = _t(h["C"])
+    V = _t(h["V"])
+    got, fd = _third_fd(tw, lambda x: tw.functional.soft_dtw_from_cost(x, gamma=0.3).sum(), c,
+                        V)
+    assert abs(got - fd) <= 1e-5 * max(1.0, abs(fd)), (got, fd)
 
 
-def test_udtw_second_order_raises(tw):
-    """Second derivatives of uDTW with a penalty are not native: asking for
-    them raises instead of returning a silently incomplete gradient."""
+def test_udtw_second_order(tw, orc):
+    """Second derivatives of uDTW with a penalty: the Hessian-vector product
+    along (V_C, V_Q) against a central difference of the native gradient."""
     g = torch.Generator().manual_seed(4)
-    C = torch.rand(2, 9, 11, generator=g, dtype=torch.float64).to(DEV).requires_grad_(True)
-    Q = torch.randn(2, 9, 11, generator=g, dtype=torch.float64).to(DEV).requires_grad_(True)
-    d, p = tw.functional.udtw_from_cost(C, Q, gamma=0.3)
-    (dC,) = torch.autograd.grad((d + p).sum(), C, create_graph=True)
-    with pytest.raises(RuntimeError):
-        torch.autograd.grad(dC.sum(), C)
+    C = torch.rand(2, 9, 11, generator=g, dtype=torch.float64).to(DEV)
+    Q = torch.randn(2, 9, 11, generator=g, dtype=torch.float64).to(DEV)
+    VC = torch.randn(2, 9, 11, generator=g, dtype=torch.float64).to(DEV)
+    VQ = torch.randn(2, 9, 11, generator=g, dtype=torch.float64).to(DEV)
+
+    def grads(c, q, create):
+        c, q = c.detach().requires_grad_(True), q.detach().requires_grad_(True)
+        d, p = tw.functional.udtw_from_cost(c, q, gamma=0.3)
+        return torch.autograd.grad((d + 2.0 * p).sum(), (c, q), create_graph=create), (c, q)
+
+    (gc, gq), (c, q) = grads(C, Q, True)
+    hc, hq = torch.autograd.grad((gc * VC).sum() + (gq * VQ).sum(), (c, q))
+    eps = 1e-6
+    (pc, pq), _ = grads(C + eps * VC, Q + eps * VQ, False)
+    (mc, mq), _ = grads(C - eps * VC, Q - eps * VQ, False)
+    for got, fd in ((hc, (pc - mc) / (2 * eps)), (hq, (pq - mq) / (2 * eps))):
+        _close(got, fd.cpu().numpy(), 1e-6, 1e-6)
 
 
 def _fd_check(f, primals, tangents, eps=1e-6):
@@ -198,12 +226,12 @@ def _jeanie_with_accumulator(tw, x):
     return d + R.sum((1, 2, 3, 4))
 
 
-def test_jeanie_accumulator_jvp_raises(tw):
-    """A tangent for the JEANIE accumulator is not native: forward mode with
-    return_accumulator=True raises instead of returning a wrong tangent."""
+def test_jeanie_accumulator_jvp(tw):
+    """Forward mode through the JEANIE accumulator (return_accumulator=True)
+    against a central difference."""
     c = torch.rand(1, 2, 2, 4, 5, dtype=torch.float64).to(DEV)
-    with pytest.raises(NotImplementedError):
-        torch.func.jvp(lambda x: _jeanie_with_accumulator(tw, x), (c,), (torch.ones_like(c),))
+    t = torch.randn(1, 2, 2, 4, 5, dtype=torch.float64).to(DEV)
+    _fd_check(lambda x: _jeanie_with_accumulator(tw, x), (c,), (t,))
 
 
 def test_features_double_backward_normalized(tw):

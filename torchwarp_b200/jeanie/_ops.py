@@ -27,6 +27,7 @@ import torch
 from torch import Tensor
 
 from .. import _native as nat
+from .. import _autodiff as AD
 from .. import _transforms
 from .._vmap import register_fold_rule, round_to_pairs
 
@@ -97,8 +98,10 @@ class JeanieDP(torch.autograd.Function):
     otherwise.
 
     Forward mode: the tangent of the distance along T is <dout/dcost, T>, from
-    one native backward with unit seeds.  A tangent for the accumulator would
-    need a tangent DP that is not native, so forward mode with keep_R raises."""
+    one native backward with unit seeds; with the accumulator requested, the
+    tangents of both outputs come from torch.func.jvp of the differentiable
+    restatement of the DP.  Differentiating the backward again goes through
+    the same restatement (native first-order values)."""
 
     generate_vmap_rule = True
 
@@ -117,12 +120,21 @@ class JeanieDP(torch.autograd.Function):
         ctx.args = (s1, s2, gamma, keep_R)
 
     @staticmethod
-    @_transforms.once_differentiable
     def backward(ctx, g_out, g_R):
         cost, R = ctx.saved_tensors
         s1, s2, gamma, _ = ctx.args
         if g_out is None:
             g_out = cost.new_zeros(cost.shape[0])
+        if torch.is_grad_enabled():
+            d_cost, = AD.first_order(_jeanie_grad_native(s1, s2, gamma),
+                                     _jeanie_grad_ref(s1, s2, gamma), 1, R, cost, g_out, g_R)
+            return d_cost, None, None, None, None
+        return JeanieDP._backward_once(ctx, cost, R, g_out, g_R)
+
+    @staticmethod
+    @_transforms.once_differentiable
+    def _backward_once(ctx, cost, R, g_out, g_R):
+        s1, s2, gamma, _ = ctx.args
         return jeanie_dp_backward(cost, R, g_out, g_R, s1, s2, gamma), None, None, None, None
 
     @staticmethod
@@ -130,13 +142,29 @@ class JeanieDP(torch.autograd.Function):
         cost, R = ctx.saved_tensors
         s1, s2, gamma, keep_R = ctx.args
         if keep_R:
-            raise NotImplementedError("forward mode through the JEANIE accumulator "
-                                      "(return_accumulator=True) is not implemented")
+            ct = torch.zeros_like(cost) if cost_t is None else cost_t.to(cost.dtype)
+            return torch.func.jvp(lambda c: AD.jeanie_dp(c, s1, s2, gamma),
+                                  (cost.contiguous(),), (ct.contiguous(),))[1]
         B = cost.shape[0]
         if cost_t is None:
             return cost.new_zeros(B), None
         w = jeanie_dp_backward(cost, R, cost.new_ones(B), None, s1, s2, gamma)
         return (w * cost_t).flatten(1).sum(1), None
+
+
+def _jeanie_grad_native(s1, s2, gamma):
+    """(R, cost, g_out, g_R) -> (d_cost,), native."""
+    def f(R, cost, g_out, g_R):
+        return (jeanie_dp_backward(cost, R, g_out, g_R, s1, s2, gamma),)
+    return f
+
+
+def _jeanie_grad_ref(s1, s2, gamma):
+    """(R, cost, g_out, g_R) -> (d_cost,), differentiable."""
+    def f(R, cost, g_out, g_R):
+        _, pull = torch.func.vjp(lambda c: AD.jeanie_dp(c, s1, s2, gamma), cost)
+        return pull((g_out, torch.zeros_like(cost) if g_R is None else g_R))
+    return f
 
 
 # ------------------------------------------------------ query/support cost
@@ -207,9 +235,25 @@ class QSCost(torch.autograd.Function):
         ctx.metric = metric
 
     @staticmethod
-    @_transforms.once_differentiable
     def backward(ctx, g):
         query, support, cost = ctx.saved_tensors
+        if torch.is_grad_enabled():
+            metric = ctx.metric
+
+            def native(cost_, q, s_, g_):
+                return qs_cost_backward(q, s_, cost_, g_, metric)
+
+            def ref(cost_, q, s_, g_):
+                _, pull = torch.func.vjp(lambda a, b: AD.qs_cost(a, b, metric), q, s_)
+                return pull(g_)
+
+            dq, ds = AD.first_order(native, ref, 1, cost, query, support, g)
+            return dq, ds, None
+        return QSCost._backward_once(ctx, query, support, cost, g)
+
+    @staticmethod
+    @_transforms.once_differentiable
+    def _backward_once(ctx, query, support, cost, g):
         dq, ds = qs_cost_backward(query, support, cost, g, ctx.metric)
         return dq, ds, None
 
@@ -297,14 +341,40 @@ class QSRbfCost(torch.autograd.Function):
     def setup_context(ctx, inputs, output):
         query, support, sigma = inputs
         ctx.save_for_backward(query, support)
+        ctx.save_for_forward(query, support)
         ctx.sigma = sigma
 
     @staticmethod
-    @_transforms.once_differentiable
     def backward(ctx, g):
         query, support = ctx.saved_tensors
+        if torch.is_grad_enabled():
+            sigma = ctx.sigma
+
+            def native(q, s_, g_):
+                return qs_rbf_cost_backward(q, s_, g_, sigma)
+
+            def ref(q, s_, g_):
+                _, pull = torch.func.vjp(lambda a, b: AD.rbf(a, b, sigma), q, s_)
+                return pull(g_)
+
+            dq, ds = AD.first_order(native, ref, 0, query, support, g)
+            return dq, ds, None
+        return QSRbfCost._backward_once(ctx, query, support, g)
+
+    @staticmethod
+    @_transforms.once_differentiable
+    def _backward_once(ctx, query, support, g):
         dq, ds = qs_rbf_cost_backward(query, support, g, ctx.sigma)
         return dq, ds, None
+
+    @staticmethod
+    def jvp(ctx, q_t, s_t, _sigma_t):
+        query, support = ctx.saved_tensors
+        q_t = torch.zeros_like(query) if q_t is None else q_t.to(query.dtype)
+        s_t = torch.zeros_like(support) if s_t is None else s_t.to(support.dtype)
+        return torch.func.jvp(lambda a, b: AD.rbf(a, b, ctx.sigma),
+                              (query.contiguous(), support.contiguous()),
+                              (q_t.contiguous(), s_t.contiguous()))[1]
 
 
 # ------------------------------------------------------------ FVM soft-min
@@ -371,9 +441,25 @@ class FvmSoftmin(torch.autograd.Function):
         ctx.gamma = gamma
 
     @staticmethod
-    @_transforms.once_differentiable
     def backward(ctx, g):
         (cost,) = ctx.saved_tensors
+        if torch.is_grad_enabled():
+            gamma = ctx.gamma
+
+            def native(c, g_):
+                return (fvm_softmin_backward(c, g_, gamma),)
+
+            def ref(c, g_):
+                _, pull = torch.func.vjp(lambda x: AD.viewpoint_softmin(x, gamma), c)
+                return pull(g_)
+
+            d_cost, = AD.first_order(native, ref, 0, cost, g)
+            return d_cost, None
+        return FvmSoftmin._backward_once(ctx, cost, g)
+
+    @staticmethod
+    @_transforms.once_differentiable
+    def _backward_once(ctx, cost, g):
         return fvm_softmin_backward(cost, g, ctx.gamma), None
 
     @staticmethod
@@ -506,7 +592,9 @@ class JeanieFused(torch.autograd.Function):
 
     Forward mode: the tangent of the distance is the inner product of its
     gradient (one native backward with unit seeds) with the input tangents;
-    with keep_R it raises, as for JeanieDP."""
+    with the accumulator requested, both tangents come from torch.func.jvp of
+    the differentiable restatement.  Differentiating the backward again goes
+    through the same restatement (native first-order values)."""
 
     generate_vmap_rule = True
 
@@ -527,13 +615,24 @@ class JeanieFused(torch.autograd.Function):
         ctx.args = (K1, K2, T, U, s1, s2, gamma, metric, fvm, keep_R)
 
     @staticmethod
-    @_transforms.once_differentiable
     def backward(ctx, g_out, g_R, _g_saved):
         query, support, cost, saved = ctx.saved_tensors
         K1, K2, T, U, s1, s2, gamma, metric, fvm, _ = ctx.args
         ref = query if query is not None else cost
         if g_out is None:
             g_out = ref.new_zeros(ref.shape[0])
+        if torch.is_grad_enabled():
+            grads = AD.first_order(_fused_grad_native(ctx.args), _fused_grad_ref(ctx.args), 1,
+                                   saved, query, support, cost, g_out, g_R)
+            if query is not None:
+                return (grads[0], grads[1], None) + (None,) * 10
+            return (None, None, grads[0]) + (None,) * 10
+        return JeanieFused._backward_once(ctx, query, support, cost, saved, g_out, g_R)
+
+    @staticmethod
+    @_transforms.once_differentiable
+    def _backward_once(ctx, query, support, cost, saved, g_out, g_R):
+        K1, K2, T, U, s1, s2, gamma, metric, fvm, _ = ctx.args
         dq, ds, dC = jeanie_fused_backward(query, support, cost, saved, g_out, g_R, K1, K2, T, U,
                                            s1, s2, gamma, metric, fvm)
         if query is not None:
@@ -545,8 +644,16 @@ class JeanieFused(torch.autograd.Function):
         query, support, cost, saved = ctx.saved_tensors
         K1, K2, T, U, s1, s2, gamma, metric, fvm, keep_R = ctx.args
         if keep_R and not fvm:
-            raise NotImplementedError("forward mode through the JEANIE accumulator "
-                                      "(return_accumulator=True) is not implemented")
+            fwd = _fused_forward_ref(ctx.args, query is not None)
+            if query is not None:
+                prim = (query.contiguous(), support.contiguous())
+                tans = (torch.zeros_like(query) if q_t is None else q_t.contiguous(),
+                        torch.zeros_like(support) if s_t is None else s_t.contiguous())
+            else:
+                prim = (cost.contiguous(),)
+                tans = (torch.zeros_like(cost) if c_t is None else c_t.contiguous(),)
+            out_t, R_t = torch.func.jvp(fwd, prim, tans)[1]
+            return out_t, R_t, None
         ref = query if query is not None else cost
         B = ref.shape[0]
         dq, ds, dC = jeanie_fused_backward(query, support, cost, saved, ref.new_ones(B), None, K1,
@@ -560,6 +667,59 @@ class JeanieFused(torch.autograd.Function):
         elif c_t is not None:
             t = t + (dC * c_t).flatten(1).sum(1)
         return t, None, None
+
+
+def _fused_forward_ref(args, features):
+    """Differentiable restatement of jeanie_fused's (out, R): a function of
+    (query, support) with features, else of the cost."""
+    K1, K2, T, U, s1, s2, gamma, metric, fvm, _ = args
+
+    def from_cost(c):
+        B = c.shape[0]
+        if fvm:
+            temporal = AD.viewpoint_softmin(c.reshape(B, K1 * K2, T, U), gamma)
+            return AD.udtw_dp(temporal, None, gamma)[0], c.new_zeros(0)
+        return AD.jeanie_dp(c.reshape(B, K1, K2, T, U), s1, s2, gamma)
+
+    def from_features(q, s_):
+        return from_cost(AD.qs_cost(q, s_, metric))
+
+    return from_features if features else from_cost
+
+
+def _fused_grad_native(args):
+    """(saved, query, support, cost, g_out, g_R) -> the native gradients of
+    the given inputs ((d_query, d_support) or (d_cost,))."""
+    K1, K2, T, U, s1, s2, gamma, metric, fvm, _ = args
+
+    def f(saved, q, s_, c, g_out, g_R):
+        dq, ds, dC = jeanie_fused_backward(q, s_, c, saved, g_out, g_R, K1, K2, T, U, s1, s2,
+                                           gamma, metric, fvm)
+        return (dq, ds) if q is not None else (dC,)
+    return f
+
+
+def _fused_grad_ref(args):
+    """The same gradients with differentiable torch operations."""
+    K1, K2, T, U, s1, s2, gamma, metric, fvm, _ = args
+
+    def f(saved, q, s_, c, g_out, g_R):
+        def fwd_cost(cc):
+            B = cc.shape[0]
+            if fvm:
+                temporal = AD.viewpoint_softmin(cc.reshape(B, K1 * K2, T, U), gamma)
+                return (AD.udtw_dp(temporal, None, gamma)[0],)
+            return AD.jeanie_dp(cc.reshape(B, K1, K2, T, U), s1, s2, gamma)
+
+        cots = (g_out,) if fvm else (g_out, torch.zeros(
+            (g_out.shape[0], K1, K2, T, U), dtype=g_out.dtype, device=g_out.device)
+            if g_R is None else g_R)
+        if q is not None:
+            _, pull = torch.func.vjp(lambda a, b: fwd_cost(AD.qs_cost(a, b, metric)), q, s_)
+        else:
+            _, pull = torch.func.vjp(fwd_cost, c)
+        return pull(cots)
+    return f
 
 
 JeanieFusedTraced = _transforms.traceable(JeanieFused)

@@ -47,6 +47,7 @@ import torch
 from torch import Tensor
 
 from .. import _native as nat
+from .. import _autodiff as AD
 from .. import _transforms
 from .._vmap import register_fold_rule, round_to_pairs
 
@@ -320,7 +321,9 @@ class SdtwCostGrad(torch.autograd.Function):
     P_s = V_s + sum_p w_p P_p ends at <E, V> with E = dd/dcost.  The native
     uDTW forward returns that value, which is the gradient for g.  The native
     uDTW backward seeded with (0, g) returns g * (d^2 d / dcost^2) V, which is
-    the gradient for the cost.  A third derivative raises."""
+    the gradient for the cost.  Third and higher derivatives, and forward
+    mode through this backward (torch.func.hessian = jacfwd(jacrev)), go
+    through torch.func on the differentiable restatement of the DP."""
 
     generate_vmap_rule = True
 
@@ -333,17 +336,64 @@ class SdtwCostGrad(torch.autograd.Function):
     def setup_context(ctx, inputs, output):
         cost, saved, g, gamma, bandwidth = inputs
         ctx.save_for_backward(cost, g)
+        ctx.save_for_forward(cost, g)
         ctx.args = (gamma, bandwidth)
 
     @staticmethod
-    @_transforms.once_differentiable
+    def _ref(gamma, bandwidth):
+        """(cost, g) -> g * dd/dcost with differentiable torch operations."""
+        def f(cost, g):
+            _, pull = torch.func.vjp(lambda c: AD.udtw_dp(c, None, gamma, bandwidth)[0], cost)
+            return pull(g)[0]
+        return f
+
+    @staticmethod
     def backward(ctx, V):
         cost, g = ctx.saved_tensors
         gamma, bandwidth = ctx.args
+        if torch.is_grad_enabled():
+            # a third derivative follows: the same products, differentiable
+            _, pull = torch.func.vjp(SdtwCostGrad._ref(gamma, bandwidth), cost, g)
+            hv, v_e = pull(V.to(cost.dtype))
+            return hv, None, v_e, None, None
+        return SdtwCostGrad._native_hvp(cost, g, V, gamma, bandwidth)
+
+    @staticmethod
+    @_transforms.once_differentiable
+    def _native_hvp_once(ctx, cost, g, V, gamma, bandwidth):
+        return SdtwCostGrad._native_hvp(cost, g, V, gamma, bandwidth)
+
+    @staticmethod
+    def _native_hvp(cost, g, V, gamma, bandwidth):
         B, N, M = cost.shape
         _, v_e, saved_v = sdtw_dp(cost, V.to(cost.dtype), gamma, bandwidth)
         hv, _ = sdtw_dp_backward(saved_v, torch.zeros_like(g), g, N, M, gamma, True)
         return hv, None, v_e, None, None
+
+    @staticmethod
+    def jvp(ctx, cost_t, _saved_t, g_t, _gamma_t, _bandwidth_t):
+        cost, g = ctx.saved_tensors
+        gamma, bandwidth = ctx.args
+        cost_t = torch.zeros_like(cost) if cost_t is None else cost_t.to(cost.dtype)
+        g_t = torch.zeros_like(g) if g_t is None else g_t.to(g.dtype)
+        return torch.func.jvp(SdtwCostGrad._ref(gamma, bandwidth),
+                              (cost.contiguous(), g.contiguous()),
+                              (cost_t.contiguous(), g_t.contiguous()))[1]
+
+
+def _dp_grad_native(N, M, gamma):
+    """(saved, cost, penalty, g_r, g_p) -> (d_cost, d_penalty), native."""
+    def f(saved, cost, penalty, g_r, g_p):
+        return sdtw_dp_backward(saved, g_r, g_p, N, M, gamma, True)
+    return f
+
+
+def _dp_grad_ref(gamma, bandwidth):
+    """(saved, cost, penalty, g_r, g_p) -> (d_cost, d_penalty), differentiable."""
+    def f(saved, cost, penalty, g_r, g_p):
+        _, pull = torch.func.vjp(lambda c, q: AD.udtw_dp(c, q, gamma, bandwidth), cost, penalty)
+        return pull((g_r, g_p))
+    return f
 
 
 @_transforms.once_differentiable
@@ -372,7 +422,7 @@ class DP(torch.autograd.Function):
         ctx.mark_non_differentiable(output[2])
         ctx.set_materialize_grads(False)
         # the cost is kept for a backward that is differentiated again (soft-DTW)
-        ctx.save_for_backward(output[2], cost if penalty is None else None)
+        ctx.save_for_backward(output[2], cost, penalty)
         if penalty is None:
             ctx.save_for_forward(cost, output[2])
         else:
@@ -383,12 +433,21 @@ class DP(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, g_r, g_p, _g_saved):
-        saved, cost = ctx.saved_tensors
+        saved, cost, penalty = ctx.saved_tensors
         gamma, has_p, bandwidth = ctx.args
         if torch.is_grad_enabled() and not has_p:
             # create_graph: a backward that is itself differentiable (natively)
             g = _zeros_if_none(g_r, cost, ctx.shape[0]).to(ctx.dtype)
             return SdtwCostGrad.apply(cost, saved, g, gamma, bandwidth), None, None, None
+        if torch.is_grad_enabled():
+            # uDTW: native values, higher orders through the restatement
+            B, N, M = ctx.shape
+            g_r = _zeros_if_none(g_r, cost, B).to(ctx.dtype)
+            g_p = _zeros_if_none(g_p, cost, B).to(ctx.dtype)
+            d_cost, d_pen = AD.first_order(_dp_grad_native(N, M, gamma),
+                                           _dp_grad_ref(gamma, bandwidth), 1, saved, cost,
+                                           penalty, g_r, g_p)
+            return d_cost, d_pen, None, None
         return _dp_backward_once(ctx, saved, g_r, g_p)
 
     @staticmethod
@@ -419,7 +478,13 @@ class DP(torch.autograd.Function):
 
 
 class Fused(torch.autograd.Function):
-    """(X, Y, vx?, vy?) -> (distance, penalty_sum, saved, cost)."""
+    """(X, Y, vx?, vy?) -> (distance, penalty_sum, saved, cost).
+
+    Differentiating the backward again (create_graph) rebuilds the cost and
+    penalty as differentiable expressions and routes the DP part through
+    the native backward with higher orders through the restatement; forward
+    mode forms the cost's tangent and contracts it with the native
+    gradients of both outputs."""
 
     generate_vmap_rule = True
 
@@ -433,14 +498,70 @@ class Fused(torch.autograd.Function):
         ctx.mark_non_differentiable(output[2], output[3])
         ctx.set_materialize_grads(False)
         ctx.save_for_backward(X, Y, vx, vy, output[2], output[3])
-        ctx.args = (gamma, beta, eps)
+        ctx.save_for_forward(X, Y, vx, vy, output[2])
+        ctx.args = (gamma, beta, eps, bandwidth)
+
+    @staticmethod
+    def backward(ctx, g_r, g_p, _g_saved, _g_cost):
+        X, Y, vx, vy, saved, cost = ctx.saved_tensors
+        if torch.is_grad_enabled() and vx is not None:
+            return Fused._backward_graph(ctx, X, Y, vx, vy, saved, g_r, g_p)
+        return Fused._backward_once(ctx, X, Y, vx, vy, saved, cost, g_r, g_p)
+
+    @staticmethod
+    def _backward_graph(ctx, X, Y, vx, vy, saved, g_r, g_p):
+        """Gradients that can be differentiated again (reverse or forward
+        mode): the cost and penalty rebuilt with torch operations, the DP
+        part native with higher orders through the restatement, and the
+        chain rule by torch.func.vjp (each argument slot its own partial
+        derivative, so normalize's d(X, X) is right)."""
+        gamma, beta, eps, bandwidth = ctx.args
+        B, N, M = X.shape[0], X.shape[1], Y.shape[1]
+        g_r = _zeros_if_none(g_r, X, B).to(X.dtype)
+        g_p = _zeros_if_none(g_p, X, B).to(X.dtype)
+
+        def mats(a, b, c, d):
+            with _full_fp32_matmul():
+                return AD.udtw_matrices(a, b, c, d, beta, eps)
+
+        (cost, pen), pull = torch.func.vjp(mats, X, Y, vx, vy)
+        d_cost, d_pen = AD.first_order(_dp_grad_native(N, M, gamma),
+                                       _dp_grad_ref(gamma, bandwidth), 1, saved, cost, pen,
+                                       g_r, g_p)
+        with _full_fp32_matmul():
+            dX, dY, dvx, dvy = pull((d_cost, d_pen))
+        return dX, dY, dvx, dvy, None, None, None, None
+
+    @staticmethod
+    def jvp(ctx, X_t, Y_t, vx_t, vy_t, *_):
+        X, Y, vx, vy, saved = ctx.saved_tensors
+        gamma, beta, eps, bandwidth = ctx.args
+        B, N, M = X.shape[0], X.shape[1], Y.shape[1]
+        prim = [t for t in (X, Y, vx, vy) if t is not None]
+        tans = [torch.zeros_like(p) if t is None else t.to(p.dtype)
+                for p, t in zip(prim, [X_t, Y_t, vx_t, vy_t])]
+        if vx is None:
+            cost_t = torch.func.jvp(AD.sq_euclid, tuple(p.contiguous() for p in prim),
+                                    tuple(t.contiguous() for t in tans))[1]
+            d_cost, _ = sdtw_dp_backward(saved, X.new_ones(B), X.new_zeros(B), N, M, gamma,
+                                         False)
+            return _pairwise_dot(d_cost, cost_t), X.new_zeros(B), None, None
+        (cost_t, pen_t) = torch.func.jvp(
+            lambda a, b, c, d: AD.udtw_matrices(a, b, c, d, beta, eps),
+            tuple(p.contiguous() for p in prim), tuple(t.contiguous() for t in tans))[1]
+        # gradients of both outputs: E = dd/dcost = dp/dpenalty, and dp/dcost
+        e, _ = sdtw_dp_backward(saved, X.new_ones(B), X.new_zeros(B), N, M, gamma, True)
+        dp_dc, _ = sdtw_dp_backward(saved, X.new_zeros(B), X.new_ones(B), N, M, gamma, True)
+        return (_pairwise_dot(e, cost_t), _pairwise_dot(dp_dc, cost_t) + _pairwise_dot(e, pen_t),
+                None, None)
 
     @staticmethod
     @_transforms.once_differentiable
-    def backward(ctx, g_r, g_p, _g_saved, _g_cost):
-        X, Y, vx, vy, saved, cost = ctx.saved_tensors
-        gamma, beta, eps = ctx.args
+    def _backward_once(ctx, X, Y, vx, vy, saved, cost, g_r, g_p):
+        gamma, beta, eps, bandwidth = ctx.args
         B = X.shape[0]
+        if cost is None:
+            cost = ctx.saved_tensors[5]
         g_r = _zeros_if_none(g_r, X, B)
         g_p = _zeros_if_none(g_p, X, B)
         dX, dY, dvx, dvy = udtw_fused_backward(X, Y, vx, vy, cost, saved, g_r, g_p, gamma, beta,
@@ -503,28 +624,16 @@ class SdtwFused(torch.autograd.Function):
         X, Y, mask, saved = ctx.saved_tensors
         if not torch.is_grad_enabled():
             return _sdtw_fused_backward_once(ctx, X, Y, mask, saved, g_r)
-        # create_graph: the cost is rebuilt as a differentiable expression and
-        # the DP part goes through SdtwCostGrad, whose own backward is native;
-        # autograd supplies the cost's second derivatives
+        # create_graph (or torch.func): the cost is rebuilt as a differentiable
+        # expression and the DP part goes through SdtwCostGrad, whose own
+        # backward is native; torch.func.vjp applies the cost's chain rule,
+        # each argument slot getting its own partial derivative (with X
+        # passed as both arguments, normalize=True's d(X, X))
         g = _zeros_if_none(g_r, X, X.shape[0]).to(X.dtype)
-        # one view per argument slot: with X passed as both arguments
-        # (normalize=True computes d(X, X)) each slot gets its own partial
-        # derivative, not the total one twice
-        Xs = X.view_as(X) if X.requires_grad else X
-        Ys = Y.view_as(Y) if Y.requires_grad else Y
-        if not (Xs.requires_grad or Ys.requires_grad):
-            # grad mode is on but nothing at this level is differentiable
-            # (vmapped cotangents of torch.func.jacrev / vjp): first order
-            return _sdtw_fused_backward_once(ctx, X, Y, mask, saved, g_r)
-        cost = _sqeuclid(Xs, Ys)
+        cost, pull = torch.func.vjp(_sqeuclid, X, Y)
         s = SdtwCostGrad.apply(cost, saved, g, ctx.gamma, ctx.bandwidth)
-        wrt = [t for t in (Xs, Ys) if t.requires_grad]
-        # the first-order values go through the cost's bmm backward: full
-        # float32 there too (second-order terms follow the caller's setting)
         with _full_fp32_matmul():
-            grads = iter(torch.autograd.grad(cost, wrt, s, create_graph=True))
-        dX = next(grads) if Xs.requires_grad else None
-        dY = next(grads) if Ys.requires_grad else None
+            dX, dY = pull(s)
         return dX, dY, None, None
 
     @staticmethod
@@ -545,6 +654,7 @@ class SdtwFused(torch.autograd.Function):
 
 
 DPTraced = _transforms.traceable(DP)
+FusedTraced = _transforms.traceable(Fused)
 SdtwFusedTraced = _transforms.traceable(SdtwFused)
 
 
@@ -557,4 +667,4 @@ def dp_apply(cost, penalty, gamma, bandwidth):
 
 
 def fused_apply(X, Y, vx, vy, gamma, beta, eps, bandwidth):
-    return Fused.apply(X, Y, vx, vy, gamma, beta, eps, bandwidth)
+    return _transforms.pick(Fused, FusedTraced).apply(X, Y, vx, vy, gamma, beta, eps, bandwidth)
