@@ -18,11 +18,17 @@ Printed (rank 0), one JSON line:
             algorithmic bytes per launch / its average CUDA-event duration in
             the timed region, against MEASURED_PEAKS.json, with the DRAM
             traffic ncu measured for that kernel (per cell, scaled);
-  cpu_baseline  the float64 CPU oracle (oracle/, one thread) on a bounded
-            sample of the same workload (rank 0, N=1 only).
-``--impl reference`` times the CPU implementation of the reference's path
-(the oracle port, all host threads) on the same workload and prints the
-same line with "impl": "reference".
+  cpu_baseline  the reference's own float32 PyTorch CPU backend on every host
+            thread, on a bounded sample of the same workload (rank 0, N=1
+            only); the float64 C port under oracle/ where the reference
+            package is not present.
+``--impl reference`` times that CPU implementation of the reference's path
+on the same workload and prints the same line with "impl": "reference".
+``--impl reference-cuda`` times the reference's own CUDA kernels (its
+JIT-built extensions, float32) on the same inputs, in chunks of pairs, as a
+secondary line with "impl": "reference-cuda".
+The reference package is read from baseline/_ref (not part of this
+package; the comparison arms only).
 """
 
 import argparse
@@ -66,7 +72,9 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-cuda"])
+    ap.add_argument("--chunk", type=int, default=512,
+                    help="pairs per call of the reference's CUDA path (memory bound)")
     ap.add_argument("--batch", type=int, default=4096)
     ap.add_argument("--length", type=int, default=1024)
     ap.add_argument("--dim", type=int, default=64)
@@ -317,13 +325,71 @@ def run_ours(a):
 
 # --------------------------------------------------------------- CPU arms
 
+REF_DIR = ROOT / "baseline" / "_ref"
+
+
+def _reference_package():
+    """The reference package (hibana2077/torchwarp) from baseline/_ref, or None."""
+    if not (REF_DIR / "torchwarp" / "__init__.py").exists():
+        return None
+    if str(REF_DIR) not in sys.path:
+        sys.path.insert(0, str(REF_DIR))
+    try:
+        import torchwarp.functional as ref_F
+    except Exception:  # pragma: no cover
+        return None
+    return ref_F
+
+
+def _cpu_model():
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:  # pragma: no cover
+        pass
+    return "unknown CPU"
+
+
+def _ref_cpu_step(ref_F, Xs, Ys, gamma):
+    x = Xs.clone().requires_grad_(True)
+    y = Ys.clone().requires_grad_(True)
+    ref_F.soft_dtw(x, y, gamma=gamma, backend="torch").sum().backward()
+
+
+def _ref_cpu_inputs(a, pairs):
+    g = torch.Generator().manual_seed(1234)
+    return (torch.randn(pairs, a.length, a.dim, generator=g),
+            torch.randn(pairs, a.length, a.dim, generator=g))
+
+
 def _oracle_sample(Xs, Ys, gamma):
     import oracle
     oracle.soft_dtw(Xs, Ys, gamma=gamma)
 
 
 def cpu_baseline(a, X, Y, sample_pairs=16):
-    """float64 oracle, one thread, on the first pairs of the same inputs."""
+    """The reference's float32 PyTorch CPU backend on every host thread, on
+    two pairs of the workload; without the reference package, the float64
+    oracle on one thread on the first pairs of the same inputs."""
+    ref_F = _reference_package()
+    if ref_F is not None:
+        threads = os.cpu_count() or 1
+        prev = torch.get_num_threads()
+        torch.set_num_threads(threads)
+        try:
+            Xs, Ys = _ref_cpu_inputs(a, 2)
+            _ref_cpu_step(ref_F, Xs[:1, :64], Ys[:1, :64], a.gamma)   # warm-up
+            t0 = time.perf_counter()
+            _ref_cpu_step(ref_F, Xs, Ys, a.gamma)
+            dt = time.perf_counter() - t0
+        finally:
+            torch.set_num_threads(prev)
+        cells = 2 * a.length * a.length
+        return {"value": cells / dt, "unit": UNIT, "cores": threads, "kind": "reference",
+                "sample": "2 of the {} pairs (N=M={}, D={}), the reference's float32 PyTorch "
+                          "CPU backend (backend='torch'), fwd+bwd, {} threads on {}, "
+                          "{:.1f} s".format(a.batch, a.length, a.dim, threads, _cpu_model(), dt)}
     import oracle
     try:
         from threadpoolctl import threadpool_limits
@@ -347,58 +413,173 @@ def cpu_baseline(a, X, Y, sample_pairs=16):
 
 
 def run_reference(a):
-    """The reference's CPU path, restated in oracle/ (the reference is Python +
-    JIT CUDA with no compiled CPU library), on every host thread."""
+    """The reference's own CPU implementation of the path: its float32
+    PyTorch backend (backend='torch') from baseline/_ref on every host thread,
+    each step a chunk of pairs of the workload.  Without the reference
+    package, its restatement in oracle/ (float64 C, all threads)."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if int(os.environ.get("RANK", "0")) != 0:
         return
-    from concurrent.futures import ThreadPoolExecutor
-
-    import oracle
-    try:
-        from threadpoolctl import threadpool_limits
-    except ImportError:  # pragma: no cover
-        threadpool_limits = None
-    oracle.lib()
     threads = os.cpu_count() or 1
-    per_thread = 1
-    pairs = threads * per_thread
-    rng = np.random.default_rng(1234)
-    Xs = rng.standard_normal((pairs, a.length, a.dim))
-    Ys = rng.standard_normal((pairs, a.length, a.dim))
+    ref_F = _reference_package()
+    if ref_F is not None:
+        torch.set_num_threads(threads)
+        pairs = 2
+        Xs, Ys = _ref_cpu_inputs(a, pairs)
+        for _ in range(a.warmup):
+            _ref_cpu_step(ref_F, Xs[:, :256], Ys[:, :256], a.gamma)
+        t0 = time.perf_counter()
+        for _ in range(a.steps):
+            _ref_cpu_step(ref_F, Xs, Ys, a.gamma)
+        dt = (time.perf_counter() - t0) / a.steps
+        kind, dtype = "reference", "f32"
+        sample = ("{} pairs per step (N=M={}, D={}) of the {}-pair workload, the reference's "
+                  "float32 PyTorch CPU backend (backend='torch'), fwd+bwd, {} threads on {}; "
+                  "warm-up steps on 256-step prefixes".format(pairs, a.length, a.dim, a.batch,
+                                                               threads, _cpu_model()))
+    else:
+        from concurrent.futures import ThreadPoolExecutor
 
-    def one(i):
-        sl = slice(i * per_thread, (i + 1) * per_thread)
-        oracle.soft_dtw(Xs[sl], Ys[sl], gamma=a.gamma)
+        import oracle
+        try:
+            from threadpoolctl import threadpool_limits
+        except ImportError:  # pragma: no cover
+            threadpool_limits = None
+        oracle.lib()
+        pairs = threads
+        rng = np.random.default_rng(1234)
+        Xn = rng.standard_normal((pairs, a.length, a.dim))
+        Yn = rng.standard_normal((pairs, a.length, a.dim))
 
-    def sample():
-        with ThreadPoolExecutor(threads) as ex:
-            list(ex.map(one, range(threads)))
+        def one(i):
+            oracle.soft_dtw(Xn[i:i + 1], Yn[i:i + 1], gamma=a.gamma)
 
-    ctx = threadpool_limits(1) if threadpool_limits else None
-    if ctx:
-        ctx.__enter__()
-    for _ in range(a.warmup):
-        sample()
-    t0 = time.perf_counter()
-    for _ in range(a.steps):
-        sample()
-    dt = (time.perf_counter() - t0) / a.steps
-    if ctx:
-        ctx.__exit__(None, None, None)
+        def sample():
+            with ThreadPoolExecutor(threads) as ex:
+                list(ex.map(one, range(threads)))
+
+        ctx = threadpool_limits(1) if threadpool_limits else None
+        if ctx:
+            ctx.__enter__()
+        for _ in range(a.warmup):
+            sample()
+        t0 = time.perf_counter()
+        for _ in range(a.steps):
+            sample()
+        dt = (time.perf_counter() - t0) / a.steps
+        if ctx:
+            ctx.__exit__(None, None, None)
+        kind, dtype = "port", "f64"
+        sample = ("{} pairs per step (N=M={}, D={}) of the {}-pair workload, the float64 C "
+                  "restatement in oracle/ (no reference package present), {} threads".format(
+                      pairs, a.length, a.dim, a.batch, threads))
     cells = pairs * a.length * a.length
     value = cells / dt
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "scaling": "strong", "vs_baseline": None, "dtype": dtype, "data": "synthetic",
             "config": config(a, world), "impl": "reference",
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                             "sample": "{} pairs per step (N=M={}, D={}) of the {}-pair "
-                                       "workload, float64 fwd+bwd".format(
-                                           pairs, a.length, a.dim, a.batch)},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind,
+                             "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     _emit(line)
+
+
+def run_reference_cuda(a):
+    """The reference's own CUDA kernels (JIT-built from baseline/_ref's
+    csrc on this GPU, float32, backend='cuda'), on the same workload in
+    chunks of --chunk pairs: one step is every chunk's fwd+bwd."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    ref_F = _reference_package()
+    if ref_F is None:
+        _emit({"impl": "reference-cuda", "unavailable": "reference package not in baseline/_ref"})
+        return
+    from torchwarp import _cuda as ref_cuda
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    ext = "jeanie" if a.workload in ("cfg3", "cfg4") else "udtw"
+    t_build = time.perf_counter()
+    if ref_cuda.load(ext) is None:
+        _emit({"impl": "reference-cuda",
+               "unavailable": "its CUDA extension did not build: {}".format(
+                   ref_cuda.build_error(ext))})
+        return
+    t_build = time.perf_counter() - t_build
+    g = torch.Generator(device=dev).manual_seed(1234)
+    metric, algo_per_step = METRIC, None
+    if a.workload in ("cfg5", "cfg5-udtw"):
+        X = torch.randn(a.batch, a.length, a.dim, device=dev, generator=g)
+        Y = torch.randn(a.batch, a.length, a.dim, device=dev, generator=g)
+        SX = torch.rand(a.batch, a.length, 1, device=dev, generator=g) + 0.5
+        SY = torch.rand(a.batch, a.length, 1, device=dev, generator=g) + 0.5
+        cells = a.batch * a.length * a.length
+        batch = a.batch
+        if a.workload == "cfg5-udtw":
+            metric = "fwd+bwd DP cells/s (uDTW B={} N=M={} D={}, beta=1)".format(
+                a.batch, a.length, a.dim)
+            algo_per_step = 16 * cells
+
+        def one(b0, b1):
+            x = X[b0:b1].detach().requires_grad_(True)
+            y = Y[b0:b1].detach().requires_grad_(True)
+            if a.workload == "cfg5":
+                ref_F.soft_dtw(x, y, gamma=a.gamma, backend="cuda").sum().backward()
+            else:
+                sx = SX[b0:b1].detach().requires_grad_(True)
+                sy = SY[b0:b1].detach().requires_grad_(True)
+                d, p = ref_F.udtw(x, y, sx, sy, gamma=a.gamma, beta=1.0, backend="cuda")
+                (d + p).sum().backward()
+    else:
+        K = (15,) if a.workload == "cfg3" else (7, 7)
+        batch = 1024
+        Q = torch.randn(batch, *K, 10, 256, device=dev, generator=g)
+        S = torch.randn(batch, 10, 256, device=dev, generator=g)
+        cells = batch * int(np.prod(K)) * 100
+        if a.workload == "cfg3":
+            metric = "fwd+bwd DP cells/s (JEANIE B=1024 K=15 T=U=10 D=256)"
+            algo_per_step = 335544320
+        else:
+            metric = "fwd+bwd DP cells/s (FVM B=1024 K1=K2=7 T=U=10 D=256)"
+            algo_per_step = 1048576000
+
+        def one(b0, b1):
+            q = Q[b0:b1].detach().requires_grad_(True)
+            s_ = S[b0:b1].detach().requires_grad_(True)
+            if a.workload == "cfg3":
+                ref_F.jeanie(q, s_, gamma=0.1, max_shift=1, backend="cuda").sum().backward()
+            else:
+                ref_F.fvm(q, s_, gamma=0.1, backend="cuda").sum().backward()
+    chunk = min(a.chunk, batch)
+    if algo_per_step is None:
+        algo_per_step = ALGO_BYTES_PER_CELL * cells
+
+    def step():
+        for b0 in range(0, batch, chunk):
+            one(b0, min(batch, b0 + chunk))
+
+    for _ in range(a.warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / a.steps
+    peak, src = peaks()
+    achieved = algo_per_step / (ms / 1e3) / 1e9
+    _emit({"metric": metric, "value": cells / (ms / 1e3), "unit": UNIT, "n_gpus": 1,
+           "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
+           "dtype": "f32", "data": "synthetic",
+           "config": config(a, 1) if a.workload.startswith("cfg5") else {"workload": a.workload},
+           "impl": "reference-cuda", "chunk_pairs": chunk, "jit_build_s": round(t_build, 1),
+           "roofline": {"bound": "hbm", "kernel": "whole step",
+                        "algorithmic_bytes_per_step": algo_per_step,
+                        "achieved": achieved, "peak": peak, "unit": "GB/s",
+                        "frac": achieved / peak, "peak_source": src}})
 
 
 # ------------------------------------------------- secondary workloads
@@ -620,6 +801,8 @@ def main():
     _stdout_to_stderr()
     if a.impl == "reference":
         run_reference(a)
+    elif a.impl == "reference-cuda":
+        run_reference_cuda(a)
     elif a.workload != "cfg5":
         _secondary(a)
     else:
