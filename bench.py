@@ -54,16 +54,18 @@ ALGO_BYTES_PER_CELL = 8      # soft-DTW fwd+bwd: cost read + cost-gradient write
 # launch, DRAM bytes per cell of one launch measured by ncu).  Algorithmic:
 # the DP forward's cost read and the backward's cost-gradient write (the
 # 8 B/cell of the step split between them), the cost builder's cost write,
-# each chain-rule launch's cost-gradient read.  Measured: DRAM read + write
-# of the full-size cfg5 launch (B=4096, N=M=1024, D=64) from a one-pass ncu
-# capture of dram__bytes_read.sum + dram__bytes_write.sum, per cell, without the
-# feature bytes (X, Y read by the cost builder, dX or dY written by each
-# chain-rule side), which are added at the timed shape.
+# each chain-rule launch's cost-gradient read.  Measured: dram__bytes_read.sum
+# + dram__bytes_write.sum of one launch of each kernel, captured one kernel at
+# a time on the small case of the step (B=4096, N=M=256, D=64), per cell,
+# less the feature bytes at N=256 (X, Y read by the cost builder; the other
+# side's features and the own gradient of each chain-rule side); the feature
+# bytes of the timed shape are added back.
 CALLS = {
-    "udtw_cost": (1, 4, 4.12),           # C write + mask
-    "sdtw_forward": (1, 4, 8.22),        # C read + saved R' write + edge stream
-    "sdtw_backward": (1, 4, 8.34),       # saved R' + edge + mask read + masked dC write
-    "udtw_features_grad": (2, 4, 4.55),  # masked dC read + the other side's features per unit
+    "udtw_cost": (1, 4, 3.91),           # C write + mask
+    "sdtw_forward": (1, 4, 8.27),        # C read + saved R' write + edge stream
+    "sdtw_backward": (1, 4, 8.39),       # saved R' + edge + mask read + masked dC write
+    "udtw_features_grad": (2, 4, 5.95),  # masked dC read + the other side's features per
+                                         # 128-row unit (2 B/cell at D=64, any N)
 }
 
 
@@ -296,8 +298,9 @@ def run_ours(a):
     roofline = {"bound": "hbm", "kernel": name, "achieved": achieved, "peak": peak,
                 "unit": "GB/s", "frac": achieved / peak, "peak_source": src,
                 "traffic": traffic,
-                "traffic_source": "ncu dram__bytes_read+write per cell of the full-size cfg5 "
-                                  "launch (one-pass capture), scaled to this launch's cells",
+                "traffic_source": "ncu dram__bytes_read+write per cell of one launch of this "
+                                  "kernel, captured alone on the small case of the step "
+                                  "(B=4096, N=M=256), scaled to this launch's cells",
                 "algorithmic_bytes_per_launch": algo, "avg_launch_ms": per_launch_ms,
                 "launches_per_call": launches_per_call,
                 "step_frac": (cells_local * ALGO_BYTES_PER_CELL / (ms_step / 1e3) / 1e9) / peak,

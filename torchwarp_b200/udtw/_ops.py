@@ -359,11 +359,6 @@ class SdtwCostGrad(torch.autograd.Function):
         return SdtwCostGrad._native_hvp(cost, g, V, gamma, bandwidth)
 
     @staticmethod
-    @_transforms.once_differentiable
-    def _native_hvp_once(ctx, cost, g, V, gamma, bandwidth):
-        return SdtwCostGrad._native_hvp(cost, g, V, gamma, bandwidth)
-
-    @staticmethod
     def _native_hvp(cost, g, V, gamma, bandwidth):
         B, N, M = cost.shape
         _, v_e, saved_v = sdtw_dp(cost, V.to(cost.dtype), gamma, bandwidth)
