@@ -85,3 +85,14 @@ def test_tensor_core_agrees_with_simt(tw, monkeypatch):
         out.append((c.detach(), a.grad, b.grad))
     for x, y in zip(*out):
         torch.testing.assert_close(x, y, rtol=1e-5, atol=1e-5)
+
+
+def test_tensor_core_cost_vmap(tw):
+    """vmap over the tensor-core route of euclidean_cost (the qs_cost fold
+    rule) matches the flattened batch."""
+    g = torch.Generator().manual_seed(10)
+    q = torch.randn(2, 3, 96, 64, generator=g).to(DEV)
+    s = torch.randn(2, 3, 64, 64, generator=g).to(DEV)
+    got = torch.func.vmap(tw.euclidean_cost)(q, s)
+    want = tw.euclidean_cost(q.reshape(6, 96, 64), s.reshape(6, 64, 64)).reshape(2, 3, 96, 64)
+    torch.testing.assert_close(got, want, rtol=1e-6, atol=1e-5)

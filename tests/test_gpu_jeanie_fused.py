@@ -173,3 +173,67 @@ def test_unsupported_shape_falls_back(tw, orc):
     d.sum().backward()
     od, _, odq, _ = orc.jeanie(q.double().numpy(), s.double().numpy(), gamma=0.1, max_shift=1)
     _fvalues((d, qq.grad), (od, odq))
+
+
+def test_fused_vmap_and_per_sample_grads(tw):
+    """vmap over the fused float32 kernels (the fold rule of jeanie_fused /
+    jeanie_fused_backward) matches the flattened batch; per-sample gradients
+    (vmap of grad) match the batch gradient."""
+    g = torch.Generator().manual_seed(12)
+    q = torch.randn(3, 2, 5, 6, 32, generator=g).to(DEV)
+    s = torch.randn(3, 2, 7, 32, generator=g).to(DEV)
+    F = tw.functional
+    for fn in (lambda a, b: F.jeanie(a, b, gamma=0.2, max_shift=1),
+               lambda a, b: F.fvm(a, b, gamma=0.2)):
+        got = torch.func.vmap(fn)(q, s)
+        want = fn(q.reshape(6, 5, 6, 32), s.reshape(6, 7, 32)).reshape(3, 2)
+        torch.testing.assert_close(got, want, rtol=1e-6, atol=1e-6)
+        per = torch.func.vmap(torch.func.grad(lambda a, b: fn(a, b).sum()))(q, s)
+        qq = q.reshape(6, 5, 6, 32).clone().requires_grad_(True)
+        fn(qq, s.reshape(6, 7, 32)).sum().backward()
+        torch.testing.assert_close(per, qq.grad.reshape(q.shape), rtol=1e-5, atol=1e-6)
+
+
+def test_fused_compile_fullgraph(tw):
+    torch._dynamo.reset()
+    g = torch.Generator().manual_seed(13)
+    q = torch.randn(4, 3, 6, 64, generator=g).to(DEV).requires_grad_(True)
+    s = torch.randn(4, 8, 64, generator=g).to(DEV).requires_grad_(True)
+    F = tw.functional
+
+    def f(a, b):
+        d, R = F.jeanie(a, b, gamma=0.3, max_shift=1, return_accumulator=True)
+        return d.sum() + 0.1 * (R ** 2).mean() + F.fvm(a, b, gamma=0.3).sum()
+
+    want, got = f(q, s), torch.compile(f, fullgraph=True)(q, s)
+    torch.testing.assert_close(got, want, rtol=1e-6, atol=1e-5)
+    for a, b in zip(torch.autograd.grad(got, (q, s)), torch.autograd.grad(want, (q, s))):
+        torch.testing.assert_close(a, b, rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("qshape,sshape,shift", [
+    ((3, 4, 1, 8), (3, 1, 8), 2),       # T = U = 1: one cell per viewpoint, shift clamped
+    ((2, 1, 9, 4), (2, 1, 4), 0),       # U = 1
+    ((2, 5, 1, 12), (2, 13, 12), 7),    # T = 1, shift beyond K - 1
+])
+def test_fused_small_grids_vs_oracle(tw, orc, qshape, sshape, shift):
+    g = torch.Generator().manual_seed(sum(qshape) * 3)
+    q = torch.randn(*qshape, generator=g, dtype=torch.float64).float()
+    s = torch.randn(*sshape, generator=g, dtype=torch.float64).float()
+    qq = q.to(DEV).requires_grad_(True)
+    ss = s.to(DEV).requires_grad_(True)
+    d = tw.functional.jeanie(qq, ss, gamma=0.1, max_shift=shift)
+    d.sum().backward()
+    od, _, odq, ods = orc.jeanie(q.double().numpy(), s.double().numpy(), gamma=0.1,
+                                 max_shift=shift)
+    _fvalues((d, qq.grad, ss.grad), (od, odq, ods))
+
+
+def test_fused_empty_batch(tw):
+    q = torch.randn(0, 3, 4, 8, device=DEV, requires_grad=True)
+    s = torch.randn(0, 5, 8, device=DEV, requires_grad=True)
+    d = tw.functional.jeanie(q, s, gamma=0.1)
+    f = tw.functional.fvm(q, s, gamma=0.1)
+    assert d.shape == (0,) and f.shape == (0,)
+    (d.sum() + f.sum()).backward()
+    assert q.grad.shape == q.shape and s.grad.shape == s.shape

@@ -150,7 +150,7 @@ def jeanie_dp(cost5, s1, s2, gamma):
         for k, t in enumerate(range(tlo, thi + 1)):
             cells[t * U + (d - t)] = r[..., k]
     R = torch.stack(cells, -1).reshape(B, K1, K2, T, U)
-    end = R[..., T - 1, U - 1].reshape(B, -1)
+    end = R[..., T - 1, U - 1].reshape(B, K1 * K2)
     out = -gamma * torch.logsumexp(-end / gamma, 1)
     return out, R
 

@@ -490,8 +490,14 @@ def fused_supported(K, T, U, D, fvm, features):
     env = os.environ.get("TW_JEANIE_UNFUSED", "")
     if env not in ("", "0"):
         return False
-    return bool(nat.lib().tw_jeanie_fused_supported(int(K), int(T), int(U), int(D), int(fvm),
-                                                    int(features)))
+    return _fused_supported_native(int(K), int(T), int(U), int(D), int(fvm), int(features))
+
+
+@torch._dynamo.assume_constant_result
+def _fused_supported_native(K, T, U, D, fvm, features):
+    # a pure function of its integer arguments: under torch.compile it is
+    # evaluated while tracing and the graph keeps the answer
+    return bool(nat.lib().tw_jeanie_fused_supported(K, T, U, D, fvm, features))
 
 
 def _fused_saved_bytes(B, K, T, U, fvm, features):

@@ -35,11 +35,13 @@ def fvm_from_cost(cost, *, gamma=0.1, backend="auto"):
     if cost.ndim < 4:
         raise ValueError("cost must be [B, K..., T, U] with at least one viewpoint dim")
     B, T, U = cost.shape[0], cost.shape[-2], cost.shape[-1]
-    flat = cost.reshape(B, -1, T, U)
+    K = 1
+    for k in cost.shape[1:-2]:
+        K *= k
+    flat = cost.reshape(B, K, T, U)
     if flat.dtype not in (torch.float32, torch.float64):
         flat = flat.float()
     _check_backend_name(backend)
-    K = flat.shape[1]
     if flat.dtype == torch.float32 and min(K, T, U) > 0 and \
             _ops.fused_supported(K, T, U, 0, True, False):
         # viewpoint soft-min and soft-DTW in one native call per direction
@@ -57,7 +59,10 @@ def fvm(query, support, *, gamma=0.1, metric="euclidean", backend="auto"):
                          "[B, K'..., U, D]")
     B, T, D = query.shape[0], query.shape[-2], query.shape[-1]
     U = support.shape[-2]
-    q = query.reshape(B, -1, T, D)
+    K = 1
+    for k in query.shape[1:-2]:
+        K *= k
+    q = query.reshape(B, K, T, D)
     if support.ndim == 3:
         K = q.shape[1]
         dtype = torch.promote_types(query.dtype, support.dtype)
@@ -79,7 +84,10 @@ def fvm(query, support, *, gamma=0.1, metric="euclidean", backend="auto"):
         # support K times; one permute of the (small) cost gives the
         # reference's [B, K, K', T, U] (jeanie/fvm.py:62-66).
         K = q.shape[1]
-        s = support.reshape(B, -1, U, D)
+        Kp = 1
+        for k in support.shape[1:-2]:
+            Kp *= k
+        s = support.reshape(B, Kp, U, D)
         Kp = s.shape[1]
         full = _METRICS[metric](q.reshape(B, K * T, D), s.reshape(B, Kp * U, D))
         cost = full.reshape(B, K, T, Kp, U).permute(0, 1, 3, 2, 4)
