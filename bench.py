@@ -65,7 +65,9 @@ CALLS = {
     "sdtw_forward": (1, 4, 8.27),        # C read + saved R' write + edge stream
     "sdtw_backward": (1, 4, 8.39),       # saved R' + edge + mask read + masked dC write
     "udtw_features_grad": (2, 4, 5.95),  # masked dC read + the other side's features per
-                                         # 128-row unit (2 B/cell at D=64, any N)
+                                         # 128-row unit (2 B/cell at D=64, any N); dense
+                                         # figures: the chain rule reads only the chunks
+                                         # of dC the DP backward flagged nonzero
 }
 
 

@@ -120,6 +120,40 @@ int tw_sdtw_backward_masked_f64(const double* grad_r, int B, int N, int M, doubl
                                 const void* saved, size_t saved_bytes, const uint32_t* mask,
                                 double* d_cost, void* workspace, size_t ws_bytes, void* stream);
 
+/* The masked soft-DTW backward above (fp32), also flagging the chunks of
+ * d_cost it writes a nonzero value into, for tw_sqeuclid_grad_flagged_f32.
+ * flags: tw_sdtw_chunk_flags_bytes(B, N, M) bytes (zeroed and filled here):
+ * one byte per 128 x 32 chunk [B][ceil(N/128)][KR], then one per 32 x 128
+ * chunk [B][ceil(M/128)][KC], each part 256-byte aligned, KR and KC the
+ * chunk counts ceil(M/32) and ceil(N/32) rounded up to multiples of 16.
+ * flags = NULL: no flags (same as tw_sdtw_backward_masked_f32). */
+size_t tw_sdtw_chunk_flags_bytes(int B, int N, int M);
+int tw_sdtw_backward_masked_flags_f32(const float* grad_r, int B, int N, int M, double gamma,
+                                      const void* saved, size_t saved_bytes,
+                                      const uint32_t* mask, float* d_cost, uint8_t* flags,
+                                      size_t flags_bytes, void* workspace, size_t ws_bytes,
+                                      void* stream);
+
+/* soft-DTW backward on features for the squared-Euclidean cost of
+ * tw_sqeuclid_cost_* (the backward half of the reference's fused soft-DTW on
+ * features: udtw_fused_backward with unit variance, src/torchwarp/udtw/_ops.py:179-183,
+ * csrc/udtw_cuda.cu:557-568): the masked DP backward, then the chain rule
+ *   dX = -2 S Y + 2 X rowsum(S), dY = -2 S^T X + 2 Y colsum(S),  S = dL/dcost.
+ * X [B,N,D], Y [B,M,D], mask and saved from tw_sqeuclid_cost_* and
+ * tw_sdtw_forward_*; dX, dY outputs.  workspace: at least
+ * tw_sdtw_features_workspace_bytes(B, N, M, dtype_bytes) bytes (dL/dcost,
+ * the DP's delay lines and, for fp32, the chunk flags).  fp32 runs
+ * tw_sdtw_backward_masked_flags_f32 then tw_sqeuclid_grad_flagged_f32. */
+size_t tw_sdtw_features_workspace_bytes(int B, int N, int M, int dtype_bytes);
+int tw_sdtw_features_backward_f32(const float* X, const float* Y, const uint32_t* mask,
+                                  const float* grad_r, int B, int N, int M, int D, double gamma,
+                                  const void* saved, size_t saved_bytes, float* dX, float* dY,
+                                  void* workspace, size_t ws_bytes, void* stream);
+int tw_sdtw_features_backward_f64(const double* X, const double* Y, const uint32_t* mask,
+                                  const double* grad_r, int B, int N, int M, int D, double gamma,
+                                  const void* saved, size_t saved_bytes, double* dX, double* dY,
+                                  void* workspace, size_t ws_bytes, void* stream);
+
 /* ---------------------------------------------------------------------
  * uDTW / soft-DTW cost from features (uDTW Eqs. 8, 16):
  *   sq_ij  = max(|x_i|^2 + |y_j|^2 - 2 x_i.y_j, 0)
@@ -178,6 +212,15 @@ int tw_sqeuclid_grad_f32(const float* X, const float* Y, const uint32_t* mask,
 int tw_sqeuclid_grad_f64(const double* X, const double* Y, const uint32_t* mask,
                          const double* d_cost, int B, int N, int M, int D, double* dX,
                          double* dY, void* stream);
+/* tw_sqeuclid_grad_f32 with mask = NULL (S = d_cost), given the chunk flags
+ * of tw_sdtw_backward_masked_flags_f32 (NULL: none).  On the tensor-core path
+ * it reads only the flagged chunks of d_cost and the first chunk of each
+ * 128-row (128-column) unit: a chunk flagged zero holds only zeros and adds
+ * exactly zero, so the result is that of the dense product.  The
+ * environment variable TW_GRAD_DENSE=1 makes it read every chunk. */
+int tw_sqeuclid_grad_flagged_f32(const float* X, const float* Y, const float* d_cost,
+                                 const uint8_t* flags, int B, int N, int M, int D, float* dX,
+                                 float* dY, void* stream);
 
 /* ---------------------------------------------------------------------
  * JEANIE on a cost [B, K1, K2, T, U] (one viewpoint axis: K2 = 1).

@@ -39,6 +39,14 @@ SIGNATURES = {
                                            _c_p, _c_sz, _c_p]),
     "tw_sdtw_backward_masked_f64": (_c_i, [_c_p, _c_i, _c_i, _c_i, _c_d, _c_p, _c_sz, _c_p, _c_p,
                                            _c_p, _c_sz, _c_p]),
+    "tw_sdtw_chunk_flags_bytes": (_c_sz, [_c_i, _c_i, _c_i]),
+    "tw_sdtw_backward_masked_flags_f32": (_c_i, [_c_p, _c_i, _c_i, _c_i, _c_d, _c_p, _c_sz, _c_p,
+                                                 _c_p, _c_p, _c_sz, _c_p, _c_sz, _c_p]),
+    "tw_sdtw_features_workspace_bytes": (_c_sz, [_c_i, _c_i, _c_i, _c_i]),
+    "tw_sdtw_features_backward_f32": (_c_i, [_c_p] * 4 + [_c_i] * 4 + [_c_d, _c_p, _c_sz, _c_p,
+                                                                   _c_p, _c_p, _c_sz, _c_p]),
+    "tw_sdtw_features_backward_f64": (_c_i, [_c_p] * 4 + [_c_i] * 4 + [_c_d, _c_p, _c_sz, _c_p,
+                                                                   _c_p, _c_p, _c_sz, _c_p]),
     "tw_udtw_cost_f32": (_c_i, [_c_p, _c_p, _c_p, _c_p, _c_i, _c_i, _c_i, _c_i, _c_d, _c_d, _c_p,
                                 _c_p, _c_p]),
     "tw_udtw_cost_f64": (_c_i, [_c_p, _c_p, _c_p, _c_p, _c_i, _c_i, _c_i, _c_i, _c_d, _c_d, _c_p,
@@ -51,6 +59,7 @@ SIGNATURES = {
                                     _c_p]),
     "tw_sqeuclid_grad_f64": (_c_i, [_c_p, _c_p, _c_p, _c_p, _c_i, _c_i, _c_i, _c_i, _c_p, _c_p,
                                     _c_p]),
+    "tw_sqeuclid_grad_flagged_f32": (_c_i, [_c_p] * 4 + [_c_i] * 4 + [_c_p, _c_p, _c_p]),
     "tw_jeanie_forward_f32": (_c_i, [_c_p, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_d, _c_p,
                                      _c_p, _c_p]),
     "tw_jeanie_forward_f64": (_c_i, [_c_p, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_d, _c_p,

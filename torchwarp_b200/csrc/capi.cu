@@ -4,6 +4,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -95,7 +96,8 @@ int sdtw_fwd(const T* cost, const T* pen, int B, int N, int M, double gamma, dou
 template <typename T>
 static int sdtw_bwd(const T* grad_r, const T* grad_p, int B, int N, int M, double gamma,
                     int has_pen, const void* saved, size_t saved_bytes, T* d_cost, T* d_pen,
-                    void* ws, size_t ws_bytes, cudaStream_t st, const uint32_t* mask = nullptr) {
+                    void* ws, size_t ws_bytes, cudaStream_t st, const uint32_t* mask = nullptr,
+                    uint8_t* tf_rows = nullptr, uint8_t* tf_cols = nullptr) {
   g_err[0] = 0;
   if (int e = check_dims("tw_sdtw_backward", B, N, M)) return e;
   if (!(gamma > 0)) return set_error(kInvalid, "tw_sdtw_backward: gamma must be > 0");
@@ -126,6 +128,10 @@ static int sdtw_bwd(const T* grad_r, const T* grad_p, int B, int N, int M, doubl
           (!d_pen || (uintptr_t)d_pen % 16 == 0);
   a.mask = mask;
   a.mask_np = (N + 3) & ~3;
+  a.tf_rows = tf_rows;
+  a.tf_cols = tf_cols;
+  a.tf_kr = (((M + 31) >> 5) + 15) & ~15;
+  a.tf_kc = (((N + 31) >> 5) + 15) & ~15;
   a.p = p;
   return sdtw_stream_backward<T>(a, has_p, false, st);
 }
@@ -151,6 +157,10 @@ int sq_grad_f32(const float*, const float*, const uint32_t*, const float*, int, 
                 float*, float*, cudaStream_t);
 int sq_grad_f64(const double*, const double*, const uint32_t*, const double*, int, int, int, int,
                 double*, double*, cudaStream_t);
+bool sq_grad_flagged_eligible(const float*, const float*, const float*, const float*,
+                              const float*, int, int);
+int sq_grad_flagged_f32(const float*, const float*, const float*, int, int, int, int, float*,
+                        float*, const uint8_t*, const uint8_t*, cudaStream_t);
 
 template <typename T>
 int jeanie_forward(const T*, int, int, int, int, int, int, int, double, T*, T*, cudaStream_t);
@@ -256,6 +266,138 @@ int tw_sdtw_backward_masked_f64(const double* grad_r, int B, int N, int M, doubl
   if (B > 0 && mask == nullptr) return set_error(kInvalid, "tw_sdtw_backward_masked: null mask");
   return sdtw_bwd<double>(grad_r, nullptr, B, N, M, gamma, 0, saved, saved_bytes, d_cost, nullptr,
                           workspace, ws_bytes, (cudaStream_t)stream, mask);
+}
+
+// Nonzero-chunk flags of dL/dcost (fp32): rows part [B][ceil(N/128)][KR],
+// then the cols part [B][ceil(M/128)][KC], each 256-byte aligned;
+// KR = 16 ceil(ceil(M/32)/16), KC = 16 ceil(ceil(N/32)/16).
+struct FlagLayout {
+  size_t rows, cols;
+};
+static FlagLayout flag_layout(int B, int N, int M) {
+  FlagLayout f;
+  f.rows = align256((size_t)B * ((N + 127) / 128) * ((((M + 31) >> 5) + 15) & ~15));
+  f.cols = align256((size_t)B * ((M + 127) / 128) * ((((N + 31) >> 5) + 15) & ~15));
+  return f;
+}
+
+size_t tw_sdtw_chunk_flags_bytes(int B, int N, int M) {
+  if (!dims_ok(B, N, M) || B == 0) return 0;
+  const FlagLayout f = flag_layout(B, N, M);
+  return f.rows + f.cols;
+}
+
+int tw_sdtw_backward_masked_flags_f32(const float* grad_r, int B, int N, int M, double gamma,
+                                      const void* saved, size_t saved_bytes,
+                                      const uint32_t* mask, float* d_cost, uint8_t* flags,
+                                      size_t flags_bytes, void* workspace, size_t ws_bytes,
+                                      void* stream) {
+  if (B > 0 && mask == nullptr) return set_error(kInvalid, "tw_sdtw_backward_masked: null mask");
+  uint8_t* rows = nullptr;
+  uint8_t* cols = nullptr;
+  if (B > 0 && dims_ok(B, N, M) && flags != nullptr) {
+    const FlagLayout f = flag_layout(B, N, M);
+    if (flags_bytes < f.rows + f.cols)
+      return set_error(kWorkspace, "tw_sdtw_backward_masked_flags: flags need %zu bytes",
+                       f.rows + f.cols);
+    const cudaError_t e = cudaMemsetAsync(flags, 0, f.rows + f.cols, (cudaStream_t)stream);
+    if (e != cudaSuccess)
+      return set_error(kLaunch, "tw_sdtw_backward_masked_flags: %s", cudaGetErrorString(e));
+    rows = flags;
+    cols = flags + f.rows;
+  }
+  return sdtw_bwd<float>(grad_r, nullptr, B, N, M, gamma, 0, saved, saved_bytes, d_cost, nullptr,
+                         workspace, ws_bytes, (cudaStream_t)stream, mask, rows, cols);
+}
+
+// TW_GRAD_DENSE=1 makes the chain rule read every chunk of dL/dcost (for
+// comparisons); by default it skips the chunks the DP backward flagged zero.
+static bool grad_dense() {
+  const char* env = std::getenv("TW_GRAD_DENSE");
+  return env != nullptr && env[0] != '\0' && env[0] != '0';
+}
+
+int tw_sqeuclid_grad_flagged_f32(const float* X, const float* Y, const float* d_cost,
+                                 const uint8_t* flags, int B, int N, int M, int D, float* dX,
+                                 float* dY, void* stream) {
+  g_err[0] = 0;
+  if (B < 0 || N <= 0 || M <= 0 || D <= 0 || (B && (!X || !Y || !d_cost || !dX || !dY)))
+    return set_error(kInvalid, "tw_sqeuclid_grad_flagged: invalid arguments");
+  const uint8_t* rows = nullptr;
+  const uint8_t* cols = nullptr;
+  if (B > 0 && flags != nullptr && !grad_dense()) {
+    rows = flags;
+    cols = flags + flag_layout(B, N, M).rows;
+  }
+  return sq_grad_flagged_f32(X, Y, d_cost, B, N, M, D, dX, dY, rows, cols, (cudaStream_t)stream);
+}
+
+// Workspace of tw_sdtw_features_backward_*: dL/dcost, the DP's delay lines
+// and (fp32) the chunk flags.
+struct FeatWs {
+  size_t dc, dp, fl;
+  size_t total() const { return dc + dp + fl; }
+};
+static FeatWs feat_ws(int B, int N, int M, int dtype_bytes) {
+  FeatWs w{0, 0, 0};
+  if (!dims_ok(B, N, M) || B == 0 || (dtype_bytes != 4 && dtype_bytes != 8)) return w;
+  w.dc = align256((size_t)B * N * M * dtype_bytes);
+  w.dp = tw_sdtw_workspace_bytes(B, N, M, dtype_bytes, 0);
+  if (dtype_bytes == 4) w.fl = tw_sdtw_chunk_flags_bytes(B, N, M);
+  return w;
+}
+
+size_t tw_sdtw_features_workspace_bytes(int B, int N, int M, int dtype_bytes) {
+  return feat_ws(B, N, M, dtype_bytes).total();
+}
+
+}  // extern "C"
+
+template <typename T>
+static int sdtw_feat_bwd(const T* X, const T* Y, const uint32_t* mask, const T* grad_r, int B,
+                         int N, int M, int D, double gamma, const void* saved, size_t saved_bytes,
+                         T* dX, T* dY, void* ws, size_t ws_bytes, cudaStream_t st) {
+  g_err[0] = 0;
+  if (int e = check_dims("tw_sdtw_features_backward", B, N, M)) return e;
+  if (D <= 0) return set_error(kInvalid, "tw_sdtw_features_backward: D must be > 0");
+  if (B == 0) return kOk;
+  if (!X || !Y || !mask || !dX || !dY || !ws)
+    return set_error(kInvalid, "tw_sdtw_features_backward: null pointer argument");
+  const FeatWs w = feat_ws(B, N, M, (int)sizeof(T));
+  if (ws_bytes < w.total())
+    return set_error(kWorkspace, "tw_sdtw_features_backward: workspace needs %zu bytes", w.total());
+  char* base = static_cast<char*>(ws);
+  T* dC = reinterpret_cast<T*>(base);
+  void* dpws = base + w.dc;
+  if constexpr (sizeof(T) == 4) {
+    uint8_t* flags = reinterpret_cast<uint8_t*>(base + w.dc + w.dp);
+    if (int rc = tw_sdtw_backward_masked_flags_f32(grad_r, B, N, M, gamma, saved, saved_bytes,
+                                                   mask, dC, flags, w.fl, dpws, w.dp, st))
+      return rc;
+    return tw_sqeuclid_grad_flagged_f32(X, Y, dC, flags, B, N, M, D, dX, dY, st);
+  } else {
+    if (int rc = sdtw_bwd<T>(grad_r, nullptr, B, N, M, gamma, 0, saved, saved_bytes, dC, nullptr,
+                             dpws, w.dp, st, mask))
+      return rc;
+    return sq_grad_f64(X, Y, nullptr, dC, B, N, M, D, dX, dY, st);
+  }
+}
+
+extern "C" {
+
+int tw_sdtw_features_backward_f32(const float* X, const float* Y, const uint32_t* mask,
+                                  const float* grad_r, int B, int N, int M, int D, double gamma,
+                                  const void* saved, size_t saved_bytes, float* dX, float* dY,
+                                  void* workspace, size_t ws_bytes, void* stream) {
+  return sdtw_feat_bwd<float>(X, Y, mask, grad_r, B, N, M, D, gamma, saved, saved_bytes, dX, dY,
+                              workspace, ws_bytes, (cudaStream_t)stream);
+}
+int tw_sdtw_features_backward_f64(const double* X, const double* Y, const uint32_t* mask,
+                                  const double* grad_r, int B, int N, int M, int D, double gamma,
+                                  const void* saved, size_t saved_bytes, double* dX, double* dY,
+                                  void* workspace, size_t ws_bytes, void* stream) {
+  return sdtw_feat_bwd<double>(X, Y, mask, grad_r, B, N, M, D, gamma, saved, saved_bytes, dX, dY,
+                               workspace, ws_bytes, (cudaStream_t)stream);
 }
 
 int tw_udtw_cost_f32(const float* X, const float* Y, const float* vx, const float* vy, int B,

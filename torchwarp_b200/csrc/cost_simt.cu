@@ -241,7 +241,8 @@ int tc_cost_f32(const float* X, const float* Y, const float* vx, const float* vy
                 int M, int D, double beta, double eps, float* C, float* Q, uint32_t* mask,
                 cudaStream_t st);
 int tc_sq_grad_f32(const float* X, const float* Y, const uint32_t* mask, const float* dC, int B,
-                   int N, int M, int D, float* dX, float* dY, cudaStream_t st);
+                   int N, int M, int D, float* dX, float* dY, cudaStream_t st,
+                   const uint8_t* tf_rows = nullptr, const uint8_t* tf_cols = nullptr);
 bool tc_grad_eligible(const float* X, const float* Y, const float* C, const float* dC,
                       const float* dQ, const float* dX, const float* dY, int M, int D);
 int tc_grad_f32(const float* X, const float* Y, const float* vx, const float* vy, const float* C,
@@ -292,6 +293,21 @@ int sq_grad_f32(const float* X, const float* Y, const uint32_t* mask, const floa
     return tc_sq_grad_f32(X, Y, mask, dC, B, N, M, D, dX, dY, st);
   return grad_launch<float>(X, Y, nullptr, nullptr, nullptr, dC, nullptr, B, N, M, D, 0.0, 1e-8,
                             dX, dY, nullptr, nullptr, st, mask);
+}
+// The soft-DTW chain rule after tw_sdtw_backward_masked (S = dC): true when
+// it runs on tensor cores, which then skip the chunks of dC that the DP
+// backward flagged as all zero (tf_rows / tf_cols, see tc_sq_grad_f32).
+bool sq_grad_flagged_eligible(const float* X, const float* Y, const float* dC, const float* dX,
+                              const float* dY, int M, int D) {
+  return tc_grad_eligible(X, Y, dC, dC, nullptr, dX, dY, M, D);
+}
+int sq_grad_flagged_f32(const float* X, const float* Y, const float* dC, int B, int N, int M,
+                        int D, float* dX, float* dY, const uint8_t* tf_rows,
+                        const uint8_t* tf_cols, cudaStream_t st) {
+  if (sq_grad_flagged_eligible(X, Y, dC, dX, dY, M, D))
+    return tc_sq_grad_f32(X, Y, nullptr, dC, B, N, M, D, dX, dY, st, tf_rows, tf_cols);
+  return grad_launch<float>(X, Y, nullptr, nullptr, nullptr, dC, nullptr, B, N, M, D, 0.0, 1e-8,
+                            dX, dY, nullptr, nullptr, st, nullptr);
 }
 int sq_grad_f64(const double* X, const double* Y, const uint32_t* mask, const double* dC, int B,
                 int N, int M, int D, double* dX, double* dY, cudaStream_t st) {

@@ -658,19 +658,21 @@ __device__ __forceinline__ const uint32_t* mask_row(const uint32_t* mask, int np
 // Write this lane's row of flush tile c (8 stream columns) from the staging
 // ring to dC (natural layout), data columns only; `mode` and `off` come from
 // row_mode for the tile's pass.  With `masked`, columns whose bit in `word` is
-// clear are written as 0.
+// clear are written as 0.  Returns true when a written value is nonzero.
 template <typename T>
-__device__ __forceinline__ void flush_row_tile(T* __restrict__ dst_base, const T* ring_row,
+__device__ __forceinline__ bool flush_row_tile(T* __restrict__ dst_base, const T* ring_row,
                                                const Cursor& c, int mode, long long off,
                                                const StreamPlan& p, int vec, bool masked,
                                                uint32_t word) {
-  if (mode != 2 || c.j0 >= p.M) return;
+  if (mode != 2 || c.j0 >= p.M) return false;
   const int j0 = c.j0;
   const T* src = ring_row + ((c.u * TILE) & (RING - 1));
   T* dst = dst_base + off + j0;
   const uint32_t bits = masked ? word >> (j0 & 31) : 0xffu;
+  bool nz = false;
   if (vec && j0 + TILE <= p.M) {
     constexpr int PER = 16 / (int)sizeof(T);
+    int any = 0;  // OR of the written words (float: magnitude bits only)
 #pragma unroll
     for (int h = 0; h < TILE / PER; ++h) {
       union {
@@ -684,11 +686,23 @@ __device__ __forceinline__ void flush_row_tile(T* __restrict__ dst_base, const T
           if (!((bits >> (h * PER + e)) & 1u)) u.v[e] = T(0);
       }
       *reinterpret_cast<int4*>(dst + h * PER) = u.i;
+      if constexpr (sizeof(T) == 4) {
+        any |= (u.i.x | u.i.y | u.i.z | u.i.w);
+      } else {
+#pragma unroll
+        for (int e = 0; e < PER; ++e) any |= u.v[e] != T(0) ? 1 : 0;
+      }
     }
+    nz = sizeof(T) == 4 ? (any & 0x7fffffff) != 0 : any != 0;
   } else {
     const int n = min(TILE, p.M - j0);
-    for (int h = 0; h < n; ++h) dst[h] = ((bits >> h) & 1u) ? src[h] : T(0);
+    for (int h = 0; h < n; ++h) {
+      const T v = ((bits >> h) & 1u) ? src[h] : T(0);
+      dst[h] = v;
+      nz = nz || v != T(0);
+    }
   }
+  return nz;
 }
 
 template <typename T, int KS, bool HAS_P, bool SEEDB, bool GRP>
@@ -954,8 +968,16 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
     // ---- between blocks
 #pragma unroll
     for (int k = 0; k < KS; ++k) {
-      flush_row_tile<T>(a.dC, myC + k * 32 * S, fl[k], fmode[k], foff[k], p, a.vec, masked,
-                        mwd[k]);
+      const bool nz = flush_row_tile<T>(a.dC, myC + k * 32 * S, fl[k], fmode[k], foff[k], p,
+                                        a.vec, masked, mwd[k]);
+      if (nz && a.tf_rows != nullptr) {
+        // this lane's 8 columns lie in one 32-column and one 128-column block
+        const int row = fl[k].band * 32 * KS + 32 * k + lane;
+        const long long b = wi.p0 + fl[k].pq;
+        const int j0 = fl[k].j0;
+        a.tf_rows[(b * ((p.N + 127) >> 7) + (row >> 7)) * a.tf_kr + (j0 >> 5)] = 1;
+        a.tf_cols[(b * ((p.M + 127) >> 7) + (j0 >> 7)) * a.tf_kc + (row >> 5)] = 1;
+      }
       if (HAS_P)
         flush_row_tile<T>(a.dQ, myQ + k * 32 * S, fl[k], fmode[k], foff[k], p, a.vec, false, 0u);
       const int oq = fl[k].q;

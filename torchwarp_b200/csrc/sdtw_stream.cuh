@@ -113,6 +113,13 @@ struct SdtwArgs {
   // [B][ceil(M/32)][mask_np]: dC is written as dC * bit (null: no mask)
   const uint32_t* mask = nullptr;
   int mask_np = 0;
+  // Nonzero-chunk flags of dC for the chain rule (optional; the caller zeroes
+  // them first): byte [b][i/128][j/32] of tf_rows (row stride tf_kr) and
+  // byte [b][j/128][i/32] of tf_cols (row stride tf_kc) are set to 1 where a
+  // written dC value of that 128 x 32 (32 x 128) chunk is nonzero.
+  uint8_t* tf_rows = nullptr;
+  uint8_t* tf_cols = nullptr;
+  int tf_kr = 0, tf_kc = 0;
   // scalars
   T kappa = 1;      // log2(e) / gamma
   T inv_kappa = 1;  // gamma * ln 2

@@ -670,6 +670,52 @@ struct GradShared {
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort;
+  int linfo[GRAD_MAX_LAND];  // chunk of each landing slot (index | kLastChunk)
+  int cinfo[GRAD_MAX_CONV];  // the same for each converted slot
+};
+
+// Chunk schedule of a chain-rule unit.  Without flags every 32-wide chunk of
+// the summed extent is processed.  With flags (one byte per chunk of the
+// unit, nonzero where the DP backward wrote a nonzero value of S into it)
+// only the flagged chunks and chunk 0 are: a chunk of S that is all zero adds
+// exactly zero to the products and to the row sums, and chunk 0 always runs
+// so that every unit writes its accumulator.  The producer walks the
+// schedule and files each landing slot's chunk in linfo; the consumers read
+// it from there, so all roles agree.
+constexpr int kLastChunk = 1 << 30;
+
+__device__ __forceinline__ uint32_t nz_bytes(uint32_t w) {
+  return (uint32_t)((w & 0xffu) != 0u) | ((uint32_t)((w & 0xff00u) != 0u) << 1) |
+         ((uint32_t)((w & 0xff0000u) != 0u) << 2) | ((uint32_t)((w >> 24) != 0u) << 3);
+}
+
+struct ChunkSched {
+  const uint8_t* fr;  // the unit's flag row (16-byte aligned, padded to 16), or null
+  int nK;
+  int w0;             // first chunk of the 64-chunk window in m
+  uint64_t m;
+  // first chunk >= c to process, or nK
+  __device__ __forceinline__ int next(int c) {
+    if (fr == nullptr) return c;
+    while (c < nK) {
+      if (c - w0 >= 64) {
+        w0 = c & ~63;
+        m = 0;
+#pragma unroll
+        for (int v = 0; v < 4; ++v)
+          if (w0 + 16 * v < nK) {
+            const uint4 q = __ldg(reinterpret_cast<const uint4*>(fr + w0 + 16 * v));
+            const uint32_t b16 = nz_bytes(q.x) | (nz_bytes(q.y) << 4) | (nz_bytes(q.z) << 8) |
+                                 (nz_bytes(q.w) << 12);
+            m |= (uint64_t)b16 << (16 * v);
+          }
+      }
+      const uint64_t rest = m >> (c - w0);
+      if (rest != 0) return c + __ffsll((long long)rest) - 1;
+      c = w0 + 64;
+    }
+    return nK;
+  }
 };
 
 struct GradGeom {
@@ -711,7 +757,8 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
                    const __grid_constant__ CUtensorMap mapOut, const float* __restrict__ A,
                    const float* __restrict__ va, const float* __restrict__ vb,
                    float* __restrict__ dva, int B, int N, int M, int D, float beta, float eps,
-                   int has_dq, GradGeom g, const uint32_t* __restrict__ mask, int sqrt_cost) {
+                   int has_dq, GradGeom g, const uint32_t* __restrict__ mask, int sqrt_cost,
+                   const uint8_t* __restrict__ tflags, int tf_k) {
   static_assert(!(PRE && (VAR || MASKED)), "PRE is the plain soft-DTW chain rule");
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* land_base = smem;
@@ -772,10 +819,14 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
     int it = 0;
     for (int u = blockIdx.x; u < total; u += gridDim.x) {
       const int b = u / nBlk, blk = u - b * nBlk;
-      for (int kc = 0; kc < nK; ++kc, ++it) {
+      ChunkSched sched{tflags != nullptr ? tflags + ((long long)b * nBlk + blk) * tf_k : nullptr,
+                       nK, -64, 0ull};
+      for (int kc = 0; kc < nK; ++it) {
+        const int nx = sched.next(kc + 1);
         const int s = it % LS;
         const unsigned ph = (unsigned)(it / LS) & 1u;
         if (!mbar_wait(&sh.lempty[s], ph ^ 1u, abort)) { record_timeout(abort); goto producer_drain; }
+        sh.linfo[s] = kc | (nx >= nK ? kLastChunk : 0);
         uint8_t* st = land_base + (size_t)s * g.l_bytes;
         unsigned tx = g.tx_fixed;
         const uint32_t* msrc[4] = {nullptr, nullptr, nullptr, nullptr};
@@ -823,6 +874,7 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
         // the other side's features: 32 summed rows x BD features
         for (int f = 0; f < g.nF; ++f)
           tma_load_3d(st + g.l_f + f * 4096, &mapF, &sh.lfull[s], 32 * f, kc * 32, b);
+        kc = nx;
       }
     }
   producer_drain:
@@ -850,7 +902,7 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
       const float va_r = VAR ? (r < R ? va[(long long)b * R + r] : 1.f) : 0.f;
       const float* vb_b = VAR ? vb + (long long)b * S : nullptr;
       float rsum = 0.f, vsum = 0.f;
-      for (int kc = 0; kc < nK && ok; ++kc, ++it) {
+      for (bool more = true; more && ok; ++it) {
         const int s = it % LS, cs = it % CS;
         if (!mbar_wait(&sh.lfull[s], (unsigned)(it / LS) & 1u, abort) ||
             !mbar_wait(&sh.cempty[cs], ((unsigned)(it / CS) & 1u) ^ 1u, abort)) {
@@ -858,6 +910,10 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
           ok = false;
           break;
         }
+        const int info = sh.linfo[s];
+        const int kc = info & (kLastChunk - 1);
+        more = (info & kLastChunk) == 0;
+        if (ct == 0) sh.cinfo[cs] = info;
         tc_fence_after();  // the MMAs that read this TMEM slot have completed
         const uint8_t* ld = land_base + (size_t)s * g.l_bytes;
         uint8_t* cv = conv_base + (size_t)cs * g.c_bytes;
@@ -1019,7 +1075,7 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
         }
       }
       float rsum[4] = {0.f, 0.f, 0.f, 0.f}, vsum[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int kc = 0; kc < nK && ok; ++kc, ++it) {
+      for (bool more = true; more && ok; ++it) {
         const int s = it % LS, cs = it % CS;
         if (!mbar_wait(&sh.lfull[s], (unsigned)(it / LS) & 1u, abort) ||
             !mbar_wait(&sh.cempty[cs], ((unsigned)(it / CS) & 1u) ^ 1u, abort)) {
@@ -1027,6 +1083,10 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
           ok = false;
           break;
         }
+        const int info = sh.linfo[s];
+        const int kc = info & (kLastChunk - 1);
+        more = (info & kLastChunk) == 0;
+        if (ct == 0) sh.cinfo[cs] = info;
         const uint8_t* ld = land_base + (size_t)s * g.l_bytes;
         uint8_t* cv = conv_base + (size_t)cs * g.c_bytes;
         if (SIDE == 0) {
@@ -1207,7 +1267,7 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem + (uint32_t)(a * ACC);
         bool ok = true;
-        for (int kc = 0; kc < nK; ++kc, ++it) {
+        for (bool more = true; more; ++it) {
           const int cs = it % CS;
           if (!mbar_wait(&sh.cfull[cs], (unsigned)(it / CS) & 1u, abort)) {
             record_timeout(abort);
@@ -1215,6 +1275,9 @@ __global__ void __launch_bounds__(GRAD_THREADS, 1)
             break;
           }
           tc_fence_after();
+          const int info = sh.cinfo[cs];
+          const int kc = info & (kLastChunk - 1);
+          more = (info & kLastChunk) == 0;
           const uint32_t st = smem_u32(conv_base + (size_t)cs * g.c_bytes);
           const uint32_t ah = st, al = st + SBOX, fh = st + g.c_fh, fl = st + g.c_fl;
           if constexpr (TA) {
@@ -1454,8 +1517,10 @@ template <int SIDE, bool VAR, bool MASKED, bool TA, bool WIDE, bool PRE>
 int grad_side_impl(const float* A, const float* F, const float* va, const float* vb,
                    const float* C, const float* dC, const float* dQ, int B, int N, int M, int D,
                    double beta, double eps, float* dA, float* dva, cudaStream_t st,
-                   const uint32_t* mask, int sqrt_cost) {
+                   const uint32_t* mask, int sqrt_cost, const uint8_t* tflags) {
   const int R = SIDE == 0 ? N : M, S = SIDE == 0 ? M : N;
+  if (((uintptr_t)tflags & 15u) != 0)
+    return set_error(kUnsupported, "tc grad: chunk flags not 16-byte aligned");
   CUtensorMap mDC, mC, mDQ, mF, mOut;
   int rc;
   // SIDE 0 reads S as a K-major operand (16-byte granules), SIDE 1 as an
@@ -1525,9 +1590,10 @@ int grad_side_impl(const float* A, const float* F, const float* va, const float*
   const int grid = (int)(units < sm_count() ? units : sm_count());
   auto kern = tc_grad_kernel<SIDE, VAR, MASKED, TA, WIDE, PRE>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const int tf_k = ((S + 31) / 32 + 15) & ~15;  // flag row: one byte per chunk, padded to 16
   kern<<<grid, GRAD_THREADS, smem, st>>>(mDC, mC, mDQ, mF, mOut, A, va, vb, dva, B, N, M, D,
                                          (float)beta, (float)eps, has_dq ? 1 : 0, g, mask,
-                                         sqrt_cost);
+                                         sqrt_cost, tflags, tf_k);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(kLaunch, "tc grad launch: %s", cudaGetErrorString(e));
   return kOk;
@@ -1540,20 +1606,21 @@ template <int SIDE, bool VAR, bool MASKED = false, bool PRE = false>
 int grad_side(const float* A, const float* F, const float* va, const float* vb, const float* C,
               const float* dC, const float* dQ, int B, int N, int M, int D, double beta,
               double eps, float* dA, float* dva, cudaStream_t st,
-              const uint32_t* mask = nullptr, int sqrt_cost = 0) {
+              const uint32_t* mask = nullptr, int sqrt_cost = 0,
+              const uint8_t* tflags = nullptr) {
   const char* env = std::getenv("TW_GRAD_SMEM_S");
   const bool smem_s = env != nullptr && env[0] != '\0' && env[0] != '0';
   const int BD = 32 * ((D + 31) / 32);
   // S in TMEM with wide MMAs while 2 x 2BD accumulator columns + one S slot
   // fit in 512 (D <= 96); wide MMAs with S in shared memory up to D = 128.
   if (!smem_s && 4 * BD + 64 <= 512)
-    return grad_side_impl<SIDE, VAR, MASKED, true, true, PRE>(A, F, va, vb, C, dC, dQ, B, N, M, D,
-                                                              beta, eps, dA, dva, st, mask, sqrt_cost);
+    return grad_side_impl<SIDE, VAR, MASKED, true, true, PRE>(
+        A, F, va, vb, C, dC, dQ, B, N, M, D, beta, eps, dA, dva, st, mask, sqrt_cost, tflags);
   if (2 * BD <= 256)
-    return grad_side_impl<SIDE, VAR, MASKED, false, true, PRE>(A, F, va, vb, C, dC, dQ, B, N, M,
-                                                               D, beta, eps, dA, dva, st, mask, sqrt_cost);
-  return grad_side_impl<SIDE, VAR, MASKED, false, false, PRE>(A, F, va, vb, C, dC, dQ, B, N, M, D,
-                                                              beta, eps, dA, dva, st, mask, sqrt_cost);
+    return grad_side_impl<SIDE, VAR, MASKED, false, true, PRE>(
+        A, F, va, vb, C, dC, dQ, B, N, M, D, beta, eps, dA, dva, st, mask, sqrt_cost, tflags);
+  return grad_side_impl<SIDE, VAR, MASKED, false, false, PRE>(
+      A, F, va, vb, C, dC, dQ, B, N, M, D, beta, eps, dA, dva, st, mask, sqrt_cost, tflags);
 }
 
 }  // namespace
@@ -1598,17 +1665,22 @@ int tc_qs_grad_f32(const float* Q, const float* Sp, const float* C, const float*
 
 // Squared-Euclidean chain rule with the positivity mask of the cost kernel in
 // place of the cost: S = dC where sq_raw > 0; with mask == nullptr, dC
-// already carries the mask (S = dC).
+// already carries the mask (S = dC), and tf_rows / tf_cols (optional, with a
+// null mask only) are the DP backward's nonzero-chunk flags of dC:
+// [B][ceil(N/128)][KR] and [B][ceil(M/128)][KC] bytes, KR = 16 ceil(ceil(M/32)/16),
+// KC = 16 ceil(ceil(N/32)/16); chunks flagged 0 are all zero and skipped.
 int tc_sq_grad_f32(const float* X, const float* Y, const uint32_t* mask, const float* dC, int B,
-                   int N, int M, int D, float* dX, float* dY, cudaStream_t st) {
+                   int N, int M, int D, float* dX, float* dY, cudaStream_t st,
+                   const uint8_t* tf_rows, const uint8_t* tf_cols) {
   if (B == 0 || N == 0 || M == 0) return kOk;
   int rc;
   if (mask == nullptr) {
     if ((rc = grad_side<0, false, false, true>(X, Y, nullptr, nullptr, nullptr, dC, nullptr, B, N,
-                                               M, D, 0.0, 1e-8, dX, nullptr, st)))
+                                               M, D, 0.0, 1e-8, dX, nullptr, st, nullptr, 0,
+                                               tf_rows)))
       return rc;
     return grad_side<1, false, false, true>(Y, X, nullptr, nullptr, nullptr, dC, nullptr, B, N, M,
-                                            D, 0.0, 1e-8, dY, nullptr, st);
+                                            D, 0.0, 1e-8, dY, nullptr, st, nullptr, 0, tf_cols);
   }
   if ((rc = grad_side<0, false, true>(X, Y, nullptr, nullptr, nullptr, dC, nullptr, B, N, M, D,
                                       0.0, 1e-8, dX, nullptr, st, mask)))

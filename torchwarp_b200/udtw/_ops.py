@@ -266,7 +266,10 @@ def sdtw_fused_backward(X: Tensor, Y: Tensor, mask: Tensor, saved: Tensor, grad_
                         gamma: float) -> Tuple[Tensor, Tensor]:
     """(dX, dY).  The DP backward writes dL/dcost with the cost's positivity
     mask applied (tw_sdtw_backward_masked), so the chain rule takes it as S
-    directly (tw_sqeuclid_grad with a null mask)."""
+    directly.  For fp32 the backward also flags the chunks of dL/dcost it
+    writes a nonzero value into, and the tensor-core chain rule reads only
+    those (tw_sdtw_backward_masked_flags_f32, tw_sqeuclid_grad_flagged_f32);
+    the composition is tw_sdtw_features_backward."""
     nat.require_cuda(X, Y, grad_r)
     B, N, D = X.shape
     M = Y.shape[1]
@@ -277,16 +280,31 @@ def sdtw_fused_backward(X: Tensor, Y: Tensor, mask: Tensor, saved: Tensor, grad_
         grad_r = grad_r.to(dtype).contiguous()
         s_cost = X.new_empty(B, N, M)
         with torch.cuda.device(X.device):
+            lib = nat.lib()
             wb = _ws_bytes(B, N, M, dtype, False)
             ws = torch.empty(wb, dtype=torch.uint8, device=X.device)
-            fn = getattr(nat.lib(), "tw_sdtw_backward_masked_" + nat.suffix(dtype))
-            nat.check(nat.call("sdtw_backward", fn, nat.ptr(grad_r), B, N, M, float(gamma),
-                               nat.ptr(saved), saved.numel(), nat.ptr(mask), nat.ptr(s_cost),
-                               nat.ptr(ws), wb, nat.stream_of(X)), "tw_sdtw_backward_masked")
-            fn = getattr(nat.lib(), "tw_sqeuclid_grad_" + nat.suffix(dtype))
-            nat.check(nat.call("udtw_features_grad", fn, nat.ptr(X), nat.ptr(Y), None,
-                               nat.ptr(s_cost), B, N, M, D, nat.ptr(dX), nat.ptr(dY),
-                               nat.stream_of(X)), "tw_sqeuclid_grad")
+            if dtype == torch.float32:
+                fb = lib.tw_sdtw_chunk_flags_bytes(B, N, M)
+                flags = torch.empty(fb, dtype=torch.uint8, device=X.device)
+                nat.check(nat.call("sdtw_backward", lib.tw_sdtw_backward_masked_flags_f32,
+                                   nat.ptr(grad_r), B, N, M, float(gamma), nat.ptr(saved),
+                                   saved.numel(), nat.ptr(mask), nat.ptr(s_cost), nat.ptr(flags),
+                                   fb, nat.ptr(ws), wb, nat.stream_of(X)),
+                          "tw_sdtw_backward_masked_flags")
+                nat.check(nat.call("udtw_features_grad", lib.tw_sqeuclid_grad_flagged_f32,
+                                   nat.ptr(X), nat.ptr(Y), nat.ptr(s_cost), nat.ptr(flags), B, N,
+                                   M, D, nat.ptr(dX), nat.ptr(dY), nat.stream_of(X)),
+                          "tw_sqeuclid_grad_flagged")
+            else:
+                fn = getattr(lib, "tw_sdtw_backward_masked_" + nat.suffix(dtype))
+                nat.check(nat.call("sdtw_backward", fn, nat.ptr(grad_r), B, N, M, float(gamma),
+                                   nat.ptr(saved), saved.numel(), nat.ptr(mask),
+                                   nat.ptr(s_cost), nat.ptr(ws), wb, nat.stream_of(X)),
+                          "tw_sdtw_backward_masked")
+                fn = getattr(lib, "tw_sqeuclid_grad_" + nat.suffix(dtype))
+                nat.check(nat.call("udtw_features_grad", fn, nat.ptr(X), nat.ptr(Y), None,
+                                   nat.ptr(s_cost), B, N, M, D, nat.ptr(dX), nat.ptr(dY),
+                                   nat.stream_of(X)), "tw_sqeuclid_grad")
     return dX, dY
 
 
