@@ -202,3 +202,49 @@ def test_features_backward_entry_matches_the_op(dtype):
     assert torch.equal(dX, Xg.grad)
     assert torch.equal(dY, Yg.grad)
     assert lib.tw_sdtw_features_workspace_bytes(0, N, M, es) == 0
+
+
+DP_CASES = [  # B, N, M, gamma, penalty, bandwidth, dtype
+    (8, 256, 256, 0.01, False, None, torch.float32),
+    (8, 256, 256, 0.01, True, None, torch.float32),
+    (3, 300, 520, 0.1, False, None, torch.float32),
+    (2, 1024, 1024, 0.01, False, None, torch.float32),   # band groups (few pairs)
+    (4, 200, 200, 1.0, True, None, torch.float32),
+    (4, 160, 200, 0.05, False, 40, torch.float32),
+    (5, 97, 130, 0.01, True, None, torch.float64),
+    (3, 64, 300, 0.01, False, None, torch.float64),
+]
+
+
+@pytest.mark.parametrize("case", DP_CASES)
+def test_dp_backward_zero_blocks_equal_full_evaluation(case, monkeypatch):
+    """The DP backward takes a shortcut through blocks of steps whose
+    adjoints are all zero; TW_DP_ALL_BLOCKS=1 evaluates them in full.  Both
+    must give the same dL/dcost and dL/dpenalty."""
+    import torchwarp_b200 as tw
+    B, N, M, gamma, pen, bw, dtype = case
+    g = torch.Generator(device="cuda").manual_seed(21)
+    C = (torch.rand(B, N, M, device="cuda", generator=g) * 4).to(dtype)
+    P = torch.randn(B, N, M, device="cuda", generator=g).to(dtype) if pen else None
+    w = torch.linspace(0.5, 2.0, B, device="cuda", dtype=dtype)
+
+    def grads():
+        c = C.clone().requires_grad_(True)
+        if pen:
+            p = P.clone().requires_grad_(True)
+            out = tw.functional.udtw_from_cost(c, p, gamma=gamma, bandwidth=bw)
+            ((out.distance * w).sum() + (out.penalty * w).sum()).backward()
+            return c.grad, p.grad
+        d = tw.functional.soft_dtw_from_cost(c, gamma=gamma, bandwidth=bw)
+        (d * w).sum().backward()
+        return (c.grad,)
+
+    monkeypatch.delenv("TW_DP_ALL_BLOCKS", raising=False)
+    fast = grads()
+    monkeypatch.setenv("TW_DP_ALL_BLOCKS", "1")
+    full = grads()
+    for a, b in zip(fast, full):
+        assert torch.equal(a, b)
+    if gamma <= 0.01 and not pen:
+        # most of dL/dcost is exactly zero there, which is what the shortcut uses
+        assert (fast[0] == 0).float().mean() > 0.5

@@ -130,6 +130,11 @@ static int sdtw_bwd(const T* grad_r, const T* grad_p, int B, int N, int M, doubl
   a.mask_np = (N + 3) & ~3;
   a.tf_rows = tf_rows;
   a.tf_cols = tf_cols;
+  {
+    // TW_DP_ALL_BLOCKS=1: no shortcut for blocks whose adjoints are all zero
+    const char* env = std::getenv("TW_DP_ALL_BLOCKS");
+    a.all_blocks = env != nullptr && env[0] != '\0' && env[0] != '0';
+  }
   a.tf_kr = (((M + 31) >> 5) + 15) & ~15;
   a.tf_kc = (((N + 31) >> 5) + 15) & ~15;
   a.p = p;

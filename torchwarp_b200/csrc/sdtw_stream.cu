@@ -853,33 +853,108 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
 
   // The 8 steps of block b, reading saved rows from Fc and loading the next
   // block's rows into Fn.  A pair's seed enters at step s_inj (-1: none).
+  //
+  // An adjoint enters the block's cells only from the warp's carried
+  // adjoints, the band below (dvs) or a seed.  When all of them are zero,
+  // every cell of the block has a zero adjoint and hands zero to each
+  // predecessor, so the soft-min weights need not be formed: such a dead
+  // block only stages zeros for dC, files zero top-row sends and moves the
+  // predecessor registers on to its last step (the sweep runs s = TILE-1 ..
+  // 0).  The test is exact (NaN is not zero) and warp-uniform.
+  // (Leaving the predecessor registers stale through dead blocks and
+  // rebuilding them in the next live one measured slower.)
   auto run_block = [&](const int t0, T (&Fc)[TILE][KS], T (&FPc)[TILE][KS], T (&Fn)[TILE][KS],
                        T (&FPn)[TILE][KS]) {
+    const int s_inj = (!SEEDB && cap_t >= t0 && cap_t < t0 + TILE) ? cap_t - t0 : -1;
+    T* coll8 = coll + (t0 & 24);  // slot of step t0 + s is coll8[s]
+    // adjoints arriving at the bottom row from the band below (column t - 32 KS)
+    T dvs[TILE], dvqs[TILE];
+    {
+      const T* sdb = sd + ((t0 - 32 * KS) & 63);
+      const T* sdpb = sdp + ((t0 - 32 * KS) & 63);
+#pragma unroll
+      for (int s = 0; s < TILE; ++s) {
+        dvs[s] = sdb[s];
+        if (HAS_P) dvqs[s] = sdpb[s];
+      }
+    }
+    bool live = a.all_blocks != 0 || (!SEEDB && s_inj >= 0);
+#pragma unroll
+    for (int k = 0; k < KS; ++k) {
+      live = live || accL[k] != T(0) || accB[k] != T(0) || dgp[k] != T(0);
+      if (HAS_P) live = live || Qacc[k] != T(0) || QaccB[k] != T(0) || dgq[k] != T(0);
+    }
+#pragma unroll
+    for (int s = 0; s < TILE; ++s) {
+      live = live || dvs[s] != T(0);
+      if (HAS_P) live = live || dvqs[s] != T(0);
+    }
+    if (!__any_sync(0xffffffffu, live)) {
+      // The next block is as surely dead when no seed enters it and the
+      // adjoints it receives from below (already in shared memory: a window
+      // is stored three blocks before its first use) are zero; it then needs
+      // no saved row but its first.
+      bool l2 = !SEEDB && cap_t >= t0 - TILE && cap_t < t0;
+      const T* sdn = sd + ((t0 - TILE - 32 * KS) & 63);
+      const T* sdpn = sdp + ((t0 - TILE - 32 * KS) & 63);
+#pragma unroll
+      for (int s = 0; s < TILE; ++s) {
+        l2 = l2 || sdn[s] != T(0);
+        if (HAS_P) l2 = l2 || sdpn[s] != T(0);
+      }
+      if (__any_sync(0xffffffffu, l2)) {
+#pragma unroll
+        for (int s = 0; s < TILE; ++s) {
+          load_saved_row<T, KS>(sRl, t0 - TILE - 2 + s, Fn[s]);
+          if (HAS_P) load_saved_row<T, KS>(sPl, t0 - TILE - 2 + s, FPn[s]);
+        }
+      } else {
+        load_saved_row<T, KS>(sRl, t0 - TILE - 2, Fn[0]);
+        if (HAS_P) load_saved_row<T, KS>(sPl, t0 - TILE - 2, FPn[0]);
+      }
+#pragma unroll
+      for (int s = 0; s < TILE; ++s) {
+        const int ia = (t0 + s - lane) & (RING - 1);
+#pragma unroll
+        for (int k = 0; k < KS; ++k) {
+          myC[k * 32 * S + ia] = T(0);
+          if (HAS_P) myQ[k * 32 * S + ia] = T(0);
+        }
+        if (lane == 0) {
+          coll8[s] = T(0);
+          if (HAS_P) coll8[32 + s] = T(0);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < KS; ++k) {
+        cur[k] = Fc[0][k];
+        if (HAS_P) Pcur[k] = FPc[0][k];
+      }
+#pragma unroll
+      for (int k = KS - 1; k >= 1; --k) {
+        Xc[k] = shfl_up1_rot(lane == 31 ? Fc[0][k - 1] : Fc[0][k]);
+        if (HAS_P) PXc[k] = shfl_up1_rot(lane == 31 ? FPc[0][k - 1] : FPc[0][k]);
+      }
+      Xc[0] = shfl_up1_rot(lane == 31 ? sb[(t0 - 1) & 63] : Fc[0][0]);
+      if (HAS_P) PXc[0] = shfl_up1_rot(lane == 31 ? sbp[(t0 - 1) & 63] : FPc[0][0]);
+      return;
+    }
 #pragma unroll
     for (int s = 0; s < TILE; ++s) {
       load_saved_row<T, KS>(sRl, t0 - TILE - 2 + s, Fn[s]);
       if (HAS_P) load_saved_row<T, KS>(sPl, t0 - TILE - 2 + s, FPn[s]);
     }
-    const int s_inj = (!SEEDB && cap_t >= t0 && cap_t < t0 + TILE) ? cap_t - t0 : -1;
-    T* coll8 = coll + (t0 & 24);  // slot of step t0 + s is coll8[s]
-    // The block's row -1 values (column t-1) and adjoints from below (column
-    // t - 32 KS), read into registers before the block's first shared-memory
-    // store so that no step waits on a shared load.
-    T bvs[TILE], bvps[TILE], dvs[TILE], dvqs[TILE];
+    // The block's row -1 values (column t-1), read into registers before the
+    // block's first shared-memory store so that no step waits on a shared load.
+    T bvs[TILE], bvps[TILE];
     {
       const int cb0 = (t0 - 1) & 63;
       const T* sb1 = sb + (t0 & 63);
       const T* sbp1 = sbp + (t0 & 63);
-      const T* sdb = sd + ((t0 - 32 * KS) & 63);
-      const T* sdpb = sdp + ((t0 - 32 * KS) & 63);
 #pragma unroll
       for (int s = 0; s < TILE; ++s) {
         bvs[s] = s == 0 ? sb[cb0] : sb1[s - 1];
-        dvs[s] = sdb[s];
-        if (HAS_P) {
-          bvps[s] = s == 0 ? sbp[cb0] : sbp1[s - 1];
-          dvqs[s] = sdpb[s];
-        }
+        if (HAS_P) bvps[s] = s == 0 ? sbp[cb0] : sbp1[s - 1];
       }
     }
 #pragma unroll

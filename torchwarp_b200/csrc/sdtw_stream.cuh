@@ -120,6 +120,9 @@ struct SdtwArgs {
   uint8_t* tf_rows = nullptr;
   uint8_t* tf_cols = nullptr;
   int tf_kr = 0, tf_kc = 0;
+  // backward: 1 = evaluate every block, also those whose adjoints are all
+  // zero (for comparisons; the result is the same)
+  int all_blocks = 0;
   // scalars
   T kappa = 1;      // log2(e) / gamma
   T inv_kappa = 1;  // gamma * ln 2
