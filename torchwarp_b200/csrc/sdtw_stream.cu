@@ -858,11 +858,15 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
   // adjoints, the band below (dvs) or a seed.  When all of them are zero,
   // every cell of the block has a zero adjoint and hands zero to each
   // predecessor, so the soft-min weights need not be formed: such a dead
-  // block only stages zeros for dC, files zero top-row sends and moves the
-  // predecessor registers on to its last step (the sweep runs s = TILE-1 ..
-  // 0).  The test is exact (NaN is not zero) and warp-uniform.
-  // (Leaving the predecessor registers stale through dead blocks and
-  // rebuilding them in the next live one measured slower.)
+  // block only stages zeros for dC and files zero top-row sends.  The test
+  // is exact (NaN is not zero) and warp-uniform.  The predecessor registers
+  // (cur, Xc) are not carried through dead blocks (`stale`): a dead block
+  // loads no saved row unless the next block is live, and then loads that
+  // block's rows and, into cur, the row it starts from; the live block
+  // forms Xc from it.  (Loading each dead block's first row to carry cur and
+  // Xc through, or deferring that consumption, measured slower: every dead
+  // block then waits on a DRAM load issued one short block earlier.)
+  bool stale = false;
   auto run_block = [&](const int t0, T (&Fc)[TILE][KS], T (&FPc)[TILE][KS], T (&Fn)[TILE][KS],
                        T (&FPn)[TILE][KS]) {
     const int s_inj = (!SEEDB && cap_t >= t0 && cap_t < t0 + TILE) ? cap_t - t0 : -1;
@@ -903,14 +907,15 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
         if (HAS_P) l2 = l2 || sdpn[s] != T(0);
       }
       if (__any_sync(0xffffffffu, l2)) {
+        // the next block is live: its rows, and in cur the saved row it
+        // starts from (t0 - 2, this block's first row)
 #pragma unroll
         for (int s = 0; s < TILE; ++s) {
           load_saved_row<T, KS>(sRl, t0 - TILE - 2 + s, Fn[s]);
           if (HAS_P) load_saved_row<T, KS>(sPl, t0 - TILE - 2 + s, FPn[s]);
         }
-      } else {
-        load_saved_row<T, KS>(sRl, t0 - TILE - 2, Fn[0]);
-        if (HAS_P) load_saved_row<T, KS>(sPl, t0 - TILE - 2, FPn[0]);
+        load_saved_row<T, KS>(sRl, t0 - 2, cur);
+        if (HAS_P) load_saved_row<T, KS>(sPl, t0 - 2, Pcur);
       }
 #pragma unroll
       for (int s = 0; s < TILE; ++s) {
@@ -925,19 +930,23 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
           if (HAS_P) coll8[32 + s] = T(0);
         }
       }
-#pragma unroll
-      for (int k = 0; k < KS; ++k) {
-        cur[k] = Fc[0][k];
-        if (HAS_P) Pcur[k] = FPc[0][k];
-      }
+      stale = true;
+      return;
+    }
+    if (stale) {
+      // after dead blocks: cur holds saved row t0 + 6, loaded by the block
+      // before; Xc = X(t0 + 7) with the row -1 value of column t0 + 7 (in
+      // this block's window of sb)
+      const T b7 = sb[(t0 + 7) & 63];
+      const T b7p = HAS_P ? sbp[(t0 + 7) & 63] : T(0);
 #pragma unroll
       for (int k = KS - 1; k >= 1; --k) {
-        Xc[k] = shfl_up1_rot(lane == 31 ? Fc[0][k - 1] : Fc[0][k]);
-        if (HAS_P) PXc[k] = shfl_up1_rot(lane == 31 ? FPc[0][k - 1] : FPc[0][k]);
+        Xc[k] = shfl_up1_rot(lane == 31 ? cur[k - 1] : cur[k]);
+        if (HAS_P) PXc[k] = shfl_up1_rot(lane == 31 ? Pcur[k - 1] : Pcur[k]);
       }
-      Xc[0] = shfl_up1_rot(lane == 31 ? sb[(t0 - 1) & 63] : Fc[0][0]);
-      if (HAS_P) PXc[0] = shfl_up1_rot(lane == 31 ? sbp[(t0 - 1) & 63] : FPc[0][0]);
-      return;
+      Xc[0] = shfl_up1_rot(lane == 31 ? b7 : cur[0]);
+      if (HAS_P) PXc[0] = shfl_up1_rot(lane == 31 ? b7p : Pcur[0]);
+      stale = false;
     }
 #pragma unroll
     for (int s = 0; s < TILE; ++s) {
