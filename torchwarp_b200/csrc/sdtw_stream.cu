@@ -668,33 +668,48 @@ __device__ __forceinline__ bool flush_row_tile(T* __restrict__ dst_base, const T
   const int j0 = c.j0;
   const T* src = ring_row + ((c.u * TILE) & (RING - 1));
   T* dst = dst_base + off + j0;
-  const uint32_t bits = masked ? word >> (j0 & 31) : 0xffu;
   bool nz = false;
   if (vec && j0 + TILE <= p.M) {
     constexpr int PER = 16 / (int)sizeof(T);
-    int any = 0;  // OR of the written words (float: magnitude bits only)
+    union {
+      int4 i;
+      T v[PER];
+    } u[TILE / PER];
+    int any = 0;  // OR of the staged words (float: magnitude bits only)
 #pragma unroll
     for (int h = 0; h < TILE / PER; ++h) {
-      union {
-        int4 i;
-        T v[PER];
-      } u;
-      u.i = *reinterpret_cast<const int4*>(src + h * PER);
-      if (masked) {
-#pragma unroll
-        for (int e = 0; e < PER; ++e)
-          if (!((bits >> (h * PER + e)) & 1u)) u.v[e] = T(0);
-      }
-      *reinterpret_cast<int4*>(dst + h * PER) = u.i;
+      u[h].i = *reinterpret_cast<const int4*>(src + h * PER);
       if constexpr (sizeof(T) == 4) {
-        any |= (u.i.x | u.i.y | u.i.z | u.i.w);
+        any |= (u[h].i.x | u[h].i.y | u[h].i.z | u[h].i.w);
       } else {
 #pragma unroll
-        for (int e = 0; e < PER; ++e) any |= u.v[e] != T(0) ? 1 : 0;
+        for (int e = 0; e < PER; ++e) any |= u[h].v[e] != T(0) ? 1 : 0;
       }
     }
     nz = sizeof(T) == 4 ? (any & 0x7fffffff) != 0 : any != 0;
+    // An all-zero tile needs no mask, so it does not wait for the mask word
+    // (loaded a block earlier; dead blocks are short).
+    if (masked && nz) {
+      const uint32_t mb = word >> (j0 & 31);
+      any = 0;
+#pragma unroll
+      for (int h = 0; h < TILE / PER; ++h) {
+#pragma unroll
+        for (int e = 0; e < PER; ++e)
+          if (!((mb >> (h * PER + e)) & 1u)) u[h].v[e] = T(0);
+        if constexpr (sizeof(T) == 4) {
+          any |= (u[h].i.x | u[h].i.y | u[h].i.z | u[h].i.w);
+        } else {
+#pragma unroll
+          for (int e = 0; e < PER; ++e) any |= u[h].v[e] != T(0) ? 1 : 0;
+        }
+      }
+      nz = sizeof(T) == 4 ? (any & 0x7fffffff) != 0 : any != 0;
+    }
+#pragma unroll
+    for (int h = 0; h < TILE / PER; ++h) *reinterpret_cast<int4*>(dst + h * PER) = u[h].i;
   } else {
+    const uint32_t bits = masked ? word >> (j0 & 31) : 0xffu;
     const int n = min(TILE, p.M - j0);
     for (int h = 0; h < n; ++h) {
       const T v = ((bits >> h) & 1u) ? src[h] : T(0);
@@ -896,8 +911,7 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
     if (!__any_sync(0xffffffffu, live)) {
       // The next block is as surely dead when no seed enters it and the
       // adjoints it receives from below (already in shared memory: a window
-      // is stored three blocks before its first use) are zero; it then needs
-      // no saved row but its first.
+      // is stored at least one block before this test reads it) are zero.
       bool l2 = !SEEDB && cap_t >= t0 - TILE && cap_t < t0;
       const T* sdn = sd + ((t0 - TILE - 32 * KS) & 63);
       const T* sdpn = sdp + ((t0 - TILE - 32 * KS) & 63);
@@ -1042,7 +1056,7 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
   unsigned gphase = 0;
   bool gdead = false;
   const int ql = wi.Q * p.L;  // local columns of the warp's passes
-  bool pend_b = false, pend_d = false;  // refills waiting for their shared-memory store
+  int pend_b = 0, pend_d = 0;  // refills waiting for their shared-memory store: blocks to go
   int pbc = 0, pdc = 0;
   T pbv = T(0), pbpv = T(0), pdv = T(0), pdpv = T(0);
   // Work between block t0 and block t0 - 8.
@@ -1086,20 +1100,20 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
       }
     }
     // Window refills are loaded from global memory at the end of one block
-    // and stored to shared memory at the end of the next, so no warp waits
-    // for the load; the slots they fill are first read three blocks later.
-    if (pend_b) {
+    // and stored to shared memory two blocks later, so no warp waits for the
+    // load even when the blocks between are dead (short); the slots they fill
+    // are first read four blocks after the load (by the dead-block test of
+    // the next block's adjoints from below: three).
+    if (pend_b > 0 && --pend_b == 0) {
       __syncwarp();
       sb[pbc & 63] = pbv;
       if (HAS_P) sbp[pbc & 63] = pbpv;
-      pend_b = false;
       __syncwarp();
     }
-    if (pend_d) {
+    if (pend_d > 0 && --pend_d == 0) {
       __syncwarp();
       sd[pdc & 63] = pdv;
       if (HAS_P) sdp[pdc & 63] = pdpv;
-      pend_d = false;
       __syncwarp();
     }
     if ((t0 & 31) == 0) {
@@ -1126,7 +1140,7 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
       pbc = t0 - 64 + lane;
       pbv = row_above_saved<T, KS, GRP>(eRa, pbc, p, wi, big);
       if (HAS_P) pbpv = row_above_saved<T, KS, GRP>(ePa, pbc, p, wi, T(0));
-      pend_b = true;
+      pend_b = 2;
     }
     // the next block (t0 - 8) may open a new window of bottom-row columns
     const int dwn = (t0 - TILE - 32 * KS) >> 5;
@@ -1135,7 +1149,7 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
       pdc = 32 * (dw - 1) + lane;
       pdv = push_from_below<T, SEEDB, GRP>(dlRb, pdc, p, wi, a.grad_r);
       if (HAS_P) pdpv = push_from_below<T, SEEDB, GRP>(dlPb, pdc, p, wi, a.grad_p);
-      pend_d = true;
+      pend_d = 2;
     }
   };
 
