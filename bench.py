@@ -56,18 +56,19 @@ ALGO_BYTES_PER_CELL = 8      # soft-DTW fwd+bwd: cost read + cost-gradient write
 # 8 B/cell of the step split between them), the cost builder's cost write,
 # each chain-rule launch's cost-gradient read.  Measured: dram__bytes_read.sum
 # + dram__bytes_write.sum of one launch of each kernel, captured one kernel at
-# a time on the small case of the step (B=4096, N=M=256, D=64), per cell,
-# less the feature bytes at N=256 (X, Y read by the cost builder; the other
-# side's features and the own gradient of each chain-rule side); the feature
-# bytes of the timed shape are added back.
+# a time.  The DP sweeps and the chain rule were captured on the timed rows'
+# shape (N=M=1024, D=64, gamma=0.01) at B=256, since what the backward and the
+# chain rule skip depends on the rows, not the batch; the chain rule's figure
+# less its own gradient write, which is added back at the timed shape.  The
+# cost builder was captured at B=4096, N=M=256, less its X, Y read at that N
+# (added back at the timed shape).
 CALLS = {
     "udtw_cost": (1, 4, 3.91),           # C write + mask
-    "sdtw_forward": (1, 4, 8.27),        # C read + saved R' write + edge stream
-    "sdtw_backward": (1, 4, 8.39),       # saved R' + edge + mask read + masked dC write
-    "udtw_features_grad": (2, 4, 5.95),  # masked dC read + the other side's features per
-                                         # 128-row unit (2 B/cell at D=64, any N); dense
-                                         # figures: the chain rule reads only the chunks
-                                         # of dC the DP backward flagged nonzero
+    "sdtw_forward": (1, 4, 8.06),        # C read + saved R' write + edge stream
+    "sdtw_backward": (1, 4, 4.59),       # masked dC write + the saved rows of the blocks
+                                         # next to the alignment corridor + mask + edge
+    "udtw_features_grad": (2, 4, 1.15),  # the chunks of dC the backward flagged nonzero and
+                                         # their features (dense: 5.95)
 }
 
 
@@ -301,8 +302,8 @@ def run_ours(a):
                 "unit": "GB/s", "frac": achieved / peak, "peak_source": src,
                 "traffic": traffic,
                 "traffic_source": "ncu dram__bytes_read+write per cell of one launch of this "
-                                  "kernel, captured alone on the small case of the step "
-                                  "(B=4096, N=M=256), scaled to this launch's cells",
+                                  "kernel, captured alone on the timed rows' shape at B=256 "
+                                  "(N=M=1024, D=64), scaled to this launch's cells",
                 "algorithmic_bytes_per_launch": algo, "avg_launch_ms": per_launch_ms,
                 "launches_per_call": launches_per_call,
                 "step_frac": (cells_local * ALGO_BYTES_PER_CELL / (ms_step / 1e3) / 1e9) / peak,
