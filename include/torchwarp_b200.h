@@ -134,6 +134,21 @@ int tw_sdtw_backward_masked_flags_f32(const float* grad_r, int B, int N, int M, 
                                       size_t flags_bytes, void* workspace, size_t ws_bytes,
                                       void* stream);
 
+/* The fastest fp32 pair for soft-DTW on features.  The masked backward
+ * above with the chunk flags, writing d_cost sparsely: an 8-column tile of a
+ * row that holds only zeros is not written, and nz_mask (uint32 words in the
+ * positivity mask's layout [B][ceil(M/32)][4 ceil(N/4)],
+ * tw_sdtw_nonzero_mask_bytes(B, N, M) bytes, zeroed and filled here) gets a
+ * set bit for every nonzero value.  Cells of d_cost whose bit is clear may
+ * hold anything; pass nz_mask along with it.  mask, nz_mask and flags are
+ * required.  (The reference writes every cell of its cost gradient.) */
+size_t tw_sdtw_nonzero_mask_bytes(int B, int N, int M);
+int tw_sdtw_backward_sparse_f32(const float* grad_r, int B, int N, int M, double gamma,
+                                const void* saved, size_t saved_bytes, const uint32_t* mask,
+                                float* d_cost, uint32_t* nz_mask, uint8_t* flags,
+                                size_t flags_bytes, void* workspace, size_t ws_bytes,
+                                void* stream);
+
 /* soft-DTW backward on features for the squared-Euclidean cost of
  * tw_sqeuclid_cost_* (the backward half of the reference's fused soft-DTW on
  * features: udtw_fused_backward with unit variance, src/torchwarp/udtw/_ops.py:179-183,
@@ -142,8 +157,8 @@ int tw_sdtw_backward_masked_flags_f32(const float* grad_r, int B, int N, int M, 
  * X [B,N,D], Y [B,M,D], mask and saved from tw_sqeuclid_cost_* and
  * tw_sdtw_forward_*; dX, dY outputs.  workspace: at least
  * tw_sdtw_features_workspace_bytes(B, N, M, dtype_bytes) bytes (dL/dcost,
- * the DP's delay lines and, for fp32, the chunk flags).  fp32 runs
- * tw_sdtw_backward_masked_flags_f32 then tw_sqeuclid_grad_flagged_f32. */
+ * the DP's delay lines and, for fp32, the chunk flags and the nonzero mask).
+ * fp32 runs tw_sdtw_backward_sparse_f32 then tw_sqeuclid_grad_sparse_f32. */
 size_t tw_sdtw_features_workspace_bytes(int B, int N, int M, int dtype_bytes);
 int tw_sdtw_features_backward_f32(const float* X, const float* Y, const uint32_t* mask,
                                   const float* grad_r, int B, int N, int M, int D, double gamma,
@@ -221,6 +236,13 @@ int tw_sqeuclid_grad_f64(const double* X, const double* Y, const uint32_t* mask,
 int tw_sqeuclid_grad_flagged_f32(const float* X, const float* Y, const float* d_cost,
                                  const uint8_t* flags, int B, int N, int M, int D, float* dX,
                                  float* dY, void* stream);
+/* The chain rule after tw_sdtw_backward_sparse_f32: S = d_cost where the
+ * nz_mask bit is set, else 0 (whatever d_cost holds there), reading only the
+ * flagged chunks on the tensor-core path.  Same result as the dense d_cost of
+ * tw_sdtw_backward_masked_f32 through tw_sqeuclid_grad_f32. */
+int tw_sqeuclid_grad_sparse_f32(const float* X, const float* Y, const uint32_t* nz_mask,
+                                const float* d_cost, const uint8_t* flags, int B, int N, int M,
+                                int D, float* dX, float* dY, void* stream);
 
 /* ---------------------------------------------------------------------
  * JEANIE on a cost [B, K1, K2, T, U] (one viewpoint axis: K2 = 1).

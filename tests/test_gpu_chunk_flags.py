@@ -248,3 +248,76 @@ def test_dp_backward_zero_blocks_equal_full_evaluation(case, monkeypatch):
     if gamma <= 0.01 and not pen:
         # most of dL/dcost is exactly zero there, which is what the shortcut uses
         assert (fast[0] == 0).float().mean() > 0.5
+
+
+def _nz_ref(S):
+    """Words [B][ceil(M/32)][4 ceil(N/4)] with bit j & 31 of word [b][j >> 5][i]
+    set where S[b, i, j] != 0."""
+    B, N, M = S.shape
+    mw, npad = -(-M // 32), (N + 3) // 4 * 4
+    nz = np.zeros((B, npad, mw * 32), np.uint64)
+    nz[:, :N, :M] = (S != 0).cpu().numpy()
+    w = (nz.reshape(B, npad, mw, 32) << np.arange(32, dtype=np.uint64)).sum(-1)
+    return w.transpose(0, 2, 1).astype(np.uint32)
+
+
+def _sparse_backward(X, Y, gamma):
+    lib = nat.lib()
+    B, N, _ = X.shape
+    M = Y.shape[1]
+    mask, saved, ws = _forward(X, Y, gamma)
+    g = torch.linspace(0.5, 1.5, B, device="cuda")
+    dC = torch.full((B, N, M), float("nan"), device="cuda")   # unwritten cells stay NaN
+    nzm = torch.full_like(mask, -1)                            # zeroed by the call
+    fb = lib.tw_sdtw_chunk_flags_bytes(B, N, M)
+    flags = torch.full((fb,), 7, dtype=torch.uint8, device="cuda")
+    assert lib.tw_sdtw_nonzero_mask_bytes(B, N, M) == nzm.numel() * 4
+    nat.check(lib.tw_sdtw_backward_sparse_f32(nat.ptr(g), B, N, M, float(gamma), nat.ptr(saved),
+                                              saved.numel(), nat.ptr(mask), nat.ptr(dC),
+                                              nat.ptr(nzm), nat.ptr(flags), fb, nat.ptr(ws),
+                                              ws.numel(), nat.stream_of(X)), "backward_sparse")
+    torch.cuda.synchronize()
+    return dC, nzm, flags
+
+
+SPARSE_CASES = CASES + [(2, 70, 45, 8, 0.01), (2, 66, 90, 64, 0.05)]
+
+
+@pytest.mark.parametrize("case", SPARSE_CASES)
+def test_sparse_backward_writes_the_nonzero_tiles(case):
+    """tw_sdtw_backward_sparse_f32: the bit mask marks exactly the nonzero
+    values of the dense dL/dcost, those cells hold its values, and the chunk
+    flags are those of the dense dL/dcost."""
+    B, N, M, D, gamma = case
+    X, Y = _inputs(B, N, M, D, 15)
+    dense, _ = _backward(X, Y, gamma, flagged=False)
+    dC, nzm, flags = _sparse_backward(X, Y, gamma)
+    want = _nz_ref(dense)
+    np.testing.assert_array_equal(nzm.cpu().numpy().view(np.uint32), want)
+    on = dense != 0
+    assert torch.equal(dC[on], dense[on])
+    np.testing.assert_array_equal(flags.cpu().numpy(), _flags_ref(dense))
+
+
+@pytest.mark.parametrize("case", SPARSE_CASES)
+def test_sparse_chain_rule_equals_dense(case, monkeypatch):
+    """The sparse pair (cells outside the mask left NaN) gives the gradients
+    of the dense dL/dcost bit for bit, with and without chunk skipping."""
+    B, N, M, D, gamma = case
+    X, Y = _inputs(B, N, M, D, 16)
+    dense, _ = _backward(X, Y, gamma, flagged=False)
+    dC, nzm, flags = _sparse_backward(X, Y, gamma)
+    want = _grad(X, Y, dense, None)
+    for env in (None, "1"):
+        if env is None:
+            monkeypatch.delenv("TW_GRAD_DENSE", raising=False)
+        else:
+            monkeypatch.setenv("TW_GRAD_DENSE", env)
+        dX, dY = torch.empty_like(X), torch.empty_like(Y)
+        nat.check(nat.lib().tw_sqeuclid_grad_sparse_f32(
+            nat.ptr(X), nat.ptr(Y), nat.ptr(nzm), nat.ptr(dC), nat.ptr(flags), B, N, M, D,
+            nat.ptr(dX), nat.ptr(dY), nat.stream_of(X)), "grad_sparse")
+        torch.cuda.synchronize()
+        assert torch.isfinite(dX).all() and torch.isfinite(dY).all()
+        assert torch.equal(dX, want[0])
+        assert torch.equal(dY, want[1])

@@ -42,6 +42,9 @@ SIGNATURES = {
     "tw_sdtw_chunk_flags_bytes": (_c_sz, [_c_i, _c_i, _c_i]),
     "tw_sdtw_backward_masked_flags_f32": (_c_i, [_c_p, _c_i, _c_i, _c_i, _c_d, _c_p, _c_sz, _c_p,
                                                  _c_p, _c_p, _c_sz, _c_p, _c_sz, _c_p]),
+    "tw_sdtw_nonzero_mask_bytes": (_c_sz, [_c_i, _c_i, _c_i]),
+    "tw_sdtw_backward_sparse_f32": (_c_i, [_c_p, _c_i, _c_i, _c_i, _c_d, _c_p, _c_sz, _c_p, _c_p,
+                                           _c_p, _c_p, _c_sz, _c_p, _c_sz, _c_p]),
     "tw_sdtw_features_workspace_bytes": (_c_sz, [_c_i, _c_i, _c_i, _c_i]),
     "tw_sdtw_features_backward_f32": (_c_i, [_c_p] * 4 + [_c_i] * 4 + [_c_d, _c_p, _c_sz, _c_p,
                                                                    _c_p, _c_p, _c_sz, _c_p]),
@@ -60,6 +63,7 @@ SIGNATURES = {
     "tw_sqeuclid_grad_f64": (_c_i, [_c_p, _c_p, _c_p, _c_p, _c_i, _c_i, _c_i, _c_i, _c_p, _c_p,
                                     _c_p]),
     "tw_sqeuclid_grad_flagged_f32": (_c_i, [_c_p] * 4 + [_c_i] * 4 + [_c_p, _c_p, _c_p]),
+    "tw_sqeuclid_grad_sparse_f32": (_c_i, [_c_p] * 5 + [_c_i] * 4 + [_c_p, _c_p, _c_p]),
     "tw_jeanie_forward_f32": (_c_i, [_c_p, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_d, _c_p,
                                      _c_p, _c_p]),
     "tw_jeanie_forward_f64": (_c_i, [_c_p, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_d, _c_p,

@@ -97,7 +97,8 @@ template <typename T>
 static int sdtw_bwd(const T* grad_r, const T* grad_p, int B, int N, int M, double gamma,
                     int has_pen, const void* saved, size_t saved_bytes, T* d_cost, T* d_pen,
                     void* ws, size_t ws_bytes, cudaStream_t st, const uint32_t* mask = nullptr,
-                    uint8_t* tf_rows = nullptr, uint8_t* tf_cols = nullptr) {
+                    uint8_t* tf_rows = nullptr, uint8_t* tf_cols = nullptr,
+                    uint8_t* nzm = nullptr) {
   g_err[0] = 0;
   if (int e = check_dims("tw_sdtw_backward", B, N, M)) return e;
   if (!(gamma > 0)) return set_error(kInvalid, "tw_sdtw_backward: gamma must be > 0");
@@ -130,6 +131,7 @@ static int sdtw_bwd(const T* grad_r, const T* grad_p, int B, int N, int M, doubl
   a.mask_np = (N + 3) & ~3;
   a.tf_rows = tf_rows;
   a.tf_cols = tf_cols;
+  a.nzm = nzm;
   {
     // TW_DP_ALL_BLOCKS=1: no shortcut for blocks whose adjoints are all zero
     const char* env = std::getenv("TW_DP_ALL_BLOCKS");
@@ -164,8 +166,8 @@ int sq_grad_f64(const double*, const double*, const uint32_t*, const double*, in
                 double*, double*, cudaStream_t);
 bool sq_grad_flagged_eligible(const float*, const float*, const float*, const float*,
                               const float*, int, int);
-int sq_grad_flagged_f32(const float*, const float*, const float*, int, int, int, int, float*,
-                        float*, const uint8_t*, const uint8_t*, cudaStream_t);
+int sq_grad_flagged_f32(const float*, const float*, const uint32_t*, const float*, int, int, int,
+                        int, float*, float*, const uint8_t*, const uint8_t*, cudaStream_t);
 
 template <typename T>
 int jeanie_forward(const T*, int, int, int, int, int, int, int, double, T*, T*, cudaStream_t);
@@ -334,21 +336,70 @@ int tw_sqeuclid_grad_flagged_f32(const float* X, const float* Y, const float* d_
     rows = flags;
     cols = flags + flag_layout(B, N, M).rows;
   }
-  return sq_grad_flagged_f32(X, Y, d_cost, B, N, M, D, dX, dY, rows, cols, (cudaStream_t)stream);
+  return sq_grad_flagged_f32(X, Y, nullptr, d_cost, B, N, M, D, dX, dY, rows, cols,
+                             (cudaStream_t)stream);
+}
+
+size_t tw_sdtw_nonzero_mask_bytes(int B, int N, int M) {
+  if (!dims_ok(B, N, M) || B == 0) return 0;
+  return (size_t)B * ((M + 31) / 32) * ((N + 3) & ~3) * 4;
+}
+
+int tw_sdtw_backward_sparse_f32(const float* grad_r, int B, int N, int M, double gamma,
+                                const void* saved, size_t saved_bytes, const uint32_t* mask,
+                                float* d_cost, uint32_t* nz_mask, uint8_t* flags,
+                                size_t flags_bytes, void* workspace, size_t ws_bytes,
+                                void* stream) {
+  g_err[0] = 0;
+  if (int e = check_dims("tw_sdtw_backward_sparse", B, N, M)) return e;
+  if (B == 0) return kOk;
+  if (!mask || !nz_mask || !flags)
+    return set_error(kInvalid, "tw_sdtw_backward_sparse: null mask, nz_mask or flags");
+  const FlagLayout f = flag_layout(B, N, M);
+  if (flags_bytes < f.rows + f.cols)
+    return set_error(kWorkspace, "tw_sdtw_backward_sparse: flags need %zu bytes", f.rows + f.cols);
+  cudaError_t e = cudaMemsetAsync(flags, 0, f.rows + f.cols, (cudaStream_t)stream);
+  if (e == cudaSuccess)
+    e = cudaMemsetAsync(nz_mask, 0, tw_sdtw_nonzero_mask_bytes(B, N, M), (cudaStream_t)stream);
+  if (e != cudaSuccess)
+    return set_error(kLaunch, "tw_sdtw_backward_sparse: %s", cudaGetErrorString(e));
+  return sdtw_bwd<float>(grad_r, nullptr, B, N, M, gamma, 0, saved, saved_bytes, d_cost, nullptr,
+                         workspace, ws_bytes, (cudaStream_t)stream, mask, flags, flags + f.rows,
+                         reinterpret_cast<uint8_t*>(nz_mask));
+}
+
+int tw_sqeuclid_grad_sparse_f32(const float* X, const float* Y, const uint32_t* nz_mask,
+                                const float* d_cost, const uint8_t* flags, int B, int N, int M,
+                                int D, float* dX, float* dY, void* stream) {
+  g_err[0] = 0;
+  if (B < 0 || N <= 0 || M <= 0 || D <= 0 ||
+      (B && (!X || !Y || !nz_mask || !d_cost || !flags || !dX || !dY)))
+    return set_error(kInvalid, "tw_sqeuclid_grad_sparse: invalid arguments");
+  const uint8_t* rows = nullptr;
+  const uint8_t* cols = nullptr;
+  if (B > 0 && !grad_dense()) {
+    rows = flags;
+    cols = flags + flag_layout(B, N, M).rows;
+  }
+  return sq_grad_flagged_f32(X, Y, nz_mask, d_cost, B, N, M, D, dX, dY, rows, cols,
+                             (cudaStream_t)stream);
 }
 
 // Workspace of tw_sdtw_features_backward_*: dL/dcost, the DP's delay lines
 // and (fp32) the chunk flags.
 struct FeatWs {
-  size_t dc, dp, fl;
-  size_t total() const { return dc + dp + fl; }
+  size_t dc, dp, fl, nz;
+  size_t total() const { return dc + dp + fl + nz; }
 };
 static FeatWs feat_ws(int B, int N, int M, int dtype_bytes) {
-  FeatWs w{0, 0, 0};
+  FeatWs w{0, 0, 0, 0};
   if (!dims_ok(B, N, M) || B == 0 || (dtype_bytes != 4 && dtype_bytes != 8)) return w;
   w.dc = align256((size_t)B * N * M * dtype_bytes);
   w.dp = tw_sdtw_workspace_bytes(B, N, M, dtype_bytes, 0);
-  if (dtype_bytes == 4) w.fl = tw_sdtw_chunk_flags_bytes(B, N, M);
+  if (dtype_bytes == 4) {
+    w.fl = tw_sdtw_chunk_flags_bytes(B, N, M);
+    w.nz = align256(tw_sdtw_nonzero_mask_bytes(B, N, M));
+  }
   return w;
 }
 
@@ -376,10 +427,11 @@ static int sdtw_feat_bwd(const T* X, const T* Y, const uint32_t* mask, const T* 
   void* dpws = base + w.dc;
   if constexpr (sizeof(T) == 4) {
     uint8_t* flags = reinterpret_cast<uint8_t*>(base + w.dc + w.dp);
-    if (int rc = tw_sdtw_backward_masked_flags_f32(grad_r, B, N, M, gamma, saved, saved_bytes,
-                                                   mask, dC, flags, w.fl, dpws, w.dp, st))
+    uint32_t* nzm = reinterpret_cast<uint32_t*>(base + w.dc + w.dp + w.fl);
+    if (int rc = tw_sdtw_backward_sparse_f32(grad_r, B, N, M, gamma, saved, saved_bytes, mask, dC,
+                                             nzm, flags, w.fl, dpws, w.dp, st))
       return rc;
-    return tw_sqeuclid_grad_flagged_f32(X, Y, dC, flags, B, N, M, D, dX, dY, st);
+    return tw_sqeuclid_grad_sparse_f32(X, Y, nzm, dC, flags, B, N, M, D, dX, dY, st);
   } else {
     if (int rc = sdtw_bwd<T>(grad_r, nullptr, B, N, M, gamma, 0, saved, saved_bytes, dC, nullptr,
                              dpws, w.dp, st, mask))

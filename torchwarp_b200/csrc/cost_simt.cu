@@ -301,13 +301,15 @@ bool sq_grad_flagged_eligible(const float* X, const float* Y, const float* dC, c
                               const float* dY, int M, int D) {
   return tc_grad_eligible(X, Y, dC, dC, nullptr, dX, dY, M, D);
 }
-int sq_grad_flagged_f32(const float* X, const float* Y, const float* dC, int B, int N, int M,
-                        int D, float* dX, float* dY, const uint8_t* tf_rows,
-                        const uint8_t* tf_cols, cudaStream_t st) {
+// mask: null (S = dC), or the mask of the cells of dC that hold S (the others
+// are 0 whatever dC holds there, e.g. dC written sparsely by the backward).
+int sq_grad_flagged_f32(const float* X, const float* Y, const uint32_t* mask, const float* dC,
+                        int B, int N, int M, int D, float* dX, float* dY,
+                        const uint8_t* tf_rows, const uint8_t* tf_cols, cudaStream_t st) {
   if (sq_grad_flagged_eligible(X, Y, dC, dX, dY, M, D))
-    return tc_sq_grad_f32(X, Y, nullptr, dC, B, N, M, D, dX, dY, st, tf_rows, tf_cols);
+    return tc_sq_grad_f32(X, Y, mask, dC, B, N, M, D, dX, dY, st, tf_rows, tf_cols);
   return grad_launch<float>(X, Y, nullptr, nullptr, nullptr, dC, nullptr, B, N, M, D, 0.0, 1e-8,
-                            dX, dY, nullptr, nullptr, st, nullptr);
+                            dX, dY, nullptr, nullptr, st, mask);
 }
 int sq_grad_f64(const double* X, const double* Y, const uint32_t* mask, const double* dC, int B,
                 int N, int M, int D, double* dX, double* dY, cudaStream_t st) {

@@ -658,17 +658,18 @@ __device__ __forceinline__ const uint32_t* mask_row(const uint32_t* mask, int np
 // Write this lane's row of flush tile c (8 stream columns) from the staging
 // ring to dC (natural layout), data columns only; `mode` and `off` come from
 // row_mode for the tile's pass.  With `masked`, columns whose bit in `word` is
-// clear are written as 0.  Returns true when a written value is nonzero.
+// clear are written as 0.  Returns nonzero when a written value is nonzero;
+// with `sparse`, the bit mask of the tile's nonzero values (bit e: column
+// j0 + e), and a whole tile of zeros is not written at all.
 template <typename T>
-__device__ __forceinline__ bool flush_row_tile(T* __restrict__ dst_base, const T* ring_row,
-                                               const Cursor& c, int mode, long long off,
-                                               const StreamPlan& p, int vec, bool masked,
-                                               uint32_t word) {
-  if (mode != 2 || c.j0 >= p.M) return false;
+__device__ __forceinline__ uint32_t flush_row_tile(T* __restrict__ dst_base, const T* ring_row,
+                                                   const Cursor& c, int mode, long long off,
+                                                   const StreamPlan& p, int vec, bool masked,
+                                                   uint32_t word, bool sparse) {
+  if (mode != 2 || c.j0 >= p.M) return 0u;
   const int j0 = c.j0;
   const T* src = ring_row + ((c.u * TILE) & (RING - 1));
   T* dst = dst_base + off + j0;
-  bool nz = false;
   if (vec && j0 + TILE <= p.M) {
     constexpr int PER = 16 / (int)sizeof(T);
     union {
@@ -686,38 +687,37 @@ __device__ __forceinline__ bool flush_row_tile(T* __restrict__ dst_base, const T
         for (int e = 0; e < PER; ++e) any |= u[h].v[e] != T(0) ? 1 : 0;
       }
     }
-    nz = sizeof(T) == 4 ? (any & 0x7fffffff) != 0 : any != 0;
+    const bool nz = sizeof(T) == 4 ? (any & 0x7fffffff) != 0 : any != 0;
+    uint32_t nzb = nz ? 1u : 0u;
     // An all-zero tile needs no mask, so it does not wait for the mask word
     // (loaded a block earlier; dead blocks are short).
-    if (masked && nz) {
-      const uint32_t mb = word >> (j0 & 31);
-      any = 0;
+    if (nz && (masked || sparse)) {
+      const uint32_t mb = masked ? word >> (j0 & 31) : 0xffu;
+      nzb = 0u;
 #pragma unroll
       for (int h = 0; h < TILE / PER; ++h) {
 #pragma unroll
-        for (int e = 0; e < PER; ++e)
+        for (int e = 0; e < PER; ++e) {
           if (!((mb >> (h * PER + e)) & 1u)) u[h].v[e] = T(0);
-        if constexpr (sizeof(T) == 4) {
-          any |= (u[h].i.x | u[h].i.y | u[h].i.z | u[h].i.w);
-        } else {
-#pragma unroll
-          for (int e = 0; e < PER; ++e) any |= u[h].v[e] != T(0) ? 1 : 0;
+          nzb |= (u[h].v[e] != T(0) ? 1u : 0u) << (h * PER + e);
         }
       }
-      nz = sizeof(T) == 4 ? (any & 0x7fffffff) != 0 : any != 0;
     }
+    if (!sparse || nzb != 0u) {
 #pragma unroll
-    for (int h = 0; h < TILE / PER; ++h) *reinterpret_cast<int4*>(dst + h * PER) = u[h].i;
-  } else {
-    const uint32_t bits = masked ? word >> (j0 & 31) : 0xffu;
-    const int n = min(TILE, p.M - j0);
-    for (int h = 0; h < n; ++h) {
-      const T v = ((bits >> h) & 1u) ? src[h] : T(0);
-      dst[h] = v;
-      nz = nz || v != T(0);
+      for (int h = 0; h < TILE / PER; ++h) *reinterpret_cast<int4*>(dst + h * PER) = u[h].i;
     }
+    return nzb;
   }
-  return nz;
+  const uint32_t bits = masked ? word >> (j0 & 31) : 0xffu;
+  const int n = min(TILE, p.M - j0);
+  uint32_t nzb = 0u;
+  for (int h = 0; h < n; ++h) {
+    const T v = ((bits >> h) & 1u) ? src[h] : T(0);
+    dst[h] = v;
+    nzb |= (v != T(0) ? 1u : 0u) << h;
+  }
+  return nzb;
 }
 
 template <typename T, int KS, bool HAS_P, bool SEEDB, bool GRP>
@@ -1066,18 +1066,24 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
     // ---- between blocks
 #pragma unroll
     for (int k = 0; k < KS; ++k) {
-      const bool nz = flush_row_tile<T>(a.dC, myC + k * 32 * S, fl[k], fmode[k], foff[k], p,
-                                        a.vec, masked, mwd[k]);
-      if (nz && a.tf_rows != nullptr) {
+      const uint32_t nzb = flush_row_tile<T>(a.dC, myC + k * 32 * S, fl[k], fmode[k], foff[k],
+                                             p, a.vec, masked, mwd[k], a.nzm != nullptr);
+      if (nzb != 0u && (a.tf_rows != nullptr || a.nzm != nullptr)) {
         // this lane's 8 columns lie in one 32-column and one 128-column block
         const int row = fl[k].band * 32 * KS + 32 * k + lane;
         const long long b = wi.p0 + fl[k].pq;
         const int j0 = fl[k].j0;
-        a.tf_rows[(b * ((p.N + 127) >> 7) + (row >> 7)) * a.tf_kr + (j0 >> 5)] = 1;
-        a.tf_cols[(b * ((p.M + 127) >> 7) + (j0 >> 7)) * a.tf_kc + (row >> 5)] = 1;
+        if (a.tf_rows != nullptr) {
+          a.tf_rows[(b * ((p.N + 127) >> 7) + (row >> 7)) * a.tf_kr + (j0 >> 5)] = 1;
+          a.tf_cols[(b * ((p.M + 127) >> 7) + (j0 >> 7)) * a.tf_kc + (row >> 5)] = 1;
+        }
+        if (a.nzm != nullptr)  // byte (j0 & 31) / 8 of word [b][j0 / 32][row]
+          a.nzm[((b * ((p.M + 31) >> 5) + (j0 >> 5)) * a.mask_np + row) * 4 + ((j0 & 31) >> 3)] =
+              (uint8_t)nzb;
       }
       if (HAS_P)
-        flush_row_tile<T>(a.dQ, myQ + k * 32 * S, fl[k], fmode[k], foff[k], p, a.vec, false, 0u);
+        flush_row_tile<T>(a.dQ, myQ + k * 32 * S, fl[k], fmode[k], foff[k], p, a.vec, false, 0u,
+                          false);
       const int oq = fl[k].q;
       cursor_prev<GRP>(fl[k], p);
       if (fl[k].q != oq) {  // a new pass

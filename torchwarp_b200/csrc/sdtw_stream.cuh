@@ -123,6 +123,11 @@ struct SdtwArgs {
   // backward: 1 = evaluate every block, also those whose adjoints are all
   // zero (for comparisons; the result is the same)
   int all_blocks = 0;
+  // Sparse dC (optional, with `mask`): 8-column tiles of a row that hold only
+  // zeros are not written, and nzm (uint32 words in the positivity mask's
+  // layout, zeroed by the caller) gets the bits of the nonzero values; cells
+  // whose bit is clear may hold anything.
+  uint8_t* nzm = nullptr;
   // scalars
   T kappa = 1;      // log2(e) / gamma
   T inv_kappa = 1;  // gamma * ln 2

@@ -1665,8 +1665,8 @@ int tc_qs_grad_f32(const float* Q, const float* Sp, const float* C, const float*
 
 // Squared-Euclidean chain rule with the positivity mask of the cost kernel in
 // place of the cost: S = dC where sq_raw > 0; with mask == nullptr, dC
-// already carries the mask (S = dC), and tf_rows / tf_cols (optional, with a
-// null mask only) are the DP backward's nonzero-chunk flags of dC:
+// already carries the mask (S = dC).  tf_rows / tf_cols (optional) are the DP
+// backward's nonzero-chunk flags of dC:
 // [B][ceil(N/128)][KR] and [B][ceil(M/128)][KC] bytes, KR = 16 ceil(ceil(M/32)/16),
 // KC = 16 ceil(ceil(N/32)/16); chunks flagged 0 are all zero and skipped.
 int tc_sq_grad_f32(const float* X, const float* Y, const uint32_t* mask, const float* dC, int B,
@@ -1683,10 +1683,10 @@ int tc_sq_grad_f32(const float* X, const float* Y, const uint32_t* mask, const f
                                             D, 0.0, 1e-8, dY, nullptr, st, nullptr, 0, tf_cols);
   }
   if ((rc = grad_side<0, false, true>(X, Y, nullptr, nullptr, nullptr, dC, nullptr, B, N, M, D,
-                                      0.0, 1e-8, dX, nullptr, st, mask)))
+                                      0.0, 1e-8, dX, nullptr, st, mask, 0, tf_rows)))
     return rc;
   return grad_side<1, false, true>(Y, X, nullptr, nullptr, nullptr, dC, nullptr, B, N, M, D, 0.0,
-                                   1e-8, dY, nullptr, st, mask);
+                                   1e-8, dY, nullptr, st, mask, 0, tf_cols);
 }
 
 }  // namespace tw

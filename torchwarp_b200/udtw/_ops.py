@@ -266,10 +266,12 @@ def sdtw_fused_backward(X: Tensor, Y: Tensor, mask: Tensor, saved: Tensor, grad_
                         gamma: float) -> Tuple[Tensor, Tensor]:
     """(dX, dY).  The DP backward writes dL/dcost with the cost's positivity
     mask applied (tw_sdtw_backward_masked), so the chain rule takes it as S
-    directly.  For fp32 the backward also flags the chunks of dL/dcost it
-    writes a nonzero value into, and the tensor-core chain rule reads only
-    those (tw_sdtw_backward_masked_flags_f32, tw_sqeuclid_grad_flagged_f32);
-    the composition is tw_sdtw_features_backward."""
+    directly.  For fp32 the backward writes it sparsely, only the 8-column
+    tiles that hold a nonzero value, with a bit mask of those values and
+    flags of the chunks that hold them, and the chain rule reads only the
+    flagged chunks and only the masked cells (tw_sdtw_backward_sparse_f32,
+    tw_sqeuclid_grad_sparse_f32); the composition is
+    tw_sdtw_features_backward."""
     nat.require_cuda(X, Y, grad_r)
     B, N, D = X.shape
     M = Y.shape[1]
@@ -286,15 +288,17 @@ def sdtw_fused_backward(X: Tensor, Y: Tensor, mask: Tensor, saved: Tensor, grad_
             if dtype == torch.float32:
                 fb = lib.tw_sdtw_chunk_flags_bytes(B, N, M)
                 flags = torch.empty(fb, dtype=torch.uint8, device=X.device)
-                nat.check(nat.call("sdtw_backward", lib.tw_sdtw_backward_masked_flags_f32,
+                nzm = torch.empty_like(mask)
+                nat.check(nat.call("sdtw_backward", lib.tw_sdtw_backward_sparse_f32,
                                    nat.ptr(grad_r), B, N, M, float(gamma), nat.ptr(saved),
-                                   saved.numel(), nat.ptr(mask), nat.ptr(s_cost), nat.ptr(flags),
-                                   fb, nat.ptr(ws), wb, nat.stream_of(X)),
-                          "tw_sdtw_backward_masked_flags")
-                nat.check(nat.call("udtw_features_grad", lib.tw_sqeuclid_grad_flagged_f32,
-                                   nat.ptr(X), nat.ptr(Y), nat.ptr(s_cost), nat.ptr(flags), B, N,
-                                   M, D, nat.ptr(dX), nat.ptr(dY), nat.stream_of(X)),
-                          "tw_sqeuclid_grad_flagged")
+                                   saved.numel(), nat.ptr(mask), nat.ptr(s_cost), nat.ptr(nzm),
+                                   nat.ptr(flags), fb, nat.ptr(ws), wb, nat.stream_of(X)),
+                          "tw_sdtw_backward_sparse")
+                nat.check(nat.call("udtw_features_grad", lib.tw_sqeuclid_grad_sparse_f32,
+                                   nat.ptr(X), nat.ptr(Y), nat.ptr(nzm), nat.ptr(s_cost),
+                                   nat.ptr(flags), B, N, M, D, nat.ptr(dX), nat.ptr(dY),
+                                   nat.stream_of(X)),
+                          "tw_sqeuclid_grad_sparse")
             else:
                 fn = getattr(lib, "tw_sdtw_backward_masked_" + nat.suffix(dtype))
                 nat.check(nat.call("sdtw_backward", fn, nat.ptr(grad_r), B, N, M, float(gamma),
