@@ -665,11 +665,26 @@ template <typename T>
 __device__ __forceinline__ uint32_t flush_row_tile(T* __restrict__ dst_base, const T* ring_row,
                                                    const Cursor& c, int mode, long long off,
                                                    const StreamPlan& p, int vec, bool masked,
-                                                   uint32_t word, bool sparse) {
+                                                   uint32_t word, bool sparse,
+                                                   bool known_zero) {
   if (mode != 2 || c.j0 >= p.M) return 0u;
   const int j0 = c.j0;
   const T* src = ring_row + ((c.u * TILE) & (RING - 1));
   T* dst = dst_base + off + j0;
+  if (known_zero) {  // every step of the tile was in a dead block
+    if (!sparse) {
+      if (vec && j0 + TILE <= p.M) {
+        constexpr int PER = 16 / (int)sizeof(T);
+#pragma unroll
+        for (int h = 0; h < TILE / PER; ++h)
+          *reinterpret_cast<int4*>(dst + h * PER) = make_int4(0, 0, 0, 0);
+      } else {
+        const int n = min(TILE, p.M - j0);
+        for (int h = 0; h < n; ++h) dst[h] = T(0);
+      }
+    }
+    return 0u;
+  }
   if (vec && j0 + TILE <= p.M) {
     constexpr int PER = 16 / (int)sizeof(T);
     union {
@@ -882,6 +897,9 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
   // Xc through, or deferring that consumption, measured slower: every dead
   // block then waits on a DRAM load issued one short block earlier.)
   bool stale = false;
+  // liveness of the block just run and of the one before it (the start
+  // counts as live, so the first tiles are flushed from the ring)
+  bool cur_live = true, prev_live = true;
   auto run_block = [&](const int t0, T (&Fc)[TILE][KS], T (&FPc)[TILE][KS], T (&Fn)[TILE][KS],
                        T (&FPn)[TILE][KS]) {
     const int s_inj = (!SEEDB && cap_t >= t0 && cap_t < t0 + TILE) ? cap_t - t0 : -1;
@@ -920,7 +938,8 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
         l2 = l2 || sdn[s] != T(0);
         if (HAS_P) l2 = l2 || sdpn[s] != T(0);
       }
-      if (__any_sync(0xffffffffu, l2)) {
+      const bool nxt_live = __any_sync(0xffffffffu, l2);
+      if (nxt_live) {
         // the next block is live: its rows, and in cur the saved row it
         // starts from (t0 - 2, this block's first row)
 #pragma unroll
@@ -931,22 +950,30 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
         load_saved_row<T, KS>(sRl, t0 - 2, cur);
         if (HAS_P) load_saved_row<T, KS>(sPl, t0 - 2, Pcur);
       }
+      // zeros in the ring only where a flushed tile also holds cells of a
+      // live block: the tiles flushed after this block and after the next
+      // one share their steps with the block before and the block after
+      const bool stage = prev_live || nxt_live;
 #pragma unroll
       for (int s = 0; s < TILE; ++s) {
-        const int ia = (t0 + s - lane) & (RING - 1);
+        if (stage) {
+          const int ia = (t0 + s - lane) & (RING - 1);
 #pragma unroll
-        for (int k = 0; k < KS; ++k) {
-          myC[k * 32 * S + ia] = T(0);
-          if (HAS_P) myQ[k * 32 * S + ia] = T(0);
+          for (int k = 0; k < KS; ++k) {
+            myC[k * 32 * S + ia] = T(0);
+            if (HAS_P) myQ[k * 32 * S + ia] = T(0);
+          }
         }
         if (lane == 0) {
           coll8[s] = T(0);
           if (HAS_P) coll8[32 + s] = T(0);
         }
       }
+      cur_live = false;
       stale = true;
       return;
     }
+    cur_live = true;
     if (stale) {
       // after dead blocks: cur holds saved row t0 + 6, loaded by the block
       // before; Xc = X(t0 + 7) with the row -1 value of column t0 + 7 (in
@@ -1062,12 +1089,17 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
   // Work between block t0 and block t0 - 8.
   auto between = [&](const int t0) {
     const bool seedhere = !SEEDB && cap_t >= t0 && cap_t < t0 + TILE;
+    // the tiles flushed here have their cells in this block and the one
+    // before it; when both were dead they are zero and the ring is not read
+    const bool zero_tiles = !cur_live && !prev_live;
+    prev_live = cur_live;
 
     // ---- between blocks
 #pragma unroll
     for (int k = 0; k < KS; ++k) {
       const uint32_t nzb = flush_row_tile<T>(a.dC, myC + k * 32 * S, fl[k], fmode[k], foff[k],
-                                             p, a.vec, masked, mwd[k], a.nzm != nullptr);
+                                             p, a.vec, masked, mwd[k], a.nzm != nullptr,
+                                             zero_tiles);
       if (nzb != 0u && (a.tf_rows != nullptr || a.nzm != nullptr)) {
         // this lane's 8 columns lie in one 32-column and one 128-column block
         const int row = fl[k].band * 32 * KS + 32 * k + lane;
@@ -1083,7 +1115,7 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
       }
       if (HAS_P)
         flush_row_tile<T>(a.dQ, myQ + k * 32 * S, fl[k], fmode[k], foff[k], p, a.vec, false, 0u,
-                          false);
+                          false, zero_tiles);
       const int oq = fl[k].q;
       cursor_prev<GRP>(fl[k], p);
       if (fl[k].q != oq) {  // a new pass
