@@ -65,10 +65,10 @@ ALGO_BYTES_PER_CELL = 8      # soft-DTW fwd+bwd: cost read + cost-gradient write
 CALLS = {
     "udtw_cost": (1, 4, 3.91),           # C write + mask
     "sdtw_forward": (1, 4, 8.06),        # C read + saved R' write + edge stream
-    "sdtw_backward": (1, 4, 4.59),       # masked dC write + the saved rows of the blocks
-                                         # next to the alignment corridor + mask + edge
-    "udtw_features_grad": (2, 4, 1.15),  # the chunks of dC the backward flagged nonzero and
-                                         # their features (dense: 5.95)
+    "sdtw_backward": (1, 4, 0.79),       # the saved rows and the dC tiles (with the bit
+                                         # mask) next to the alignment corridor, mask, edge
+    "udtw_features_grad": (2, 4, 1.18),  # the chunks of dC the backward flagged nonzero, their
+                                         # mask words and features (dense: 5.95)
 }
 
 
