@@ -900,13 +900,17 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
   // liveness of the block just run and of the one before it (the start
   // counts as live, so the first tiles are flushed from the ring)
   bool cur_live = true, prev_live = true;
+  // the next block is proved dead (set by a dead block)
+  bool next_dead = false;
   auto run_block = [&](const int t0, T (&Fc)[TILE][KS], T (&FPc)[TILE][KS], T (&Fn)[TILE][KS],
                        T (&FPn)[TILE][KS]) {
     const int s_inj = (!SEEDB && cap_t >= t0 && cap_t < t0 + TILE) ? cap_t - t0 : -1;
     T* coll8 = coll + (t0 & 24);  // slot of step t0 + s is coll8[s]
     // adjoints arriving at the bottom row from the band below (column t - 32 KS)
     T dvs[TILE], dvqs[TILE];
-    {
+    // a block that the dead block before it proved dead needs no test
+    bool blk_live = false;
+    if (!next_dead) {
       const T* sdb = sd + ((t0 - 32 * KS) & 63);
       const T* sdpb = sdp + ((t0 - 32 * KS) & 63);
 #pragma unroll
@@ -914,19 +918,20 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
         dvs[s] = sdb[s];
         if (HAS_P) dvqs[s] = sdpb[s];
       }
-    }
-    bool live = a.all_blocks != 0 || (!SEEDB && s_inj >= 0);
+      bool live = a.all_blocks != 0 || (!SEEDB && s_inj >= 0);
 #pragma unroll
-    for (int k = 0; k < KS; ++k) {
-      live = live || accL[k] != T(0) || accB[k] != T(0) || dgp[k] != T(0);
-      if (HAS_P) live = live || Qacc[k] != T(0) || QaccB[k] != T(0) || dgq[k] != T(0);
-    }
+      for (int k = 0; k < KS; ++k) {
+        live = live || accL[k] != T(0) || accB[k] != T(0) || dgp[k] != T(0);
+        if (HAS_P) live = live || Qacc[k] != T(0) || QaccB[k] != T(0) || dgq[k] != T(0);
+      }
 #pragma unroll
-    for (int s = 0; s < TILE; ++s) {
-      live = live || dvs[s] != T(0);
-      if (HAS_P) live = live || dvqs[s] != T(0);
+      for (int s = 0; s < TILE; ++s) {
+        live = live || dvs[s] != T(0);
+        if (HAS_P) live = live || dvqs[s] != T(0);
+      }
+      blk_live = __any_sync(0xffffffffu, live);
     }
-    if (!__any_sync(0xffffffffu, live)) {
+    if (!blk_live) {
       // The next block is as surely dead when no seed enters it and the
       // adjoints it receives from below (already in shared memory: a window
       // is stored at least one block before this test reads it) are zero.
@@ -939,6 +944,7 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
         if (HAS_P) l2 = l2 || sdpn[s] != T(0);
       }
       const bool nxt_live = __any_sync(0xffffffffu, l2);
+      next_dead = !nxt_live;
       if (nxt_live) {
         // the next block is live: its rows, and in cur the saved row it
         // starts from (t0 - 2, this block's first row)
@@ -974,6 +980,7 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
       return;
     }
     cur_live = true;
+    next_dead = false;
     if (stale) {
       // after dead blocks: cur holds saved row t0 + 6, loaded by the block
       // before; Xc = X(t0 + 7) with the row -1 value of column t0 + 7 (in
@@ -1122,7 +1129,9 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
         fmode[k] = row_mode<KS>(fl[k], k, p, wi, foff[k]);
         if (masked) mrow[k] = mask_row<KS>(a.mask, a.mask_np, fl[k], k, p, wi);
       }
-      if (masked) mwd[k] = mrow[k][min(fl[k].j0 >> 5, mwl) * a.mask_np];
+      // the word is for the next flush; when the next block is proved dead
+      // that flush reads nothing (this block is dead too)
+      if (masked && !next_dead) mwd[k] = mrow[k][min(fl[k].j0 >> 5, mwl) * a.mask_np];
     }
     if (seedhere) {
       --cap_i;
