@@ -902,6 +902,9 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
   bool cur_live = true, prev_live = true;
   // the next block is proved dead (set by a dead block)
   bool next_dead = false;
+  // window zw_idx of adjoints from below holds a nonzero value (zw_any)
+  int zw_idx = INT_MIN;
+  bool zw_any = true;
   auto run_block = [&](const int t0, T (&Fc)[TILE][KS], T (&FPc)[TILE][KS], T (&Fn)[TILE][KS],
                        T (&FPn)[TILE][KS]) {
     const int s_inj = (!SEEDB && cap_t >= t0 && cap_t < t0 + TILE) ? cap_t - t0 : -1;
@@ -935,15 +938,17 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
       // The next block is as surely dead when no seed enters it and the
       // adjoints it receives from below (already in shared memory: a window
       // is stored at least one block before this test reads it) are zero.
-      bool l2 = !SEEDB && cap_t >= t0 - TILE && cap_t < t0;
-      const T* sdn = sd + ((t0 - TILE - 32 * KS) & 63);
-      const T* sdpn = sdp + ((t0 - TILE - 32 * KS) & 63);
-#pragma unroll
-      for (int s = 0; s < TILE; ++s) {
-        l2 = l2 || sdn[s] != T(0);
-        if (HAS_P) l2 = l2 || sdpn[s] != T(0);
+      // The test reads the 32-column window of the next block's adjoints
+      // from below once (lane l its column l) and keeps the answer for the
+      // window's four blocks.
+      const int wn = (t0 - TILE - 32 * KS) >> 5;
+      if (wn != zw_idx) {
+        const int c = (32 * wn + lane) & 63;
+        const bool nzw = sd[c] != T(0) || (HAS_P && sdp[c] != T(0));
+        zw_any = __any_sync(0xffffffffu, nzw);
+        zw_idx = wn;
       }
-      const bool nxt_live = __any_sync(0xffffffffu, l2);
+      const bool nxt_live = zw_any || (!SEEDB && cap_t >= t0 - TILE && cap_t < t0);
       next_dead = !nxt_live;
       if (nxt_live) {
         // the next block is live: its rows, and in cur the saved row it
