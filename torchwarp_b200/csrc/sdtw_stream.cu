@@ -975,9 +975,13 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
             if (HAS_P) myQ[k * 32 * S + ia] = T(0);
           }
         }
-        if (lane == 0) {
-          coll8[s] = T(0);
-          if (HAS_P) coll8[32 + s] = T(0);
+      }
+      if (lane == 0) {  // zero top-row sends: 16-byte stores (coll8 is 32-byte aligned)
+        constexpr int PER = 16 / (int)sizeof(T);
+#pragma unroll
+        for (int h = 0; h < TILE / PER; ++h) {
+          reinterpret_cast<int4*>(coll8)[h] = make_int4(0, 0, 0, 0);
+          if (HAS_P) reinterpret_cast<int4*>(coll8 + 32)[h] = make_int4(0, 0, 0, 0);
         }
       }
       cur_live = false;
@@ -1152,10 +1156,10 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
       }
     }
     // Window refills are loaded from global memory at the end of one block
-    // and stored to shared memory two blocks later, so no warp waits for the
-    // load even when the blocks between are dead (short); the slots they fill
-    // are first read four blocks after the load (by the dead-block test of
-    // the next block's adjoints from below: three).
+    // and stored to shared memory three blocks later, so no warp waits for
+    // the load even when the blocks between are dead (short); the slots they
+    // fill are first read four blocks after the load (by the dead-block test
+    // of the next block's adjoints from below, at the start of the fourth).
     if (pend_b > 0 && --pend_b == 0) {
       __syncwarp();
       sb[pbc & 63] = pbv;
@@ -1192,7 +1196,7 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
       pbc = t0 - 64 + lane;
       pbv = row_above_saved<T, KS, GRP>(eRa, pbc, p, wi, big);
       if (HAS_P) pbpv = row_above_saved<T, KS, GRP>(ePa, pbc, p, wi, T(0));
-      pend_b = 2;
+      pend_b = 3;
     }
     // the next block (t0 - 8) may open a new window of bottom-row columns
     const int dwn = (t0 - TILE - 32 * KS) >> 5;
@@ -1201,7 +1205,7 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
       pdc = 32 * (dw - 1) + lane;
       pdv = push_from_below<T, SEEDB, GRP>(dlRb, pdc, p, wi, a.grad_r);
       if (HAS_P) pdpv = push_from_below<T, SEEDB, GRP>(dlPb, pdc, p, wi, a.grad_p);
-      pend_d = 2;
+      pend_d = 3;
     }
   };
 
