@@ -106,6 +106,16 @@ int tw_sdtw_backward_f64(const double* grad_r, const double* grad_p, int B, int 
                          double* d_cost, double* d_penalty, void* workspace, size_t ws_bytes,
                          void* stream);
 
+/* tw_sdtw_backward_f32 that also flags, in `flags` (layout of
+ * tw_sdtw_backward_masked_flags_f32, zeroed here; NULL: none), the chunks
+ * where d_cost or d_penalty holds a nonzero value, for
+ * tw_udtw_features_grad_flagged_f32. */
+int tw_sdtw_backward_flags_f32(const float* grad_r, const float* grad_p, int B, int N, int M,
+                               double gamma, int has_penalty, const void* saved,
+                               size_t saved_bytes, float* d_cost, float* d_penalty,
+                               uint8_t* flags, size_t flags_bytes, void* workspace,
+                               size_t ws_bytes, void* stream);
+
 /* soft-DTW backward that also applies the positivity mask of
  * tw_sqeuclid_cost_* (no penalty): writes d_cost[b,i,j] = dL/dcost[b,i,j] where
  * the mask bit of (b,i,j) is set, else 0 -- the S operand of the squared-
@@ -201,6 +211,15 @@ int tw_udtw_features_grad_f64(const double* X, const double* Y, const double* vx
                               const double* d_penalty, int B, int N, int M, int D, double beta,
                               double eps, double* dX, double* dY, double* dvx, double* dvy,
                               void* stream);
+/* tw_udtw_features_grad_f32 given the chunk flags of tw_sdtw_backward_flags_f32
+ * (NULL: none): on the tensor-core path it reads only the chunks where d_cost
+ * or d_penalty is nonzero; the others add exactly zero to every output.
+ * TW_GRAD_DENSE=1 reads every chunk. */
+int tw_udtw_features_grad_flagged_f32(const float* X, const float* Y, const float* vx,
+                                      const float* vy, const float* cost, const float* d_cost,
+                                      const float* d_penalty, const uint8_t* flags, int B, int N,
+                                      int M, int D, double beta, double eps, float* dX, float* dY,
+                                      float* dvx, float* dvy, void* stream);
 
 /* ---------------------------------------------------------------------
  * soft-DTW's squared-Euclidean cost with a positivity mask in place of the

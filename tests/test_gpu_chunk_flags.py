@@ -321,3 +321,72 @@ def test_sparse_chain_rule_equals_dense(case, monkeypatch):
         assert torch.isfinite(dX).all() and torch.isfinite(dY).all()
         assert torch.equal(dX, want[0])
         assert torch.equal(dY, want[1])
+
+
+UDTW_CASES = [  # B, N, M, D, gamma
+    (3, 256, 256, 64, 0.01),
+    (2, 200, 300, 64, 0.05),
+    (2, 160, 192, 64, 1.0),
+    (2, 130, 140, 128, 0.01),
+    (1, 70, 45, 8, 0.01),      # SIMT chain rule (flags ignored)
+]
+
+
+@pytest.mark.parametrize("case", UDTW_CASES)
+def test_udtw_flagged_backward_and_chain_rule_equal_dense(case, monkeypatch):
+    """uDTW on features: tw_sdtw_backward_flags_f32 flags the chunks where dL/dcost or
+    dL/dpenalty is nonzero, and tw_udtw_features_grad_flagged_f32 gives the dense
+    chain rule's dX, dY, dvx, dvy bit for bit."""
+    lib = nat.lib()
+    B, N, M, D, gamma = case
+    X, Y = _inputs(B, N, M, D, 17)
+    g = torch.Generator(device="cuda").manual_seed(18)
+    vx = 0.25 + torch.rand(B, N, device="cuda", generator=g)
+    vy = 0.25 + torch.rand(B, M, device="cuda", generator=g)
+    beta, eps = 0.7, 1e-8
+    C = torch.empty(B, N, M, device="cuda")
+    Q = torch.empty(B, N, M, device="cuda")
+    st = nat.stream_of(X)
+    nat.check(lib.tw_udtw_cost_f32(nat.ptr(X), nat.ptr(Y), nat.ptr(vx), nat.ptr(vy), B, N, M, D,
+                                   beta, eps, nat.ptr(C), nat.ptr(Q), st), "cost")
+    sb = lib.tw_sdtw_saved_bytes(B, N, M, 4, 1)
+    wb = lib.tw_sdtw_workspace_bytes(B, N, M, 4, 1)
+    saved = torch.empty(sb, dtype=torch.uint8, device="cuda")
+    ws = torch.empty(wb, dtype=torch.uint8, device="cuda")
+    out_r, out_p = torch.empty(B, device="cuda"), torch.empty(B, device="cuda")
+    nat.check(lib.tw_sdtw_forward_f32(nat.ptr(C), nat.ptr(Q), B, N, M, float(gamma), 0.0,
+                                      nat.ptr(out_r), nat.ptr(out_p), nat.ptr(saved), sb,
+                                      nat.ptr(ws), wb, st), "forward")
+    gr = torch.linspace(0.5, 1.5, B, device="cuda")
+    gp = torch.linspace(1.0, 2.0, B, device="cuda")
+    dC0, dQ0 = torch.empty_like(C), torch.empty_like(C)
+    nat.check(lib.tw_sdtw_backward_f32(nat.ptr(gr), nat.ptr(gp), B, N, M, float(gamma), 1,
+                                       nat.ptr(saved), sb, nat.ptr(dC0), nat.ptr(dQ0),
+                                       nat.ptr(ws), wb, st), "backward")
+    dC, dQ = torch.empty_like(C), torch.empty_like(C)
+    fb = lib.tw_sdtw_chunk_flags_bytes(B, N, M)
+    flags = torch.full((fb,), 7, dtype=torch.uint8, device="cuda")
+    nat.check(lib.tw_sdtw_backward_flags_f32(nat.ptr(gr), nat.ptr(gp), B, N, M, float(gamma), 1,
+                                             nat.ptr(saved), sb, nat.ptr(dC), nat.ptr(dQ),
+                                             nat.ptr(flags), fb, nat.ptr(ws), wb, st),
+              "backward_flags")
+    torch.cuda.synchronize()
+    assert torch.equal(dC, dC0) and torch.equal(dQ, dQ0)
+    np.testing.assert_array_equal(flags.cpu().numpy(), _flags_ref((dC0 != 0) | (dQ0 != 0)))
+
+    def grads(flagged):
+        outs = [torch.empty_like(X), torch.empty_like(Y), torch.zeros_like(vx),
+                torch.zeros_like(vy)]
+        args = [nat.ptr(X), nat.ptr(Y), nat.ptr(vx), nat.ptr(vy), nat.ptr(C), nat.ptr(dC),
+                nat.ptr(dQ)]
+        tail = [B, N, M, D, beta, eps] + [nat.ptr(o) for o in outs] + [st]
+        if flagged:
+            nat.check(lib.tw_udtw_features_grad_flagged_f32(*args, nat.ptr(flags), *tail), "fl")
+        else:
+            nat.check(lib.tw_udtw_features_grad_f32(*args, *tail), "dense")
+        torch.cuda.synchronize()
+        return outs
+
+    monkeypatch.delenv("TW_GRAD_DENSE", raising=False)
+    for a, b in zip(grads(True), grads(False)):
+        assert torch.equal(a, b)

@@ -43,6 +43,10 @@ SIGNATURES = {
     "tw_sdtw_backward_masked_flags_f32": (_c_i, [_c_p, _c_i, _c_i, _c_i, _c_d, _c_p, _c_sz, _c_p,
                                                  _c_p, _c_p, _c_sz, _c_p, _c_sz, _c_p]),
     "tw_sdtw_nonzero_mask_bytes": (_c_sz, [_c_i, _c_i, _c_i]),
+    "tw_sdtw_backward_flags_f32": (_c_i, [_c_p, _c_p, _c_i, _c_i, _c_i, _c_d, _c_i, _c_p, _c_sz,
+                                          _c_p, _c_p, _c_p, _c_sz, _c_p, _c_sz, _c_p]),
+    "tw_udtw_features_grad_flagged_f32": (_c_i, [_c_p] * 8 + [_c_i] * 4 + [_c_d, _c_d]
+                                          + [_c_p] * 5),
     "tw_sdtw_backward_sparse_f32": (_c_i, [_c_p, _c_i, _c_i, _c_i, _c_d, _c_p, _c_sz, _c_p, _c_p,
                                            _c_p, _c_p, _c_sz, _c_p, _c_sz, _c_p]),
     "tw_sdtw_features_workspace_bytes": (_c_sz, [_c_i, _c_i, _c_i, _c_i]),

@@ -153,7 +153,8 @@ int udtw_cost_f64(const double*, const double*, const double*, const double*, in
                   double, double, double*, double*, cudaStream_t);
 int udtw_grad_f32(const float*, const float*, const float*, const float*, const float*,
                   const float*, const float*, int, int, int, int, double, double, float*, float*,
-                  float*, float*, cudaStream_t);
+                  float*, float*, cudaStream_t, const uint8_t* = nullptr,
+                  const uint8_t* = nullptr);
 int udtw_grad_f64(const double*, const double*, const double*, const double*, const double*,
                   const double*, const double*, int, int, int, int, double, double, double*,
                   double*, double*, double*, cudaStream_t);
@@ -338,6 +339,48 @@ int tw_sqeuclid_grad_flagged_f32(const float* X, const float* Y, const float* d_
   }
   return sq_grad_flagged_f32(X, Y, nullptr, d_cost, B, N, M, D, dX, dY, rows, cols,
                              (cudaStream_t)stream);
+}
+
+int tw_sdtw_backward_flags_f32(const float* grad_r, const float* grad_p, int B, int N, int M,
+                               double gamma, int has_penalty, const void* saved,
+                               size_t saved_bytes, float* d_cost, float* d_penalty,
+                               uint8_t* flags, size_t flags_bytes, void* workspace,
+                               size_t ws_bytes, void* stream) {
+  uint8_t* rows = nullptr;
+  uint8_t* cols = nullptr;
+  if (B > 0 && dims_ok(B, N, M) && flags != nullptr) {
+    const FlagLayout f = flag_layout(B, N, M);
+    if (flags_bytes < f.rows + f.cols)
+      return set_error(kWorkspace, "tw_sdtw_backward_flags: flags need %zu bytes",
+                       f.rows + f.cols);
+    const cudaError_t e = cudaMemsetAsync(flags, 0, f.rows + f.cols, (cudaStream_t)stream);
+    if (e != cudaSuccess)
+      return set_error(kLaunch, "tw_sdtw_backward_flags: %s", cudaGetErrorString(e));
+    rows = flags;
+    cols = flags + f.rows;
+  }
+  return sdtw_bwd<float>(grad_r, grad_p, B, N, M, gamma, has_penalty, saved, saved_bytes, d_cost,
+                         d_penalty, workspace, ws_bytes, (cudaStream_t)stream, nullptr, rows,
+                         cols);
+}
+
+int tw_udtw_features_grad_flagged_f32(const float* X, const float* Y, const float* vx,
+                                      const float* vy, const float* cost, const float* d_cost,
+                                      const float* d_penalty, const uint8_t* flags, int B, int N,
+                                      int M, int D, double beta, double eps, float* dX, float* dY,
+                                      float* dvx, float* dvy, void* stream) {
+  g_err[0] = 0;
+  if (B < 0 || N <= 0 || M <= 0 || D <= 0 || !X || !Y || !cost || !d_cost || !dX || !dY ||
+      ((vx == nullptr) != (vy == nullptr)))
+    return set_error(kInvalid, "tw_udtw_features_grad_flagged: invalid arguments");
+  const uint8_t* rows = nullptr;
+  const uint8_t* cols = nullptr;
+  if (B > 0 && flags != nullptr && !grad_dense()) {
+    rows = flags;
+    cols = flags + flag_layout(B, N, M).rows;
+  }
+  return udtw_grad_f32(X, Y, vx, vy, cost, d_cost, d_penalty, B, N, M, D, beta, eps, dX, dY, dvx,
+                       dvy, (cudaStream_t)stream, rows, cols);
 }
 
 size_t tw_sdtw_nonzero_mask_bytes(int B, int N, int M) {

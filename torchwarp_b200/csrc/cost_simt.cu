@@ -247,7 +247,8 @@ bool tc_grad_eligible(const float* X, const float* Y, const float* C, const floa
                       const float* dQ, const float* dX, const float* dY, int M, int D);
 int tc_grad_f32(const float* X, const float* Y, const float* vx, const float* vy, const float* C,
                 const float* dC, const float* dQ, int B, int N, int M, int D, double beta,
-                double eps, float* dX, float* dY, float* dvx, float* dvy, cudaStream_t st);
+                double eps, float* dX, float* dY, float* dvx, float* dvy, cudaStream_t st,
+                const uint8_t* tf_rows = nullptr, const uint8_t* tf_cols = nullptr);
 
 int udtw_cost_f32(const float* X, const float* Y, const float* vx, const float* vy, int B, int N,
                   int M, int D, double beta, double eps, float* C, float* Q, cudaStream_t st) {
@@ -262,9 +263,11 @@ int udtw_cost_f64(const double* X, const double* Y, const double* vx, const doub
 }
 int udtw_grad_f32(const float* X, const float* Y, const float* vx, const float* vy, const float* C,
                   const float* dC, const float* dQ, int B, int N, int M, int D, double beta,
-                  double eps, float* dX, float* dY, float* dvx, float* dvy, cudaStream_t st) {
+                  double eps, float* dX, float* dY, float* dvx, float* dvy, cudaStream_t st,
+                  const uint8_t* tf_rows, const uint8_t* tf_cols) {
   if (tc_grad_eligible(X, Y, C, dC, dQ, dX, dY, M, D))
-    return tc_grad_f32(X, Y, vx, vy, C, dC, dQ, B, N, M, D, beta, eps, dX, dY, dvx, dvy, st);
+    return tc_grad_f32(X, Y, vx, vy, C, dC, dQ, B, N, M, D, beta, eps, dX, dY, dvx, dvy, st,
+                       tf_rows, tf_cols);
   return grad_launch(X, Y, vx, vy, C, dC, dQ, B, N, M, D, beta, eps, dX, dY, dvx, dvy, st);
 }
 int udtw_grad_f64(const double* X, const double* Y, const double* vx, const double* vy,

@@ -1116,7 +1116,12 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
       const uint32_t nzb = flush_row_tile<T>(a.dC, myC + k * 32 * S, fl[k], fmode[k], foff[k],
                                              p, a.vec, masked, mwd[k], a.nzm != nullptr,
                                              zero_tiles);
-      if (nzb != 0u && (a.tf_rows != nullptr || a.nzm != nullptr)) {
+      // a chunk is flagged where dC or (uDTW) dQ holds a nonzero value
+      uint32_t nzf = nzb;
+      if (HAS_P)
+        nzf |= flush_row_tile<T>(a.dQ, myQ + k * 32 * S, fl[k], fmode[k], foff[k], p, a.vec, false,
+                                 0u, false, zero_tiles);
+      if (nzf != 0u && (a.tf_rows != nullptr || a.nzm != nullptr)) {
         // this lane's 8 columns lie in one 32-column and one 128-column block
         const int row = fl[k].band * 32 * KS + 32 * k + lane;
         const long long b = wi.p0 + fl[k].pq;
@@ -1125,13 +1130,10 @@ __global__ void __launch_bounds__(128) sdtw_bwd_kernel(const SdtwArgs<T> a) {
           a.tf_rows[(b * ((p.N + 127) >> 7) + (row >> 7)) * a.tf_kr + (j0 >> 5)] = 1;
           a.tf_cols[(b * ((p.M + 127) >> 7) + (j0 >> 7)) * a.tf_kc + (row >> 5)] = 1;
         }
-        if (a.nzm != nullptr)  // byte (j0 & 31) / 8 of word [b][j0 / 32][row]
+        if (a.nzm != nullptr && nzb != 0u)  // byte (j0 & 31) / 8 of word [b][j0 / 32][row]
           a.nzm[((b * ((p.M + 31) >> 5) + (j0 >> 5)) * a.mask_np + row) * 4 + ((j0 & 31) >> 3)] =
               (uint8_t)nzb;
       }
-      if (HAS_P)
-        flush_row_tile<T>(a.dQ, myQ + k * 32 * S, fl[k], fmode[k], foff[k], p, a.vec, false, 0u,
-                          false, zero_tiles);
       const int oq = fl[k].q;
       cursor_prev<GRP>(fl[k], p);
       if (fl[k].q != oq) {  // a new pass

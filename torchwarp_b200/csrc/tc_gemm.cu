@@ -1633,21 +1633,25 @@ bool tc_grad_eligible(const float* X, const float* Y, const float* C, const floa
          aligned16(dX) && aligned16(dY);
 }
 
+// tf_rows / tf_cols: optional chunk flags of dC and dQ (see tc_sq_grad_f32).
 int tc_grad_f32(const float* X, const float* Y, const float* vx, const float* vy, const float* C,
                 const float* dC, const float* dQ, int B, int N, int M, int D, double beta,
-                double eps, float* dX, float* dY, float* dvx, float* dvy, cudaStream_t st) {
+                double eps, float* dX, float* dY, float* dvx, float* dvy, cudaStream_t st,
+                const uint8_t* tf_rows, const uint8_t* tf_cols) {
   if (B == 0 || N == 0 || M == 0) return kOk;
   int rc;
   if (vx != nullptr) {
-    if ((rc = grad_side<0, true>(X, Y, vx, vy, C, dC, dQ, B, N, M, D, beta, eps, dX, dvx, st)))
+    if ((rc = grad_side<0, true>(X, Y, vx, vy, C, dC, dQ, B, N, M, D, beta, eps, dX, dvx, st,
+                                 nullptr, 0, tf_rows)))
       return rc;
-    return grad_side<1, true>(Y, X, vy, vx, C, dC, dQ, B, N, M, D, beta, eps, dY, dvy, st);
+    return grad_side<1, true>(Y, X, vy, vx, C, dC, dQ, B, N, M, D, beta, eps, dY, dvy, st,
+                              nullptr, 0, tf_cols);
   }
   if ((rc = grad_side<0, false>(X, Y, nullptr, nullptr, C, dC, nullptr, B, N, M, D, beta, eps, dX,
-                                nullptr, st)))
+                                nullptr, st, nullptr, 0, tf_rows)))
     return rc;
   return grad_side<1, false>(Y, X, nullptr, nullptr, C, dC, nullptr, B, N, M, D, beta, eps, dY,
-                             nullptr, st);
+                             nullptr, st, nullptr, 0, tf_cols);
 }
 
 // Chain rule of a query/support cost built by tc_cost_f32 (no variance):

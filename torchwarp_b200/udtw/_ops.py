@@ -117,6 +117,28 @@ def _dp_backward(saved, grad_r, grad_p, N, M, gamma, has_p):
     return d_cost, d_pen
 
 
+def _dp_backward_flagged(saved, grad_r, grad_p, N, M, gamma, has_p):
+    """fp32 _dp_backward through tw_sdtw_backward_flags_f32: also the chunk
+    flags of d_cost / d_penalty for tw_udtw_features_grad_flagged_f32."""
+    B = grad_r.shape[0]
+    d_cost = grad_r.new_empty(B, N, M)
+    d_pen = grad_r.new_empty(B, N, M) if has_p else grad_r.new_empty(0)
+    grad_r = grad_r.contiguous()
+    grad_p = grad_p.to(grad_r.dtype).contiguous()
+    with torch.cuda.device(grad_r.device):
+        lib = nat.lib()
+        wb = _ws_bytes(B, N, M, grad_r.dtype, has_p)
+        ws = torch.empty(wb, dtype=torch.uint8, device=grad_r.device)
+        fb = lib.tw_sdtw_chunk_flags_bytes(B, N, M)
+        flags = torch.empty(fb, dtype=torch.uint8, device=grad_r.device)
+        nat.check(nat.call("sdtw_backward", lib.tw_sdtw_backward_flags_f32, nat.ptr(grad_r),
+                           nat.ptr(grad_p) if has_p else None, B, N, M, float(gamma),
+                           int(has_p), nat.ptr(saved), saved.numel(), nat.ptr(d_cost),
+                           nat.ptr(d_pen) if has_p else None, nat.ptr(flags), fb, nat.ptr(ws),
+                           wb, nat.stream_of(grad_r)), "tw_sdtw_backward_flags")
+    return d_cost, d_pen, flags
+
+
 # ------------------------------------------------- DP on precomputed matrices
 
 @torch.library.custom_op("torchwarp_b200::sdtw_dp", mutates_args=())
@@ -190,21 +212,32 @@ def udtw_fused_backward(X: Tensor, Y: Tensor, vx: Optional[Tensor], vy: Optional
     B, N, D = X.shape
     M = Y.shape[1]
     has_p = vx is not None
-    d_cost, d_pen = _dp_backward(saved, grad_r, grad_p, N, M, gamma, has_p)
+    flags = None
+    if X.dtype == torch.float32 and B:
+        # fp32: the backward flags the chunks of dC / dQ holding a nonzero
+        # value and the chain rule reads only those
+        d_cost, d_pen, flags = _dp_backward_flagged(saved, grad_r, grad_p, N, M, gamma, has_p)
+    else:
+        d_cost, d_pen = _dp_backward(saved, grad_r, grad_p, N, M, gamma, has_p)
     X, Y = X.contiguous(), Y.contiguous()
     dX, dY = torch.empty_like(X), torch.empty_like(Y)
     dvx = torch.zeros_like(vx) if has_p else X.new_zeros(B, N)
     dvy = torch.zeros_like(vy) if has_p else X.new_zeros(B, M)
     if B:
         with torch.cuda.device(X.device):
-            fn = getattr(nat.lib(), "tw_udtw_features_grad_" + nat.suffix(X.dtype))
-            nat.check(nat.call("udtw_features_grad", fn, nat.ptr(X), nat.ptr(Y),
-                               nat.ptr(vx.contiguous() if has_p else None),
-                         nat.ptr(vy.contiguous() if has_p else None), nat.ptr(cost),
-                         nat.ptr(d_cost), nat.ptr(d_pen) if has_p else None, B, N, M, D,
-                         float(beta), float(eps), nat.ptr(dX), nat.ptr(dY),
-                         nat.ptr(dvx) if has_p else None, nat.ptr(dvy) if has_p else None,
-                         nat.stream_of(X)), "tw_udtw_features_grad")
+            args = (nat.ptr(X), nat.ptr(Y), nat.ptr(vx.contiguous() if has_p else None),
+                    nat.ptr(vy.contiguous() if has_p else None), nat.ptr(cost),
+                    nat.ptr(d_cost), nat.ptr(d_pen) if has_p else None)
+            tail = (B, N, M, D, float(beta), float(eps), nat.ptr(dX), nat.ptr(dY),
+                    nat.ptr(dvx) if has_p else None, nat.ptr(dvy) if has_p else None,
+                    nat.stream_of(X))
+            if flags is not None:
+                nat.check(nat.call("udtw_features_grad", nat.lib().tw_udtw_features_grad_flagged_f32,
+                                   *args, nat.ptr(flags), *tail), "tw_udtw_features_grad_flagged")
+            else:
+                fn = getattr(nat.lib(), "tw_udtw_features_grad_" + nat.suffix(X.dtype))
+                nat.check(nat.call("udtw_features_grad", fn, *args, *tail),
+                          "tw_udtw_features_grad")
     return dX, dY, dvx, dvy
 
 
